@@ -1,0 +1,224 @@
+/*
+ * lcpp_b200.h -- C ABI of the B200-native (sm_100a) sort / scan / reduce path.
+ *
+ * Drop-in boundary for LuisaCompute-ParallelPrimitive's Device-level modules
+ * DeviceRadixSort, DeviceScan and DeviceReduce.  Every entry point below names
+ * the reference member function it replaces (path:line inside the reference
+ * project).  Conventions shared by all entry points:
+ *
+ *  - All pointers are device pointers owned by the caller.  The library never
+ *    allocates device memory: scratch ("temp storage") is sized with the
+ *    matching *_temp_bytes query and passed in, exactly like the reference's
+ *    CUB-style GetTempStorageBytes + BufferView<uint> temp_storage pair.
+ *  - Work is enqueued asynchronously on the given cudaStream_t (the reference
+ *    records into a caller CommandList instead).  No host synchronisation
+ *    happens on the hot path.
+ *  - Counts are 64-bit (the reference takes `uint num_items`).
+ *  - Misuse returns a status code instead of aborting (the reference aborts
+ *    through LUISA_ASSERT, src/lcpp/device/device_radix_sort.h:976-1016).
+ *  - Temp storage must be 256-byte aligned; it may be reused by consecutive
+ *    calls on one stream, but two calls that may run concurrently need
+ *    distinct temp storage.
+ */
+#ifndef LCPP_B200_H
+#define LCPP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef struct CUstream_st* lcpp_stream_t;
+
+typedef enum lcpp_status {
+    LCPP_OK = 0,
+    LCPP_ERR_INVALID_ARG = 1,       /* bad pointer, bit range, selector, ... */
+    LCPP_ERR_TEMP_TOO_SMALL = 2,    /* temp_bytes below the *_temp_bytes query */
+    LCPP_ERR_UNSUPPORTED_DTYPE = 3, /* dtype / op combination not provided */
+    LCPP_ERR_CUDA = 4,              /* a CUDA runtime call failed */
+    LCPP_ERR_LOOKBACK_TIMEOUT = 5,  /* a bounded device-side wait expired */
+    LCPP_ERR_COMM = 6,              /* distributed exchange failed */
+    LCPP_ERR_INTERNAL = 7           /* a device-side consistency check failed */
+} lcpp_status;
+
+/* Element types.  Numbering is part of the ABI. */
+typedef enum lcpp_dtype {
+    LCPP_U32 = 0,
+    LCPP_I32 = 1,
+    LCPP_F32 = 2,
+    LCPP_U64 = 3,
+    LCPP_I64 = 4,
+    LCPP_F64 = 5,
+    LCPP_NONE = 255 /* "no values" (keys-only) */
+} lcpp_dtype;
+
+/* Binary operators for scan / reduce (the reference takes DSL lambdas; the
+ * ones its Device modules name are SumOp, MinOp and MaxOp,
+ * src/lcpp/common/thread_operators.h:49-75). */
+typedef enum lcpp_op {
+    LCPP_OP_SUM = 0,
+    LCPP_OP_MIN = 1,
+    LCPP_OP_MAX = 2
+} lcpp_op;
+
+/* Human-readable status name (static storage). */
+const char* lcpp_status_string(lcpp_status status);
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int lcpp_version(void);
+
+/* ------------------------------------------------------------------------
+ * DeviceRadixSort  (src/lcpp/device/device_radix_sort.h)
+ *
+ * Stable LSD radix sort over key bits [begin_bit, end_bit).  Keys are
+ * compared through the reference's order-preserving bijection
+ * (src/lcpp/common/util_type.h:97-175): unsigned keys as is, signed keys with
+ * the sign bit flipped, floating-point keys with all bits flipped when
+ * negative and only the sign bit otherwise; -0.0 and +0.0 produce identical
+ * digits (src/lcpp/agent/radix_rank_sort_operations.h:31-43).  Descending
+ * order inverts the transformed key (radix_rank_sort_operations.h:123-155).
+ * Output keys and values are the original bit patterns.
+ *
+ * Key dtypes: U32, I32, F32, U64, I64, F64.  Value dtypes: any of those
+ * (4- or 8-byte payload, moved bit-exactly).
+ * ---------------------------------------------------------------------- */
+
+/* Replaces DeviceRadixSort::GetSortKeysTempStorageBytes<K>
+ * (device_radix_sort.h:358-362).  n == 0 gives 0 bytes, as the reference
+ * (tests/device_radix_sort_interface_test.cpp:197-203). */
+lcpp_status lcpp_radix_sort_keys_temp_bytes(lcpp_dtype key_dtype, uint64_t num_items,
+                                            size_t* temp_bytes);
+
+/* Replaces DeviceRadixSort::GetSortPairsTempStorageBytes<K,V>
+ * (device_radix_sort.h:351-356). */
+lcpp_status lcpp_radix_sort_pairs_temp_bytes(lcpp_dtype key_dtype, lcpp_dtype value_dtype,
+                                             uint64_t num_items, size_t* temp_bytes);
+
+/* Replaces DeviceRadixSort::SortKeys / SortKeysDescending, copy API
+ * (device_radix_sort.h:399-425 and :457-483).  keys_in is not modified;
+ * the sorted keys land in keys_out.  begin_bit == end_bit copies
+ * (device_radix_sort.h:413-417); num_items == 0 is a no-op. */
+lcpp_status lcpp_radix_sort_keys(void* temp, size_t temp_bytes,
+                                 const void* keys_in, void* keys_out,
+                                 uint64_t num_items, int begin_bit, int end_bit,
+                                 int descending, lcpp_dtype key_dtype,
+                                 lcpp_stream_t stream);
+
+/* Replaces DeviceRadixSort::SortPairs / SortPairsDescending, copy API
+ * (device_radix_sort.h:369-398 and :427-456). */
+lcpp_status lcpp_radix_sort_pairs(void* temp, size_t temp_bytes,
+                                  const void* keys_in, void* keys_out,
+                                  const void* values_in, void* values_out,
+                                  uint64_t num_items, int begin_bit, int end_bit,
+                                  int descending, lcpp_dtype key_dtype,
+                                  lcpp_dtype value_dtype, lcpp_stream_t stream);
+
+/* Replaces the DoubleBuffer overloads of SortKeys / SortKeysDescending
+ * (device_radix_sort.h:497-519 and :533-555).  key_buffers[2] are the two
+ * slots of the reference's DoubleBuffer (src/lcpp/common/util_type.h:57-74);
+ * *selector (0 or 1) names the slot holding the input and is flipped once per
+ * 8-bit pass, so that on return key_buffers[*selector] holds the result.  Both
+ * slots may be overwritten.  Zero items or begin_bit == end_bit leave the
+ * selector unchanged (device_radix_sort.h:507-510). */
+lcpp_status lcpp_radix_sort_keys_double_buffer(void* temp, size_t temp_bytes,
+                                               void* key_buffers[2], int* selector,
+                                               uint64_t num_items, int begin_bit, int end_bit,
+                                               int descending, lcpp_dtype key_dtype,
+                                               lcpp_stream_t stream);
+
+/* Replaces the DoubleBuffer overloads of SortPairs / SortPairsDescending
+ * (device_radix_sort.h:484-495, :520-531, dispatch_double_buffer :951-974).
+ * One selector serves keys and values (the reference asserts they match). */
+lcpp_status lcpp_radix_sort_pairs_double_buffer(void* temp, size_t temp_bytes,
+                                                void* key_buffers[2], void* value_buffers[2],
+                                                int* selector, uint64_t num_items,
+                                                int begin_bit, int end_bit, int descending,
+                                                lcpp_dtype key_dtype, lcpp_dtype value_dtype,
+                                                lcpp_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * DeviceScan  (src/lcpp/device/device_scan.h)
+ *
+ * Single-pass decoupled look-back scan.  dtypes: I32, U32 (wrapping
+ * two's-complement arithmetic), F32, I64, U64, F64.  In-place operation
+ * (d_in == d_out) is allowed, as in the reference
+ * (tests/device_scan_test.cpp:288-322).
+ * ---------------------------------------------------------------------- */
+
+/* Replaces DeviceScan::GetTempStorageBytes<T> (device_scan.h:295-308). */
+lcpp_status lcpp_scan_temp_bytes(lcpp_dtype dtype, uint64_t num_items, size_t* temp_bytes);
+
+/* Replaces DeviceScan::ExclusiveScan (device_scan.h:321-332):
+ * out[i] = init (+) in[0] (+) ... (+) in[i-1].  `init` points to one host
+ * value of `dtype`.  ExclusiveSum (device_scan.h:370-385) is op = SUM with a
+ * zero init. */
+lcpp_status lcpp_scan_exclusive(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                                uint64_t num_items, lcpp_op op, const void* init,
+                                lcpp_dtype dtype, lcpp_stream_t stream);
+
+/* Replaces DeviceScan::InclusiveScan without an initial value
+ * (device_scan.h:333-344): out[i] = in[0] (+) ... (+) in[i].
+ * InclusiveSum (device_scan.h:408-419) is op = SUM. */
+lcpp_status lcpp_scan_inclusive(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                                uint64_t num_items, lcpp_op op, lcpp_dtype dtype,
+                                lcpp_stream_t stream);
+
+/* Replaces DeviceScan::InclusiveScanInit and the InclusiveScan overload with
+ * an initial value (device_scan.h:346-368): out[i] = init (+) in[0] (+) ... (+) in[i]. */
+lcpp_status lcpp_scan_inclusive_init(void* temp, size_t temp_bytes, const void* d_in,
+                                     void* d_out, uint64_t num_items, lcpp_op op,
+                                     const void* init, lcpp_dtype dtype, lcpp_stream_t stream);
+
+/* Convenience forms of the two Sum entry points (device_scan.h:370-419). */
+lcpp_status lcpp_scan_exclusive_sum(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                                    uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
+lcpp_status lcpp_scan_inclusive_sum(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                                    uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * DeviceReduce  (src/lcpp/device/device_reduce.h)
+ *
+ * Deterministic two-level reduction: a fixed partition of the input over a
+ * persistent grid, then a fixed-order fold of the per-block partials, so a
+ * floating-point result is identical from run to run.
+ * ---------------------------------------------------------------------- */
+
+/* Replaces DeviceReduce::GetTempStorageBytes<T> (device_reduce.h:183-189). */
+lcpp_status lcpp_reduce_temp_bytes(lcpp_dtype dtype, uint64_t num_items, size_t* temp_bytes);
+
+/* Replaces DeviceReduce::Reduce (device_reduce.h:229-252):
+ * *d_out = init (+) in[0] (+) ... (+) in[n-1]; n == 0 writes init. */
+lcpp_status lcpp_reduce(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                        uint64_t num_items, lcpp_op op, const void* init, lcpp_dtype dtype,
+                        lcpp_stream_t stream);
+
+/* Replaces DeviceReduce::Sum (init 0), Min (init numeric max) and Max (init
+ * numeric lowest) (device_reduce.h:280-308). */
+lcpp_status lcpp_reduce_sum(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                            uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
+lcpp_status lcpp_reduce_min(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                            uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
+lcpp_status lcpp_reduce_max(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                            uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Device diagnostics (no reference counterpart: the reference's look-back
+ * spins are unbounded, src/lcpp/agent/agent_radix_sort_onesweep.h:324-334).
+ *
+ * Every device-side wait in the kernels above is bounded.  When one expires
+ * the kernel records LCPP_ERR_LOOKBACK_TIMEOUT in a status word inside the
+ * temp storage of that call and returns normally.  This call synchronises
+ * `stream`, reads that word and returns it (LCPP_OK when clear).  `temp` must
+ * be the temp storage of the call being checked and must not have been
+ * reused since.
+ * ---------------------------------------------------------------------- */
+lcpp_status lcpp_device_status(const void* temp, lcpp_stream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* LCPP_B200_H */

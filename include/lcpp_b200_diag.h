@@ -1,0 +1,45 @@
+/*
+ * lcpp_b200_diag.h -- kernel timing hooks of liblcpp_b200.
+ *
+ * No counterpart in the reference (its timing lives in the benchmark,
+ * tests/lcpp_cub_bench.cpp:225-260).  When enabled, every kernel the library
+ * launches is bracketed by two CUDA events recorded on the launch stream, so
+ * a benchmark can attribute device time to the individual kernels of one
+ * sort / scan / reduce call.  Disabled by default; when disabled the hooks
+ * cost one relaxed atomic load per launch.
+ */
+#ifndef LCPP_B200_DIAG_H
+#define LCPP_B200_DIAG_H
+
+#include "lcpp_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum lcpp_kernel_kind {
+    LCPP_KERNEL_SORT_HISTOGRAM = 0, /* all-pass digit histogram + digit offsets */
+    LCPP_KERNEL_SORT_ONESWEEP = 1,  /* one 8-bit onesweep pass */
+    LCPP_KERNEL_SCAN = 2,           /* decoupled look-back scan */
+    LCPP_KERNEL_REDUCE = 3          /* two-level reduce */
+} lcpp_kernel_kind;
+
+typedef struct lcpp_kernel_time {
+    int kind;          /* lcpp_kernel_kind */
+    float ms;          /* device time between the launch's two events */
+    uint64_t items;    /* items the launch processed */
+} lcpp_kernel_time;
+
+/* Enable (1) or disable (0) event recording, process-wide.  Enabling clears
+ * earlier records. */
+lcpp_status lcpp_diag_timing_enable(int enable);
+
+/* Synchronise the recorded events and copy up to `capacity` records (in
+ * launch order) to `out`; *count receives the number of records held. */
+lcpp_status lcpp_diag_timing_read(lcpp_kernel_time* out, int capacity, int* count);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* LCPP_B200_DIAG_H */

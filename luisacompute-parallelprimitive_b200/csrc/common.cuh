@@ -1,0 +1,175 @@
+// common.cuh -- shared device helpers for the sm_100a sort / scan / reduce
+// kernels: dtype plumbing, relaxed GPU-scope status-word access, bounded
+// waits and the radix key bijection.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <type_traits>
+
+#include "../../include/lcpp_b200.h"
+
+namespace lcpp {
+
+constexpr int kWarp = 32;
+constexpr size_t kTempAlign = 256;  // every temp sub-buffer starts 256-B aligned
+
+__host__ __device__ constexpr size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+__host__ __device__ constexpr uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
+
+inline int dtype_bytes(lcpp_dtype dt)
+{
+    switch (dt) {
+    case LCPP_U32: case LCPP_I32: case LCPP_F32: return 4;
+    case LCPP_U64: case LCPP_I64: case LCPP_F64: return 8;
+    default: return 0;
+    }
+}
+
+// Device-side error word values (written into temp storage; read back by
+// lcpp_device_status).
+constexpr uint32_t kDevErrTimeout = LCPP_ERR_LOOKBACK_TIMEOUT;
+constexpr uint32_t kDevErrInternal = LCPP_ERR_INTERNAL;
+
+// A bounded wait gives up after this many nanoseconds of %globaltimer.  A
+// legitimate wait in these kernels is a few microseconds (one predecessor
+// tile publishing its partial); the bound only exists so that a broken
+// protocol reports an error instead of hanging the GPU.
+constexpr uint64_t kWaitLimitNs = 4000000000ull;
+
+__device__ __forceinline__ uint64_t global_timer_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t lanemask_lt()
+{
+    uint32_t m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
+// Relaxed GPU-scope loads / stores of self-contained status words: each word
+// carries its own flag and value, so no ordering with other data is needed.
+__device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p)
+{
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t ld_relaxed(const uint64_t* p)
+{
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed(uint32_t* p, uint32_t v)
+{
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed(uint64_t* p, uint64_t v)
+{
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Non-zero once any thread of the call recorded an error.
+__device__ __forceinline__ bool error_raised(const uint32_t* err)
+{
+    return err && ld_relaxed(err) != 0u;
+}
+
+// Record a device error once (first writer wins).
+__device__ __forceinline__ void report_error(uint32_t* err, uint32_t code)
+{
+    if (err) atomicCAS(err, 0u, code);
+}
+
+// ---------------------------------------------------------------------------
+// Radix key bijection.
+//
+// The reference maps keys to order-preserving unsigned bits with
+// Traits<T>::TwiddleIn (src/lcpp/common/util_type.h:97-175), inverts them for
+// descending order (src/lcpp/agent/radix_rank_sort_operations.h:123-155) and
+// folds -0.0 onto +0.0 before extracting digits (same file, :31-43).  All
+// three key kinds and both directions reduce to one formula with two XOR
+// masks chosen by the key's sign bit, so one kernel serves every key dtype of
+// a given width:
+//   unsigned : pos = neg = 0            (descending: ~0)
+//   signed   : pos = neg = HIGH         (descending: ~HIGH)
+//   float    : pos = HIGH, neg = ~0     (descending: ~HIGH, 0)
+// and for float keys +-0.0 map to HIGH in both directions (the transformed
+// +0.0 in ascending order, and the value the reference's fold produces in
+// descending order).
+// ---------------------------------------------------------------------------
+template <typename U>
+struct KeyCodec {
+    U xor_pos;
+    U xor_neg;
+    uint32_t fold_zero;  // 1 for floating-point keys
+};
+
+template <typename U>
+__device__ __forceinline__ U transform_key(U k, const KeyCodec<U>& c)
+{
+    constexpr int kBits = sizeof(U) * 8;
+    constexpr U kHigh = U(1) << (kBits - 1);
+    using S = typename std::conditional<sizeof(U) == 4, int32_t, int64_t>::type;
+    const U sign = U(S(k) >> (kBits - 1));  // all ones when the high bit is set
+    U t = k ^ (c.xor_pos ^ (sign & (c.xor_pos ^ c.xor_neg)));
+    if (c.fold_zero && U(k << 1) == U(0)) t = kHigh;
+    return t;
+}
+
+template <typename U>
+inline KeyCodec<U> make_codec(lcpp_dtype dt, bool descending)
+{
+    constexpr int kBits = sizeof(U) * 8;
+    constexpr U kHigh = U(1) << (kBits - 1);
+    KeyCodec<U> c{};
+    switch (dt) {
+    case LCPP_I32: case LCPP_I64: c.xor_pos = kHigh; c.xor_neg = kHigh; break;
+    case LCPP_F32: case LCPP_F64: c.xor_pos = kHigh; c.xor_neg = U(~U(0)); c.fold_zero = 1; break;
+    default: c.xor_pos = 0; c.xor_neg = 0; break;
+    }
+    if (descending) {
+        c.xor_pos = U(~c.xor_pos);
+        c.xor_neg = U(~c.xor_neg);
+    }
+    return c;
+}
+
+// Cached per-device SM count (grid sizing in multiples of the SM count).
+int device_sm_count();
+
+// Raise a kernel's dynamic shared-memory limit on the current device (once
+// per kernel, device and size).
+void set_max_dynamic_smem(const void* kernel, size_t bytes);
+
+namespace diag {
+// Brackets one kernel launch with CUDA events when timing is enabled
+// (lcpp_diag_timing_enable); otherwise a no-op.
+class KernelTimer {
+public:
+    KernelTimer(int kind, uint64_t items, cudaStream_t stream);
+    void stop();
+    ~KernelTimer() { stop(); }
+
+private:
+    int index_;
+    cudaStream_t stream_;
+};
+}  // namespace diag
+
+}  // namespace lcpp
+
+#define LCPP_CUDA_TRY(expr)                              \
+    do {                                                 \
+        cudaError_t _e = (expr);                         \
+        if (_e != cudaSuccess) return LCPP_ERR_CUDA;     \
+    } while (0)

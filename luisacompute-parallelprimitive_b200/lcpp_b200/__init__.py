@@ -1,0 +1,358 @@
+"""Python front end of liblcpp_b200 (sm_100a sort / scan / reduce).
+
+A thin ctypes layer over the C ABI in ``include/lcpp_b200.h`` plus class
+wrappers that mirror the reference's Device-level modules
+(``DeviceRadixSort``, ``DeviceScan``, ``DeviceReduce`` in
+``src/lcpp/device/``): same method names, same argument order, CUB-style
+temp-storage queries.  Device buffers are torch CUDA tensors (torch is only
+the allocator and stream provider here); every call enqueues on the current
+torch CUDA stream unless a stream is given.
+
+There is no CPU fallback: if ``liblcpp_b200.so`` has not been built, importing
+the library raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "liblcpp_b200.so"
+
+# lcpp_status
+OK, ERR_INVALID_ARG, ERR_TEMP_TOO_SMALL, ERR_UNSUPPORTED_DTYPE = 0, 1, 2, 3
+ERR_CUDA, ERR_LOOKBACK_TIMEOUT, ERR_COMM, ERR_INTERNAL = 4, 5, 6, 7
+# lcpp_dtype
+U32, I32, F32, U64, I64, F64, NONE = 0, 1, 2, 3, 4, 5, 255
+# lcpp_op
+OP_SUM, OP_MIN, OP_MAX = 0, 1, 2
+# lcpp_testgen_dist
+GEN_U32_UNIFORM, GEN_U32_AND3, GEN_U32_CONST, GEN_U64_UNIFORM = 0, 1, 2, 3
+GEN_I32_SCAN, GEN_F32_UNIT, GEN_I64_UNIFORM, GEN_U32_INDEX = 4, 5, 6, 7
+GEN_F32_NORMAL, GEN_U32_ZIPF = 8, 9
+
+# lcpp_kernel_kind
+KERNEL_SORT_HISTOGRAM, KERNEL_SORT_ONESWEEP, KERNEL_SCAN, KERNEL_REDUCE = 0, 1, 2, 3
+
+_lib = None
+
+
+class KernelTime(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int), ("ms", ctypes.c_float), ("items", ctypes.c_uint64)]
+
+
+class LcppError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        name = lib().lcpp_status_string(status).decode() if _lib is not None else str(status)
+        super().__init__(f"{what}: {name}")
+
+
+def lib() -> ctypes.CDLL:
+    """Load liblcpp_b200.so (raises when it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with "
+            "`python luisacompute-parallelprimitive_b200/build.py` (no CPU fallback exists)")
+    l = ctypes.CDLL(str(LIB_PATH))
+    vp, sz, u64, i = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_int
+    szp = ctypes.POINTER(ctypes.c_size_t)
+    ip = ctypes.POINTER(ctypes.c_int)
+    vpa = ctypes.c_void_p * 2
+    sigs = {
+        "lcpp_status_string": ([i], ctypes.c_char_p),
+        "lcpp_version": ([], i),
+        "lcpp_radix_sort_keys_temp_bytes": ([i, u64, szp], i),
+        "lcpp_radix_sort_pairs_temp_bytes": ([i, i, u64, szp], i),
+        "lcpp_radix_sort_keys": ([vp, sz, vp, vp, u64, i, i, i, i, vp], i),
+        "lcpp_radix_sort_pairs": ([vp, sz, vp, vp, vp, vp, u64, i, i, i, i, i, vp], i),
+        "lcpp_radix_sort_keys_double_buffer": ([vp, sz, vpa, ip, u64, i, i, i, i, vp], i),
+        "lcpp_radix_sort_pairs_double_buffer": ([vp, sz, vpa, vpa, ip, u64, i, i, i, i, i, vp], i),
+        "lcpp_scan_temp_bytes": ([i, u64, szp], i),
+        "lcpp_scan_exclusive": ([vp, sz, vp, vp, u64, i, vp, i, vp], i),
+        "lcpp_scan_inclusive": ([vp, sz, vp, vp, u64, i, i, vp], i),
+        "lcpp_scan_inclusive_init": ([vp, sz, vp, vp, u64, i, vp, i, vp], i),
+        "lcpp_scan_exclusive_sum": ([vp, sz, vp, vp, u64, i, vp], i),
+        "lcpp_scan_inclusive_sum": ([vp, sz, vp, vp, u64, i, vp], i),
+        "lcpp_reduce_temp_bytes": ([i, u64, szp], i),
+        "lcpp_reduce": ([vp, sz, vp, vp, u64, i, vp, i, vp], i),
+        "lcpp_reduce_sum": ([vp, sz, vp, vp, u64, i, vp], i),
+        "lcpp_reduce_min": ([vp, sz, vp, vp, u64, i, vp], i),
+        "lcpp_reduce_max": ([vp, sz, vp, vp, u64, i, vp], i),
+        "lcpp_device_status": ([vp, vp], i),
+        "lcpp_testgen_fill": ([vp, u64, u64, u64, i, vp], i),
+        "lcpp_diag_timing_enable": ([i], i),
+        "lcpp_diag_timing_read": ([ctypes.POINTER(KernelTime), i, ip], i),
+    }
+    for name, (args, res) in sigs.items():
+        f = getattr(l, name)
+        f.argtypes = args
+        f.restype = res
+    _lib = l
+    return l
+
+
+def check(status: int, what: str) -> None:
+    if status != OK:
+        raise LcppError(status, what)
+
+
+# ---------------------------------------------------------------------------
+# torch helpers (plumbing only)
+# ---------------------------------------------------------------------------
+def _torch():
+    import torch
+    return torch
+
+
+def dtype_code(t) -> int:
+    torch = _torch()
+    m = {torch.uint32: U32, torch.int32: I32, torch.float32: F32, torch.uint64: U64,
+         torch.int64: I64, torch.float64: F64}
+    if t.dtype not in m:
+        raise TypeError(f"unsupported dtype {t.dtype}")
+    return m[t.dtype]
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    torch = _torch()
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def _host_scalar(value, code):
+    import numpy as np
+    np_t = {U32: np.uint32, I32: np.int32, F32: np.float32, U64: np.uint64, I64: np.int64,
+            F64: np.float64}[code]
+    arr = np.array([value], dtype=np_t)
+    return arr, ctypes.c_void_p(arr.ctypes.data)
+
+
+def alloc_temp(nbytes: int, device=None):
+    """A 256-byte aligned uint8 CUDA tensor of at least nbytes (>= 1)."""
+    torch = _torch()
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device or "cuda")
+
+
+# ---------------------------------------------------------------------------
+# Reference-shaped module wrappers
+# ---------------------------------------------------------------------------
+class DoubleBuffer:
+    """Mirror of the reference's DoubleBuffer<T> (src/lcpp/common/util_type.h:57-74)."""
+
+    def __init__(self, current, alternate, selector: int = 0):
+        self.d_buffers = [current, alternate]
+        self.selector = selector
+
+    def current(self):
+        return self.d_buffers[self.selector]
+
+    def alternate(self):
+        return self.d_buffers[self.selector ^ 1]
+
+
+def _bit_range(rest):
+    """(begin_bit, end_bit) from trailing positional arguments; end None = key width."""
+    if len(rest) > 2:
+        raise TypeError("too many arguments")
+    begin = rest[0] if len(rest) >= 1 else 0
+    end = rest[1] if len(rest) == 2 else None
+    return begin, end
+
+
+class DeviceRadixSort:
+    """Mirror of lcpp::DeviceRadixSort (src/lcpp/device/device_radix_sort.h:50-1489)."""
+
+    @staticmethod
+    def GetSortKeysTempStorageBytes(key_dtype: int, num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_radix_sort_keys_temp_bytes(key_dtype, num_items, ctypes.byref(out)),
+              "GetSortKeysTempStorageBytes")
+        return out.value
+
+    @staticmethod
+    def GetSortPairsTempStorageBytes(key_dtype: int, value_dtype: int, num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_radix_sort_pairs_temp_bytes(key_dtype, value_dtype, num_items,
+                                                     ctypes.byref(out)),
+              "GetSortPairsTempStorageBytes")
+        return out.value
+
+    def _keys(self, temp, kin, kout, n, begin, end, desc, stream):
+        kd = dtype_code(kin)
+        end = kin.element_size() * 8 if end is None else end
+        check(lib().lcpp_radix_sort_keys(_ptr(temp), temp.numel() if temp is not None else 0,
+                                         _ptr(kin), _ptr(kout), n, begin, end, int(desc), kd,
+                                         _stream(stream)), "SortKeys")
+
+    def _pairs(self, temp, kin, kout, vin, vout, n, begin, end, desc, stream):
+        kd, vd = dtype_code(kin), dtype_code(vin)
+        end = kin.element_size() * 8 if end is None else end
+        check(lib().lcpp_radix_sort_pairs(_ptr(temp), temp.numel() if temp is not None else 0,
+                                          _ptr(kin), _ptr(kout), _ptr(vin), _ptr(vout), n, begin,
+                                          end, int(desc), kd, vd, _stream(stream)), "SortPairs")
+
+    # Overloads as in the reference: copy form (temp, keys_in, keys_out, n, begin, end) and
+    # DoubleBuffer form (temp, keys_db, n, begin, end) (device_radix_sort.h:369-555).
+    def SortKeys(self, temp, *args, stream=None):
+        self._dispatch_keys(temp, args, False, stream)
+
+    def SortKeysDescending(self, temp, *args, stream=None):
+        self._dispatch_keys(temp, args, True, stream)
+
+    # Copy form (temp, keys_in, keys_out, values_in, values_out, n, begin, end) and
+    # DoubleBuffer form (temp, keys_db, values_db, n, begin, end).
+    def SortPairs(self, temp, *args, stream=None):
+        self._dispatch_pairs(temp, args, False, stream)
+
+    def SortPairsDescending(self, temp, *args, stream=None):
+        self._dispatch_pairs(temp, args, True, stream)
+
+    def _dispatch_keys(self, temp, args, desc, stream):
+        if isinstance(args[0], DoubleBuffer):
+            db, n, *rest = args
+            begin, end = _bit_range(rest)
+            return self._keys_db(temp, db, n, begin, end, desc, stream)
+        kin, kout, n, *rest = args
+        begin, end = _bit_range(rest)
+        self._keys(temp, kin, kout, n, begin, end, desc, stream)
+
+    def _dispatch_pairs(self, temp, args, desc, stream):
+        if isinstance(args[0], DoubleBuffer):
+            kdb, vdb, n, *rest = args
+            begin, end = _bit_range(rest)
+            return self._pairs_db(temp, kdb, vdb, n, begin, end, desc, stream)
+        kin, kout, vin, vout, n, *rest = args
+        begin, end = _bit_range(rest)
+        self._pairs(temp, kin, kout, vin, vout, n, begin, end, desc, stream)
+
+    # DoubleBuffer forms: SortKeys(temp, db, n, begin, end)
+    def _keys_db(self, temp, db, n, begin, end, desc, stream):
+        kd = dtype_code(db.d_buffers[0])
+        end = db.d_buffers[0].element_size() * 8 if end is None else end
+        bufs = (ctypes.c_void_p * 2)(db.d_buffers[0].data_ptr(), db.d_buffers[1].data_ptr())
+        sel = ctypes.c_int(db.selector)
+        check(lib().lcpp_radix_sort_keys_double_buffer(
+            _ptr(temp), temp.numel() if temp is not None else 0, bufs, ctypes.byref(sel), n,
+            begin, end, int(desc), kd, _stream(stream)), "SortKeys(DoubleBuffer)")
+        db.selector = sel.value
+
+    def _pairs_db(self, temp, kdb, vdb, n, begin, end, desc, stream):
+        if kdb.selector != vdb.selector:
+            raise LcppError(ERR_INVALID_ARG, "key and value DoubleBuffer selectors must match")
+        kd, vd = dtype_code(kdb.d_buffers[0]), dtype_code(vdb.d_buffers[0])
+        end = kdb.d_buffers[0].element_size() * 8 if end is None else end
+        kb = (ctypes.c_void_p * 2)(kdb.d_buffers[0].data_ptr(), kdb.d_buffers[1].data_ptr())
+        vb = (ctypes.c_void_p * 2)(vdb.d_buffers[0].data_ptr(), vdb.d_buffers[1].data_ptr())
+        sel = ctypes.c_int(kdb.selector)
+        check(lib().lcpp_radix_sort_pairs_double_buffer(
+            _ptr(temp), temp.numel() if temp is not None else 0, kb, vb, ctypes.byref(sel), n,
+            begin, end, int(desc), kd, vd, _stream(stream)), "SortPairs(DoubleBuffer)")
+        kdb.selector = vdb.selector = sel.value
+
+
+class DeviceScan:
+    """Mirror of lcpp::DeviceScan (src/lcpp/device/device_scan.h:40-1560)."""
+
+    @staticmethod
+    def GetTempStorageBytes(dtype: int, num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_scan_temp_bytes(dtype, num_items, ctypes.byref(out)), "GetTempStorageBytes")
+        return out.value
+
+    def ExclusiveSum(self, temp, d_in, d_out, num_items, stream=None):
+        check(lib().lcpp_scan_exclusive_sum(_ptr(temp), temp.numel() if temp is not None else 0,
+                                            _ptr(d_in), _ptr(d_out), num_items, dtype_code(d_in),
+                                            _stream(stream)), "ExclusiveSum")
+
+    def InclusiveSum(self, temp, d_in, d_out, num_items, stream=None):
+        check(lib().lcpp_scan_inclusive_sum(_ptr(temp), temp.numel() if temp is not None else 0,
+                                            _ptr(d_in), _ptr(d_out), num_items, dtype_code(d_in),
+                                            _stream(stream)), "InclusiveSum")
+
+    def ExclusiveScan(self, temp, d_in, d_out, num_items, op, initial_value, stream=None):
+        code = dtype_code(d_in)
+        keep, init = _host_scalar(initial_value, code)
+        check(lib().lcpp_scan_exclusive(_ptr(temp), temp.numel() if temp is not None else 0,
+                                        _ptr(d_in), _ptr(d_out), num_items, op, init, code,
+                                        _stream(stream)), "ExclusiveScan")
+        del keep
+
+    def InclusiveScan(self, temp, d_in, d_out, num_items, op, initial_value=None, stream=None):
+        code = dtype_code(d_in)
+        if initial_value is None:
+            check(lib().lcpp_scan_inclusive(_ptr(temp), temp.numel() if temp is not None else 0,
+                                            _ptr(d_in), _ptr(d_out), num_items, op, code,
+                                            _stream(stream)), "InclusiveScan")
+        else:
+            self.InclusiveScanInit(temp, d_in, d_out, num_items, op, initial_value, stream)
+
+    def InclusiveScanInit(self, temp, d_in, d_out, num_items, op, initial_value, stream=None):
+        code = dtype_code(d_in)
+        keep, init = _host_scalar(initial_value, code)
+        check(lib().lcpp_scan_inclusive_init(_ptr(temp), temp.numel() if temp is not None else 0,
+                                             _ptr(d_in), _ptr(d_out), num_items, op, init, code,
+                                             _stream(stream)), "InclusiveScanInit")
+        del keep
+
+
+class DeviceReduce:
+    """Mirror of lcpp::DeviceReduce (src/lcpp/device/device_reduce.h:102-1187)."""
+
+    @staticmethod
+    def GetTempStorageBytes(dtype: int, num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_reduce_temp_bytes(dtype, num_items, ctypes.byref(out)), "GetTempStorageBytes")
+        return out.value
+
+    def Reduce(self, temp, d_in, d_out, num_items, op, initial_value, stream=None):
+        code = dtype_code(d_in)
+        keep, init = _host_scalar(initial_value, code)
+        check(lib().lcpp_reduce(_ptr(temp), temp.numel() if temp is not None else 0, _ptr(d_in),
+                                _ptr(d_out), num_items, op, init, code, _stream(stream)), "Reduce")
+        del keep
+
+    def _named(self, fn, temp, d_in, d_out, num_items, stream, what):
+        check(fn(_ptr(temp), temp.numel() if temp is not None else 0, _ptr(d_in), _ptr(d_out),
+                 num_items, dtype_code(d_out), _stream(stream)), what)
+
+    def Sum(self, temp, d_in, d_out, num_items, stream=None):
+        self._named(lib().lcpp_reduce_sum, temp, d_in, d_out, num_items, stream, "Sum")
+
+    def Min(self, temp, d_in, d_out, num_items, stream=None):
+        self._named(lib().lcpp_reduce_min, temp, d_in, d_out, num_items, stream, "Min")
+
+    def Max(self, temp, d_in, d_out, num_items, stream=None):
+        self._named(lib().lcpp_reduce_max, temp, d_in, d_out, num_items, stream, "Max")
+
+
+def device_status(temp, stream=None) -> int:
+    """Synchronise and read the device error word of the call that used `temp`."""
+    return lib().lcpp_device_status(_ptr(temp), _stream(stream))
+
+
+def testgen_fill(dst, dist: int, seed: int, offset: int = 0, stream=None) -> None:
+    check(lib().lcpp_testgen_fill(_ptr(dst), dst.numel(), offset, seed, dist, _stream(stream)),
+          "testgen_fill")
+
+
+def diag_timing_enable(enable: bool) -> None:
+    """Record CUDA events around every library kernel launch (lcpp_b200_diag.h)."""
+    check(lib().lcpp_diag_timing_enable(int(enable)), "diag_timing_enable")
+
+
+def diag_timing_read() -> list[tuple[int, float, int]]:
+    """(kind, ms, items) of every launch recorded since timing was enabled."""
+    count = ctypes.c_int()
+    check(lib().lcpp_diag_timing_read(None, 0, ctypes.byref(count)), "diag_timing_read")
+    buf = (KernelTime * max(count.value, 1))()
+    check(lib().lcpp_diag_timing_read(buf, count.value, ctypes.byref(count)), "diag_timing_read")
+    return [(buf[i].kind, buf[i].ms, buf[i].items) for i in range(count.value)]

@@ -1,0 +1,147 @@
+"""ctypes front end of the CPU oracle (TEST INFRASTRUCTURE ONLY).
+
+The oracle is the checker for the CUDA library and the timed CPU baseline.
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+leg import this module; the product path never does.
+
+Every function takes and returns numpy arrays.  The C source
+(``oracle/lcpp_oracle.c``) cites the reference file:line each routine
+restates.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+_HERE = Path(__file__).resolve().parent
+_LIB_PATH = _HERE / "_build" / "liblcpp_oracle.so"
+
+# lcpp_dtype codes (include/lcpp_b200.h)
+U32, I32, F32, U64, I64, F64 = 0, 1, 2, 3, 4, 5
+OP_SUM, OP_MIN, OP_MAX = 0, 1, 2
+
+NP_TO_DTYPE = {
+    np.dtype(np.uint32): U32,
+    np.dtype(np.int32): I32,
+    np.dtype(np.float32): F32,
+    np.dtype(np.uint64): U64,
+    np.dtype(np.int64): I64,
+    np.dtype(np.float64): F64,
+}
+
+# generator codes (oracle_generate)
+GEN_U32_UNIFORM, GEN_U32_AND3, GEN_U32_CONST, GEN_U64_UNIFORM = 0, 1, 2, 3
+GEN_I32_SCAN, GEN_F32_UNIT, GEN_I64_UNIFORM, GEN_U32_INDEX = 4, 5, 6, 7
+GEN_NP_DTYPE = {
+    GEN_U32_UNIFORM: np.uint32, GEN_U32_AND3: np.uint32, GEN_U32_CONST: np.uint32,
+    GEN_U64_UNIFORM: np.uint64, GEN_I32_SCAN: np.int32, GEN_F32_UNIT: np.float32,
+    GEN_I64_UNIFORM: np.int64, GEN_U32_INDEX: np.uint32,
+}
+
+_lib = None
+
+
+def build() -> Path:
+    """Compile the oracle with its Makefile (idempotent)."""
+    subprocess.run(["make", "-s", "-C", str(_HERE)], check=True)
+    return _LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not _LIB_PATH.exists():
+            build()
+        l = ctypes.CDLL(str(_LIB_PATH))
+        vp, u64, i = ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int
+        l.oracle_radix_sort.argtypes = [vp, vp, vp, vp, u64, i, i, i, i, i, i]
+        l.oracle_radix_sort.restype = i
+        l.oracle_digit.argtypes = [u64, i, i, i, i]
+        l.oracle_digit.restype = ctypes.c_uint32
+        l.oracle_scan.argtypes = [vp, vp, u64, i, i, i, vp]
+        l.oracle_scan.restype = i
+        l.oracle_reduce.argtypes = [vp, vp, u64, i, i, vp]
+        l.oracle_reduce.restype = i
+        l.oracle_sum_f64.argtypes = [vp, u64, i]
+        l.oracle_sum_f64.restype = ctypes.c_double
+        l.oracle_generate.argtypes = [vp, u64, u64, u64, i]
+        l.oracle_generate.restype = i
+        _lib = l
+    return _lib
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def radix_sort(keys: np.ndarray, values: np.ndarray | None = None, begin_bit: int = 0,
+               end_bit: int | None = None, descending: bool = False, threads: int = 1):
+    """Stable LSD radix sort with the reference's semantics.
+
+    Returns ``keys_out`` or ``(keys_out, values_out)``.
+    """
+    keys = np.ascontiguousarray(keys)
+    kd = NP_TO_DTYPE[keys.dtype]
+    if end_bit is None:
+        end_bit = keys.dtype.itemsize * 8
+    kout = np.empty_like(keys)
+    vout = None
+    vbytes = 0
+    if values is not None:
+        values = np.ascontiguousarray(values)
+        assert values.shape == keys.shape
+        vbytes = values.dtype.itemsize
+        vout = np.empty_like(values)
+    rc = lib().oracle_radix_sort(_ptr(keys), _ptr(kout), _ptr(values), _ptr(vout), keys.size,
+                                 begin_bit, end_bit, int(descending), kd, vbytes, threads)
+    if rc != 0:
+        raise ValueError(f"oracle_radix_sort failed with {rc}")
+    return kout if values is None else (kout, vout)
+
+
+def digit(key: int, dtype, descending: bool, bit_start: int, num_bits: int) -> int:
+    return int(lib().oracle_digit(int(key), NP_TO_DTYPE[np.dtype(dtype)], int(descending),
+                                  bit_start, num_bits))
+
+
+def scan(x: np.ndarray, mode: str, op: int = OP_SUM, init=None) -> np.ndarray:
+    """mode: 'exclusive' (needs init), 'inclusive', 'inclusive_init' (needs init)."""
+    x = np.ascontiguousarray(x)
+    out = np.empty_like(x)
+    m = {"exclusive": 0, "inclusive": 1, "inclusive_init": 2}[mode]
+    init_arr = None if init is None else np.array([init], dtype=x.dtype)
+    rc = lib().oracle_scan(_ptr(x), _ptr(out), x.size, NP_TO_DTYPE[x.dtype], op, m, _ptr(init_arr))
+    if rc != 0:
+        raise ValueError(f"oracle_scan failed with {rc}")
+    return out
+
+
+def reduce(x: np.ndarray, op: int, init):
+    x = np.ascontiguousarray(x)
+    out = np.empty(1, dtype=x.dtype)
+    init_arr = np.array([init], dtype=x.dtype)
+    rc = lib().oracle_reduce(_ptr(x), _ptr(out), x.size, NP_TO_DTYPE[x.dtype], op, _ptr(init_arr))
+    if rc != 0:
+        raise ValueError(f"oracle_reduce failed with {rc}")
+    return out[0]
+
+
+def sum_f64(x: np.ndarray) -> float:
+    x = np.ascontiguousarray(x)
+    return float(lib().oracle_sum_f64(_ptr(x), x.size, NP_TO_DTYPE[x.dtype]))
+
+
+def generate(dist: int, n: int, seed: int, offset: int = 0) -> np.ndarray:
+    out = np.empty(n, dtype=GEN_NP_DTYPE[dist])
+    rc = lib().oracle_generate(_ptr(out), n, offset, seed, dist)
+    if rc != 0:
+        raise ValueError(f"oracle_generate failed with {rc}")
+    return out
+
+
+def cpu_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)

@@ -1,0 +1,240 @@
+// make_golden.cpp -- writes the golden fixtures for the sort / scan / reduce
+// parity tests.
+//
+// Inputs follow the input generators of the reference project's own tests and
+// expected outputs come from the host algorithms those tests check the GPU
+// against (std::sort, std::stable_sort with a selected-bits comparator,
+// std::inclusive_scan / std::exclusive_scan, std::min_element ...).  Each case
+// names the reference test it follows (path:line inside the reference
+// project).  Sizes are cut down where the reference's would make the fixture
+// file large; the generator formulas are unchanged.
+//
+// Output: one raw file per array into the directory given as argv[1], plus
+// an index file "arrays.txt" with lines "<name> <dtype> <count>".
+// tests/golden/make_golden.py compiles and runs this program and packs the
+// result into golden.npz.
+#include <algorithm>
+#include <cstdint>
+#include <cstdio>
+#include <functional>
+#include <numeric>
+#include <random>
+#include <string>
+#include <vector>
+
+static std::string g_dir;
+static FILE* g_index = nullptr;
+
+template <typename T>
+static const char* dtype_name();
+template <> const char* dtype_name<uint32_t>() { return "u32"; }
+template <> const char* dtype_name<int32_t>() { return "i32"; }
+template <> const char* dtype_name<float>() { return "f32"; }
+template <> const char* dtype_name<uint64_t>() { return "u64"; }
+
+template <typename T>
+static void emit(const std::string& name, const std::vector<T>& v)
+{
+    std::string path = g_dir + "/" + name + ".bin";
+    FILE* f = std::fopen(path.c_str(), "wb");
+    if (!f) { std::perror(path.c_str()); std::exit(1); }
+    if (!v.empty()) std::fwrite(v.data(), sizeof(T), v.size(), f);
+    std::fclose(f);
+    std::fprintf(g_index, "%s %s %zu\n", name.c_str(), dtype_name<T>(), v.size());
+}
+
+// tests/device_radix_sort_one_sweep.cpp:79-136 -- float keys U[0,1) from
+// std::mt19937(114521); the ascending and descending inputs are drawn
+// alternately from one engine; expected = std::sort and std::sort(greater).
+static void float_keys()
+{
+    for (unsigned loop = 5; loop <= 14; ++loop) {
+        const unsigned n = 1u << loop;
+        std::vector<float> asc(n), desc(n);
+        std::mt19937 rng(114521);
+        std::uniform_real_distribution<float> dist(0.0f, 1.0f);
+        for (unsigned i = 0; i < n; ++i) {
+            asc[i] = dist(rng);
+            desc[i] = dist(rng);
+        }
+        emit("float_keys_asc_in_" + std::to_string(n), asc);
+        emit("float_keys_desc_in_" + std::to_string(n), desc);
+        std::sort(asc.begin(), asc.end());
+        std::sort(desc.begin(), desc.end(), std::greater<float>());
+        emit("float_keys_asc_out_" + std::to_string(n), asc);
+        emit("float_keys_desc_out_" + std::to_string(n), desc);
+    }
+}
+
+// tests/device_radix_sort_one_sweep.cpp:175-205 -- u64 keys (n-i-1)*2654435761,
+// n = 65536, expected = std::sort.
+static void u64_keys()
+{
+    const unsigned n = 65536;
+    std::vector<uint64_t> keys(n);
+    for (unsigned i = 0; i < n; ++i) keys[i] = static_cast<uint64_t>((n - i - 1) * 2654435761ull);
+    emit("u64_keys_in", keys);
+    std::sort(keys.begin(), keys.end());
+    emit("u64_keys_out", keys);
+}
+
+// tests/device_radix_sort_one_sweep.cpp:207-333 -- pairs: shuffled index keys
+// (std::shuffle with std::mt19937(114521), ascending input first, then the
+// descending one), float values U[0,1) drawn afterwards from the same engine;
+// expected = std::sort of (key, value) by key, ascending and descending.
+// The reference uses 524288 items; 32768 keeps the fixture small.
+static void pairs_u32_f32()
+{
+    const int n = 32768;
+    std::vector<uint32_t> key(n), dkey(n);
+    std::vector<float> val(n), dval(n);
+    std::mt19937 rng(114521);
+    std::uniform_real_distribution<float> dist(0.0f, 1.0f);
+    for (int i = 0; i < n; ++i) key[i] = dkey[i] = static_cast<uint32_t>(i);
+    std::shuffle(key.begin(), key.end(), rng);
+    std::shuffle(dkey.begin(), dkey.end(), rng);
+    for (int i = 0; i < n; ++i) {
+        val[i] = dist(rng);
+        dval[i] = dist(rng);
+    }
+    emit("pairs_asc_keys_in", key);
+    emit("pairs_asc_vals_in", val);
+    emit("pairs_desc_keys_in", dkey);
+    emit("pairs_desc_vals_in", dval);
+    std::vector<std::pair<uint32_t, float>> a(n), d(n);
+    for (int i = 0; i < n; ++i) {
+        a[i] = {key[i], val[i]};
+        d[i] = {dkey[i], dval[i]};
+    }
+    std::sort(a.begin(), a.end(), [](auto& x, auto& y) { return x.first < y.first; });
+    std::sort(d.begin(), d.end(), [](auto& x, auto& y) { return x.first > y.first; });
+    std::vector<uint32_t> ak(n), dk(n);
+    std::vector<float> av(n), dv(n);
+    for (int i = 0; i < n; ++i) {
+        ak[i] = a[i].first; av[i] = a[i].second;
+        dk[i] = d[i].first; dv[i] = d[i].second;
+    }
+    emit("pairs_asc_keys_out", ak);
+    emit("pairs_asc_vals_out", av);
+    emit("pairs_desc_keys_out", dk);
+    emit("pairs_desc_vals_out", dv);
+}
+
+// Stable order of indices by the selected bits, ascending / descending.
+static void stable_orders(const std::vector<uint32_t>& keys, unsigned begin, unsigned end,
+                          std::vector<uint32_t>& asc, std::vector<uint32_t>& desc)
+{
+    auto sel = [&](uint32_t k) { return (k >> begin) & ((1u << (end - begin)) - 1u); };
+    asc.resize(keys.size());
+    desc.resize(keys.size());
+    std::iota(asc.begin(), asc.end(), 0u);
+    std::iota(desc.begin(), desc.end(), 0u);
+    std::stable_sort(asc.begin(), asc.end(), [&](uint32_t l, uint32_t r) { return sel(keys[l]) < sel(keys[r]); });
+    std::stable_sort(desc.begin(), desc.end(), [&](uint32_t l, uint32_t r) { return sel(keys[l]) > sel(keys[r]); });
+}
+
+// tests/device_radix_sort_interface_test.cpp:68-158 -- 257 keys
+// ((i*53)%64) | (((i*17)%11)<<8), values = i, bits [1,6).
+// tests/device_radix_sort_interface_test.cpp:205-283 -- 65 keys
+// ((i*19)%32) | ((i%7)<<8), bits [0,5), DoubleBuffer.
+static void interface_cases()
+{
+    {
+        const unsigned n = 257;
+        std::vector<uint32_t> keys(n), vals(n), asc, desc;
+        for (unsigned i = 0; i < n; ++i) {
+            keys[i] = ((i * 53u) % 64u) | (((i * 17u) % 11u) << 8u);
+            vals[i] = i;
+        }
+        stable_orders(keys, 1, 6, asc, desc);
+        emit("partial_bits_keys", keys);
+        emit("partial_bits_vals", vals);
+        emit("partial_bits_asc_order", asc);
+        emit("partial_bits_desc_order", desc);
+    }
+    {
+        const unsigned n = 65;
+        std::vector<uint32_t> keys(n), vals(n), asc, desc;
+        for (unsigned i = 0; i < n; ++i) {
+            keys[i] = ((i * 19u) % 32u) | ((i % 7u) << 8u);
+            vals[i] = i;
+        }
+        stable_orders(keys, 0, 5, asc, desc);
+        emit("double_buffer_keys", keys);
+        emit("double_buffer_vals", vals);
+        emit("double_buffer_asc_order", asc);
+        emit("double_buffer_desc_order", desc);
+    }
+}
+
+// tests/device_scan_test.cpp:189-265 -- (i%7)-3 at 384*22*3+17 and
+// 320*25*3+17, expected = running (inclusive) sum.
+// tests/scan_optimization_regression_test.cpp:124-190 -- tile-boundary sizes,
+// value(i) = i%7+1, exclusive / inclusive sums and init-3 forms at 16003.
+static void scan_cases()
+{
+    for (size_t n : {size_t(384 * 22 * 3 + 17), size_t(320 * 25 * 3 + 17)}) {
+        std::vector<int32_t> in(n), out(n);
+        for (size_t i = 0; i < n; ++i) in[i] = static_cast<int32_t>(i % 7u) - 3;
+        std::inclusive_scan(in.begin(), in.end(), out.begin());
+        emit("scan_mod7_in_" + std::to_string(n), in);
+        emit("scan_mod7_inclusive_" + std::to_string(n), out);
+    }
+    const size_t sizes[] = {0, 1, 31, 32, 33, 255, 256, 257, 3839, 3840, 3841, 4095, 4096, 4097,
+                            7999, 8000, 8001, 16003, 262147};
+    for (size_t n : sizes) {
+        std::vector<int32_t> in(n), ex(n), inc(n);
+        for (size_t i = 0; i < n; ++i) in[i] = static_cast<int32_t>(i % 7u + 1u);
+        std::exclusive_scan(in.begin(), in.end(), ex.begin(), 0);
+        std::inclusive_scan(in.begin(), in.end(), inc.begin());
+        emit("scan_tiles_exclusive_" + std::to_string(n), ex);
+        emit("scan_tiles_inclusive_" + std::to_string(n), inc);
+        if (n == 16003) {
+            std::vector<int32_t> ex3(n), inc3(n);
+            std::exclusive_scan(in.begin(), in.end(), ex3.begin(), 3);
+            std::inclusive_scan(in.begin(), in.end(), inc3.begin(), std::plus<int32_t>(), 3);
+            emit("scan_tiles_exclusive_init3_16003", ex3);
+            emit("scan_tiles_inclusive_init3_16003", inc3);
+        }
+    }
+    // tests/device_scan_test.cpp:288-322 -- InclusiveScanInit {1,2,3,4}, init 10.
+    std::vector<int32_t> in{1, 2, 3, 4}, out(4);
+    std::inclusive_scan(in.begin(), in.end(), out.begin(), std::plus<int32_t>(), 10);
+    emit("scan_init_in", in);
+    emit("scan_init_out", out);
+}
+
+// tests/device_reduce_test.cpp:78-91 and :160-217 -- 0..4095 shuffled with
+// std::mt19937(114521); expected min / max via std::min_element /
+// std::max_element.
+static void reduce_cases()
+{
+    const int n = 1 << 12;
+    std::vector<int32_t> data(n);
+    for (int i = 0; i < n; ++i) data[i] = i;
+    std::mt19937 rng(114521);
+    std::shuffle(data.begin(), data.end(), rng);
+    emit("reduce_shuffled_in", data);
+    std::vector<int32_t> mm{*std::min_element(data.begin(), data.end()),
+                            *std::max_element(data.begin(), data.end())};
+    emit("reduce_shuffled_minmax", mm);
+}
+
+int main(int argc, char** argv)
+{
+    if (argc != 2) {
+        std::fprintf(stderr, "usage: %s <out_dir>\n", argv[0]);
+        return 2;
+    }
+    g_dir = argv[1];
+    g_index = std::fopen((g_dir + "/arrays.txt").c_str(), "w");
+    if (!g_index) { std::perror("arrays.txt"); return 1; }
+    float_keys();
+    u64_keys();
+    pairs_u32_f32();
+    interface_cases();
+    scan_cases();
+    reduce_cases();
+    std::fclose(g_index);
+    return 0;
+}

@@ -1,0 +1,214 @@
+"""Pin the CPU oracle against the golden fixtures (reference tests' own host
+oracles on the reference tests' own inputs) and against independent numpy
+restatements.  CPU only."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+
+# ------------------------------------------------------------------ sorting
+@pytest.mark.parametrize("n", [1 << k for k in range(5, 15)])
+def test_float_keys_golden(oracle, golden, n):
+    """tests/device_radix_sort_one_sweep.cpp:79-136 (std::sort, std::greater)."""
+    asc_in = golden[f"float_keys_asc_in_{n}"]
+    desc_in = golden[f"float_keys_desc_in_{n}"]
+    assert golden.matches(f"float_keys_asc_out_{n}", oracle.radix_sort(asc_in))
+    assert golden.matches(f"float_keys_desc_out_{n}", oracle.radix_sort(desc_in, descending=True))
+
+
+def test_u64_keys_golden(oracle, golden):
+    """tests/device_radix_sort_one_sweep.cpp:175-205."""
+    assert golden.matches("u64_keys_out", oracle.radix_sort(golden["u64_keys_in"]))
+
+
+@pytest.mark.parametrize("desc", [False, True])
+def test_pairs_golden(oracle, golden, desc):
+    """tests/device_radix_sort_one_sweep.cpp:207-333 (uint keys, float values)."""
+    tag = "desc" if desc else "asc"
+    k, v = oracle.radix_sort(golden[f"pairs_{tag}_keys_in"], golden[f"pairs_{tag}_vals_in"],
+                             descending=desc)
+    assert golden.matches(f"pairs_{tag}_keys_out", k)
+    assert golden.matches(f"pairs_{tag}_vals_out", v)
+
+
+@pytest.mark.parametrize("case,begin,end", [("partial_bits", 1, 6), ("double_buffer", 0, 5)])
+@pytest.mark.parametrize("desc", [False, True])
+def test_partial_bits_golden(oracle, golden, case, begin, end, desc):
+    """tests/device_radix_sort_interface_test.cpp:68-158 and :205-283
+    (std::stable_sort with a selected-bits comparator)."""
+    keys, vals = golden[f"{case}_keys"], golden[f"{case}_vals"]
+    order = golden[f"{case}_{'desc' if desc else 'asc'}_order"]
+    k = oracle.radix_sort(keys, begin_bit=begin, end_bit=end, descending=desc)
+    np.testing.assert_array_equal(k, keys[order])
+    k, v = oracle.radix_sort(keys, vals, begin_bit=begin, end_bit=end, descending=desc)
+    np.testing.assert_array_equal(k, keys[order])
+    np.testing.assert_array_equal(v, vals[order])
+
+
+def test_zero_width_copy(oracle):
+    """tests/device_radix_sort_interface_test.cpp:161-195."""
+    keys = (np.arange(17, dtype=np.int64) * 7 - 31).astype(np.int32)
+    vals = (17 - np.arange(17)).astype(np.uint32)
+    k, v = oracle.radix_sort(keys, vals, begin_bit=9, end_bit=9)
+    np.testing.assert_array_equal(k, keys)
+    np.testing.assert_array_equal(v, vals)
+
+
+def test_reversed_u32(oracle):
+    """tests/device_radix_sort_one_sweep.cpp:138-173: keys n-i-1 sort to 0..n-1."""
+    for k in range(0, 17):
+        n = 1 << k
+        keys = (n - 1 - np.arange(n)).astype(np.uint32)
+        np.testing.assert_array_equal(oracle.radix_sort(keys), np.arange(n, dtype=np.uint32))
+
+
+def _np_sort_key(keys: np.ndarray, desc: bool, begin: int, end: int):
+    """Independent numpy restatement of the comparison key (order-preserving
+    bits with +-0 merged), used with a stable argsort."""
+    bits = keys.dtype.itemsize * 8
+    u = keys.view(np.uint32 if bits == 32 else np.uint64).astype(np.uint64)
+    high = np.uint64(1 << (bits - 1))
+    mask = np.uint64((1 << bits) - 1)
+    if keys.dtype.kind == "i":
+        t = u ^ high
+    elif keys.dtype.kind == "f":
+        neg = (u & high) != 0
+        t = np.where(neg, (~u) & mask, u ^ high)
+    else:
+        t = u
+    if desc:
+        t = (~t) & mask
+    if keys.dtype.kind == "f":
+        # the fold runs after the descending inversion and sends both zeros to HIGH
+        t = np.where((u & ~high & mask) == 0, high, t)
+    sel = (t >> np.uint64(begin)) & np.uint64((1 << (end - begin)) - 1)
+    return sel
+
+
+@pytest.mark.parametrize("dtype", [np.uint32, np.int32, np.float32, np.uint64, np.int64, np.float64])
+@pytest.mark.parametrize("desc", [False, True])
+@pytest.mark.parametrize("bits", ["full", "partial"])
+def test_random_vs_numpy_stable(oracle, dtype, desc, bits):
+    rng = np.random.default_rng(7)
+    n = 5003
+    w = np.dtype(dtype).itemsize * 8
+    raw = rng.integers(0, 2**63, size=n, dtype=np.uint64)
+    if w == 32:
+        raw = (raw & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+    keys = raw.view(dtype).copy()
+    if np.dtype(dtype).kind == "f":
+        keys[np.isnan(keys)] = 0
+        keys[::97] = 0.0
+        keys[5::89] = -0.0
+        keys[7::50] = keys[3]  # duplicates
+    begin, end = (0, w) if bits == "full" else (3, w - 5)
+    vals = np.arange(n, dtype=np.uint32)
+    k, v = oracle.radix_sort(keys, vals, begin_bit=begin, end_bit=end, descending=desc)
+    order = np.argsort(_np_sort_key(keys, desc, begin, end), kind="stable")
+    np.testing.assert_array_equal(k.view(np.uint8), keys[order].view(np.uint8))
+    np.testing.assert_array_equal(v, vals[order])
+
+
+def test_threads_identical(oracle):
+    keys = oracle.generate(oracle.GEN_U32_AND3, 200_003, seed=3)
+    vals = np.arange(keys.size, dtype=np.uint32)
+    k1, v1 = oracle.radix_sort(keys, vals, threads=1)
+    k8, v8 = oracle.radix_sort(keys, vals, threads=8)
+    np.testing.assert_array_equal(k1, k8)
+    np.testing.assert_array_equal(v1, v8)
+
+
+def test_float_zero_digits(oracle):
+    """+0.0 and -0.0 give identical digits in both directions
+    (radix_rank_sort_operations.h:31-43)."""
+    pz, nz = 0x00000000, 0x80000000
+    for desc in (False, True):
+        for shift in (0, 8, 16, 24):
+            assert oracle.digit(pz, np.float32, desc, shift, 8) == oracle.digit(nz, np.float32, desc, shift, 8)
+    # ascending: both map to the transformed +0.0 = 0x80000000
+    assert oracle.digit(nz, np.float32, False, 24, 8) == 0x80
+
+
+# -------------------------------------------------------------------- scan
+@pytest.mark.parametrize("n", [384 * 22 * 3 + 17, 320 * 25 * 3 + 17])
+def test_scan_mod7_golden(oracle, golden, n):
+    """tests/device_scan_test.cpp:189-265."""
+    x = golden[f"scan_mod7_in_{n}"]
+    assert golden.matches(f"scan_mod7_inclusive_{n}", oracle.scan(x, "inclusive"))
+
+
+@pytest.mark.parametrize("n", [0, 1, 31, 32, 33, 255, 256, 257, 3839, 3840, 3841, 4095, 4096, 4097,
+                               7999, 8000, 8001, 16003, 262147])
+def test_scan_tiles_golden(oracle, golden, n):
+    """tests/scan_optimization_regression_test.cpp:124-190 (value(i) = i%7+1)."""
+    x = (np.arange(n) % 7 + 1).astype(np.int32)
+    assert golden.matches(f"scan_tiles_exclusive_{n}", oracle.scan(x, "exclusive", init=0))
+    assert golden.matches(f"scan_tiles_inclusive_{n}", oracle.scan(x, "inclusive"))
+    if n == 16003:
+        assert golden.matches("scan_tiles_exclusive_init3_16003", oracle.scan(x, "exclusive", init=3))
+        assert golden.matches("scan_tiles_inclusive_init3_16003", oracle.scan(x, "inclusive_init", init=3))
+
+
+def test_scan_init_golden(oracle, golden):
+    """tests/device_scan_test.cpp:288-322: InclusiveScanInit {1,2,3,4}, 10 -> {11,13,16,20}."""
+    out = oracle.scan(golden["scan_init_in"], "inclusive_init", init=10)
+    np.testing.assert_array_equal(out, golden["scan_init_out"])
+
+
+def test_scan_wraps(oracle):
+    x = np.full(10, 2**31 - 1, dtype=np.int32)
+    out = oracle.scan(x, "inclusive")
+    ref = np.cumsum(x.astype(np.int64)).astype(np.uint64).astype(np.uint32).view(np.int32)
+    np.testing.assert_array_equal(out, ref)
+
+
+def test_scan_minmax(oracle):
+    rng = np.random.default_rng(1)
+    x = rng.integers(-1000, 1000, 777).astype(np.int32)
+    np.testing.assert_array_equal(oracle.scan(x, "inclusive", oracle.OP_MAX), np.maximum.accumulate(x))
+    np.testing.assert_array_equal(oracle.scan(x, "inclusive", oracle.OP_MIN), np.minimum.accumulate(x))
+
+
+# ------------------------------------------------------------------ reduce
+def test_reduce_shuffled_golden(oracle, golden):
+    """tests/device_reduce_test.cpp:160-217."""
+    x = golden["reduce_shuffled_in"]
+    mn, mx = golden["reduce_shuffled_minmax"]
+    assert oracle.reduce(x, oracle.OP_MIN, np.iinfo(np.int32).max) == mn
+    assert oracle.reduce(x, oracle.OP_MAX, np.iinfo(np.int32).min) == mx
+
+
+def test_reduce_identities(oracle):
+    """device_reduce_test.cpp:95-118 (ones, 2^k+1) and :220-236 (float max identity)."""
+    for k in range(0, 16):
+        n = (1 << k) + 1
+        assert oracle.reduce(np.ones(n, np.uint32), oracle.OP_SUM, 0) == n
+    x = np.array([-8.0, -2.5, -9.0, -4.0], np.float32)
+    assert oracle.reduce(x, oracle.OP_MAX, np.finfo(np.float32).min) == np.float32(-2.5)
+    assert oracle.reduce(np.zeros(0, np.float32), oracle.OP_SUM, 0) == 0
+
+
+def test_sum_f64(oracle):
+    x = oracle.generate(oracle.GEN_F32_UNIT, 100_000, seed=5)
+    assert abs(oracle.sum_f64(x) - float(np.sum(x.astype(np.float64)))) < 1e-6
+
+
+# -------------------------------------------------------------- generators
+def test_generators_match_numpy(oracle):
+    """Counter-based generator restated in numpy (splitmix64)."""
+    def splitmix(x):
+        with np.errstate(over="ignore"):
+            z = x + np.uint64(0x9E3779B97F4A7C15)
+            z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+            z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+            return z ^ (z >> np.uint64(31))
+    i = np.arange(1000, 2000, dtype=np.uint64)
+    seed = np.uint64(1)
+    r = [splitmix((seed << np.uint64(40)) + (np.uint64(s) << np.uint64(36)) + i) for s in range(3)]
+    np.testing.assert_array_equal(oracle.generate(oracle.GEN_U32_UNIFORM, 1000, 1, 1000),
+                                  (r[0] & np.uint64(0xFFFFFFFF)).astype(np.uint32))
+    np.testing.assert_array_equal(oracle.generate(oracle.GEN_U32_AND3, 1000, 1, 1000),
+                                  ((r[0] & r[1] & r[2]) & np.uint64(0xFFFFFFFF)).astype(np.uint32))
+    np.testing.assert_array_equal(oracle.generate(oracle.GEN_I32_SCAN, 1000, 1, 1000),
+                                  ((r[0] % np.uint64(2001)).astype(np.int64) - 1000).astype(np.int32))

@@ -1,0 +1,342 @@
+"""GPU parity tests for DeviceRadixSort (C ABI), mirroring the reference's
+tests/device_radix_sort_one_sweep.cpp and tests/device_radix_sort_interface_test.cpp,
+plus oracle comparisons across dtypes / bit ranges / edge sizes and
+size-independent properties at the BASELINE sizes (2^27, 2^28)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+from gpu_helpers import dev, empty_like_np, gpu_sort, host, transformed_key_u64  # noqa: E402
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+
+
+# ------------------------------------------------------------ golden vectors
+@pytest.mark.parametrize("n", [1 << k for k in range(5, 15)])
+def test_float_keys_golden(golden, n):
+    """device_radix_sort_one_sweep.cpp:79-136: float keys, SortKeys + SortKeysDescending."""
+    assert golden.matches(f"float_keys_asc_out_{n}", gpu_sort(golden[f"float_keys_asc_in_{n}"]))
+    assert golden.matches(f"float_keys_desc_out_{n}",
+                          gpu_sort(golden[f"float_keys_desc_in_{n}"], descending=True))
+
+
+def test_reversed_u32_all_sizes():
+    """device_radix_sort_one_sweep.cpp:138-173: keys n-i-1, n = 2^0 .. 2^23."""
+    for k in range(0, 24):
+        n = 1 << k
+        keys = (n - 1 - np.arange(n)).astype(np.uint32)
+        np.testing.assert_array_equal(gpu_sort(keys), np.arange(n, dtype=np.uint32), err_msg=f"n={n}")
+
+
+def test_u64_keys_golden(golden):
+    """device_radix_sort_one_sweep.cpp:175-205."""
+    assert golden.matches("u64_keys_out", gpu_sort(golden["u64_keys_in"]))
+
+
+@pytest.mark.parametrize("desc", [False, True])
+def test_pairs_golden(golden, desc):
+    """device_radix_sort_one_sweep.cpp:207-333 (uint keys, float values)."""
+    tag = "desc" if desc else "asc"
+    k, v = gpu_sort(golden[f"pairs_{tag}_keys_in"], golden[f"pairs_{tag}_vals_in"], descending=desc)
+    assert golden.matches(f"pairs_{tag}_keys_out", k)
+    assert golden.matches(f"pairs_{tag}_vals_out", v)
+
+
+@pytest.mark.parametrize("desc", [False, True])
+def test_partial_bits_golden(golden, desc):
+    """device_radix_sort_interface_test.cpp:68-158: 257 keys, bits [1,6), stable."""
+    keys, vals = golden["partial_bits_keys"], golden["partial_bits_vals"]
+    order = golden[f"partial_bits_{'desc' if desc else 'asc'}_order"]
+    np.testing.assert_array_equal(gpu_sort(keys, begin_bit=1, end_bit=6, descending=desc), keys[order])
+    k, v = gpu_sort(keys, vals, begin_bit=1, end_bit=6, descending=desc)
+    np.testing.assert_array_equal(k, keys[order])
+    np.testing.assert_array_equal(v, vals[order])
+
+
+def test_double_buffer_selectors_golden(golden, lcpp):
+    """device_radix_sort_interface_test.cpp:205-283."""
+    keys, vals = golden["double_buffer_keys"], golden["double_buffer_vals"]
+    n = keys.size
+    rs = lcpp.DeviceRadixSort()
+    temp = lcpp.alloc_temp(rs.GetSortPairsTempStorageBytes(lcpp.U32, lcpp.U32, n))
+    kb = lcpp.DoubleBuffer(empty_like_np(keys), dev(keys), selector=1)
+    rs.SortKeys(temp, kb, n, 0, 5)
+    assert kb.selector == 0
+    pk = lcpp.DoubleBuffer(dev(keys), empty_like_np(keys))
+    pv = lcpp.DoubleBuffer(dev(vals), empty_like_np(vals))
+    rs.SortPairsDescending(temp, pk, pv, n, 0, 5)
+    assert pk.selector == 1 and pv.selector == pk.selector
+    asc, desc = golden["double_buffer_asc_order"], golden["double_buffer_desc_order"]
+    np.testing.assert_array_equal(host(kb.current()), keys[asc])
+    np.testing.assert_array_equal(host(pk.current()), keys[desc])
+    np.testing.assert_array_equal(host(pv.current()), vals[desc])
+
+
+def test_double_buffer_zero_width_keeps_current(lcpp):
+    """device_radix_sort_interface_test.cpp:285-300: begin == end leaves the selector."""
+    data = np.array([7, 2, 5], np.int32)
+    db = lcpp.DoubleBuffer(torch.zeros(3, dtype=torch.int32, device="cuda"), dev(data), selector=1)
+    lcpp.DeviceRadixSort().SortKeys(None, db, 3, 4, 4)
+    assert db.selector == 1
+    np.testing.assert_array_equal(host(db.current()), data)
+
+
+def test_zero_width_copy(lcpp):
+    """device_radix_sort_interface_test.cpp:161-195."""
+    keys = (np.arange(17) * 7 - 31).astype(np.int32)
+    vals = (17 - np.arange(17)).astype(np.uint32)
+    kin, vin = dev(keys), dev(vals)
+    kout, vout = empty_like_np(keys), empty_like_np(vals)
+    lcpp.DeviceRadixSort().SortPairs(None, kin, kout, vin, vout, 17, 9, 9)
+    np.testing.assert_array_equal(host(kout), keys)
+    np.testing.assert_array_equal(host(vout), vals)
+
+
+def test_empty_input(lcpp):
+    """device_radix_sort_interface_test.cpp:197-203."""
+    e = torch.empty(0, dtype=torch.int32, device="cuda")
+    lcpp.DeviceRadixSort().SortKeys(None, e, e, 0)
+    assert lcpp.DeviceRadixSort.GetSortKeysTempStorageBytes(lcpp.I32, 0) == 0
+
+
+# ------------------------------------------------- oracle, dtypes x edge sizes
+EDGE_SIZES = [1, 2, 31, 33, 255, 4095, 5759, 5760, 5761, 7679, 7680, 7681, 65537, 1_000_003]
+
+
+def _random_keys(dtype, n, seed):
+    rng = np.random.default_rng(seed)
+    w = np.dtype(dtype).itemsize * 8
+    raw = rng.integers(0, 2**63, size=n, dtype=np.uint64) * np.uint64(2) + rng.integers(0, 2, size=n, dtype=np.uint64)
+    if w == 32:
+        raw = (raw & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+    keys = raw.view(dtype).copy()
+    if np.dtype(dtype).kind == "f":
+        keys[np.isnan(keys)] = 1.5
+        keys[::53] = 0.0
+        keys[7::61] = -0.0
+    keys[3::17] = keys[0]  # duplicates exercise stability
+    return keys
+
+
+@pytest.mark.parametrize("dtype", [np.uint32, np.int32, np.float32, np.uint64, np.int64, np.float64])
+@pytest.mark.parametrize("n", EDGE_SIZES)
+def test_keys_vs_oracle(oracle, dtype, n):
+    keys = _random_keys(dtype, n, n)
+    for desc in (False, True):
+        got = gpu_sort(keys, descending=desc)
+        exp = oracle.radix_sort(keys, descending=desc, threads=4)
+        np.testing.assert_array_equal(got.view(np.uint8), exp.view(np.uint8), err_msg=f"desc={desc}")
+
+
+@pytest.mark.parametrize("kdtype,vdtype", [(np.uint32, np.uint32), (np.float32, np.uint32),
+                                           (np.uint64, np.int32), (np.int32, np.float64),
+                                           (np.float64, np.uint64), (np.int64, np.float32)])
+@pytest.mark.parametrize("n", [1, 33, 4097, 5761, 7681, 262147, 1_000_003])
+def test_pairs_vs_oracle(oracle, kdtype, vdtype, n):
+    keys = _random_keys(kdtype, n, n + 1)
+    vals = np.arange(n, dtype=np.uint64).astype(vdtype)
+    for desc in (False, True):
+        k, v = gpu_sort(keys, vals, descending=desc)
+        ek, ev = oracle.radix_sort(keys, vals, descending=desc, threads=4)
+        np.testing.assert_array_equal(k.view(np.uint8), ek.view(np.uint8))
+        np.testing.assert_array_equal(v.view(np.uint8), ev.view(np.uint8))
+
+
+@pytest.mark.parametrize("dtype", [np.uint32, np.float32, np.int64])
+@pytest.mark.parametrize("begin,end", [(0, 1), (1, 6), (3, 11), (8, 24), (5, 29), (16, 32), (7, 8)])
+def test_bit_ranges_vs_oracle(oracle, dtype, begin, end):
+    n = 300_007
+    keys = _random_keys(dtype, n, begin * 100 + end)
+    vals = np.arange(n, dtype=np.uint32)
+    for desc in (False, True):
+        k, v = gpu_sort(keys, vals, begin_bit=begin, end_bit=end, descending=desc)
+        ek, ev = oracle.radix_sort(keys, vals, begin_bit=begin, end_bit=end, descending=desc, threads=4)
+        np.testing.assert_array_equal(k.view(np.uint8), ek.view(np.uint8))
+        np.testing.assert_array_equal(v, ev)
+
+
+@pytest.mark.parametrize("dist", ["U32_UNIFORM", "U32_AND3", "U32_CONST", "U32_ZIPF", "F32_NORMAL",
+                                  "U64_UNIFORM"])
+def test_distributions_vs_oracle(oracle, lcpp, dist):
+    """BASELINE key distributions at 2^22 (device-generated), bit-exact vs the oracle."""
+    n = 1 << 22
+    code = getattr(lcpp, f"GEN_{dist}")
+    tdt = {"U64": torch.uint64, "F32": torch.float32}.get(dist[:3], torch.uint32)
+    keys_t = torch.empty(n, dtype=tdt, device="cuda")
+    lcpp.testgen_fill(keys_t, code, seed=1)
+    keys = host(keys_t)
+    vals = np.arange(n, dtype=np.uint32)
+    k, v = gpu_sort(keys, vals)
+    ek, ev = oracle.radix_sort(keys, vals, threads=8)
+    np.testing.assert_array_equal(k.view(np.uint8), ek.view(np.uint8))
+    np.testing.assert_array_equal(v, ev)
+
+
+def test_input_untouched_and_repeatable():
+    keys = _random_keys(np.uint32, 100_003, 11)
+    kin = dev(keys)
+    import lcpp_b200 as L
+    rs = L.DeviceRadixSort()
+    temp = L.alloc_temp(rs.GetSortKeysTempStorageBytes(L.U32, keys.size))
+    outs = []
+    for _ in range(3):
+        kout = torch.empty_like(kin)
+        rs.SortKeys(temp, kin, kout, keys.size)
+        outs.append(host(kout))
+    np.testing.assert_array_equal(host(kin), keys)
+    for o in outs[1:]:
+        np.testing.assert_array_equal(o, outs[0])
+
+
+def test_guarded_temp_canaries(lcpp):
+    """The sort writes nothing past the queried temp size (the reference's
+    GuardedTemp fixture, tests/pr6_review_regression_test.cpp:69-98)."""
+    for n in (1, 7681, 300_000):
+        keys = _random_keys(np.uint32, n, 5)
+        vals = np.arange(n, dtype=np.uint32)
+        rs = lcpp.DeviceRadixSort()
+        tb = rs.GetSortPairsTempStorageBytes(lcpp.U32, lcpp.U32, n)
+        backing = torch.full((tb + 16384,), 0xA5, dtype=torch.uint8, device="cuda")
+        temp = backing[:tb]
+        kout, vout = empty_like_np(keys), empty_like_np(vals)
+        rs.SortPairs(temp, dev(keys), kout, dev(vals), vout, n)
+        torch.cuda.synchronize()
+        assert bool((backing[tb:] == 0xA5).all())
+
+
+# --------------------------------------- size-independent properties, full size
+def _check_sorted_stable_permutation(keys_in, keys_out, vals_out, kind, bits, desc=False):
+    """keys_out[i] == keys_in[vals_out[i]] (bit-exact), vals_out a permutation,
+    keys ordered by the transformed key, ties in increasing index order."""
+    n = keys_in.numel()
+    idx = vals_out.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    seen = torch.zeros(n, dtype=torch.bool, device="cuda")
+    seen[idx] = True
+    assert bool(seen.all()), "values are not a permutation of the indices"
+    del seen
+    if bits == 32:
+        assert torch.equal(keys_out.view(torch.int32), keys_in.view(torch.int32)[idx])
+    else:
+        assert torch.equal(keys_out.view(torch.int64), keys_in.view(torch.int64)[idx])
+    t = transformed_key_u64(keys_out, kind, bits)
+    if desc:
+        t = -t if bits == 32 else ~t
+    d = t[1:] - t[:-1] if bits == 32 else None
+    if bits == 32:
+        assert bool((d >= 0).all()), "keys out of order"
+        ties = d == 0
+    else:
+        assert bool((t[1:] >= t[:-1]).all()), "keys out of order"
+        ties = t[1:] == t[:-1]
+    assert bool((idx[1:][ties] > idx[:-1][ties]).all()), "equal keys lost their input order"
+
+
+@pytest.mark.parametrize("dist", ["U32_UNIFORM", "U32_AND3", "U32_CONST"])
+def test_pairs_2p28_properties(lcpp, dist):
+    """SortPairs u32 -> u32 index, n = 2^28, seed 1."""
+    n = 1 << 28
+    keys = torch.empty(n, dtype=torch.uint32, device="cuda")
+    lcpp.testgen_fill(keys, getattr(lcpp, f"GEN_{dist}"), seed=1)
+    vals = torch.empty(n, dtype=torch.uint32, device="cuda")
+    lcpp.testgen_fill(vals, lcpp.GEN_U32_INDEX, seed=1)
+    rs = lcpp.DeviceRadixSort()
+    temp = lcpp.alloc_temp(rs.GetSortPairsTempStorageBytes(lcpp.U32, lcpp.U32, n))
+    kout, vout = torch.empty_like(keys), torch.empty_like(vals)
+    rs.SortPairs(temp, keys, kout, vals, vout, n)
+    assert lcpp.device_status(temp) == lcpp.OK
+    del temp
+    _check_sorted_stable_permutation(keys, kout, vout, "u", 32)
+
+
+def test_keys_2p28_uniform_properties(lcpp):
+    """Headline config: SortKeys u32 n = 2^28, uniform; sorted and a permutation
+    of the input (checked through a stable SortPairs run on the same keys)."""
+    n = 1 << 28
+    keys = torch.empty(n, dtype=torch.uint32, device="cuda")
+    lcpp.testgen_fill(keys, lcpp.GEN_U32_UNIFORM, seed=0)
+    rs = lcpp.DeviceRadixSort()
+    temp = lcpp.alloc_temp(rs.GetSortKeysTempStorageBytes(lcpp.U32, n))
+    kout = torch.empty_like(keys)
+    rs.SortKeys(temp, keys, kout, n)
+    assert lcpp.device_status(temp) == lcpp.OK
+    t = transformed_key_u64(kout, "u", 32)
+    assert bool((t[1:] >= t[:-1]).all())
+    # multiset equality: per-bucket counts of the top 16 bits and a sum of a
+    # hash of every key must agree between input and output
+    ti = transformed_key_u64(keys, "u", 32)
+    assert torch.equal(torch.bincount(ti >> 16, minlength=1 << 16), torch.bincount(t >> 16, minlength=1 << 16))
+    h = lambda x: ((x * 0x9E3779B1) & 0xFFFFFFFF) ^ (x >> 7)  # noqa: E731
+    assert int(h(ti).sum()) == int(h(t).sum())
+
+
+@pytest.mark.parametrize("desc", [False, True])
+def test_f32_normal_2p27_properties(lcpp, desc):
+    """SortPairs f32 N(0,1) with +-0.0 -> u32 index, n = 2^27."""
+    n = 1 << 27
+    keys = torch.empty(n, dtype=torch.float32, device="cuda")
+    lcpp.testgen_fill(keys, lcpp.GEN_F32_NORMAL, seed=1)
+    vals = torch.empty(n, dtype=torch.uint32, device="cuda")
+    lcpp.testgen_fill(vals, lcpp.GEN_U32_INDEX, seed=1)
+    rs = lcpp.DeviceRadixSort()
+    temp = lcpp.alloc_temp(rs.GetSortPairsTempStorageBytes(lcpp.F32, lcpp.U32, n))
+    kout, vout = torch.empty_like(keys), torch.empty_like(vals)
+    (rs.SortPairsDescending if desc else rs.SortPairs)(temp, keys, kout, vals, vout, n)
+    assert lcpp.device_status(temp) == lcpp.OK
+    del temp
+    _check_sorted_stable_permutation(keys, kout, vout, "f", 32, desc)
+    # both zeros present, kept in input order within the merged zero run
+    z = kout == 0
+    assert int(z.sum()) == 2 * (n // 65536)
+    assert bool(torch.signbit(kout[z]).any()) and bool((~torch.signbit(kout[z])).any())
+
+
+def test_u64_2p27_properties(lcpp):
+    """SortPairs u64 uniform -> i32 index, n = 2^27."""
+    n = 1 << 27
+    keys = torch.empty(n, dtype=torch.uint64, device="cuda")
+    lcpp.testgen_fill(keys, lcpp.GEN_U64_UNIFORM, seed=1)
+    vals = torch.empty(n, dtype=torch.int32, device="cuda")
+    lcpp.testgen_fill(vals, lcpp.GEN_U32_INDEX, seed=1)
+    rs = lcpp.DeviceRadixSort()
+    temp = lcpp.alloc_temp(rs.GetSortPairsTempStorageBytes(lcpp.U64, lcpp.I32, n))
+    kout, vout = torch.empty_like(keys), torch.empty_like(vals)
+    rs.SortPairs(temp, keys, kout, vals, vout, n)
+    assert lcpp.device_status(temp) == lcpp.OK
+    del temp
+    _check_sorted_stable_permutation(keys, kout, vout, "u", 64)
+
+
+def test_partial_bits_2p27(lcpp, oracle):
+    """SortKeys u32 bits [8,24), n = 2^27; checked against
+    the oracle on a 2^22 prefix and by properties at full size."""
+    n = 1 << 27
+    keys = torch.empty(n, dtype=torch.uint32, device="cuda")
+    lcpp.testgen_fill(keys, lcpp.GEN_U32_UNIFORM, seed=1)
+    rs = lcpp.DeviceRadixSort()
+    temp = lcpp.alloc_temp(rs.GetSortPairsTempStorageBytes(lcpp.U32, lcpp.U32, n))
+    vals = torch.empty(n, dtype=torch.uint32, device="cuda")
+    lcpp.testgen_fill(vals, lcpp.GEN_U32_INDEX, seed=1)
+    kout, vout = torch.empty_like(keys), torch.empty_like(vals)
+    rs.SortPairs(temp, keys, kout, vals, vout, n, 8, 24)
+    assert lcpp.device_status(temp) == lcpp.OK
+    idx = vout.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    assert torch.equal(kout.view(torch.int32), keys.view(torch.int32)[idx])
+    sel = (transformed_key_u64(kout, "u", 32) >> 8) & 0xFFFF
+    d = sel[1:] - sel[:-1]
+    assert bool((d >= 0).all())
+    assert bool((idx[1:][d == 0] > idx[:-1][d == 0]).all())
+    kout2 = torch.empty_like(keys)
+    rs.SortKeys(temp, keys, kout2, n, 8, 24)
+    assert torch.equal(kout2.view(torch.int32), kout.view(torch.int32))
+    # small-prefix bit-exact oracle check
+    m = 1 << 22
+    ks = host(keys[:m])
+    got = gpu_sort(ks, begin_bit=8, end_bit=24)
+    np.testing.assert_array_equal(got, oracle.radix_sort(ks, begin_bit=8, end_bit=24, threads=8))
