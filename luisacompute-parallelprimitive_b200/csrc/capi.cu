@@ -41,8 +41,9 @@ void set_max_dynamic_smem(const void* kernel, size_t bytes)
     std::lock_guard<std::mutex> lk(mu);
     auto key = std::make_pair(std::make_pair(kernel, dev), bytes);
     if (done.count(key)) return;
-    if (bytes > 48 * 1024)
-        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    // Always set: the 48 KB default also has to hold the kernel's static
+    // shared memory, so a dynamic size just under it can still need opt-in.
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
     done.insert(key);
 }
 

@@ -103,9 +103,10 @@ __device__ __forceinline__ void report_error(uint32_t* err, uint32_t code)
 //   unsigned : pos = neg = 0            (descending: ~0)
 //   signed   : pos = neg = HIGH         (descending: ~HIGH)
 //   float    : pos = HIGH, neg = ~0     (descending: ~HIGH, 0)
-// and for float keys +-0.0 map to HIGH in both directions (the transformed
-// +0.0 in ascending order, and the value the reference's fold produces in
-// descending order).
+// For float keys the reference's fold gives +-0.0 the digits of HIGH in both
+// directions (the transformed +0.0 ascending, the folded value descending);
+// the kernels apply it when extracting digits only, so stored keys keep
+// their bits.
 // ---------------------------------------------------------------------------
 template <typename U>
 struct KeyCodec {
@@ -113,18 +114,6 @@ struct KeyCodec {
     U xor_neg;
     uint32_t fold_zero;  // 1 for floating-point keys
 };
-
-template <typename U>
-__device__ __forceinline__ U transform_key(U k, const KeyCodec<U>& c)
-{
-    constexpr int kBits = sizeof(U) * 8;
-    constexpr U kHigh = U(1) << (kBits - 1);
-    using S = typename std::conditional<sizeof(U) == 4, int32_t, int64_t>::type;
-    const U sign = U(S(k) >> (kBits - 1));  // all ones when the high bit is set
-    U t = k ^ (c.xor_pos ^ (sign & (c.xor_pos ^ c.xor_neg)));
-    if (c.fold_zero && U(k << 1) == U(0)) t = kHigh;
-    return t;
-}
 
 template <typename U>
 inline KeyCodec<U> make_codec(lcpp_dtype dt, bool descending)

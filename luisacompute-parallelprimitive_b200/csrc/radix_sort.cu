@@ -10,21 +10,32 @@
 //      finish turns them into exclusive digit offsets (the reference runs a
 //      separate RadixSortExclusiveSumModule, details/radix_sort.h:81-123);
 //   3. one onesweep_kernel per 8-bit pass: load a tile, rank it stably with
-//      warp match-any and per-warp shared-memory counters, publish per-digit
+//      warp ballots and per-warp shared-memory counters, publish per-digit
 //      tile counts, resolve the global digit offsets with a bounded decoupled
 //      look-back, stage the tile in shared memory in digit order and write it
 //      out so that each digit's run is stored contiguously (the reference's
 //      AgentRadixSortOneSweep, agent_radix_sort_onesweep.h:224-511, with
 //      BlockRadixRankMatchEarlyCounts, block_radix_rank.h:207-486).
 //
+// B200 budget: at the measured ~6.5 TB/s an 8-bit pass over 4-byte keys has
+// about 11 SM cycles per 32 keys, and the integer ALU pipe issues about two
+// warp instructions per cycle, so the kernels are written for instruction
+// count: keys are transformed once on load and once on store (not at every
+// digit extraction), the key kind is a template parameter (unsigned
+// ascending keys need no transform at all), full tiles use unguarded loads
+// with immediate offsets, the tile-base and per-warp offsets are merged into
+// one table (one shared load per key), and consistency checks run per digit
+// rather than per key.
+//
 // Differences from the reference that are part of this design:
 //  - look-back status rows are double-buffered and each pass clears the rows
 //    the next pass will use, instead of a separate reset kernel per pass and
 //    portion (device_radix_sort.h:1389-1398);
-//  - one portion at any size: counts and offsets are 64-bit above 2^30 keys
+//  - one portion at any size: counts and offsets are 64-bit from 2^30 keys
 //    (the reference splits at 2^28 keys into portions, :1056, and its
 //    portion carry is never written, agent_radix_sort_onesweep.h:362);
 //  - every spin is bounded (kWaitLimitNs) and reports LCPP_ERR_LOOKBACK_TIMEOUT.
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -62,6 +73,64 @@ struct Ctrl {
 };
 static_assert(sizeof(Ctrl) <= 256, "control block must fit 256 bytes");
 
+// ---------------------------------------------------------------------------
+// Key transform, specialised by kind (see KeyCodec in common.cuh):
+//   kPlain : unsigned keys, ascending   -> identity
+//   kXor   : unsigned descending, signed ascending / descending -> k ^ xor_pos
+//   kFloat : floating point -> sign-dependent XOR, and +-0.0 share digits
+// ---------------------------------------------------------------------------
+enum : int { kPlain = 0, kXor = 1, kFloat = 2 };
+
+template <int KIND, typename U>
+__device__ __forceinline__ U twiddle_in(U k, const KeyCodec<U>& c)
+{
+    if constexpr (KIND == kPlain) {
+        return k;
+    } else if constexpr (KIND == kXor) {
+        return k ^ c.xor_pos;
+    } else {
+        // Pure bijection (no +-0 fold: the stored key keeps its bits; the
+        // fold only applies to digits, see digit_of).
+        constexpr int kBits = sizeof(U) * 8;
+        using S = typename std::conditional<sizeof(U) == 4, int32_t, int64_t>::type;
+        const U sign = U(S(k) >> (kBits - 1));
+        return k ^ U(c.xor_pos ^ (sign & (c.xor_pos ^ c.xor_neg)));
+    }
+}
+
+template <int KIND, typename U>
+__device__ __forceinline__ U twiddle_out(U t, const KeyCodec<U>& c)
+{
+    if constexpr (KIND == kPlain) {
+        return t;
+    } else if constexpr (KIND == kXor) {
+        return t ^ c.xor_pos;
+    } else {
+        // Undo the optional descending inversion, then the float bijection:
+        // a transformed key with the high bit set came from a non-negative
+        // key (flip the high bit back), otherwise from a negative one (flip all).
+        constexpr int kBits = sizeof(U) * 8;
+        constexpr U kHigh = U(1) << (kBits - 1);
+        using S = typename std::conditional<sizeof(U) == 4, int32_t, int64_t>::type;
+        const U u = t ^ U(c.xor_pos ^ kHigh);  // xor_pos is kHigh ascending, ~kHigh descending
+        const U sign = U(S(u) >> (kBits - 1));
+        return u ^ U(~U(0) ^ (sign & ~kHigh));
+    }
+}
+
+// Digit of a transformed key.  For floats, the transformed -0.0 (ascending)
+// or +0.0 (descending), kHigh - 1, takes the digits of kHigh, the value the
+// other zero maps to (radix_rank_sort_operations.h:31-43).
+template <int KIND, typename U>
+__device__ __forceinline__ uint32_t digit_of(U t, int shift, uint32_t mask)
+{
+    if constexpr (KIND == kFloat) {
+        constexpr U kHigh = U(1) << (sizeof(U) * 8 - 1);
+        t = t == U(kHigh - 1) ? kHigh : t;
+    }
+    return uint32_t(t >> shift) & mask;
+}
+
 // Exclusive scan of one value per thread over threads [0, 256) of a block of
 // BLOCK >= 256 threads.  Every thread of the block must call it.
 template <typename T, int BLOCK>
@@ -86,71 +155,71 @@ __device__ __forceinline__ T exclusive_scan_256(T v, T* s_warp_sums)
 
 // ---------------------------------------------------------------------------
 // Histogram of every pass in one read.
-// Shared counters are replicated COPIES times and lane i uses copy i % COPIES,
-// which bounds same-address conflicts of a warp's shared atomics to
-// 32 / COPIES even when every key has the same digit.
+// Shared counters are replicated COPIES times, interleaved so that copy c of
+// bin b sits at word b * COPIES + c, and lane l counts into copy l % COPIES.
+// With COPIES = 32 every lane of a warp hits its own bank, so the shared
+// atomics never conflict, whatever the key distribution.
 // ---------------------------------------------------------------------------
-template <typename U, int BLOCK, int COPIES, bool VECTOR>
-__global__ void __launch_bounds__(BLOCK)
+template <typename U, int KIND, int PASSES, int BLOCK, int COPIES>
+__global__ void __launch_bounds__(BLOCK, 1)
 histogram_kernel(const U* __restrict__ keys, uint64_t n, KeyCodec<U> codec, int begin_bit,
-                 int end_bit, int passes, uint64_t chunk, Ctrl* ctrl,
+                 uint32_t last_mask, uint64_t chunk, Ctrl* ctrl,
                  unsigned long long* __restrict__ g_hist, unsigned long long* __restrict__ g_bins)
 {
-    extern __shared__ __align__(16) uint32_t s_hist[];  // [passes * 256][COPIES]
+    extern __shared__ __align__(16) uint32_t s_hist[];  // [PASSES * 256][COPIES]
     __shared__ unsigned long long s_sums[8];
     __shared__ int s_last;
     const int tid = threadIdx.x;
     const int copy = (tid & 31) % COPIES;
-    for (int i = tid; i < passes * kDigits * COPIES; i += BLOCK) s_hist[i] = 0;
+    for (int i = tid; i < PASSES * kDigits * COPIES; i += BLOCK) s_hist[i] = 0;
     __syncthreads();
 
     auto count = [&](U k) {
-        const U t = transform_key(k, codec);
+        const U t = twiddle_in<KIND>(k, codec);
 #pragma unroll
-        for (int p = 0; p < kMaxPasses; ++p) {
-            if (p < passes) {
-                const int shift = begin_bit + kRadixBits * p;
-                const int nb = min(kRadixBits, end_bit - shift);
-                const uint32_t d = uint32_t(t >> shift) & ((1u << nb) - 1u);
-                atomicAdd(&s_hist[(p * kDigits + d) * COPIES + copy], 1u);
-            }
+        for (int p = 0; p < PASSES; ++p) {
+            const uint32_t d = digit_of<KIND>(t, begin_bit + kRadixBits * p, p + 1 == PASSES ? last_mask : 0xffu);
+            atomicAdd(&s_hist[(p * kDigits + d) * COPIES + copy], 1u);
         }
     };
 
+    constexpr int VEC = 16 / sizeof(U);
+    using VT = typename std::conditional<sizeof(U) == 4, uint4, ulonglong2>::type;
     const uint64_t lo = uint64_t(blockIdx.x) * chunk;
     const uint64_t hi = min(lo + chunk, n);
     if (lo < hi) {
-        if constexpr (VECTOR) {
-            constexpr int VEC = 16 / sizeof(U);
-            using V = typename std::conditional<sizeof(U) == 4, uint4, ulonglong2>::type;
-            const uint64_t nvec = (hi - lo) / VEC;
-            const V* vp = reinterpret_cast<const V*>(keys + lo);
-            uint64_t j = tid;
-            for (; j + 3 * BLOCK < nvec; j += 4 * BLOCK) {
-                V a = vp[j], b = vp[j + BLOCK], c = vp[j + 2 * BLOCK], d = vp[j + 3 * BLOCK];
-                const U* pa = reinterpret_cast<const U*>(&a);
-                const U* pb = reinterpret_cast<const U*>(&b);
-                const U* pc = reinterpret_cast<const U*>(&c);
-                const U* pd = reinterpret_cast<const U*>(&d);
+        // Scalar head up to the first 16-byte boundary, vector body, scalar tail.
+        const uint64_t mis = (reinterpret_cast<uintptr_t>(keys + lo) & 15) / sizeof(U);
+        const uint64_t head = min(hi - lo, uint64_t(mis ? VEC - mis : 0));
+        if (uint64_t(tid) < head) count(keys[lo + tid]);
+        const uint64_t vlo = lo + head;
+        const uint64_t nvec = (hi - vlo) / VEC;
+        const VT* vp = reinterpret_cast<const VT*>(keys + vlo);
+        uint64_t j = tid;
+        for (; j + 3 * BLOCK < nvec; j += 4 * BLOCK) {
+            VT v[4];
 #pragma unroll
-                for (int e = 0; e < VEC; ++e) { count(pa[e]); count(pb[e]); count(pc[e]); count(pd[e]); }
-            }
-            for (; j < nvec; j += BLOCK) {
-                V a = vp[j];
-                const U* pa = reinterpret_cast<const U*>(&a);
+            for (int u = 0; u < 4; ++u) v[u] = vp[j + u * BLOCK];
 #pragma unroll
-                for (int e = 0; e < VEC; ++e) count(pa[e]);
+            for (int u = 0; u < 4; ++u) {
+                const U* e = reinterpret_cast<const U*>(&v[u]);
+#pragma unroll
+                for (int q = 0; q < VEC; ++q) count(e[q]);
             }
-            for (uint64_t i = lo + nvec * VEC + tid; i < hi; i += BLOCK) count(keys[i]);
-        } else {
-            for (uint64_t i = lo + tid; i < hi; i += BLOCK) count(keys[i]);
         }
+        for (; j < nvec; j += BLOCK) {
+            const VT v = vp[j];
+            const U* e = reinterpret_cast<const U*>(&v);
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) count(e[q]);
+        }
+        for (uint64_t i = vlo + nvec * VEC + tid; i < hi; i += BLOCK) count(keys[i]);
     }
     __syncthreads();
-    for (int i = tid; i < passes * kDigits; i += BLOCK) {
+    for (int i = tid; i < PASSES * kDigits; i += BLOCK) {
         uint32_t s = 0;
 #pragma unroll
-        for (int c = 0; c < COPIES; ++c) s += s_hist[i * COPIES + c];
+        for (int c = 0; c < COPIES; ++c) s += s_hist[i * COPIES + ((c + i) & (COPIES - 1))];  // rotated: no bank conflicts
         if (s) atomicAdd(&g_hist[i], (unsigned long long)s);
     }
     __threadfence();
@@ -160,7 +229,7 @@ histogram_kernel(const U* __restrict__ keys, uint64_t n, KeyCodec<U> codec, int 
     if (!s_last) return;
     __threadfence();
     // Last block: exclusive digit offsets of every pass.
-    for (int p = 0; p < passes; ++p) {
+    for (int p = 0; p < PASSES; ++p) {
         const unsigned long long v = tid < kDigits ? __ldcg(&g_hist[p * kDigits + tid]) : 0ull;
         const unsigned long long ex = exclusive_scan_256<unsigned long long, BLOCK>(v, s_sums);
         if (tid < kDigits) g_bins[p * kDigits + tid] = ex;
@@ -179,7 +248,7 @@ struct OnesweepArgs {
     uint64_t n;
     KeyCodec<U> codec;
     int shift;
-    int nbits;
+    uint32_t digit_mask;             // (1 << bits of this pass) - 1
     const unsigned long long* bins;  // [256] exclusive global digit offsets of this pass
     ST* status;                      // [tiles][256] look-back rows of this pass
     ST* status_next;                 // rows the next pass uses (cleared here), or null
@@ -187,177 +256,374 @@ struct OnesweepArgs {
     uint32_t* error;
 };
 
-template <typename U, typename V, bool PAIRS, int BLOCK, int ITEMS, typename OffT>
+template <typename U, typename V, bool PAIRS, int BLOCK, int ITEMS, int PEERS, typename OffT>
 struct OnesweepSmem {
     static constexpr int kTile = BLOCK * ITEMS;
     static constexpr int kWarps = BLOCK / kWarp;
     union {
-        U keys[kTile];
-        uint32_t counters[kWarps * kDigits];  // per-warp digit counters while ranking
+        U keys[kTile];                        // transformed keys in tile-rank order
+        uint32_t counters[kWarps * kDigits];  // per-warp digit counters, then rank bases
     } u;
     V vals[PAIRS ? kTile : 1];
-    uint32_t digit_start[kDigits];  // first tile position of each digit
-    OffT gofs[kDigits];             // output index = gofs[digit] + tile position
+    // per slot parity: lanes holding each digit (PEERS 1) or each low-5-bit
+    // digit class (PEERS 2)
+    uint32_t peer_masks[2][PEERS == 1 ? kWarps * kDigits : (PEERS == 2 ? kWarps * 32 : 1)];
+    OffT gofs[kDigits];  // output index = gofs[digit] + tile position
+    uint32_t totals[kDigits];   // keys of each digit in the tile
+    uint32_t dstarts[kDigits];  // first tile rank of each digit
     uint32_t warp_sums[8];
     uint32_t tile_id;
+    int bad;
 };
 
-template <typename U, typename V, bool PAIRS, int BLOCK, int ITEMS, typename ST, typename OffT>
-__global__ void __launch_bounds__(BLOCK)
-onesweep_kernel(OnesweepArgs<U, V, ST, OffT> a)
+// Bounded wait until a status word is published (flag bits set).  Backs off
+// with __nanosleep so that waiting warps leave issue slots to the warps of
+// other tiles on the same SM.  On timeout (or when another thread already
+// reported an error) returns an inclusive zero so that the caller finishes.
+template <typename ST>
+__device__ __forceinline__ ST wait_status(const ST* p, ST w, uint32_t* error)
 {
-    using Smem = OnesweepSmem<U, V, PAIRS, BLOCK, ITEMS, OffT>;
     using SB = StatusBits<ST>;
-    constexpr int kTile = Smem::kTile;
-    constexpr int kWarps = Smem::kWarps;
-    static_assert(BLOCK >= kDigits, "one thread per digit");
-    static_assert(kTile <= 65536, "tile positions are packed in 16 bits");
-    static_assert(sizeof(U) * kTile >= sizeof(uint32_t) * kWarps * kDigits, "counter overlay");
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    Smem& s = *reinterpret_cast<Smem*>(smem_raw);
+    uint32_t spins = 0;
+    uint64_t t0 = 0;
+    while ((w & SB::kFlags) == 0) {
+        __nanosleep(32);
+        w = ld_relaxed(p);
+        if (++spins == 32) {
+            spins = 0;
+            const uint64_t now = global_timer_ns();
+            if (t0 == 0) {
+                t0 = now;
+            } else if (now - t0 > kWaitLimitNs) {
+                report_error(error, kDevErrTimeout);
+                return SB::kInclusive;
+            }
+            if (error_raised(error)) return SB::kInclusive;
+        }
+    }
+    return w;
+}
 
+// Exclusive prefix of one digit over tiles [0, tile): walk back from
+// tile - 1, W tiles per round trip, adding partial counts until an inclusive
+// count is found.  Tile 0 always publishes an inclusive count.
+template <typename ST, typename OffT, int W>
+__device__ __forceinline__ OffT lookback_digit(const ST* status, uint32_t tile, int digit, uint32_t* error)
+{
+    using SB = StatusBits<ST>;
+    OffT prefix = 0;
+    int64_t base = int64_t(tile) - 1;
+    while (true) {
+        ST w[W];
+#pragma unroll
+        for (int q = 0; q < W; ++q) {
+            const int64_t j = base - q;
+            w[q] = j >= 0 ? ld_relaxed(status + uint64_t(j) * kDigits + digit) : SB::kInclusive;
+        }
+        bool done = false;
+#pragma unroll
+        for (int q = 0; q < W; ++q) {
+            if (!done) {
+                const int64_t j = base - q;
+                if (j >= 0) w[q] = wait_status(status + uint64_t(j) * kDigits + digit, w[q], error);
+                prefix += OffT(w[q] & SB::kValue);
+                done = (w[q] & SB::kInclusive) != 0;
+            }
+        }
+        if (done) return prefix;
+        base -= W;
+    }
+}
+
+// Predicated shared-memory atomic add: returns the old value when `pred`,
+// else 0, without a branch.
+__device__ __forceinline__ uint32_t shared_add_if(bool pred, uint32_t smem_addr, uint32_t inc)
+{
+    uint32_t old = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "@p atom.shared.add.u32 %0, [%2], %3;\n\t}"
+        : "+r"(old)
+        : "r"(uint32_t(pred)), "r"(smem_addr), "r"(inc)
+        : "memory");
+    return old;
+}
+
+// Lanes of the warp holding the same 8-bit digit: one ballot per digit bit
+// narrows the set (warp-level multisplit, Ashkiani et al., PPoPP 2016).  On
+// sm_100 this is cheaper than __match_any_sync.
+__device__ __forceinline__ uint32_t digit_peers(uint32_t d)
+{
+    uint32_t peers = 0xffffffffu;
+#pragma unroll
+    for (int b = 0; b < kRadixBits; ++b) {
+        const bool bit = (d >> b) & 1u;
+        const uint32_t vote = __ballot_sync(0xffffffffu, bit);
+        peers &= bit ? vote : ~vote;
+    }
+    return peers;
+}
+
+// Digit extraction for the onesweep kernel.  BYTE: the pass covers a whole
+// byte of a 4-byte key (shift % 8 == 0, 8 bits), so one byte permute
+// extracts it.
+template <int KIND, bool BYTE, typename U>
+__device__ __forceinline__ uint32_t pass_digit(U t, int shift, uint32_t mask, uint32_t byte_sel)
+{
+    if constexpr (BYTE && sizeof(U) == 4) {
+        if constexpr (KIND == kFloat) {
+            constexpr U kHigh = U(1) << 31;
+            t = t == U(kHigh - 1) ? kHigh : t;
+        }
+        return __byte_perm(uint32_t(t), 0u, byte_sel);
+    } else {
+        return digit_of<KIND>(t, shift, mask);
+    }
+}
+
+// Fire-and-forget shared-memory OR.
+__device__ __forceinline__ void shared_red_or(uint32_t smem_addr, uint32_t bits)
+{
+    asm volatile("red.shared.or.b32 [%0], %1;" ::"r"(smem_addr), "r"(bits) : "memory");
+}
+
+__device__ __forceinline__ uint32_t shared_load(uint32_t smem_addr)
+{
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void shared_store_if(bool pred, uint32_t smem_addr, uint32_t v)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.u32 p, %0, 0;\n\t"
+        "@p st.shared.u32 [%1], %2;\n\t}" ::"r"(uint32_t(pred)), "r"(smem_addr), "r"(v)
+        : "memory");
+}
+
+// Fire-and-forget shared-memory add.
+__device__ __forceinline__ void shared_red_add(uint32_t smem_addr, uint32_t inc)
+{
+    asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(smem_addr), "r"(inc) : "memory");
+}
+
+// Everything after the tile id is known.  FULL: the tile has kTile keys (all
+// but possibly the last tile), compiled without any per-key bounds logic.
+template <bool FULL, bool BYTE, int PEERS, typename U, typename V, bool PAIRS, int BLOCK, int ITEMS,
+          int KIND, int LB_WINDOW, typename ST, typename OffT>
+__device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>& a,
+                                             OnesweepSmem<U, V, PAIRS, BLOCK, ITEMS, PEERS, OffT>& s,
+                                             uint32_t tile, int valid)
+{
+    using SB = StatusBits<ST>;
+    constexpr int kTile = BLOCK * ITEMS;
+    constexpr int kWarps = BLOCK / kWarp;
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
-
-    if (tid == 0) s.tile_id = atomicAdd(a.tile_counter, 1u);
-    for (int i = tid; i < kWarps * kDigits; i += BLOCK) s.u.counters[i] = 0;
-    __syncthreads();
-    const uint32_t tile = s.tile_id;
     const uint64_t tile_base = uint64_t(tile) * kTile;
-    const int valid = int(a.n - tile_base < uint64_t(kTile) ? a.n - tile_base : uint64_t(kTile));
-    const uint32_t max_digit = (1u << a.nbits) - 1u;
+    const uint32_t dmask = a.digit_mask;
+    const uint32_t byte_sel = 0x4440u | uint32_t(a.shift >> 3);
+    auto digit = [&](U t) { return pass_digit<KIND, BYTE>(t, a.shift, dmask, byte_sel); };
+    auto in_tile = [&](int i) { return FULL || warp * ITEMS * kWarp + lane + i * kWarp < valid; };
 
     // Warp-striped load: warp w owns positions [w*ITEMS*32, (w+1)*ITEMS*32) of
     // the tile, slot i of lane l is position w*ITEMS*32 + i*32 + l.
     U keys[ITEMS];
     V vals[PAIRS ? ITEMS : 1];
-    uint32_t packed[ITEMS];
-    const int warp_base = warp * ITEMS * kWarp + lane;
+    uint32_t rank[ITEMS];
+    const uint32_t counters_base =
+        static_cast<uint32_t>(__cvta_generic_to_shared(s.u.counters + warp * kDigits));
+    {
+        const int warp_base = warp * ITEMS * kWarp + lane;
+        const U* src = a.keys_in + tile_base + warp_base;
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-        const int pos = warp_base + i * kWarp;
-        keys[i] = pos < valid ? a.keys_in[tile_base + pos] : U(0);
-    }
-    if constexpr (PAIRS) {
+        for (int i = 0; i < ITEMS; ++i) keys[i] = in_tile(i) ? src[i * kWarp] : U(0);
+        if constexpr (PAIRS) {
+            const V* vsrc = a.vals_in + tile_base + warp_base;
 #pragma unroll
-        for (int i = 0; i < ITEMS; ++i) {
-            const int pos = warp_base + i * kWarp;
-            vals[i] = pos < valid ? a.vals_in[tile_base + pos] : V(0);
+            for (int i = 0; i < ITEMS; ++i) vals[i] = in_tile(i) ? vsrc[i * kWarp] : V(0);
         }
-    }
-
-    // Stable in-warp ranking: keys of one slot are ranked in lane order among
-    // equal digits, slots in order; the digit's leader lane bumps the warp's
-    // shared counter by the number of peers.
-    const uint32_t lt = lanemask_lt();
-    uint32_t* my_counters = s.u.counters + warp * kDigits;
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-        const int pos = warp_base + i * kWarp;
-        const uint32_t d =
-            pos < valid ? uint32_t(transform_key(keys[i], a.codec) >> a.shift) & max_digit : max_digit;
-        const uint32_t peers = __match_any_sync(0xffffffffu, d);
-        const int leader = 31 - __clz(peers);
-        uint32_t base = 0;
-        if (lane == leader) base = atomicAdd(&my_counters[d], uint32_t(__popc(peers)));
-        base = __shfl_sync(0xffffffffu, base, leader);
-        packed[i] = (d << 16) | (base + __popc(peers & lt));
+        for (int i = 0; i < ITEMS; ++i) keys[i] = twiddle_in<KIND>(keys[i], a.codec);
+        // Early counts: per-warp digit histograms.  Positions past the end
+        // of the last tile take the largest digit, so they rank after every
+        // real key and are never stored.
+#pragma unroll
+        for (int i = 0; i < ITEMS; ++i)
+            shared_red_add(counters_base + (in_tile(i) ? digit(keys[i]) : dmask) * 4u, 1u);
     }
     __syncthreads();
 
-    // Per digit: exclusive prefix over warps, tile total, early publication.
+    // Per digit: tile total (published at once), block-wide digit start,
+    // then counters[w][d] := digit start + count of d in warps < w, the
+    // first tile rank of warp w's keys with digit d.
     uint32_t total = 0;
     if (tid < kDigits) {
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-            const uint32_t c = s.u.counters[w * kDigits + tid];
-            s.u.counters[w * kDigits + tid] = total;
-            total += c;
-        }
-        ST* mine = a.status + uint64_t(tile) * kDigits + tid;
-        st_relaxed(mine, ST(total) | (tile == 0 ? SB::kInclusive : SB::kPartial));
+        for (int w = 0; w < kWarps; ++w) total += s.u.counters[w * kDigits + tid];
+        st_relaxed(a.status + uint64_t(tile) * kDigits + tid,
+                   ST(total) | (tile == 0 ? SB::kInclusive : SB::kPartial));
     }
     const uint32_t dstart = exclusive_scan_256<uint32_t, BLOCK>(total, s.warp_sums);
-    if (tid < kDigits) s.digit_start[tid] = dstart;
+    if (tid < kDigits) {
+        uint32_t run = dstart;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) {
+            const uint32_t c = s.u.counters[w * kDigits + tid];
+            s.u.counters[w * kDigits + tid] = run;
+            run += c;
+        }
+        s.totals[tid] = total;
+        s.dstarts[tid] = dstart;
+    }
     __syncthreads();
 
-    // Tile rank = digit start + earlier warps' count of the digit + in-warp rank.
-#pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-        const uint32_t d = packed[i] >> 16;
-        packed[i] = s.digit_start[d] + s.u.counters[warp * kDigits + d] + (packed[i] & 0xffffu);
-    }
-    __syncthreads();  // counters are dead; the key tile reuses their storage
+    // Publishes the inclusive count of digit d and its output base, and
+    // checks that the digit's keys land inside the output (a broken
+    // invariant becomes an error code, never a wild write).
+    auto finish_digit = [&](int d, OffT prefix) {
+        const uint32_t tot = s.totals[d];
+        if (tile > 0) st_relaxed(a.status + uint64_t(tile) * kDigits + d, ST(prefix + tot) | SB::kInclusive);
+        s.gofs[d] = OffT(a.bins[d]) + prefix - OffT(s.dstarts[d]);
+        // positions past the end of the last tile all carry the largest digit
+        const uint32_t stored = tot - ((!FULL && uint32_t(d) == dmask) ? uint32_t(kTile - valid) : 0u);
+        if (uint64_t(a.bins[d]) + uint64_t(prefix) + stored > a.n) s.bad = 1;
+        if (a.status_next) a.status_next[uint64_t(tile) * kDigits + d] = 0;
+    };
 
-    // Decoupled look-back, one digit per thread.
+    // Stable ranking: keys of one slot are ranked in lane order among equal
+    // digits, slots in order; the digit's leader lane advances the warp's
+    // rank counter by the number of peers and the returned value is the
+    // first tile rank of the group.  The leader's atomic is predicated rather
+    // than branched around, so the atomics of all slots are issued back to
+    // back; shared-memory operations of one warp complete in issue order,
+    // which keeps consecutive slots consistent.
+    {
+        const uint32_t lt = lanemask_lt();
+        constexpr int kMaskWords = PEERS == 1 ? kDigits : 32;  // mask words per warp and parity
+        const uint32_t masks_base =
+            static_cast<uint32_t>(__cvta_generic_to_shared(s.peer_masks[0] + warp * kMaskWords));
+#pragma unroll
+        for (int i = 0; i < ITEMS; ++i) {
+            const uint32_t d = in_tile(i) ? digit(keys[i]) : dmask;
+            uint32_t peers;
+            uint32_t maddr = 0;
+            if constexpr (PEERS == 0) {
+                peers = digit_peers(d);
+            } else {
+                // Each lane ORs its bit into the slot's mask word of its digit
+                // (PEERS 1) or of its digit's low 5 bits (PEERS 2: 32 words,
+                // one per bank, so these accesses never conflict, and one
+                // ballot per remaining bit narrows the class to the digit).
+                // Masks alternate between two arrays by slot parity; every
+                // lane clears its word once all lanes have read it (the
+                // shuffle below depends on every lane's read), so a word is
+                // clean again two slots later.
+                const uint32_t w = PEERS == 1 ? d : (d & 31u);
+                maddr = masks_base + ((i & 1) * kWarps * kMaskWords + w) * 4u;
+                shared_red_or(maddr, 1u << lane);
+                __syncwarp();
+                peers = shared_load(maddr);
+                if constexpr (PEERS == 2) {
+#pragma unroll
+                    for (int b = 5; b < kRadixBits; ++b) {
+                        const bool bit = (d >> b) & 1u;
+                        const uint32_t vote = __ballot_sync(0xffffffffu, bit);
+                        peers &= bit ? vote : ~vote;
+                    }
+                }
+            }
+            const int leader = 31 - __clz(peers);
+            uint32_t base = shared_add_if(lane == leader, counters_base + d * 4u, uint32_t(__popc(peers)));
+            base = __shfl_sync(0xffffffffu, base, leader);
+            if constexpr (PEERS == 1) shared_store_if(lane == leader, maddr, 0u);
+            if constexpr (PEERS == 2) shared_store_if(true, maddr, 0u);
+            rank[i] = base + __popc(peers & lt);
+        }
+    }
+    __syncthreads();  // rank counters are dead; the key tile reuses their storage
+
+    // Decoupled look-back, one digit per thread, LB_WINDOW predecessor tiles
+    // per round trip.
     if (tid < kDigits) {
         OffT prefix = 0;
-        if (tile > 0) {
-            int64_t j = int64_t(tile) - 1;
-            uint32_t spins = 0;
-            uint64_t t0 = 0;
-            while (true) {
-                const ST w = ld_relaxed(a.status + uint64_t(j) * kDigits + tid);
-                if ((w & SB::kFlags) == 0) {
-                    if (++spins == 64) {
-                        spins = 0;
-                        const uint64_t now = global_timer_ns();
-                        if (t0 == 0) {
-                            t0 = now;
-                        } else if (now - t0 > kWaitLimitNs) {
-                            report_error(a.error, kDevErrTimeout);
-                            break;
-                        }
-                        if (error_raised(a.error)) break;  // another waiter gave up
-                    }
-                    continue;
-                }
-                prefix += OffT(w & SB::kValue);
-                if ((w & SB::kInclusive) || j == 0) break;
-                --j;
-            }
-            st_relaxed(a.status + uint64_t(tile) * kDigits + tid,
-                       ST(prefix + total) | SB::kInclusive);
-        }
-        s.gofs[tid] = OffT(a.bins[tid]) + prefix - OffT(dstart);
-        if (a.status_next) a.status_next[uint64_t(tile) * kDigits + tid] = 0;
+        if (tile > 0) prefix = lookback_digit<ST, OffT, LB_WINDOW>(a.status, tile, tid, a.error);
+        finish_digit(tid, prefix);
     }
 
-    // Tile ranks are a permutation of [0, kTile) by construction; the check
-    // turns a broken invariant into an error code instead of a wild write.
-    bool rank_ok = true;
+    {
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) rank_ok &= packed[i] < uint32_t(kTile);
-    if (rank_ok) {
-#pragma unroll
-        for (int i = 0; i < ITEMS; ++i) s.u.keys[packed[i]] = keys[i];
+        for (int i = 0; i < ITEMS; ++i) s.u.keys[rank[i]] = keys[i];
         if constexpr (PAIRS) {
 #pragma unroll
-            for (int i = 0; i < ITEMS; ++i) s.vals[packed[i]] = vals[i];
+            for (int i = 0; i < ITEMS; ++i) s.vals[rank[i]] = vals[i];
         }
-    } else {
-        report_error(a.error, kDevErrInternal);
     }
     __syncthreads();
+    if (s.bad) {
+        if (tid == 0) report_error(a.error, kDevErrInternal);
+        return;
+    }
 
     // Digit-ordered tile -> global: consecutive threads write consecutive
-    // positions of one digit run.
+    // positions of one digit run.  Loads, offset lookups and stores are done
+    // in separate unrolled phases so that their latencies overlap.
+    {
+        OffT out_pos[ITEMS];
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-        const int idx = i * BLOCK + tid;
-        if (idx < valid) {
-            const U k = s.u.keys[idx];
-            const uint32_t d = uint32_t(transform_key(k, a.codec) >> a.shift) & max_digit;
-            const OffT pos = s.gofs[d] + OffT(idx);
-            if (uint64_t(pos) < a.n) {  // always true when the offsets are consistent
-                a.keys_out[pos] = k;
-                if constexpr (PAIRS) a.vals_out[pos] = s.vals[idx];
-            } else {
-                report_error(a.error, kDevErrInternal);
+        for (int i = 0; i < ITEMS; ++i) keys[i] = s.u.keys[i * BLOCK + tid];
+#pragma unroll
+        for (int i = 0; i < ITEMS; ++i) out_pos[i] = s.gofs[digit(keys[i])] + OffT(i * BLOCK + tid);
+        if constexpr (PAIRS) {
+#pragma unroll
+            for (int i = 0; i < ITEMS; ++i) vals[i] = s.vals[i * BLOCK + tid];
+        }
+#pragma unroll
+        for (int i = 0; i < ITEMS; ++i) {
+            if (FULL || i * BLOCK + tid < valid) {
+                a.keys_out[out_pos[i]] = twiddle_out<KIND>(keys[i], a.codec);
+                if constexpr (PAIRS) a.vals_out[out_pos[i]] = vals[i];
             }
         }
     }
+}
+
+template <typename U, typename V, bool PAIRS, int BLOCK, int ITEMS, int KIND, bool BYTE, int PEERS, int LB_WINDOW,
+          typename ST, typename OffT>
+__global__ void __launch_bounds__(BLOCK)
+onesweep_kernel(OnesweepArgs<U, V, ST, OffT> a)
+{
+    using Smem = OnesweepSmem<U, V, PAIRS, BLOCK, ITEMS, PEERS, OffT>;
+    constexpr int kTile = Smem::kTile;
+    constexpr int kWarps = Smem::kWarps;
+    static_assert(BLOCK >= kDigits, "one thread per digit");
+    static_assert(kTile <= 65536, "tile ranks fit 16 bits");
+    static_assert(sizeof(U) * kTile >= sizeof(uint32_t) * kWarps * kDigits, "counter overlay");
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    Smem& s = *reinterpret_cast<Smem*>(smem_raw);
+
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        s.tile_id = atomicAdd(a.tile_counter, 1u);
+        s.bad = 0;
+    }
+    for (int i = tid; i < kWarps * kDigits; i += BLOCK) s.u.counters[i] = 0;
+    if constexpr (PEERS != 0) {
+        constexpr int kMaskWords = 2 * kWarps * (PEERS == 1 ? kDigits : 32);
+        for (int i = tid; i < kMaskWords; i += BLOCK) s.peer_masks[0][i] = 0;
+    }
+    __syncthreads();
+    const uint32_t tile = s.tile_id;
+    const uint64_t tile_base = uint64_t(tile) * kTile;
+    if (tile_base + kTile <= a.n)
+        process_tile<true, BYTE, PEERS, U, V, PAIRS, BLOCK, ITEMS, KIND, LB_WINDOW, ST, OffT>(a, s, tile, kTile);
+    else
+        process_tile<false, BYTE, PEERS, U, V, PAIRS, BLOCK, ITEMS, KIND, LB_WINDOW, ST, OffT>(
+            a, s, tile, int(a.n - tile_base));
 }
 
 // ---------------------------------------------------------------------------
@@ -365,49 +631,30 @@ onesweep_kernel(OnesweepArgs<U, V, ST, OffT> a)
 // ---------------------------------------------------------------------------
 namespace {
 
-// Tile geometry per (key bytes, value bytes).
-struct Geometry {
-    int block;
-    int items;
-    int tile() const { return block * items; }
-};
-
-Geometry geometry(int kb, int vb)
-{
-    if (kb == 4 && vb == 0) return {384, 20};
-    if (kb == 4 && vb == 4) return {384, 15};
-    if (kb == 4 && vb == 8) return {256, 16};
-    if (kb == 8 && vb == 0) return {256, 16};
-    if (kb == 8 && vb == 4) return {256, 14};
-    return {256, 12};  // 8-byte keys, 8-byte values
-}
-
-constexpr int kHistBlock = 512;
-
-int hist_copies(int kb) { return kb == 4 ? 8 : 4; }
+// Smallest tile (keys per onesweep block) of any configuration; sizes the
+// look-back rows in temp storage.
+constexpr uint64_t kMinTile = 4096;
+constexpr int kHistBlock = 1024;
 
 struct Layout {
     size_t ctrl, hist, bins, status_a, status_b, keys_alt, vals_alt, total;
-    size_t status_bytes;  // per buffer
-    uint64_t tiles;
-    bool wide;
+    bool wide;  // 64-bit status words and offsets (n >= 2^30)
 };
 
 Layout make_layout(int kb, int vb, uint64_t n)
 {
     Layout L{};
-    const Geometry g = geometry(kb, vb);
     L.wide = n >= (1ull << 30);
-    L.tiles = ceil_div(n, uint64_t(g.tile()));
+    const uint64_t max_tiles = ceil_div(n, kMinTile);
     const size_t st = L.wide ? 8 : 4;
     const int max_passes = kb;  // 8-bit passes over the full key width
     size_t off = 0;
     L.ctrl = off; off += kTempAlign;
     L.hist = off; off = align_up(off + size_t(max_passes) * kDigits * 8, kTempAlign);
     L.bins = off; off = align_up(off + size_t(max_passes) * kDigits * 8, kTempAlign);
-    L.status_bytes = align_up(size_t(L.tiles) * kDigits * st, kTempAlign);
-    L.status_a = off; off += L.status_bytes;
-    L.status_b = off; off += L.status_bytes;
+    const size_t status_bytes = align_up(size_t(max_tiles) * kDigits * st, kTempAlign);
+    L.status_a = off; off += status_bytes;
+    L.status_b = off; off += status_bytes;
     L.keys_alt = off; off = align_up(off + size_t(n) * kb, kTempAlign);
     L.vals_alt = off; off = align_up(off + size_t(n) * vb, kTempAlign);
     L.total = off;
@@ -427,19 +674,88 @@ struct SortCall {
     void* vals_dst[kMaxPasses];
 };
 
-template <typename U, typename V, bool PAIRS, int BLOCK, int ITEMS, typename ST, typename OffT>
+template <typename U, int KIND, int PASSES>
+void launch_histogram_p(unsigned grid, size_t smem, uint64_t chunk, const U* keys, uint64_t n,
+                        const KeyCodec<U>& codec, int begin_bit, uint32_t last_mask, Ctrl* ctrl,
+                        unsigned long long* hist, unsigned long long* bins, cudaStream_t stream)
+{
+    constexpr int COPIES = sizeof(U) == 4 ? 32 : 16;
+    auto k = histogram_kernel<U, KIND, PASSES, kHistBlock, COPIES>;
+    set_smem_once(k, smem);
+    k<<<grid, kHistBlock, smem, stream>>>(keys, n, codec, begin_bit, last_mask, chunk, ctrl, hist, bins);
+}
+
+template <typename U, int KIND>
+lcpp_status launch_histogram(const Layout& L, unsigned char* temp, const U* keys, uint64_t n,
+                             const KeyCodec<U>& codec, int begin_bit, int end_bit, int passes,
+                             cudaStream_t stream)
+{
+    // 128 KB of counters at most (4 passes x 32 copies, or 8 passes x 16
+    // copies): one block of kHistBlock threads per SM.
+    constexpr int COPIES = sizeof(U) == 4 ? 32 : 16;
+    const int vec = 16 / int(sizeof(U));
+    const uint64_t per_block_min = uint64_t(kHistBlock) * vec * 4;
+    const uint64_t max_blocks = uint64_t(device_sm_count());
+    uint64_t blocks = std::max<uint64_t>(1, std::min(max_blocks, ceil_div(n, per_block_min)));
+    const uint64_t chunk = align_up(ceil_div(n, blocks), size_t(vec) * kHistBlock);
+    blocks = ceil_div(n, chunk);
+    const size_t smem = size_t(passes) * kDigits * COPIES * sizeof(uint32_t);
+    Ctrl* ctrl = reinterpret_cast<Ctrl*>(temp + L.ctrl);
+    auto* hist = reinterpret_cast<unsigned long long*>(temp + L.hist);
+    auto* bins = reinterpret_cast<unsigned long long*>(temp + L.bins);
+    const int last_bits = end_bit - begin_bit - kRadixBits * (passes - 1);
+    const uint32_t last_mask = (1u << last_bits) - 1u;
+    const unsigned grid = unsigned(blocks);
+    diag::KernelTimer timer(0 /* LCPP_KERNEL_SORT_HISTOGRAM */, n, stream);
+#define LCPP_HIST(P) launch_histogram_p<U, KIND, P>(grid, smem, chunk, keys, n, codec, begin_bit, last_mask, ctrl, hist, bins, stream)
+    switch (passes) {
+    case 1: LCPP_HIST(1); break;
+    case 2: LCPP_HIST(2); break;
+    case 3: LCPP_HIST(3); break;
+    case 4: LCPP_HIST(4); break;
+    default:
+        if constexpr (sizeof(U) == 8) {
+            switch (passes) {
+            case 5: LCPP_HIST(5); break;
+            case 6: LCPP_HIST(6); break;
+            case 7: LCPP_HIST(7); break;
+            default: LCPP_HIST(8); break;
+            }
+        }
+        break;
+    }
+#undef LCPP_HIST
+    return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;
+}
+
+template <typename U, typename V, bool PAIRS, int BLOCK, int ITEMS, int KIND, int PEERS, int LB_WINDOW,
+          typename ST, typename OffT, bool BYTE>
+void launch_pass(const OnesweepArgs<U, V, ST, OffT>& a, uint64_t tiles, cudaStream_t stream)
+{
+    using Smem = OnesweepSmem<U, V, PAIRS, BLOCK, ITEMS, PEERS, OffT>;
+    auto kernel = onesweep_kernel<U, V, PAIRS, BLOCK, ITEMS, KIND, BYTE, PEERS, LB_WINDOW, ST, OffT>;
+    set_smem_once(kernel, sizeof(Smem));
+    kernel<<<unsigned(tiles), BLOCK, sizeof(Smem), stream>>>(a);
+}
+
+template <typename U, typename V, bool PAIRS, int BLOCK, int ITEMS, int KIND, int PEERS, int LB_WINDOW,
+          typename ST, typename OffT>
 lcpp_status launch_passes(const Layout& L, unsigned char* temp, const SortCall& c, uint64_t n,
                           const KeyCodec<U>& codec, int begin_bit, int end_bit, int passes,
                           cudaStream_t stream)
 {
-    using Smem = OnesweepSmem<U, V, PAIRS, BLOCK, ITEMS, OffT>;
-    auto kernel = onesweep_kernel<U, V, PAIRS, BLOCK, ITEMS, ST, OffT>;
-    const size_t smem = sizeof(Smem);
-    set_smem_once(kernel, smem);
+    static_assert(BLOCK * ITEMS >= kMinTile, "look-back rows are sized for kMinTile");
     Ctrl* ctrl = reinterpret_cast<Ctrl*>(temp + L.ctrl);
     const unsigned long long* bins = reinterpret_cast<const unsigned long long*>(temp + L.bins);
     ST* status[2] = {reinterpret_cast<ST*>(temp + L.status_a), reinterpret_cast<ST*>(temp + L.status_b)};
-    const unsigned grid = unsigned(L.tiles);
+    const uint64_t tiles = ceil_div(n, uint64_t(BLOCK) * ITEMS);
+    // Control block, histograms, offsets and the pass-0 look-back rows are
+    // contiguous in the layout: one memset clears them.
+    LCPP_CUDA_TRY(cudaMemsetAsync(temp + L.ctrl, 0, L.status_a + size_t(tiles) * kDigits * sizeof(ST) - L.ctrl,
+                                  stream));
+    lcpp_status st = launch_histogram<U, KIND>(L, temp, static_cast<const U*>(c.keys_src[0]), n, codec,
+                                               begin_bit, end_bit, passes, stream);
+    if (st != LCPP_OK) return st;
     for (int p = 0; p < passes; ++p) {
         OnesweepArgs<U, V, ST, OffT> a;
         a.keys_in = static_cast<const U*>(c.keys_src[p]);
@@ -449,49 +765,63 @@ lcpp_status launch_passes(const Layout& L, unsigned char* temp, const SortCall& 
         a.n = n;
         a.codec = codec;
         a.shift = begin_bit + kRadixBits * p;
-        a.nbits = min(kRadixBits, end_bit - a.shift);
+        a.digit_mask = (1u << min(kRadixBits, end_bit - a.shift)) - 1u;
         a.bins = bins + p * kDigits;
         a.status = status[p & 1];
         a.status_next = (p + 1 < passes) ? status[(p + 1) & 1] : nullptr;
         a.tile_counter = &ctrl->tile_counter[p];
         a.error = &ctrl->error;
         diag::KernelTimer timer(1 /* LCPP_KERNEL_SORT_ONESWEEP */, n, stream);
-        kernel<<<grid, BLOCK, smem, stream>>>(a);
+        if (sizeof(U) == 4 && a.shift % 8 == 0 && a.digit_mask == 0xffu)
+            launch_pass<U, V, PAIRS, BLOCK, ITEMS, KIND, PEERS, LB_WINDOW, ST, OffT, true>(a, tiles, stream);
+        else
+            launch_pass<U, V, PAIRS, BLOCK, ITEMS, KIND, PEERS, LB_WINDOW, ST, OffT, false>(a, tiles, stream);
         timer.stop();
     }
     return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;
 }
 
-template <typename U>
-lcpp_status launch_histogram(const Layout& L, unsigned char* temp, const U* keys, uint64_t n,
-                             const KeyCodec<U>& codec, int begin_bit, int end_bit, int passes,
-                             cudaStream_t stream)
+// Onesweep tile variant for 4-byte unsigned ascending keys without values,
+// selectable with the environment variable LCPP_ONESWEEP_VARIANT (tuning
+// sweeps); read once per process.
+int onesweep_variant()
 {
-    constexpr int COPIES = sizeof(U) == 4 ? 8 : 4;
-    const int vec = 16 / int(sizeof(U));
-    const bool aligned = (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
-    const uint64_t per_block_min = uint64_t(kHistBlock) * vec * 4;
-    const uint64_t max_blocks = uint64_t(device_sm_count()) * 2;
-    uint64_t blocks = std::max<uint64_t>(1, std::min(max_blocks, ceil_div(n, per_block_min)));
-    uint64_t chunk = align_up(ceil_div(n, blocks), size_t(vec) * kHistBlock);
-    blocks = ceil_div(n, chunk);
-    const size_t smem = size_t(passes) * kDigits * COPIES * sizeof(uint32_t);
-    Ctrl* ctrl = reinterpret_cast<Ctrl*>(temp + L.ctrl);
-    auto* hist = reinterpret_cast<unsigned long long*>(temp + L.hist);
-    auto* bins = reinterpret_cast<unsigned long long*>(temp + L.bins);
-    diag::KernelTimer timer(0 /* LCPP_KERNEL_SORT_HISTOGRAM */, n, stream);
-    if (aligned) {
-        auto k = histogram_kernel<U, kHistBlock, COPIES, true>;
-        set_smem_once(k, smem);
-        k<<<unsigned(blocks), kHistBlock, smem, stream>>>(keys, n, codec, begin_bit, end_bit, passes,
-                                                          chunk, ctrl, hist, bins);
+    static const int v = [] {
+        const char* e = std::getenv("LCPP_ONESWEEP_VARIANT");
+        return e ? std::atoi(e) : 0;
+    }();
+    return v;
+}
+
+template <typename U, typename V, bool PAIRS, int KIND>
+lcpp_status run_kind(const Layout& L, unsigned char* temp, const SortCall& c, uint64_t n,
+                     const KeyCodec<U>& codec, int begin_bit, int end_bit, int passes, cudaStream_t stream)
+{
+#define LCPP_PASSES(B, I, SP, W)                                                                      \
+    (L.wide ? launch_passes<U, V, PAIRS, B, I, KIND, SP, W, uint64_t, uint64_t>(L, temp, c, n, codec,  \
+                                                                                begin_bit, end_bit,   \
+                                                                                passes, stream)       \
+            : launch_passes<U, V, PAIRS, B, I, KIND, SP, W, uint32_t, uint32_t>(L, temp, c, n, codec,  \
+                                                                                begin_bit, end_bit,   \
+                                                                                passes, stream))
+    if constexpr (sizeof(U) == 4 && !PAIRS) {
+        if constexpr (KIND == kPlain) {
+            switch (onesweep_variant()) {
+            case 1: return LCPP_PASSES(384, 20, 0, 8);  // 8 ballots per digit
+            case 2: return LCPP_PASSES(256, 24, 1, 8);  // shared-memory peer masks
+            case 3: return LCPP_PASSES(384, 20, 2, 8);
+            default: break;
+            }
+        }
+        // Measured best on B200 for 4-byte keys: 256 x 24 keys per tile,
+        // peers from low-5-bit shared masks plus 3 ballots.
+        return LCPP_PASSES(256, 24, 2, 8);
+    } else if constexpr (sizeof(U) == 4 && sizeof(V) == 4) {
+        return LCPP_PASSES(384, 15, 0, 8);
     } else {
-        auto k = histogram_kernel<U, kHistBlock, COPIES, false>;
-        set_smem_once(k, smem);
-        k<<<unsigned(blocks), kHistBlock, smem, stream>>>(keys, n, codec, begin_bit, end_bit, passes,
-                                                          chunk, ctrl, hist, bins);
+        return LCPP_PASSES(256, 16, 0, 8);
     }
-    return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;
+#undef LCPP_PASSES
 }
 
 template <typename U, typename V, bool PAIRS>
@@ -500,37 +830,11 @@ lcpp_status run_typed(const Layout& L, unsigned char* temp, const SortCall& c, u
                       cudaStream_t stream)
 {
     const KeyCodec<U> codec = make_codec<U>(kdt, descending);
-    // Zero control block, histograms, offsets and the pass-0 look-back rows
-    // (contiguous in the layout).
-    const size_t zero_bytes = L.status_a + size_t(L.tiles) * kDigits * (L.wide ? 8 : 4) - L.ctrl;
-    LCPP_CUDA_TRY(cudaMemsetAsync(temp + L.ctrl, 0, zero_bytes, stream));
-    lcpp_status st = launch_histogram<U>(L, temp, static_cast<const U*>(c.keys_src[0]), n, codec,
-                                         begin_bit, end_bit, passes, stream);
-    if (st != LCPP_OK) return st;
-    const int kb = sizeof(U), vb = PAIRS ? int(sizeof(V)) : 0;
-    const Geometry g = geometry(kb, vb);
-#define LCPP_PASSES(B, I)                                                                       \
-    (L.wide ? launch_passes<U, V, PAIRS, B, I, uint64_t, uint64_t>(L, temp, c, n, codec,         \
-                                                                   begin_bit, end_bit, passes,  \
-                                                                   stream)                      \
-            : launch_passes<U, V, PAIRS, B, I, uint32_t, uint32_t>(L, temp, c, n, codec,         \
-                                                                   begin_bit, end_bit, passes,  \
-                                                                   stream))
-    if constexpr (sizeof(U) == 4 && !PAIRS) {
-        return LCPP_PASSES(384, 20);
-    } else if constexpr (sizeof(U) == 4 && sizeof(V) == 4) {
-        return LCPP_PASSES(384, 15);
-    } else if constexpr (sizeof(U) == 4) {
-        return LCPP_PASSES(256, 16);
-    } else if constexpr (!PAIRS) {
-        return LCPP_PASSES(256, 16);
-    } else if constexpr (sizeof(V) == 4) {
-        return LCPP_PASSES(256, 14);
-    } else {
-        return LCPP_PASSES(256, 12);
-    }
-#undef LCPP_PASSES
-    (void)g;
+    const bool is_float = kdt == LCPP_F32 || kdt == LCPP_F64;
+    const bool is_plain = !is_float && codec.xor_pos == U(0);
+    if (is_float) return run_kind<U, V, PAIRS, kFloat>(L, temp, c, n, codec, begin_bit, end_bit, passes, stream);
+    if (is_plain) return run_kind<U, V, PAIRS, kPlain>(L, temp, c, n, codec, begin_bit, end_bit, passes, stream);
+    return run_kind<U, V, PAIRS, kXor>(L, temp, c, n, codec, begin_bit, end_bit, passes, stream);
 }
 
 bool key_dtype_ok(lcpp_dtype dt) { return dtype_bytes(dt) != 0; }
@@ -573,6 +877,15 @@ lcpp_status sort(void* temp, size_t temp_bytes_given, const void* keys_in, void*
         return LCPP_OK;
     }
     if (!temp || (reinterpret_cast<uintptr_t>(temp) & (kTempAlign - 1))) return LCPP_ERR_INVALID_ARG;
+    // Element alignment of every key / value buffer.
+    auto misaligned = [](const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) != 0; };
+    if (double_buffer) {
+        if (misaligned(key_bufs[0], kb) || misaligned(key_bufs[1], kb)) return LCPP_ERR_INVALID_ARG;
+        if (pairs && (misaligned(val_bufs[0], vb) || misaligned(val_bufs[1], vb))) return LCPP_ERR_INVALID_ARG;
+    } else {
+        if (misaligned(keys_in, kb) || misaligned(keys_out, kb)) return LCPP_ERR_INVALID_ARG;
+        if (pairs && (misaligned(vals_in, vb) || misaligned(vals_out, vb))) return LCPP_ERR_INVALID_ARG;
+    }
     const Layout L = make_layout(kb, vb, n);
     if (temp_bytes_given < L.total) return LCPP_ERR_TEMP_TOO_SMALL;
     unsigned char* t = static_cast<unsigned char*>(temp);
