@@ -1,23 +1,26 @@
 #!/usr/bin/env python
-"""Benchmark: uint32 SortKeys at 2^28 keys per GPU (BASELINE metric
-"Gkeys/s uint32 SortKeys @2^28 (1/2/4/8 B200) and % of HBM roofline").
+"""Benchmark of the sort / scan / reduce path (BASELINE metric "Gkeys/s
+uint32 SortKeys @2^28 (1/2/4/8 B200) and % of HBM roofline").
 
-One step = one DeviceRadixSort::SortKeys (copy API) of 2^28 uniform uint32
-keys (seed 0, bits [0,32)) through the library's C ABI.
+Default (--op sort): one step = one DeviceRadixSort::SortKeys (copy API) of
+2^28 uniform uint32 keys per GPU (seed 0, bits [0,32)) through the library's
+C ABI.  The other BASELINE configurations are available with --op (pairs,
+pairs_f32, pairs_u64, bits, scan, reduce, reduce_max); the driver only runs
+the default.
 
 Arms:
   default           our sm_100a library.  N = 1: device-resident `value`
                     (inputs in HBM), `e2e` through the same public call with
-                    pinned host buffers (H2D of the keys + sort + D2H of the
-                    sorted keys inside the timed region), live roofline of the
-                    dominant kernel (onesweep pass) from CUDA events on the
-                    library's launch stream, clocks sampled during the timed
-                    region, and the CPU baseline (oracle port, all host
-                    threads, bounded sample) on rank 0.
+                    pinned host buffers (H2D of the inputs + the op + D2H of
+                    the result inside the timed region), live roofline of the
+                    dominant kernel from CUDA events on the library's launch
+                    stream, clocks sampled during the timed region, and the
+                    CPU baseline (oracle port, all host threads, bounded
+                    sample) on rank 0.
                     N > 1 (torchrun): the distributed sort, 2^28 keys per GPU
                     (weak scaling), max over ranks.
   --impl reference  the reference's own path on the host cores: its CPU
-                    restatement (oracle port, the reference cannot be built
+                    restatement (oracle port; the reference cannot be built
                     here), all host threads, a bounded sample of the same
                     workload per step.  Rank 0 only.
 """
@@ -38,11 +41,39 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "luisacompute-parallelprimitive_b200"))
 sys.path.insert(0, str(ROOT))
 
-METRIC = "Gkeys/s uint32 SortKeys @2^28"
-UNIT = "Gkeys/s"
-BYTES_PER_KEY_SORT = 36       # k*(1+2P), k=4, P=4 (8-bit passes)
-BYTES_PER_KEY_ONESWEEP = 8    # one pass reads and writes each 4-byte key
 FALLBACK_HBM_GBS = 6650.0
+DATA = "synthetic (splitmix64 counter streams; see include/lcpp_b200_testgen.h)"
+
+
+# ---------------------------------------------------------------------------
+# Workloads.  bytes: algorithmic HBM bytes per item of
+# the whole op (k*(1+2P) + v*2P for sorts with P 8-bit passes); kbytes:
+# algorithmic bytes per item of ONE launch of the dominant kernel.
+# ---------------------------------------------------------------------------
+OPS = {
+    "sort": dict(metric="Gkeys/s uint32 SortKeys @2^28", unit="Gkeys/s", log2n=28, dtype="u32",
+                 workload="SortKeys u32 uniform full range, bits [0,32), seed 0", bytes=36, kbytes=8,
+                 kernel="onesweep_kernel (one 8-bit pass)"),
+    "pairs": dict(metric="Gkeys/s uint32->uint32 SortPairs @2^28", unit="Gkeys/s", log2n=28, dtype="u32",
+                  workload="SortPairs u32 uniform keys, u32 values = index, seed 1", bytes=68, kbytes=16,
+                  kernel="onesweep_kernel (one 8-bit pass)"),
+    "pairs_f32": dict(metric="Gkeys/s float32->uint32 SortPairs @2^27", unit="Gkeys/s", log2n=27, dtype="f32",
+                      workload="SortPairs f32 N(0,1) keys with +-0.0, u32 values = index, seed 1",
+                      bytes=68, kbytes=16, kernel="onesweep_kernel (one 8-bit pass)"),
+    "pairs_u64": dict(metric="Gkeys/s uint64->int32 SortPairs @2^27", unit="Gkeys/s", log2n=27, dtype="u64",
+                      workload="SortPairs u64 uniform keys, i32 values = index, seed 1", bytes=200, kbytes=24,
+                      kernel="onesweep_kernel (one 8-bit pass)"),
+    "bits": dict(metric="Gkeys/s uint32 SortKeys bits [8,24) @2^27", unit="Gkeys/s", log2n=27, dtype="u32",
+                 workload="SortKeys u32 uniform, begin_bit 8, end_bit 24, seed 1", bytes=20, kbytes=8,
+                 kernel="onesweep_kernel (one 8-bit pass)"),
+    "scan": dict(metric="Gitems/s int32 InclusiveSum @2^30", unit="Gitems/s", log2n=30, dtype="i32",
+                 workload="InclusiveSum i32 uniform in [-1000,1000], seed 1", bytes=8, kbytes=8,
+                 kernel="scan_kernel"),
+    "reduce": dict(metric="Gitems/s float32 Reduce Sum @2^30", unit="Gitems/s", log2n=30, dtype="f32",
+                   workload="DeviceReduce::Sum f32 U[0,1), seed 1", bytes=4, kbytes=4, kernel="reduce_kernel"),
+    "reduce_max": dict(metric="Gitems/s int64 Reduce Max @2^30", unit="Gitems/s", log2n=30, dtype="i64",
+                       workload="DeviceReduce::Max i64 uniform, seed 1", bytes=8, kbytes=8, kernel="reduce_kernel"),
+}
 
 
 def parse_args():
@@ -51,7 +82,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--log2n", type=int, default=28, help="keys per GPU = 2^log2n")
+    ap.add_argument("--op", choices=sorted(OPS), default="sort")
+    ap.add_argument("--log2n", type=int, default=None, help="items per GPU = 2^log2n (default: the config's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -66,13 +98,13 @@ def measured_peak():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic():
-    """Per-launch DRAM bytes of the onesweep kernel from the committed ncu
-    summary (line 'traffic_bytes_per_key: X'), scaled to the workload."""
-    p = ROOT / "profiles" / "onesweep_u32_keys.md"
+def profiled_traffic(op: str):
+    """DRAM bytes per item of the dominant kernel from the committed ncu
+    summary (a line 'traffic_bytes_per_item[<op>]: X')."""
+    p = ROOT / "profiles" / "README.md"
     if not p.exists():
         return None
-    m = re.search(r"traffic_bytes_per_key:\s*([0-9.]+)", p.read_text())
+    m = re.search(rf"traffic_bytes_per_item\[{op}\]:\s*([0-9.]+)", p.read_text())
     return float(m.group(1)) if m else None
 
 
@@ -129,48 +161,149 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows), "power_w_max": max(r[2] for r in rows)}
 
 
-def cpu_sort_sample(n_sample: int, threads: int, min_seconds: float):
-    """Time the oracle port (multi-threaded LSD restatement) on a bounded
-    sample of the workload; returns (Gkeys/s, reps)."""
-    from oracle import oracle
-    keys = oracle.generate(oracle.GEN_U32_UNIFORM, n_sample, seed=0)
-    oracle.radix_sort(keys, threads=threads)  # warm
+# ---------------------------------------------------------------------------
+# Workload objects for our arm: inputs in HBM, one `step` = one public call.
+# ---------------------------------------------------------------------------
+class Workload:
+    def __init__(self, op: str, n: int):
+        import torch
+
+        import lcpp_b200 as L
+        self.op, self.n, self.L, self.torch = op, n, L, torch
+        dev = "cuda"
+        T = torch
+
+        def fill(dt, dist, seed):
+            t = T.empty(n, dtype=dt, device=dev)
+            L.testgen_fill(t, dist, seed=seed)
+            return t
+
+        if op == "sort":
+            self.inputs = [fill(T.uint32, L.GEN_U32_UNIFORM, 0)]
+            self.outputs = [T.empty_like(self.inputs[0])]
+            self.temp = L.alloc_temp(L.DeviceRadixSort.GetSortKeysTempStorageBytes(L.U32, n))
+        elif op == "bits":
+            self.inputs = [fill(T.uint32, L.GEN_U32_UNIFORM, 1)]
+            self.outputs = [T.empty_like(self.inputs[0])]
+            self.temp = L.alloc_temp(L.DeviceRadixSort.GetSortKeysTempStorageBytes(L.U32, n))
+        elif op in ("pairs", "pairs_f32", "pairs_u64"):
+            kdt, kdist, vdt, kc, vc = {
+                "pairs": (T.uint32, L.GEN_U32_UNIFORM, T.uint32, L.U32, L.U32),
+                "pairs_f32": (T.float32, L.GEN_F32_NORMAL, T.uint32, L.F32, L.U32),
+                "pairs_u64": (T.uint64, L.GEN_U64_UNIFORM, T.int32, L.U64, L.I32),
+            }[op]
+            self.inputs = [fill(kdt, kdist, 1), fill(vdt, L.GEN_U32_INDEX, 1)]
+            self.outputs = [T.empty_like(self.inputs[0]), T.empty_like(self.inputs[1])]
+            self.temp = L.alloc_temp(L.DeviceRadixSort.GetSortPairsTempStorageBytes(kc, vc, n))
+        elif op == "scan":
+            self.inputs = [fill(T.int32, L.GEN_I32_SCAN, 1)]
+            self.outputs = [T.empty_like(self.inputs[0])]
+            self.temp = L.alloc_temp(L.DeviceScan.GetTempStorageBytes(L.I32, n))
+        elif op == "reduce":
+            self.inputs = [fill(T.float32, L.GEN_F32_UNIT, 1)]
+            self.outputs = [T.empty(1, dtype=T.float32, device=dev)]
+            self.temp = L.alloc_temp(L.DeviceReduce.GetTempStorageBytes(L.F32, n))
+        elif op == "reduce_max":
+            self.inputs = [fill(T.int64, L.GEN_I64_UNIFORM, 1)]
+            self.outputs = [T.empty(1, dtype=T.int64, device=dev)]
+            self.temp = L.alloc_temp(L.DeviceReduce.GetTempStorageBytes(L.I64, n))
+        self.rs, self.sc, self.rd = L.DeviceRadixSort(), L.DeviceScan(), L.DeviceReduce()
+
+    def step(self, inputs=None):
+        op, n, i, o, t = self.op, self.n, inputs or self.inputs, self.outputs, self.temp
+        if op == "sort":
+            self.rs.SortKeys(t, i[0], o[0], n)
+        elif op == "bits":
+            self.rs.SortKeys(t, i[0], o[0], n, 8, 24)
+        elif op.startswith("pairs"):
+            self.rs.SortPairs(t, i[0], o[0], i[1], o[1], n)
+        elif op == "scan":
+            self.sc.InclusiveSum(t, i[0], o[0], n)
+        elif op == "reduce":
+            self.rd.Sum(t, i[0], o[0], n)
+        elif op == "reduce_max":
+            self.rd.Max(t, i[0], o[0], n)
+
+    def dominant_kind(self):
+        L = self.L
+        if self.op in ("scan",):
+            return L.KERNEL_SCAN
+        if self.op.startswith("reduce"):
+            return L.KERNEL_REDUCE
+        return L.KERNEL_SORT_ONESWEEP
+
+
+def cpu_fn(op: str, n_sample: int, threads: int):
+    """One run of the oracle port on a bounded sample of the workload (the
+    reference tests' host algorithms restated)."""
+    from oracle import oracle as O
+    if op in ("sort", "bits"):
+        x = O.generate(O.GEN_U32_UNIFORM, n_sample, seed=0 if op == "sort" else 1)
+        kw = dict(begin_bit=8, end_bit=24) if op == "bits" else {}
+        return lambda: O.radix_sort(x, threads=threads, **kw)
+    if op.startswith("pairs"):
+        dist = {"pairs": O.GEN_U32_UNIFORM, "pairs_f32": O.GEN_F32_UNIT, "pairs_u64": O.GEN_U64_UNIFORM}[op]
+        x = O.generate(dist, n_sample, seed=1)
+        v = O.generate(O.GEN_U32_INDEX, n_sample, seed=1)
+        return lambda: O.radix_sort(x, v, threads=threads)
+    if op == "scan":
+        x = O.generate(O.GEN_I32_SCAN, n_sample, seed=1)
+        return lambda: O.scan(x, "inclusive")
+    if op == "reduce":
+        x = O.generate(O.GEN_F32_UNIT, n_sample, seed=1)
+        return lambda: O.sum_f64(x)
+    x = O.generate(O.GEN_I64_UNIFORM, n_sample, seed=1)
+    return lambda: O.reduce(x, O.OP_MAX, -(1 << 63))
+
+
+def cpu_sample(op: str, n_sample: int, threads: int, min_seconds: float):
+    """Items per second of the oracle port over at least min_seconds."""
+    fn = cpu_fn(op, n_sample, threads)
+    fn()
     reps, t0 = 0, time.perf_counter()
     while True:
-        oracle.radix_sort(keys, threads=threads)
+        fn()
         reps += 1
         el = time.perf_counter() - t0
         if el >= min_seconds:
             break
-    return n_sample * reps / el / 1e9, reps
+    return n_sample * reps / el, reps
+
+
+def cpu_threads_for(op: str) -> int:
+    from oracle import oracle as O
+    # the sort restatement is multi-threaded; the scan / reduce host
+    # references of the reference's tests are sequential
+    return O.cpu_threads() if (op in ("sort", "bits") or op.startswith("pairs")) else 1
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    from oracle import oracle
-    threads = oracle.cpu_threads()
+    cfg = OPS[args.op]
+    log2n = args.log2n or cfg["log2n"]
+    threads = cpu_threads_for(args.op)
     n_sample = 1 << 22
-    keys = oracle.generate(oracle.GEN_U32_UNIFORM, n_sample, seed=0)
+    fn = cpu_fn(args.op, n_sample, threads)
     for _ in range(args.warmup):
-        oracle.radix_sort(keys, threads=threads)
+        fn()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.radix_sort(keys, threads=threads)
+        fn()
     el = time.perf_counter() - t0
     v = n_sample * args.steps / el / 1e9
+    sample = (f"2^22 items of the {cfg['workload']} stream per step; "
+              + ("multi-threaded LSD restatement of the onesweep semantics" if threads > 1
+                 else "sequential host reference of the reference's tests"))
     line = {
-        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+        "impl": "reference", "metric": cfg["metric"], "value": v, "unit": cfg["unit"], "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u32",
-        "data": "synthetic (splitmix64 counter stream, seed 0)",
-        "config": {"workload": f"SortKeys u32 uniform, 2^{args.log2n} keys per GPU; each step sorts a "
-                               f"bounded 2^22-key sample of it on the host", "begin_bit": 0, "end_bit": 32},
-        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": "2^22 uniform u32 keys (first 2^22 of the seed-0 stream) per step; "
-                                   "multi-threaded LSD restatement of the onesweep semantics"},
-        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"], "data": DATA,
+        "config": {"workload": f"{cfg['workload']}, 2^{log2n} items per GPU; each step runs a bounded "
+                               f"2^22-item sample of it on the host"},
+        "cpu_baseline": {"value": v, "unit": cfg["unit"], "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": cfg["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -187,36 +320,34 @@ def run_ours(args):
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
     torch.cuda.set_device(local)
-    dist = None
+    cfg = OPS[args.op]
+    log2n = args.log2n or cfg["log2n"]
+    n = 1 << log2n
+
     if world > 1:
         import torch.distributed as dist
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    n = 1 << args.log2n
-    stream = torch.cuda.current_stream()
 
-    if world > 1:
         from lcpp_b200 import distributed as D
-        res = D.bench_distributed_sort(n, args.steps, args.warmup, dist)
-        if rank == 0:
-            print(json.dumps(res), flush=True)
-        dist.barrier()
-        dist.destroy_process_group()
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        try:
+            res = D.bench_distributed_sort(n, args.steps, args.warmup, dist, ClockSampler, measured_peak())
+            if rank == 0:
+                print(json.dumps(res), flush=True)
+            dist.barrier()
+        finally:
+            dist.destroy_process_group()
         return 0
 
-    rs = L.DeviceRadixSort()
-    keys = torch.empty(n, dtype=torch.uint32, device="cuda")
-    L.testgen_fill(keys, L.GEN_U32_UNIFORM, seed=0)
-    out = torch.empty_like(keys)
-    temp = L.alloc_temp(rs.GetSortKeysTempStorageBytes(L.U32, n))
-
+    w = Workload(args.op, n)
+    stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
-        rs.SortKeys(temp, keys, out, n)
+        w.step()
     torch.cuda.synchronize()
-    assert L.device_status(temp) == L.OK
+    assert L.device_status(w.temp) == L.OK
 
-    bus = torch.cuda.get_device_properties(local).pci_bus_id if hasattr(
-        torch.cuda.get_device_properties(local), "pci_bus_id") else None
+    props = torch.cuda.get_device_properties(local)
+    bus = getattr(props, "pci_bus_id", None)
     bus_id = f"{bus:02x}:00.0" if isinstance(bus, int) else None
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(bus_id) as clocks:
@@ -224,74 +355,83 @@ def run_ours(args):
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(args.steps):
-            rs.SortKeys(temp, keys, out, n)
+            w.step()
         e1.record(stream)
         torch.cuda.synchronize()
         recs = L.diag_timing_read()
         L.diag_timing_enable(False)
     ms = e0.elapsed_time(e1) / args.steps
-    assert L.device_status(temp) == L.OK
+    assert L.device_status(w.temp) == L.OK
     value = n / (ms * 1e-3) / 1e9
     clk = clocks.summary()
 
-    onesweep = [r[1] for r in recs if r[0] == L.KERNEL_SORT_ONESWEEP]
-    hist = [r[1] for r in recs if r[0] == L.KERNEL_SORT_HISTOGRAM]
-    avg_pass_ms = sum(onesweep) / len(onesweep)
+    kind = w.dominant_kind()
+    dom = [r[1] for r in recs if r[0] == kind]
+    avg_ms = sum(dom) / len(dom)
     peak, peak_kind = measured_peak()
-    achieved = BYTES_PER_KEY_ONESWEEP * n / (avg_pass_ms * 1e-3) / 1e9
-    tpk = profiled_traffic()
-    roofline = {"bound": "hbm", "kernel": "onesweep_kernel (one 8-bit pass)", "achieved": achieved,
-                "peak": peak, "peak_source": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                "algorithmic_bytes_per_launch": BYTES_PER_KEY_ONESWEEP * n,
-                "avg_launch_ms": avg_pass_ms,
-                "traffic": (tpk * n) if tpk is not None else None}
-    sort_ach = BYTES_PER_KEY_SORT * n / (ms * 1e-3) / 1e9
-    sort_roofline = {"bytes_per_key": BYTES_PER_KEY_SORT, "achieved": sort_ach, "peak": peak,
-                     "unit": "GB/s", "frac": sort_ach / peak,
-                     "histogram_ms": sum(hist) / len(hist), "onesweep_ms_per_pass": avg_pass_ms}
+    achieved = cfg["kbytes"] * n / (avg_ms * 1e-3) / 1e9
+    tpi = profiled_traffic(args.op)
+    roofline = {"bound": "hbm", "kernel": cfg["kernel"], "achieved": achieved, "peak": peak,
+                "peak_source": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                "algorithmic_bytes_per_launch": cfg["kbytes"] * n, "avg_launch_ms": avg_ms,
+                "traffic": (tpi * n) if tpi is not None else None}
+    op_ach = cfg["bytes"] * n / (ms * 1e-3) / 1e9
+    op_roofline = {"bytes_per_item": cfg["bytes"], "achieved": op_ach, "peak": peak, "unit": "GB/s",
+                   "frac": op_ach / peak}
+    if kind == L.KERNEL_SORT_ONESWEEP:
+        hist = [r[1] for r in recs if r[0] == L.KERNEL_SORT_HISTOGRAM]
+        op_roofline.update({"histogram_ms": sum(hist) / len(hist), "onesweep_ms_per_pass": avg_ms})
 
-    # e2e: the same public call, host buffers, copies inside the timed region.
-    host_in = torch.empty(n, dtype=torch.uint32, pin_memory=True)
-    host_in.copy_(keys)
-    host_out = torch.empty(n, dtype=torch.uint32, pin_memory=True)
-    d_in = torch.empty_like(keys)
+    # e2e: the same public call with host buffers, copies inside the timed region.
+    host_in = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t) for t in w.inputs]
+    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in w.outputs]
+    d_in = [torch.empty_like(t) for t in w.inputs]
     k_e2e = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        for d, h in zip(d_in, host_in):
+            d.copy_(h, non_blocking=True)
+        w.step(d_in)
+        for h, d in zip(host_out, w.outputs):
+            h.copy_(d, non_blocking=True)
+
     for _ in range(2):
-        d_in.copy_(host_in, non_blocking=True)
-        rs.SortKeys(temp, d_in, out, n)
-        host_out.copy_(out, non_blocking=True)
+        e2e_step()
     torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(k_e2e):
-        d_in.copy_(host_in, non_blocking=True)
-        rs.SortKeys(temp, d_in, out, n)
-        host_out.copy_(out, non_blocking=True)
+        e2e_step()
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / k_e2e
-    e2e = {"value": n / (e2e_ms * 1e-3) / 1e9, "unit": UNIT, "h2d_bytes_per_step": 4 * n,
-           "d2h_bytes_per_step": 4 * n, "steps": k_e2e, "ms_per_step": e2e_ms}
-    # sanity: the result that came back is sorted
-    ho = host_out.numpy()
-    assert bool((ho[1:] >= ho[:-1]).all())
+    e2e = {"value": n / (e2e_ms * 1e-3) / 1e9, "unit": cfg["unit"],
+           "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in w.inputs),
+           "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in w.outputs),
+           "steps": k_e2e, "ms_per_step": e2e_ms}
+    if args.op in ("sort", "bits"):  # sanity: what came back is ordered
+        ho = host_out[0].numpy()
+        if args.op == "bits":
+            ho = (ho >> 8) & 0xFFFF
+        assert bool((ho[1:] >= ho[:-1]).all())
 
     cpu = None
     if not args.no_cpu_baseline and rank == 0:
-        from oracle import oracle
-        threads = oracle.cpu_threads()
-        v, reps = cpu_sort_sample(1 << 24, threads, 10.0)
-        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"2^24 uniform u32 keys (first 2^24 of the seed-0 stream) x {reps} sorts; "
-                         "multi-threaded LSD restatement of the onesweep semantics"}
+        threads = cpu_threads_for(args.op)
+        ips, reps = cpu_sample(args.op, 1 << 24, threads, 10.0)
+        cpu = {"value": ips / 1e9, "unit": cfg["unit"], "cores": threads, "kind": "port",
+               "sample": f"2^24 items of the {cfg['workload']} stream x {reps} runs; "
+                         + ("multi-threaded LSD restatement of the onesweep semantics" if threads > 1
+                            else "sequential host reference of the reference's tests")}
 
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "metric": cfg["metric"], "value": value, "unit": cfg["unit"], "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "u32", "data": "synthetic (splitmix64 counter stream, seed 0)",
-        "config": {"workload": f"SortKeys u32 uniform full range, n=2^{args.log2n} per GPU, bits [0,32)",
-                   "keys_per_gpu": n, "parallelism": "single GPU",
-                   "l2": "inputs larger than L2 (1 GiB of keys per step vs 126 MB L2); no flush"},
-        "roofline": roofline, "sort_roofline": sort_roofline, "e2e": e2e,
+        "vs_baseline": None, "dtype": cfg["dtype"], "data": DATA,
+        "config": {"workload": f"{cfg['workload']}, n=2^{log2n} per GPU", "items_per_gpu": n,
+                   "parallelism": "single GPU",
+                   "l2": f"inputs larger than L2 ({n * w.inputs[0].element_size() / 2**20:.0f} MiB per step "
+                         "vs 126 MB L2); no flush"},
+        "roofline": roofline, "op_roofline": op_roofline, "e2e": e2e,
         "gpu_launches": len(recs), "clocks": clk, "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
