@@ -178,6 +178,24 @@ lcpp_status lcpp_scan_exclusive_sum(void* temp, size_t temp_bytes, const void* d
 lcpp_status lcpp_scan_inclusive_sum(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
                                     uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
 
+/* No counterpart in the reference.  InclusiveSum for callers that cannot
+ * allocate device memory when they scan (code running inside an allocator or
+ * a memory-pool callback, a plugin host that hands out fixed buffers only, a
+ * real-time loop that must not call cudaMalloc after start-up).  Same result
+ * as lcpp_scan_inclusive_sum, but the scratch lives in a fixed 1 MiB + 4 KiB
+ * device array inside the library, so the caller passes only input and
+ * output.  Limits: at most 1,077,673,984 items of a 4-byte type or
+ * 215,482,368 items of an 8-byte type; larger counts return
+ * LCPP_ERR_TEMP_TOO_SMALL before any device work.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress, with
+ * that device current) and caches it; make that first call before any stream
+ * capture.  All calls on one device share the array: calls that may overlap
+ * on the GPU (different streams, no ordering between them) race and give
+ * wrong results.  Every GPU that loads the library holds the array until the
+ * process exits.  Nothing in this call allocates memory. */
+lcpp_status lcpp_scan_inclusive_sum_noalloc(const void* d_in, void* d_out, uint64_t num_items,
+                                            lcpp_dtype dtype, lcpp_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * DeviceReduce  (src/lcpp/device/device_reduce.h)
  *

@@ -1,0 +1,77 @@
+// noalloc.cu -- an InclusiveSum entry point that needs no caller scratch.
+//
+// Some callers cannot allocate device memory when they want to scan: code
+// running inside a custom allocator or a memory-pool callback (allocating
+// would re-enter it), a plugin host that hands the plugin fixed buffers and
+// no allocation rights, or a real-time loop that must not call cudaMalloc
+// (it may synchronise the device) after start-up.  For them this file keeps
+// the scan's scratch in a statically sized device array instead of caller
+// temp storage.  Nothing here calls cudaMalloc, cudaFree or any allocating
+// library routine.
+//
+// The array is file-scope device memory of the library image: every GPU that
+// loads the library holds it until the process exits, and every call on a
+// device shares that device's copy.  Its host-side name is only a stand-in,
+// so host code passes the device address obtained with cudaGetSymbolAddress.
+#include <mutex>
+
+#include "common.cuh"
+#include "scan.cuh"
+
+namespace lcpp {
+namespace noalloc {
+
+// 1 MiB + 4 KiB: holds the scan's control block and tile status words for up
+// to 1,077,673,984 items of a 4-byte type (a little above 2^30) or
+// 215,482,368 items of an 8-byte type.
+constexpr size_t kScratchBytes = (1u << 20) + 4096;
+
+static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
+
+namespace {
+
+std::mutex g_mu;
+void* g_addr[64] = {};
+
+// Device address of g_scratch on the current device, looked up once per
+// device (with that device current) and cached.
+cudaError_t scratch_address(void** out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_scratch);
+        if (e != cudaSuccess) return e;
+        g_addr[dev] = p;
+    }
+    *out = g_addr[dev];
+    return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace noalloc
+}  // namespace lcpp
+
+extern "C" lcpp_status lcpp_scan_inclusive_sum_noalloc(const void* d_in, void* d_out, uint64_t num_items,
+                                                       lcpp_dtype dtype, lcpp_stream_t stream)
+{
+    using namespace lcpp;
+    if (!dtype_bytes(dtype)) return LCPP_ERR_UNSUPPORTED_DTYPE;
+    if (num_items == 0) return LCPP_OK;
+    // Reject sizes whose scratch would not fit the static array (checked on
+    // the host before any device work).
+    if (scan::temp_bytes(dtype, num_items) > noalloc::kScratchBytes) return LCPP_ERR_TEMP_TOO_SMALL;
+    void* scratch = nullptr;
+    if (noalloc::scratch_address(&scratch) != cudaSuccess) {
+        cudaGetLastError();
+        return LCPP_ERR_CUDA;
+    }
+    // The scan clears the control block and status words it uses at the
+    // start of every call, so the previous call's contents do not matter.
+    return scan::run(scratch, noalloc::kScratchBytes, d_in, d_out, num_items, LCPP_OP_SUM, nullptr, dtype, 1,
+                     reinterpret_cast<cudaStream_t>(stream));
+}

@@ -77,6 +77,7 @@ def lib() -> ctypes.CDLL:
         "lcpp_scan_inclusive_init": ([vp, sz, vp, vp, u64, i, vp, i, vp], i),
         "lcpp_scan_exclusive_sum": ([vp, sz, vp, vp, u64, i, vp], i),
         "lcpp_scan_inclusive_sum": ([vp, sz, vp, vp, u64, i, vp], i),
+        "lcpp_scan_inclusive_sum_noalloc": ([vp, vp, u64, i, vp], i),
         "lcpp_reduce_temp_bytes": ([i, u64, szp], i),
         "lcpp_reduce": ([vp, sz, vp, vp, u64, i, vp, i, vp], i),
         "lcpp_reduce_sum": ([vp, sz, vp, vp, u64, i, vp], i),

@@ -1,0 +1,68 @@
+"""GPU test of lcpp_scan_inclusive_sum_noalloc, the InclusiveSum entry point
+for callers that cannot allocate device memory (it keeps its scratch in a
+fixed array inside the library).  It must give exactly what the regular
+lcpp_scan_inclusive_sum gives, call after call, since every call reuses the
+same array.  Kept in its own file, named to be collected last."""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _regular(lcpp, x):
+    out = torch.empty_like(x)
+    temp = lcpp.alloc_temp(lcpp.DeviceScan.GetTempStorageBytes(lcpp.dtype_code(x), x.numel()))
+    lcpp.check(lcpp.lib().lcpp_scan_inclusive_sum(ctypes.c_void_p(temp.data_ptr()), temp.numel(),
+                                                  ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                                  x.numel(), lcpp.dtype_code(x),
+                                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+               "lcpp_scan_inclusive_sum")
+    return out
+
+
+def _noalloc(lcpp, x, n=None):
+    out = torch.empty_like(x)
+    status = lcpp.lib().lcpp_scan_inclusive_sum_noalloc(
+        ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(out.data_ptr()), x.numel() if n is None else n,
+        lcpp.dtype_code(x), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    return status, out
+
+
+@pytest.mark.parametrize("dtype,n", [(torch.int32, 1), (torch.int32, 1_000_003), (torch.int32, 1 << 26),
+                                     (torch.float32, 262_147), (torch.int64, 3_000_001),
+                                     (torch.float64, 65_537)])
+def test_noalloc_matches_regular_twice(lcpp, dtype, n):
+    assert torch.cuda.is_available()
+    g = torch.Generator(device="cuda").manual_seed(n)
+    if dtype.is_floating_point:
+        x = torch.rand(n, dtype=dtype, device="cuda", generator=g)
+    else:
+        x = torch.randint(-1000, 1001, (n,), dtype=dtype, device="cuda", generator=g)
+    ref = _regular(lcpp, x)
+    for _ in range(2):  # the second call starts from the first call's scratch contents
+        status, out = _noalloc(lcpp, x)
+        assert status == lcpp.OK
+        torch.cuda.synchronize()
+        if dtype.is_floating_point:
+            # the two calls may associate floating-point partial sums differently
+            tol = 1e-5 if dtype == torch.float32 else 1e-12
+            rel = ((out.double() - ref.double()).abs() / ref.double().abs().clamp_min(1.0)).max().item()
+            assert rel < tol
+        else:
+            assert torch.equal(out, ref)
+
+
+def test_noalloc_rejects_too_many_items(lcpp):
+    x = torch.zeros(4, dtype=torch.int32, device="cuda")
+    status, _ = _noalloc(lcpp, x, n=1_077_673_984 + 1)
+    assert status == lcpp.ERR_TEMP_TOO_SMALL
+    status, _ = _noalloc(lcpp, torch.zeros(4, dtype=torch.int64, device="cuda"), n=215_482_368 + 1)
+    assert status == lcpp.ERR_TEMP_TOO_SMALL
+    status, _ = _noalloc(lcpp, x, n=0)
+    assert status == lcpp.OK
