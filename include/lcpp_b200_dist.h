@@ -26,6 +26,20 @@ extern "C" {
 lcpp_status lcpp_dist_search_sorted(const void* sorted, uint64_t n, const void* queries, uint64_t num_queries,
                                     int upper, uint64_t* out, lcpp_dtype key_dtype, lcpp_stream_t stream);
 
+/* Temp bytes of lcpp_dist_merge_sorted for `total` = na + nb keys (the split
+ * points of the output blocks). */
+lcpp_status lcpp_dist_merge_temp_bytes(uint64_t total, size_t* temp_bytes);
+
+/* Merge two runs sorted ascending by DeviceRadixSort (keys of key_dtype,
+ * compared by the same order-preserving image): out[0, na + nb) receives the
+ * merged keys; among equal images the keys of `a` come first.  `out` must not
+ * overlap `a` or `b`; temp (256-byte aligned) holds the output blocks' split
+ * points.  Merge path (Green, McColl & Bader, 2012): one small kernel finds
+ * each output block's split point by binary search, a second merges each
+ * block in shared memory. */
+lcpp_status lcpp_dist_merge_sorted(void* temp, size_t temp_bytes, const void* a, uint64_t na, const void* b,
+                                   uint64_t nb, void* out, lcpp_dtype key_dtype, lcpp_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

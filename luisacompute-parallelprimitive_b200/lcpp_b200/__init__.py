@@ -86,6 +86,8 @@ def lib() -> ctypes.CDLL:
         "lcpp_device_status": ([vp, vp], i),
         "lcpp_testgen_fill": ([vp, u64, u64, u64, i, vp], i),
         "lcpp_dist_search_sorted": ([vp, u64, vp, u64, i, vp, i, vp], i),
+        "lcpp_dist_merge_temp_bytes": ([u64, szp], i),
+        "lcpp_dist_merge_sorted": ([vp, sz, vp, u64, vp, u64, vp, i, vp], i),
         "lcpp_diag_timing_enable": ([i], i),
         "lcpp_diag_timing_read": ([ctypes.POINTER(KernelTime), i, ip], i),
     }

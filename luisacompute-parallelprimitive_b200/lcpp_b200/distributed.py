@@ -16,7 +16,8 @@ Sort (keys only), per rank:
      boundary in rank order, so every rank receives exactly its share even
      when one key value fills several ranks (heavy hitters);
   4. one all-to-all exchange of the sorted runs (NCCL send / recv);
-  5. a local sort of the received runs.
+  5. the G received runs (each sorted) are merged pairwise, ceil(log2 G)
+     merge-path levels (lcpp_dist_merge_sorted), instead of a second sort.
 Rank r ends with global sorted positions [P_r, P_{r+1}).
 
 Scan and reduce: local pass, one all-gather of per-rank totals, then the
@@ -61,6 +62,7 @@ class GpuOps:
         self.device = torch.device("cuda", torch.cuda.current_device())
         self._temps = {}
         self.rs = DeviceRadixSort()
+        self.launches = 0  # search and merge kernels launched (the sorts are counted by diag timing)
 
     def _temp(self, key, nbytes):
         t = self._temps.get(key)
@@ -84,11 +86,30 @@ class GpuOps:
         q = torch.from_numpy(queries_np.astype(np.uint32 if kbits == 32 else np.uint64)).to(self.device)
         out = torch.empty(q.numel(), dtype=torch.int64, device=self.device)
         if q.numel():
+            self.launches += 1
             check(lib().lcpp_dist_search_sorted(
                 ctypes.c_void_p(sorted_keys.data_ptr()), sorted_keys.numel(), ctypes.c_void_p(q.data_ptr()),
                 q.numel(), int(upper), ctypes.c_void_p(out.data_ptr()), dtype_code(sorted_keys),
                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "lcpp_dist_search_sorted")
         return out
+
+    def merge(self, a, b, out):
+        """out[:a.numel() + b.numel()] = stable merge of sorted runs a, b."""
+        torch = self.torch
+        total = a.numel() + b.numel()
+        if total == 0:
+            return
+        nbytes = ctypes.c_size_t(0)
+        check(lib().lcpp_dist_merge_temp_bytes(total, ctypes.byref(nbytes)), "lcpp_dist_merge_temp_bytes")
+        temp = self._temp("merge", nbytes.value)
+        self.launches += 2
+        check(lib().lcpp_dist_merge_sorted(
+            ctypes.c_void_p(temp.data_ptr()), temp.numel(), ctypes.c_void_p(a.data_ptr()), a.numel(),
+            ctypes.c_void_p(b.data_ptr()), b.numel(), ctypes.c_void_p(out.data_ptr()), dtype_code(a),
+            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "lcpp_dist_merge_sorted")
+
+    def empty_like(self, t):
+        return self.torch.empty_like(t)
 
 
 def _all_gather_int64(dist, values, device):
@@ -186,7 +207,35 @@ def distributed_sort_keys(keys_local, dist, ops=None):
     send, recv, _ = exact_splits(local, dist, ops)
     out = torch.empty(sum(recv), dtype=local.dtype, device=local.device)
     dist.all_to_all_single(_bitcast_for_comm(out), _bitcast_for_comm(local), recv, send)
-    return ops.local_sort(out)
+    return merge_runs(out, recv, ops)
+
+
+def merge_runs(buf, counts, ops):
+    """Merge the consecutive sorted runs of `buf` (lengths `counts`, in rank
+    order) into one sorted run: pairwise merge-path levels ping-ponging
+    between `buf` and one scratch buffer.  Merging adjacent runs with ties
+    taken from the left run keeps equal keys in rank order."""
+    bounds = [0]
+    for c in counts:
+        bounds.append(bounds[-1] + int(c))
+    runs = [(bounds[i], bounds[i + 1]) for i in range(len(counts))]
+    src, dst = buf, None
+    while len(runs) > 1:
+        if dst is None:
+            dst = ops.empty_like(buf)
+        nxt = []
+        for i in range(0, len(runs), 2):
+            if i + 1 == len(runs):
+                s0, s1 = runs[i]
+                dst[s0:s1].copy_(src[s0:s1])
+                nxt.append(runs[i])
+                continue
+            (a0, a1), (b0, b1) = runs[i], runs[i + 1]
+            ops.merge(src[a0:a1], src[b0:b1], dst[a0:b1])
+            nxt.append((a0, b1))
+        runs = nxt
+        src, dst = dst, src
+    return src
 
 
 # ---------------------------------------------------------------------------
@@ -309,6 +358,7 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
         diag_timing_enable(True)
         dist.barrier()
         torch.cuda.synchronize()
+        ops.launches = 0
         e0.record(stream)
         for _ in range(steps):
             distributed_sort_keys(keys, dist, ops)
@@ -316,6 +366,7 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
         torch.cuda.synchronize()
         recs = diag_timing_read()
         diag_timing_enable(False)
+        other_launches = ops.launches
     ms = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = ms.item()
@@ -348,9 +399,11 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
     avg_pass = sum(onesweep) / max(1, len(onesweep))
     achieved = 8 * n_local / (avg_pass * 1e-3) / 1e9
     peak_gbs, peak_src = peak
-    # per GPU: two local sorts (36 B/key each) + the exchange (read + write 8 B/key) in HBM;
+    # per GPU in HBM: the local sort (4 passes x 8 B/key + 4 B/key histogram read), the
+    # exchange (read + write 8 B/key) and ceil(log2 G) merge levels (8 B/key each);
     # (G-1)/G of the keys cross NVLink in each direction.
-    hbm_bytes = (36 + 36 + 8) * n_local
+    levels = (G - 1).bit_length()
+    hbm_bytes = (36 + 8 + 8 * levels) * n_local
     nvlink_bytes = (G - 1) / G * 4 * n_local
     return {
         "metric": "Gkeys/s uint32 SortKeys @2^28", "value": value, "unit": "Gkeys/s", "n_gpus": G,
@@ -361,7 +414,7 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
                                f"(global 2^{(G * n_local).bit_length() - 1})",
                    "items_per_gpu": n_local, "parallelism": f"sort-partitioned over {G} GPUs (NCCL all-to-all)",
                    "algorithm": "local onesweep -> exact 16-bit-refined splitters (2 all-reduce rounds) -> "
-                                "all-to-all -> local onesweep",
+                                "all-to-all -> pairwise merge-path merge of the G received runs",
                    "l2": "inputs larger than L2; no flush", "globally_sorted_check": ordered},
         "roofline": {"bound": "hbm", "kernel": "onesweep_kernel (one 8-bit pass)", "achieved": achieved,
                      "peak": peak_gbs, "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak_gbs,
@@ -372,5 +425,5 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
         "e2e": {"value": G * n_local / (e2e_ms * 1e-3) / 1e9, "unit": "Gkeys/s",
                 "h2d_bytes_per_step": 4 * n_local * G, "d2h_bytes_per_step": 4 * n_local * G, "steps": k_e2e,
                 "ms_per_step": e2e_ms},
-        "gpu_launches": len(recs), "clocks": clocks.summary(), "cpu_baseline": None,
+        "gpu_launches": len(recs) + other_launches, "clocks": clocks.summary(), "cpu_baseline": None,
     }

@@ -5,6 +5,7 @@ from __future__ import annotations
 
 import os
 import socket
+import zlib
 
 import numpy as np
 import pytest
@@ -97,3 +98,74 @@ def test_two_ranks_nccl():
     np.testing.assert_array_equal(np.concatenate([got[r][2] for r in range(world)]).astype(np.int64),
                                   np.cumsum(allx))
     assert got[0][4] == got[1][4] == int(allx.sum())
+
+
+def _stable_merge_np(a, b):
+    from lcpp_b200.distributed import key_images_np
+    ab = np.concatenate([a, b])
+    return ab[np.argsort(key_images_np(ab), kind="stable")]
+
+
+def _sorted_run(rng, n, np_dt, case):
+    from lcpp_b200.distributed import key_images_np
+    if np_dt == np.float32 or np_dt == np.float64:
+        x = rng.standard_normal(n).astype(np_dt)
+        x[::9] = 0.0
+        x[4::9] = -0.0
+    elif case == "ties":
+        x = rng.integers(0, 4, n).astype(np_dt)
+    else:
+        info = np.iinfo(np_dt)
+        x = rng.integers(info.min, info.max, n, dtype=np_dt, endpoint=True)
+    return x[np.argsort(key_images_np(x), kind="stable")]
+
+
+@pytest.mark.parametrize("np_dt", [np.uint32, np.int32, np.float32, np.uint64, np.int64, np.float64])
+@pytest.mark.parametrize("sizes", [(0, 0), (0, 5), (7, 0), (1, 1), (3840, 3840), (3839, 3841),
+                                   (100_003, 17), (1 << 20, (1 << 20) + 3), (1 << 22, 999_999)])
+@pytest.mark.parametrize("case", ["uniform", "ties"])
+def test_merge_sorted_parity(np_dt, sizes, case):
+    """lcpp_dist_merge_sorted against a stable host merge, bit for bit (ties:
+    keys of the first run first; +-0.0 compare equal and keep their bits)."""
+    from lcpp_b200.distributed import GpuOps
+    rng = np.random.default_rng(zlib.crc32(repr((np.dtype(np_dt).str, sizes, case)).encode()))
+    a = _sorted_run(rng, sizes[0], np_dt, case)
+    b = _sorted_run(rng, sizes[1], np_dt, case)
+    ops = GpuOps()
+    ta, tb = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    out = torch.full((a.size + b.size,), 0x5A, dtype=ta.dtype, device="cuda") if a.size + b.size else \
+        torch.empty(0, dtype=ta.dtype, device="cuda")
+    ops.merge(ta, tb, out)
+    ub = np.uint32 if np.dtype(np_dt).itemsize == 4 else np.uint64
+    np.testing.assert_array_equal(out.cpu().numpy().view(ub), _stable_merge_np(a, b).view(ub))
+
+
+def test_merge_sorted_rejects_misuse(lcpp):
+    import ctypes
+    L = lcpp.lib()
+    need = ctypes.c_size_t(0)
+    assert L.lcpp_dist_merge_temp_bytes(10_000, ctypes.byref(need)) == lcpp.OK and need.value > 0
+    a = torch.zeros(5000, dtype=torch.int32, device="cuda")
+    b = torch.zeros(5000, dtype=torch.int32, device="cuda")
+    out = torch.empty(10_000, dtype=torch.int32, device="cuda")
+    temp = lcpp.alloc_temp(need.value)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    assert L.lcpp_dist_merge_sorted(p(temp), need.value - 1, p(a), 5000, p(b), 5000, p(out), lcpp.I32,
+                                    None) == lcpp.ERR_TEMP_TOO_SMALL
+    assert L.lcpp_dist_merge_sorted(p(temp), need.value, p(a), 5000, p(b), 5000, p(out), 99,
+                                    None) == lcpp.ERR_UNSUPPORTED_DTYPE
+    assert L.lcpp_dist_merge_sorted(p(temp), need.value, None, 5000, p(b), 5000, p(out), lcpp.I32,
+                                    None) == lcpp.ERR_INVALID_ARG
+
+
+@pytest.mark.parametrize("counts", [[5], [3, 0, 4], [1 << 20, 77, (1 << 19) + 1, 0, 4096, 12345, 1 << 18],
+                                    [1000] * 8])
+def test_merge_runs_tree(counts):
+    """The pairwise merge tree over G received runs equals the stable sort of
+    their concatenation (equal keys in run order)."""
+    from lcpp_b200.distributed import GpuOps, key_images_np, merge_runs
+    rng = np.random.default_rng(len(counts))
+    runs = [_sorted_run(rng, c, np.uint32, "ties" if i % 2 else "uniform") for i, c in enumerate(counts)]
+    allk = np.concatenate(runs)
+    res = merge_runs(torch.from_numpy(allk).cuda(), counts, GpuOps())
+    np.testing.assert_array_equal(res.cpu().numpy(), allk[np.argsort(key_images_np(allk), kind="stable")])
