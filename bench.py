@@ -68,7 +68,7 @@ OPS = {
                  kernel="onesweep_kernel (one 8-bit pass)"),
     "scan": dict(metric="Gitems/s int32 InclusiveSum @2^30", unit="Gitems/s", log2n=30, dtype="i32",
                  workload="InclusiveSum i32 uniform in [-1000,1000], seed 1", bytes=8, kbytes=8,
-                 kernel="scan_kernel"),
+                 kernel="scan_bulk_kernel"),
     "reduce": dict(metric="Gitems/s float32 Reduce Sum @2^30", unit="Gitems/s", log2n=30, dtype="f32",
                    workload="DeviceReduce::Sum f32 U[0,1), seed 1", bytes=4, kbytes=4, kernel="reduce_kernel"),
     "reduce_max": dict(metric="Gitems/s int64 Reduce Max @2^30", unit="Gitems/s", log2n=30, dtype="i64",

@@ -182,10 +182,10 @@ lcpp_status lcpp_scan_inclusive_sum(void* temp, size_t temp_bytes, const void* d
  * allocate device memory when they scan (code running inside an allocator or
  * a memory-pool callback, a plugin host that hands out fixed buffers only, a
  * real-time loop that must not call cudaMalloc after start-up).  Same result
- * as lcpp_scan_inclusive_sum, but the scratch lives in a fixed 1 MiB + 4 KiB
+ * as lcpp_scan_inclusive_sum, but the scratch lives in a fixed 2 MiB + 4 KiB
  * device array inside the library, so the caller passes only input and
- * output.  Limits: at most 1,077,673,984 items of a 4-byte type or
- * 215,482,368 items of an 8-byte type; larger counts return
+ * output.  Limits: at most 1,075,707,904 items of a 4-byte type or
+ * 215,089,152 items of an 8-byte type; larger counts return
  * LCPP_ERR_TEMP_TOO_SMALL before any device work.  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress, with
  * that device current) and caches it; make that first call before any stream

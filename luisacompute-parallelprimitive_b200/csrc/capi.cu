@@ -2,6 +2,7 @@
 #include <cstring>
 #include <limits>
 #include <mutex>
+#include <map>
 #include <set>
 #include <utility>
 
@@ -45,6 +46,26 @@ void set_max_dynamic_smem(const void* kernel, size_t bytes)
     // shared memory, so a dynamic size just under it can still need opt-in.
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
     done.insert(key);
+}
+
+int resident_blocks(const void* kernel, int block, size_t dynamic_smem)
+{
+    static std::mutex mu;
+    static std::map<std::pair<std::pair<const void*, int>, std::pair<int, size_t>>, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    const auto key = std::make_pair(std::make_pair(kernel, dev), std::make_pair(block, dynamic_smem));
+    const auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    int blocks = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, block, dynamic_smem) != cudaSuccess) {
+        cudaGetLastError();
+        blocks = 1;
+    }
+    blocks = blocks < 1 ? 1 : blocks;
+    cache[key] = blocks;
+    return blocks;
 }
 
 }  // namespace lcpp

@@ -140,6 +140,10 @@ int device_sm_count();
 // per kernel, device and size).
 void set_max_dynamic_smem(const void* kernel, size_t bytes);
 
+// Resident blocks per SM of a kernel at this block size and dynamic shared
+// memory on the current device (cached; at least 1).
+int resident_blocks(const void* kernel, int block, size_t dynamic_smem);
+
 namespace diag {
 // Brackets one kernel launch with CUDA events when timing is enabled
 // (lcpp_diag_timing_enable); otherwise a no-op.

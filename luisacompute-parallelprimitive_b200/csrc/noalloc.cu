@@ -21,10 +21,10 @@
 namespace lcpp {
 namespace noalloc {
 
-// 1 MiB + 4 KiB: holds the scan's control block and tile status words for up
-// to 1,077,673,984 items of a 4-byte type (a little above 2^30) or
-// 215,482,368 items of an 8-byte type.
-constexpr size_t kScratchBytes = (1u << 20) + 4096;
+// 2 MiB + 4 KiB: holds the scan's control block and tile status words for up
+// to 1,075,707,904 items of a 4-byte type (a little above 2^30) or
+// 215,089,152 items of an 8-byte type.
+constexpr size_t kScratchBytes = (2u << 20) + 4096;
 
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 

@@ -256,18 +256,45 @@ struct OnesweepArgs {
     uint32_t* error;
 };
 
-template <typename U, typename V, bool PAIRS, int BLOCK, int ITEMS, int PEERS, typename OffT>
-struct OnesweepSmem {
+// Tile policy of one onesweep configuration.
+//   BLOCK x ITEMS keys per tile (warp-striped, ITEMS slots per lane);
+//   PEERS: how a lane finds the lanes holding its digit in one slot --
+//     0: 8 ballots; 1: a shared-memory mask word per digit; 2: a mask word
+//     per low-5-bit digit class (one per bank: conflict-free) + 3 ballots;
+//   WINDOW: predecessor tiles read per look-back round trip;
+//   GROUP: slots ranked together (their mask ORs, loads and ballots are
+//     independent, so one __syncwarp covers the group and the chains overlap);
+//   MIN_BLOCKS: resident blocks per SM requested from the register allocator
+//     (0: left to the compiler);
+//   PACK: tile ranks kept as 16-bit pairs (fewer live registers).
+template <int BLOCK, int ITEMS, int PEERS, int WINDOW, int GROUP = 1, int MIN_BLOCKS = 0, bool PACK = false>
+struct Policy {
+    static constexpr int kBlock = BLOCK;
+    static constexpr int kItems = ITEMS;
+    static constexpr int kPeers = PEERS;
+    static constexpr int kWindow = WINDOW;
+    static constexpr int kGroup = GROUP;
+    static constexpr int kMinBlocks = MIN_BLOCKS;
+    static constexpr bool kPack = PACK;
     static constexpr int kTile = BLOCK * ITEMS;
     static constexpr int kWarps = BLOCK / kWarp;
+    // mask words per warp and mask set; mask sets alternate by group parity
+    static constexpr int kMaskWords = PEERS == 1 ? kDigits : (PEERS == 2 ? 32 : 0);
+    static constexpr int kMaskSets = 2 * GROUP;
+};
+
+template <typename U, typename V, bool PAIRS, typename P, typename OffT>
+struct OnesweepSmem {
+    static constexpr int kTile = P::kTile;
+    static constexpr int kWarps = P::kWarps;
     union {
         U keys[kTile];                        // transformed keys in tile-rank order
         uint32_t counters[kWarps * kDigits];  // per-warp digit counters, then rank bases
     } u;
     V vals[PAIRS ? kTile : 1];
-    // per slot parity: lanes holding each digit (PEERS 1) or each low-5-bit
+    // per mask set: lanes holding each digit (PEERS 1) or each low-5-bit
     // digit class (PEERS 2)
-    uint32_t peer_masks[2][PEERS == 1 ? kWarps * kDigits : (PEERS == 2 ? kWarps * 32 : 1)];
+    uint32_t peer_masks[P::kMaskWords ? P::kMaskSets * kWarps * P::kMaskWords : 1];
     OffT gofs[kDigits];  // output index = gofs[digit] + tile position
     uint32_t totals[kDigits];   // keys of each digit in the tile
     uint32_t dstarts[kDigits];  // first tile rank of each digit
@@ -412,15 +439,17 @@ __device__ __forceinline__ void shared_red_add(uint32_t smem_addr, uint32_t inc)
 
 // Everything after the tile id is known.  FULL: the tile has kTile keys (all
 // but possibly the last tile), compiled without any per-key bounds logic.
-template <bool FULL, bool BYTE, int PEERS, typename U, typename V, bool PAIRS, int BLOCK, int ITEMS,
-          int KIND, int LB_WINDOW, typename ST, typename OffT>
+template <bool FULL, bool BYTE, typename P, typename U, typename V, bool PAIRS, int KIND, typename ST, typename OffT>
 __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>& a,
-                                             OnesweepSmem<U, V, PAIRS, BLOCK, ITEMS, PEERS, OffT>& s,
-                                             uint32_t tile, int valid)
+                                             OnesweepSmem<U, V, PAIRS, P, OffT>& s, uint32_t tile, int valid)
 {
     using SB = StatusBits<ST>;
-    constexpr int kTile = BLOCK * ITEMS;
-    constexpr int kWarps = BLOCK / kWarp;
+    constexpr int BLOCK = P::kBlock;
+    constexpr int ITEMS = P::kItems;
+    constexpr int PEERS = P::kPeers;
+    constexpr int G = P::kGroup;
+    constexpr int kTile = P::kTile;
+    constexpr int kWarps = P::kWarps;
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
@@ -434,7 +463,24 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
     // the tile, slot i of lane l is position w*ITEMS*32 + i*32 + l.
     U keys[ITEMS];
     V vals[PAIRS ? ITEMS : 1];
-    uint32_t rank[ITEMS];
+    // tile rank of each slot; 16-bit pairs when P::kPack (ranks < 65536)
+    uint32_t rank[P::kPack ? (ITEMS + 1) / 2 : ITEMS];
+    auto set_rank = [&](int i, uint32_t r) {
+        if constexpr (P::kPack) {
+            if (i & 1)
+                rank[i >> 1] |= r << 16;
+            else
+                rank[i >> 1] = r;
+        } else {
+            rank[i] = r;
+        }
+    };
+    auto get_rank = [&](int i) -> uint32_t {
+        if constexpr (P::kPack)
+            return (i & 1) ? (rank[i >> 1] >> 16) : (rank[i >> 1] & 0xffffu);
+        else
+            return rank[i];
+    };
     const uint32_t counters_base =
         static_cast<uint32_t>(__cvta_generic_to_shared(s.u.counters + warp * kDigits));
     {
@@ -504,63 +550,86 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
     // which keeps consecutive slots consistent.
     {
         const uint32_t lt = lanemask_lt();
-        constexpr int kMaskWords = PEERS == 1 ? kDigits : 32;  // mask words per warp and parity
+        constexpr int kMaskWords = P::kMaskWords;
+        constexpr uint32_t kSetBytes = uint32_t(kWarps * kMaskWords) * 4u;
         const uint32_t masks_base =
-            static_cast<uint32_t>(__cvta_generic_to_shared(s.peer_masks[0] + warp * kMaskWords));
+            static_cast<uint32_t>(__cvta_generic_to_shared(s.peer_masks + warp * kMaskWords));
 #pragma unroll
-        for (int i = 0; i < ITEMS; ++i) {
-            const uint32_t d = in_tile(i) ? digit(keys[i]) : dmask;
-            uint32_t peers;
-            uint32_t maddr = 0;
-            if constexpr (PEERS == 0) {
-                peers = digit_peers(d);
-            } else {
-                // Each lane ORs its bit into the slot's mask word of its digit
-                // (PEERS 1) or of its digit's low 5 bits (PEERS 2: 32 words,
-                // one per bank, so these accesses never conflict, and one
-                // ballot per remaining bit narrows the class to the digit).
-                // Masks alternate between two arrays by slot parity; every
-                // lane clears its word once all lanes have read it (the
-                // shuffle below depends on every lane's read), so a word is
-                // clean again two slots later.
-                const uint32_t w = PEERS == 1 ? d : (d & 31u);
-                maddr = masks_base + ((i & 1) * kWarps * kMaskWords + w) * 4u;
-                shared_red_or(maddr, 1u << lane);
-                __syncwarp();
-                peers = shared_load(maddr);
-                if constexpr (PEERS == 2) {
+        for (int i0 = 0; i0 < ITEMS; i0 += G) {
+            uint32_t d[G], peers[G], maddr[G], base[G];
+            // Each lane ORs its bit into the mask word of its digit (PEERS 1)
+            // or of its digit's low 5 bits (PEERS 2: 32 words, one per bank,
+            // so these accesses never conflict, and one ballot per remaining
+            // bit narrows the class to the digit).  Slot g of a group uses
+            // mask set g of the group's parity; every lane clears its word
+            // once all lanes have read it (the shuffle below depends on every
+            // lane's read), and the next group's __syncwarp orders the clears
+            // before the group after it reuses the set.
 #pragma unroll
-                    for (int b = 5; b < kRadixBits; ++b) {
-                        const bool bit = (d >> b) & 1u;
-                        const uint32_t vote = __ballot_sync(0xffffffffu, bit);
-                        peers &= bit ? vote : ~vote;
+            for (int g = 0; g < G; ++g) {
+                if (i0 + g < ITEMS) {
+                    const int i = i0 + g;
+                    d[g] = in_tile(i) ? digit(keys[i]) : dmask;
+                    if constexpr (PEERS != 0) {
+                        const uint32_t w = PEERS == 1 ? d[g] : (d[g] & 31u);
+                        maddr[g] = masks_base + uint32_t(((i0 / G) & 1) * G + g) * kSetBytes + w * 4u;
+                        shared_red_or(maddr[g], 1u << lane);
                     }
                 }
             }
-            const int leader = 31 - __clz(peers);
-            uint32_t base = shared_add_if(lane == leader, counters_base + d * 4u, uint32_t(__popc(peers)));
-            base = __shfl_sync(0xffffffffu, base, leader);
-            if constexpr (PEERS == 1) shared_store_if(lane == leader, maddr, 0u);
-            if constexpr (PEERS == 2) shared_store_if(true, maddr, 0u);
-            rank[i] = base + __popc(peers & lt);
+            if constexpr (PEERS != 0) __syncwarp();
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                if (i0 + g < ITEMS) {
+                    if constexpr (PEERS == 0) {
+                        peers[g] = digit_peers(d[g]);
+                    } else {
+                        peers[g] = shared_load(maddr[g]);
+                        if constexpr (PEERS == 2) {
+#pragma unroll
+                            for (int b = 5; b < kRadixBits; ++b) {
+                                const bool bit = (d[g] >> b) & 1u;
+                                const uint32_t vote = __ballot_sync(0xffffffffu, bit);
+                                peers[g] &= bit ? vote : ~vote;
+                            }
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                if (i0 + g < ITEMS) {
+                    const int leader = 31 - __clz(peers[g]);
+                    base[g] = shared_add_if(lane == leader, counters_base + d[g] * 4u, uint32_t(__popc(peers[g])));
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                if (i0 + g < ITEMS) {
+                    base[g] = __shfl_sync(0xffffffffu, base[g], 31 - __clz(peers[g]));
+                    if constexpr (PEERS == 1) shared_store_if(lane == 31 - __clz(peers[g]), maddr[g], 0u);
+                    if constexpr (PEERS == 2) shared_store_if(true, maddr[g], 0u);
+                    set_rank(i0 + g, base[g] + __popc(peers[g] & lt));
+                }
+            }
         }
     }
     __syncthreads();  // rank counters are dead; the key tile reuses their storage
 
-    // Decoupled look-back, one digit per thread, LB_WINDOW predecessor tiles
+    // Decoupled look-back, one digit per thread, P::kWindow predecessor tiles
     // per round trip.
     if (tid < kDigits) {
         OffT prefix = 0;
-        if (tile > 0) prefix = lookback_digit<ST, OffT, LB_WINDOW>(a.status, tile, tid, a.error);
+        if (tile > 0) prefix = lookback_digit<ST, OffT, P::kWindow>(a.status, tile, tid, a.error);
         finish_digit(tid, prefix);
     }
 
     {
 #pragma unroll
-        for (int i = 0; i < ITEMS; ++i) s.u.keys[rank[i]] = keys[i];
+        for (int i = 0; i < ITEMS; ++i) s.u.keys[get_rank(i)] = keys[i];
         if constexpr (PAIRS) {
 #pragma unroll
-            for (int i = 0; i < ITEMS; ++i) s.vals[rank[i]] = vals[i];
+            for (int i = 0; i < ITEMS; ++i) s.vals[get_rank(i)] = vals[i];
         }
     }
     __syncthreads();
@@ -592,12 +661,12 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
     }
 }
 
-template <typename U, typename V, bool PAIRS, int BLOCK, int ITEMS, int KIND, bool BYTE, int PEERS, int LB_WINDOW,
-          typename ST, typename OffT>
-__global__ void __launch_bounds__(BLOCK)
+template <typename U, typename V, bool PAIRS, typename P, int KIND, bool BYTE, typename ST, typename OffT>
+__global__ void __launch_bounds__(P::kBlock, P::kMinBlocks)
 onesweep_kernel(OnesweepArgs<U, V, ST, OffT> a)
 {
-    using Smem = OnesweepSmem<U, V, PAIRS, BLOCK, ITEMS, PEERS, OffT>;
+    using Smem = OnesweepSmem<U, V, PAIRS, P, OffT>;
+    constexpr int BLOCK = P::kBlock;
     constexpr int kTile = Smem::kTile;
     constexpr int kWarps = Smem::kWarps;
     static_assert(BLOCK >= kDigits, "one thread per digit");
@@ -612,18 +681,16 @@ onesweep_kernel(OnesweepArgs<U, V, ST, OffT> a)
         s.bad = 0;
     }
     for (int i = tid; i < kWarps * kDigits; i += BLOCK) s.u.counters[i] = 0;
-    if constexpr (PEERS != 0) {
-        constexpr int kMaskWords = 2 * kWarps * (PEERS == 1 ? kDigits : 32);
-        for (int i = tid; i < kMaskWords; i += BLOCK) s.peer_masks[0][i] = 0;
+    if constexpr (P::kMaskWords != 0) {
+        for (int i = tid; i < P::kMaskSets * kWarps * P::kMaskWords; i += BLOCK) s.peer_masks[i] = 0;
     }
     __syncthreads();
     const uint32_t tile = s.tile_id;
     const uint64_t tile_base = uint64_t(tile) * kTile;
     if (tile_base + kTile <= a.n)
-        process_tile<true, BYTE, PEERS, U, V, PAIRS, BLOCK, ITEMS, KIND, LB_WINDOW, ST, OffT>(a, s, tile, kTile);
+        process_tile<true, BYTE, P, U, V, PAIRS, KIND, ST, OffT>(a, s, tile, kTile);
     else
-        process_tile<false, BYTE, PEERS, U, V, PAIRS, BLOCK, ITEMS, KIND, LB_WINDOW, ST, OffT>(
-            a, s, tile, int(a.n - tile_base));
+        process_tile<false, BYTE, P, U, V, PAIRS, KIND, ST, OffT>(a, s, tile, int(a.n - tile_base));
 }
 
 // ---------------------------------------------------------------------------
@@ -728,27 +795,25 @@ lcpp_status launch_histogram(const Layout& L, unsigned char* temp, const U* keys
     return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;
 }
 
-template <typename U, typename V, bool PAIRS, int BLOCK, int ITEMS, int KIND, int PEERS, int LB_WINDOW,
-          typename ST, typename OffT, bool BYTE>
+template <typename U, typename V, bool PAIRS, typename P, int KIND, typename ST, typename OffT, bool BYTE>
 void launch_pass(const OnesweepArgs<U, V, ST, OffT>& a, uint64_t tiles, cudaStream_t stream)
 {
-    using Smem = OnesweepSmem<U, V, PAIRS, BLOCK, ITEMS, PEERS, OffT>;
-    auto kernel = onesweep_kernel<U, V, PAIRS, BLOCK, ITEMS, KIND, BYTE, PEERS, LB_WINDOW, ST, OffT>;
+    using Smem = OnesweepSmem<U, V, PAIRS, P, OffT>;
+    auto kernel = onesweep_kernel<U, V, PAIRS, P, KIND, BYTE, ST, OffT>;
     set_smem_once(kernel, sizeof(Smem));
-    kernel<<<unsigned(tiles), BLOCK, sizeof(Smem), stream>>>(a);
+    kernel<<<unsigned(tiles), P::kBlock, sizeof(Smem), stream>>>(a);
 }
 
-template <typename U, typename V, bool PAIRS, int BLOCK, int ITEMS, int KIND, int PEERS, int LB_WINDOW,
-          typename ST, typename OffT>
+template <typename U, typename V, bool PAIRS, typename P, int KIND, typename ST, typename OffT>
 lcpp_status launch_passes(const Layout& L, unsigned char* temp, const SortCall& c, uint64_t n,
                           const KeyCodec<U>& codec, int begin_bit, int end_bit, int passes,
                           cudaStream_t stream)
 {
-    static_assert(BLOCK * ITEMS >= kMinTile, "look-back rows are sized for kMinTile");
+    static_assert(P::kTile >= kMinTile, "look-back rows are sized for kMinTile");
     Ctrl* ctrl = reinterpret_cast<Ctrl*>(temp + L.ctrl);
     const unsigned long long* bins = reinterpret_cast<const unsigned long long*>(temp + L.bins);
     ST* status[2] = {reinterpret_cast<ST*>(temp + L.status_a), reinterpret_cast<ST*>(temp + L.status_b)};
-    const uint64_t tiles = ceil_div(n, uint64_t(BLOCK) * ITEMS);
+    const uint64_t tiles = ceil_div(n, uint64_t(P::kTile));
     // Control block, histograms, offsets and the pass-0 look-back rows are
     // contiguous in the layout: one memset clears them.
     LCPP_CUDA_TRY(cudaMemsetAsync(temp + L.ctrl, 0, L.status_a + size_t(tiles) * kDigits * sizeof(ST) - L.ctrl,
@@ -773,9 +838,9 @@ lcpp_status launch_passes(const Layout& L, unsigned char* temp, const SortCall& 
         a.error = &ctrl->error;
         diag::KernelTimer timer(1 /* LCPP_KERNEL_SORT_ONESWEEP */, n, stream);
         if (sizeof(U) == 4 && a.shift % 8 == 0 && a.digit_mask == 0xffu)
-            launch_pass<U, V, PAIRS, BLOCK, ITEMS, KIND, PEERS, LB_WINDOW, ST, OffT, true>(a, tiles, stream);
+            launch_pass<U, V, PAIRS, P, KIND, ST, OffT, true>(a, tiles, stream);
         else
-            launch_pass<U, V, PAIRS, BLOCK, ITEMS, KIND, PEERS, LB_WINDOW, ST, OffT, false>(a, tiles, stream);
+            launch_pass<U, V, PAIRS, P, KIND, ST, OffT, false>(a, tiles, stream);
         timer.stop();
     }
     return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;
@@ -797,24 +862,28 @@ template <typename U, typename V, bool PAIRS, int KIND>
 lcpp_status run_kind(const Layout& L, unsigned char* temp, const SortCall& c, uint64_t n,
                      const KeyCodec<U>& codec, int begin_bit, int end_bit, int passes, cudaStream_t stream)
 {
-#define LCPP_PASSES(B, I, SP, W)                                                                      \
-    (L.wide ? launch_passes<U, V, PAIRS, B, I, KIND, SP, W, uint64_t, uint64_t>(L, temp, c, n, codec,  \
-                                                                                begin_bit, end_bit,   \
-                                                                                passes, stream)       \
-            : launch_passes<U, V, PAIRS, B, I, KIND, SP, W, uint32_t, uint32_t>(L, temp, c, n, codec,  \
-                                                                                begin_bit, end_bit,   \
-                                                                                passes, stream))
+#define LCPP_PASSES(...)                                                                                    \
+    (L.wide ? launch_passes<U, V, PAIRS, Policy<__VA_ARGS__>, KIND, uint64_t, uint64_t>(L, temp, c, n, codec,      \
+                                                                                      begin_bit, end_bit, passes, \
+                                                                                      stream)                     \
+            : launch_passes<U, V, PAIRS, Policy<__VA_ARGS__>, KIND, uint32_t, uint32_t>(L, temp, c, n, codec,      \
+                                                                                      begin_bit, end_bit, passes, \
+                                                                                      stream))
     if constexpr (sizeof(U) == 4 && !PAIRS) {
         if constexpr (KIND == kPlain) {
             switch (onesweep_variant()) {
             case 1: return LCPP_PASSES(384, 20, 0, 8);  // 8 ballots per digit
             case 2: return LCPP_PASSES(256, 24, 1, 8);  // shared-memory peer masks
-            case 3: return LCPP_PASSES(384, 20, 2, 8);
+            case 3: return LCPP_PASSES(256, 24, 2, 8, 2);  // slots ranked in pairs
+            case 4: return LCPP_PASSES(256, 24, 2, 8, 4);  // slots ranked in fours
+            case 5: return LCPP_PASSES(256, 24, 2, 8, 1, 4, true);  // 4 blocks per SM, 16-bit ranks
+            case 6: return LCPP_PASSES(256, 24, 2, 8, 1, 1);        // 2 blocks per SM (116 registers)
             default: break;
             }
         }
         // Measured best on B200 for 4-byte keys: 256 x 24 keys per tile,
-        // peers from low-5-bit shared masks plus 3 ballots.
+        // peers from low-5-bit shared masks plus 3 ballots, 3 blocks per SM
+        // (80 registers).  Variants 3-6 were within 1.5 % of it or slower.
         return LCPP_PASSES(256, 24, 2, 8);
     } else if constexpr (sizeof(U) == 4 && sizeof(V) == 4) {
         return LCPP_PASSES(384, 15, 0, 8);

@@ -60,9 +60,9 @@ def test_noalloc_matches_regular_twice(lcpp, dtype, n):
 
 def test_noalloc_rejects_too_many_items(lcpp):
     x = torch.zeros(4, dtype=torch.int32, device="cuda")
-    status, _ = _noalloc(lcpp, x, n=1_077_673_984 + 1)
+    status, _ = _noalloc(lcpp, x, n=1_075_707_904 + 1)
     assert status == lcpp.ERR_TEMP_TOO_SMALL
-    status, _ = _noalloc(lcpp, torch.zeros(4, dtype=torch.int64, device="cuda"), n=215_482_368 + 1)
+    status, _ = _noalloc(lcpp, torch.zeros(4, dtype=torch.int64, device="cuda"), n=215_089_152 + 1)
     assert status == lcpp.ERR_TEMP_TOO_SMALL
     status, _ = _noalloc(lcpp, x, n=0)
     assert status == lcpp.OK
