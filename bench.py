@@ -5,8 +5,9 @@ uint32 SortKeys @2^28 (1/2/4/8 B200) and % of HBM roofline").
 Default (--op sort): one step = one DeviceRadixSort::SortKeys (copy API) of
 2^28 uniform uint32 keys per GPU (seed 0, bits [0,32)) through the library's
 C ABI.  The other BASELINE configurations are available with --op (pairs,
-pairs_f32, pairs_u64, bits, scan, reduce, reduce_max); the driver only runs
-the default.
+pairs_f32, pairs_u64, bits, scan, reduce, reduce_max, and the distributed
+sort of 2^32 keys in total, dist / dist_zipf, at any N); the driver only
+runs the default.
 
 Arms:
   default           our sm_100a library.  N = 1: device-resident `value`
@@ -73,6 +74,14 @@ OPS = {
                    workload="DeviceReduce::Sum f32 U[0,1), seed 1", bytes=4, kbytes=4, kernel="reduce_kernel"),
     "reduce_max": dict(metric="Gitems/s int64 Reduce Max @2^30", unit="Gitems/s", log2n=30, dtype="i64",
                        workload="DeviceReduce::Max i64 uniform, seed 1", bytes=8, kbytes=8, kernel="reduce_kernel"),
+    # Distributed SortKeys of 2^32 keys in total (seed 7), sharded evenly:
+    # strong scaling over N GPUs (N = 1 is the 1-GPU-equivalent run).
+    "dist": dict(metric="Gkeys/s uint32 distributed SortKeys @2^32", unit="Gkeys/s", log2n=32, dtype="u32",
+                 workload="distributed SortKeys u32 uniform, seed 7", bytes=36, kbytes=8,
+                 kernel="onesweep_kernel (one 8-bit pass)", distributed=True, seed=7, zipf=False),
+    "dist_zipf": dict(metric="Gkeys/s uint32 distributed SortKeys Zipf(1.1) @2^32", unit="Gkeys/s", log2n=32,
+                      dtype="u32", workload="distributed SortKeys u32 Zipf(1.1) hashed, seed 7", bytes=36, kbytes=8,
+                      kernel="onesweep_kernel (one 8-bit pass)", distributed=True, seed=7, zipf=True),
 }
 
 
@@ -237,6 +246,11 @@ def cpu_fn(op: str, n_sample: int, threads: int):
     """One run of the oracle port on a bounded sample of the workload (the
     reference tests' host algorithms restated)."""
     from oracle import oracle as O
+    if op.startswith("dist"):
+        # LSD radix sort time does not depend on the key distribution: the
+        # uniform seed-7 stream stands in for both distributed workloads
+        x = O.generate(O.GEN_U32_UNIFORM, n_sample, seed=7)
+        return lambda: O.radix_sort(x, threads=threads)
     if op in ("sort", "bits"):
         x = O.generate(O.GEN_U32_UNIFORM, n_sample, seed=0 if op == "sort" else 1)
         kw = dict(begin_bit=8, end_bit=24) if op == "bits" else {}
@@ -274,7 +288,7 @@ def cpu_threads_for(op: str) -> int:
     from oracle import oracle as O
     # the sort restatement is multi-threaded; the scan / reduce host
     # references of the reference's tests are sequential
-    return O.cpu_threads() if (op in ("sort", "bits") or op.startswith("pairs")) else 1
+    return O.cpu_threads() if (op in ("sort", "bits") or op.startswith(("pairs", "dist"))) else 1
 
 
 def run_reference(args):
@@ -299,8 +313,10 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": cfg["metric"], "value": v, "unit": cfg["unit"], "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"], "data": DATA,
-        "config": {"workload": f"{cfg['workload']}, 2^{log2n} items per GPU; each step runs a bounded "
+        "higher_is_better": True, "scaling": "strong" if cfg.get("distributed") else "weak", "vs_baseline": None,
+        "dtype": cfg["dtype"], "data": DATA,
+        "config": {"workload": f"{cfg['workload']}, 2^{log2n} items " + ("in total" if cfg.get("distributed") else "per GPU")
+                   + "; each step runs a bounded "
                                f"2^22-item sample of it on the host"},
         "cpu_baseline": {"value": v, "unit": cfg["unit"], "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": cfg["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -324,19 +340,48 @@ def run_ours(args):
     log2n = args.log2n or cfg["log2n"]
     n = 1 << log2n
 
-    if world > 1:
+    if world > 1 or cfg.get("distributed"):
+        import socket
+
         import torch.distributed as dist
         from datetime import timedelta
 
         from lcpp_b200 import distributed as D
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+        # stdout carries exactly one JSON line: whatever NCCL prints on its own
+        # (its version banner goes to file descriptor 1) is sent to stderr
+        sys.stdout.flush()
+        json_out = os.dup(1)
+        os.dup2(2, 1)
+        init = {}
+        if world == 1 and "MASTER_ADDR" not in os.environ:  # one process, no torchrun
+            with socket.socket() as sk:
+                sk.bind(("127.0.0.1", 0))
+                port = sk.getsockname()[1]
+            init = dict(init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local),
+                                **init)
         try:
-            res = D.bench_distributed_sort(n, args.steps, args.warmup, dist, ClockSampler, measured_peak())
+            if cfg.get("distributed"):  # fixed total, sharded evenly (strong scaling)
+                n_local = (1 << log2n) // world
+                res = D.bench_distributed_sort(n_local, args.steps, args.warmup, dist, ClockSampler,
+                                               measured_peak(), seed=cfg["seed"], zipf=cfg["zipf"],
+                                               metric=cfg["metric"], scaling="strong")
+            else:  # the default sort: 2^28 keys per GPU (weak scaling)
+                res = D.bench_distributed_sort(n, args.steps, args.warmup, dist, ClockSampler, measured_peak())
+            if rank == 0 and world == 1 and not args.no_cpu_baseline:
+                threads = cpu_threads_for("sort")
+                ips, reps = cpu_sample("sort", 1 << 24, threads, 10.0)
+                res["cpu_baseline"] = {"value": ips / 1e9, "unit": "Gkeys/s", "cores": threads, "kind": "port",
+                                       "sample": f"2^24 keys of the uniform u32 stream x {reps} runs; "
+                                                 "multi-threaded LSD restatement of the onesweep semantics"}
             if rank == 0:
-                print(json.dumps(res), flush=True)
+                os.write(json_out, (json.dumps(res) + "\n").encode())
             dist.barrier()
         finally:
             dist.destroy_process_group()
+            sys.stdout.flush()
+            os.dup2(json_out, 1)
+            os.close(json_out)
         return 0
 
     w = Workload(args.op, n)

@@ -40,6 +40,25 @@ lcpp_status lcpp_dist_merge_temp_bytes(uint64_t total, size_t* temp_bytes);
 lcpp_status lcpp_dist_merge_sorted(void* temp, size_t temp_bytes, const void* a, uint64_t na, const void* b,
                                    uint64_t nb, void* out, lcpp_dtype key_dtype, lcpp_stream_t stream);
 
+/* Exchange buffers shared between the processes of one node (CUDA IPC), so
+ * that a rank's merge kernel reads the sorted runs of the other ranks straight
+ * from their memory over NVLink (plain loads).  Set-up calls, not hot-path
+ * calls: the distributed sort allocates its buffers once and reuses them.
+ *
+ * lcpp_dist_ipc_alloc: cudaMalloc of `bytes` on the current device and its
+ *   IPC handle (LCPP_IPC_HANDLE_BYTES bytes written to `handle`).
+ * lcpp_dist_ipc_open: maps another process's buffer from its handle on the
+ *   current device (peer access enabled lazily); `*dptr` is usable by kernels
+ *   on this device.
+ * lcpp_dist_ipc_close: unmaps a buffer opened with lcpp_dist_ipc_open.
+ * lcpp_dist_ipc_free: frees a buffer from lcpp_dist_ipc_alloc (after every
+ *   peer has closed its mapping). */
+#define LCPP_IPC_HANDLE_BYTES 64
+lcpp_status lcpp_dist_ipc_alloc(size_t bytes, void** dptr, void* handle);
+lcpp_status lcpp_dist_ipc_open(const void* handle, void** dptr);
+lcpp_status lcpp_dist_ipc_close(void* dptr);
+lcpp_status lcpp_dist_ipc_free(void* dptr);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -1,5 +1,7 @@
 // dist.cu -- device building blocks of the distributed sort
 // (include/lcpp_b200_dist.h).
+#include <cstring>
+
 #include "../../include/lcpp_b200_dist.h"
 #include "common.cuh"
 
@@ -105,7 +107,22 @@ __global__ void merge_split_kernel(const U* __restrict__ a, uint64_t na, const U
                            [&](uint64_t j) { return key_image(b[j], codec); });
 }
 
-template <typename U>
+// Comparison image of a key inside the merge: the identity for unsigned keys
+// (PLAIN), else the sort's bijection with the +-0.0 fold.
+template <bool PLAIN, typename U>
+__device__ __forceinline__ U merge_image(U k, const KeyCodec<U>& c)
+{
+    if constexpr (PLAIN)
+        return k;
+    else
+        return key_image(k, c);
+}
+
+// One output tile per block: gather a[i0, i1) ++ b[j0, j1) into shared
+// memory, each thread finds where its kMergeItems outputs start (co-rank by
+// binary search in shared memory, 32-bit indices) and merges them serially
+// with one shared-memory load per output, then the tile is stored coalesced.
+template <typename U, bool PLAIN>
 __global__ void __launch_bounds__(kMergeBlock)
 merge_block_kernel(const U* __restrict__ a, uint64_t na, const U* __restrict__ b, uint64_t nb,
                    const uint64_t* __restrict__ splits, U* __restrict__ out, KeyCodec<U> codec)
@@ -118,24 +135,53 @@ merge_block_kernel(const U* __restrict__ a, uint64_t na, const U* __restrict__ b
     const uint64_t i0 = splits[blockIdx.x], i1 = splits[blockIdx.x + 1];
     const uint64_t j0 = o0 - i0, j1 = o1 - i1;
     const int la = int(i1 - i0), lb = int(j1 - j0), len = int(o1 - o0);
-    for (int k = tid; k < la; k += kMergeBlock) s[k] = a[i0 + k];
-    for (int k = tid; k < lb; k += kMergeBlock) s[la + k] = b[j0 + k];
+    // Gather: all of a thread's loads are issued before any is stored, so
+    // their latencies (HBM, or NVLink when a run lives in another GPU's
+    // memory) overlap.
+    {
+        const U* pa = a + i0;
+        const U* pb = b + j0 - la;  // pb[idx] = b[j0 + idx - la] for idx >= la
+        U v[kMergeItems];
+#pragma unroll
+        for (int k = 0; k < kMergeItems; ++k) {
+            const int idx = tid + k * kMergeBlock;
+            if (idx < len) v[k] = (idx < la ? pa : pb)[idx];
+        }
+#pragma unroll
+        for (int k = 0; k < kMergeItems; ++k) {
+            const int idx = tid + k * kMergeBlock;
+            if (idx < len) s[idx] = v[k];
+        }
+    }
     __syncthreads();
-    const U* sa = s;
-    const U* sb = s + la;
     U v[kMergeItems];
     const int ot = tid * kMergeItems;
     if (ot < len) {
-        int ia = int(co_rank<U>(uint64_t(ot), uint64_t(la), uint64_t(lb),
-                                [&](uint64_t i) { return key_image(sa[i], codec); },
-                                [&](uint64_t j) { return key_image(sb[j], codec); }));
-        int ib = ot - ia;
+        // co-rank: number of a-keys among this thread's first ot outputs
+        int lo = ot > lb ? ot - lb : 0;
+        int hi = ot < la ? ot : la;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (merge_image<PLAIN>(s[mid], codec) <= merge_image<PLAIN>(s[la + ot - mid - 1], codec))
+                lo = mid + 1;
+            else
+                hi = mid;
+        }
+        // serial merge; ia / ib index s[] (the b part starts at la)
+        int ia = lo, ib = la + ot - lo;
+        const int a_end = la, b_end = la + lb;
+        U ka = s[ia < b_end ? ia : b_end - 1];
+        U kb = s[ib < b_end ? ib : b_end - 1];
 #pragma unroll
         for (int k = 0; k < kMergeItems; ++k) {
-            const bool take_a = ia < la && (ib >= lb || key_image(sa[ia], codec) <= key_image(sb[ib], codec));
-            v[k] = take_a ? sa[ia] : sb[ib < lb ? ib : lb - 1];
-            ia += take_a;
-            ib += !take_a;
+            const bool take_a =
+                ib >= b_end || (ia < a_end && merge_image<PLAIN>(ka, codec) <= merge_image<PLAIN>(kb, codec));
+            v[k] = take_a ? ka : kb;
+            int next = take_a ? ++ia : ++ib;
+            next = next < b_end ? next : b_end - 1;
+            const U x = s[next];
+            ka = take_a ? x : ka;
+            kb = take_a ? kb : x;
         }
     }
     __syncthreads();
@@ -145,7 +191,11 @@ merge_block_kernel(const U* __restrict__ a, uint64_t na, const U* __restrict__ b
             if (ot + k < len) s[ot + k] = v[k];
     }
     __syncthreads();
-    for (int k = tid; k < len; k += kMergeBlock) out[o0 + k] = s[k];
+#pragma unroll
+    for (int k = 0; k < kMergeItems; ++k) {
+        const int idx = tid + k * kMergeBlock;
+        if (idx < len) out[o0 + idx] = s[idx];
+    }
 }
 
 inline uint64_t merge_blocks(uint64_t total) { return ceil_div(total, kMergeTile); }
@@ -180,20 +230,83 @@ extern "C" lcpp_status lcpp_dist_merge_sorted(void* temp, size_t temp_bytes, con
     uint64_t* splits = static_cast<uint64_t*>(temp);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const unsigned sgrid = unsigned(ceil_div(blocks + 1, 256));
-    if (kb == 4) {
-        const auto c = make_codec<uint32_t>(key_dtype, false);
-        merge_split_kernel<uint32_t><<<sgrid, 256, 0, s>>>(static_cast<const uint32_t*>(a), na,
-                                                          static_cast<const uint32_t*>(b), nb, splits, blocks + 1, c);
-        merge_block_kernel<uint32_t><<<unsigned(blocks), kMergeBlock, 0, s>>>(
-            static_cast<const uint32_t*>(a), na, static_cast<const uint32_t*>(b), nb, splits,
-            static_cast<uint32_t*>(out), c);
-    } else {
-        const auto c = make_codec<uint64_t>(key_dtype, false);
-        merge_split_kernel<uint64_t><<<sgrid, 256, 0, s>>>(static_cast<const uint64_t*>(a), na,
-                                                          static_cast<const uint64_t*>(b), nb, splits, blocks + 1, c);
-        merge_block_kernel<uint64_t><<<unsigned(blocks), kMergeBlock, 0, s>>>(
-            static_cast<const uint64_t*>(a), na, static_cast<const uint64_t*>(b), nb, splits,
-            static_cast<uint64_t*>(out), c);
-    }
+    const bool plain = key_dtype == LCPP_U32 || key_dtype == LCPP_U64;
+    auto go = [&](auto tag) {
+        using U = decltype(tag);
+        const auto c = make_codec<U>(key_dtype, false);
+        const U* pa = static_cast<const U*>(a);
+        const U* pb = static_cast<const U*>(b);
+        merge_split_kernel<U><<<sgrid, 256, 0, s>>>(pa, na, pb, nb, splits, blocks + 1, c);
+        if (plain)
+            merge_block_kernel<U, true><<<unsigned(blocks), kMergeBlock, 0, s>>>(pa, na, pb, nb, splits,
+                                                                              static_cast<U*>(out), c);
+        else
+            merge_block_kernel<U, false><<<unsigned(blocks), kMergeBlock, 0, s>>>(pa, na, pb, nb, splits,
+                                                                               static_cast<U*>(out), c);
+    };
+    if (kb == 4)
+        go(uint32_t{});
+    else
+        go(uint64_t{});
     return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------
+// Exchange buffers shared through CUDA IPC.
+// ---------------------------------------------------------------------------
+static_assert(sizeof(cudaIpcMemHandle_t) == LCPP_IPC_HANDLE_BYTES, "IPC handle size");
+
+extern "C" lcpp_status lcpp_dist_ipc_alloc(size_t bytes, void** dptr, void* handle)
+{
+    if (!dptr || !handle || bytes == 0) return LCPP_ERR_INVALID_ARG;
+    *dptr = nullptr;
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return LCPP_ERR_CUDA;
+    }
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(p);
+        return LCPP_ERR_CUDA;
+    }
+    memcpy(handle, &h, sizeof(h));
+    *dptr = p;
+    return LCPP_OK;
+}
+
+extern "C" lcpp_status lcpp_dist_ipc_open(const void* handle, void** dptr)
+{
+    if (!dptr || !handle) return LCPP_ERR_INVALID_ARG;
+    *dptr = nullptr;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        return LCPP_ERR_CUDA;
+    }
+    *dptr = p;
+    return LCPP_OK;
+}
+
+extern "C" lcpp_status lcpp_dist_ipc_close(void* dptr)
+{
+    if (!dptr) return LCPP_ERR_INVALID_ARG;
+    if (cudaIpcCloseMemHandle(dptr) != cudaSuccess) {
+        cudaGetLastError();
+        return LCPP_ERR_CUDA;
+    }
+    return LCPP_OK;
+}
+
+extern "C" lcpp_status lcpp_dist_ipc_free(void* dptr)
+{
+    if (!dptr) return LCPP_ERR_INVALID_ARG;
+    if (cudaFree(dptr) != cudaSuccess) {
+        cudaGetLastError();
+        return LCPP_ERR_CUDA;
+    }
+    return LCPP_OK;
 }

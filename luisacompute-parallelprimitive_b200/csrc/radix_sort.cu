@@ -886,9 +886,25 @@ lcpp_status run_kind(const Layout& L, unsigned char* temp, const SortCall& c, ui
         // (80 registers).  Variants 3-6 were within 1.5 % of it or slower.
         return LCPP_PASSES(256, 24, 2, 8);
     } else if constexpr (sizeof(U) == 4 && sizeof(V) == 4) {
-        return LCPP_PASSES(384, 15, 0, 8);
+        switch (onesweep_variant()) {
+        case 11: return LCPP_PASSES(384, 15, 0, 8);  // 8 ballots per digit
+        case 12: return LCPP_PASSES(512, 12, 2, 8);
+        case 13: return LCPP_PASSES(512, 16, 2, 8);
+        default: break;
+        }
+        // Measured best on B200 for 4-byte keys with 4-byte values (u32/u32
+        // 2^28: 42.0 Gkeys/s against 38.2 with 8 ballots at 384 x 15).
+        return LCPP_PASSES(512, 14, 2, 8);
     } else {
-        return LCPP_PASSES(256, 16, 0, 8);
+        switch (onesweep_variant()) {
+        case 21: return LCPP_PASSES(256, 16, 0, 8);  // 8 ballots per digit
+        case 22: return LCPP_PASSES(256, 20, 2, 8);
+        case 23: return LCPP_PASSES(384, 16, 2, 8);
+        default: break;
+        }
+        // Measured best on B200 with an 8-byte key or value (u64/i32 2^27:
+        // 16.2 Gkeys/s against 13.1 with 8 ballots at 256 x 16).
+        return LCPP_PASSES(256, 24, 2, 8);
     }
 #undef LCPP_PASSES
 }

@@ -15,9 +15,16 @@ Sort (keys only), per rank:
   3. keys equal to k_j are split between the ranks below and above the
      boundary in rank order, so every rank receives exactly its share even
      when one key value fills several ranks (heavy hitters);
-  4. one all-to-all exchange of the sorted runs (NCCL send / recv);
-  5. the G received runs (each sorted) are merged pairwise, ceil(log2 G)
-     merge-path levels (lcpp_dist_merge_sorted), instead of a second sort.
+  4. exchange and merge.  Ranks of one node whose GPUs reach each other
+     (NVLink / NVSwitch peer access): the local sort writes into an exchange
+     buffer shared with the other ranks through CUDA IPC, and each rank's
+     first merge level reads its G incoming runs straight from the other
+     ranks' buffers with plain loads over NVLink (no all-to-all buffer in
+     between); the remaining ceil(log2 G) - 1 levels merge locally.
+     Otherwise: one NCCL all-to-all of the sorted runs, then the pairwise
+     merge of the G received runs.  Merging adjacent runs with ties taken
+     from the left keeps equal keys in rank order (the result is the stable
+     global sort).
 Rank r ends with global sorted positions [P_r, P_{r+1}).
 
 Scan and reduce: local pass, one all-gather of per-rank totals, then the
@@ -63,6 +70,8 @@ class GpuOps:
         self._temps = {}
         self.rs = DeviceRadixSort()
         self.launches = 0  # search and merge kernels launched (the sorts are counted by diag timing)
+        self._peer = None
+        self._exchange = None
 
     def _temp(self, key, nbytes):
         t = self._temps.get(key)
@@ -93,6 +102,71 @@ class GpuOps:
                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "lcpp_dist_search_sorted")
         return out
 
+    def local_sort_into(self, keys, out_ptr):
+        """SortKeys of `keys` (all bits) into the device buffer at out_ptr."""
+        n = keys.numel()
+        if n == 0:
+            return
+        code = dtype_code(keys)
+        temp = self._temp("sort", DeviceRadixSort.GetSortKeysTempStorageBytes(code, n))
+        check(lib().lcpp_radix_sort_keys(
+            ctypes.c_void_p(temp.data_ptr()), temp.numel(), ctypes.c_void_p(keys.data_ptr()),
+            ctypes.c_void_p(out_ptr), n, 0, keys.element_size() * 8, 0, code,
+            ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)), "lcpp_radix_sort_keys")
+
+    def merge_ptrs(self, a_ptr, na, b_ptr, nb, out_ptr, code):
+        """Stable merge of two sorted runs given as device pointers (local or
+        mapped from a peer)."""
+        total = na + nb
+        if total == 0:
+            return
+        nbytes = ctypes.c_size_t(0)
+        check(lib().lcpp_dist_merge_temp_bytes(total, ctypes.byref(nbytes)), "lcpp_dist_merge_temp_bytes")
+        temp = self._temp("merge", nbytes.value)
+        self.launches += 2
+        check(lib().lcpp_dist_merge_sorted(
+            ctypes.c_void_p(temp.data_ptr()), temp.numel(), ctypes.c_void_p(a_ptr), na, ctypes.c_void_p(b_ptr), nb,
+            ctypes.c_void_p(out_ptr), code, ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)),
+            "lcpp_dist_merge_sorted")
+
+    def peer_capable(self, dist):
+        """Whether every pair of ranks shares a node and has GPU peer access
+        (decided once, collectively)."""
+        if self._peer is None:
+            import socket
+            import zlib
+            torch = self.torch
+            G = dist.get_world_size()
+            me = [zlib.crc32(socket.gethostname().encode()), self.device.index]
+            rows = _all_gather_int64(dist, me, self.device)
+            same_host = all(r[0] == rows[0][0] for r in rows)
+            ok = same_host and all(torch.cuda.can_device_access_peer(self.device.index, r[1])
+                                   for r in rows if r[1] != self.device.index)
+            flag = torch.tensor([0 if ok else 1], dtype=torch.int64, device=self.device)
+            dist.all_reduce(flag)  # peer mode only when every rank can use it
+            self._peer = G > 1 and flag.item() == 0
+        return self._peer
+
+    def exchange(self, dist, nbytes):
+        """The node's shared exchange buffers, with room for nbytes per rank
+        (re-created, collectively, when some rank needs more)."""
+        torch = self.torch
+        need = torch.tensor([nbytes], dtype=torch.int64, device=self.device)
+        dist.all_reduce(need, op=dist.ReduceOp.MAX)
+        need = int(need.item())
+        if self._exchange is None or self._exchange.capacity < need:
+            if self._exchange is not None:
+                self._exchange.close(dist)
+            self._exchange = PeerExchange(dist, max(need, 256), self.device)
+        return self._exchange
+
+    def close(self, dist):
+        """Releases the exchange buffers (collective; before the process
+        group is destroyed)."""
+        if self._exchange is not None:
+            self._exchange.close(dist)
+            self._exchange = None
+
     def merge(self, a, b, out):
         """out[:a.numel() + b.numel()] = stable merge of sorted runs a, b."""
         torch = self.torch
@@ -110,6 +184,76 @@ class GpuOps:
 
     def empty_like(self, t):
         return self.torch.empty_like(t)
+
+
+class _DeviceArray:
+    """A device buffer as __cuda_array_interface__ (for a zero-copy torch view)."""
+
+    def __init__(self, ptr, n, itemsize):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i4" if itemsize == 4 else "<i8",
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+def device_view(ptr, n, dtype):
+    """torch tensor of n elements of dtype over device memory at ptr."""
+    import torch
+    itemsize = torch.empty(0, dtype=dtype).element_size()
+    if n == 0:
+        return torch.empty(0, dtype=dtype, device="cuda")
+    return torch.as_tensor(_DeviceArray(ptr, n, itemsize), device="cuda").view(dtype)
+
+
+class PeerExchange:
+    """Two exchange buffers per rank, shared with every rank of the node
+    through CUDA IPC.  Step s of the distributed sort writes this rank's
+    sorted keys into buffer s % 2 and the other ranks read their runs from
+    it; buffer s % 2 is written again only at step s + 2, after the
+    collectives of step s + 1, which no rank passes before its step-s merge
+    has run.  Set-up cost (cudaMalloc, handle exchange, mapping) is paid
+    once per capacity."""
+
+    def __init__(self, dist, capacity, device):
+        import torch
+        self.capacity = capacity
+        self.rank, G = dist.get_rank(), dist.get_world_size()
+        self.local = []
+        raw = bytearray()
+        for _ in range(2):
+            p = ctypes.c_void_p()
+            h = (ctypes.c_ubyte * 64)()
+            check(lib().lcpp_dist_ipc_alloc(capacity, ctypes.byref(p), h), "lcpp_dist_ipc_alloc")
+            self.local.append(p.value)
+            raw += bytes(h)
+        t = torch.tensor(list(raw), dtype=torch.uint8, device=device)
+        parts = [torch.empty_like(t) for _ in range(G)]
+        dist.all_gather(parts, t)
+        self.ptrs, self.opened = [], []
+        for r, part in enumerate(parts):
+            if r == self.rank:
+                self.ptrs.append(list(self.local))
+                continue
+            hb = bytes(part.cpu().tolist())
+            row = []
+            for slot in range(2):
+                h = (ctypes.c_ubyte * 64).from_buffer_copy(hb[slot * 64:(slot + 1) * 64])
+                p = ctypes.c_void_p()
+                check(lib().lcpp_dist_ipc_open(h, ctypes.byref(p)), "lcpp_dist_ipc_open")
+                row.append(p.value)
+                self.opened.append(p.value)
+            self.ptrs.append(row)
+        self.step = 0
+
+    def close(self, dist):
+        import torch
+        torch.cuda.synchronize()
+        dist.barrier()  # every rank's reads of the buffers are done
+        for p in self.opened:
+            check(lib().lcpp_dist_ipc_close(ctypes.c_void_p(p)), "lcpp_dist_ipc_close")
+        torch.cuda.synchronize()
+        dist.barrier()  # every mapping is gone
+        for p in self.local:
+            check(lib().lcpp_dist_ipc_free(ctypes.c_void_p(p)), "lcpp_dist_ipc_free")
+        self.opened, self.local, self.ptrs = [], [], []
 
 
 def _all_gather_int64(dist, values, device):
@@ -198,16 +342,50 @@ def _bitcast_for_comm(t):
     return t
 
 
-def distributed_sort_keys(keys_local, dist, ops=None):
+def distributed_sort_keys(keys_local, dist, ops=None, exchange="auto"):
     """Globally sort the keys held by all ranks; returns this rank's slice of
-    the result (global positions [floor(r N / G), floor((r+1) N / G)))."""
+    the result (global positions [floor(r N / G), floor((r+1) N / G))).
+    exchange: "peer" (merge straight from the other ranks' memory, ranks of
+    one node with peer access), "nccl" (all-to-all, then merge) or "auto"."""
     import torch
-    ops = ops or GpuOps()
-    local = ops.local_sort(keys_local)
-    send, recv, _ = exact_splits(local, dist, ops)
-    out = torch.empty(sum(recv), dtype=local.dtype, device=local.device)
-    dist.all_to_all_single(_bitcast_for_comm(out), _bitcast_for_comm(local), recv, send)
-    return merge_runs(out, recv, ops)
+    G, r = dist.get_world_size(), dist.get_rank()
+    if ops is None:  # one-off call: the exchange buffers live for this call only
+        ops = GpuOps()
+        try:
+            return distributed_sort_keys(keys_local, dist, ops, exchange)
+        finally:
+            ops.close(dist)
+    if G == 1:
+        return ops.local_sort(keys_local)
+    peer = exchange == "peer" or (exchange == "auto" and hasattr(ops, "peer_capable") and ops.peer_capable(dist))
+    if not peer:
+        local = ops.local_sort(keys_local)
+        send, recv, _ = exact_splits(local, dist, ops)
+        out = torch.empty(sum(recv), dtype=local.dtype, device=local.device)
+        dist.all_to_all_single(_bitcast_for_comm(out), _bitcast_for_comm(local), recv, send)
+        return merge_runs(out, recv, ops)
+
+    kb = keys_local.element_size()
+    n = keys_local.numel()
+    ex = ops.exchange(dist, n * kb)
+    slot = ex.step & 1
+    ex.step += 1
+    ops.local_sort_into(keys_local, ex.ptrs[r][slot])
+    local = device_view(ex.ptrs[r][slot], n, keys_local.dtype)
+    _, recv, idx = exact_splits(local, dist, ops)
+    code = dtype_code(keys_local)
+    total = sum(recv)
+    # first level straight from the owners' exchange buffers (run i = the
+    # keys rank i sends here, in rank order), into `out`
+    runs = [(ex.ptrs[i][slot] + idx[i][r] * kb, idx[i][r + 1] - idx[i][r]) for i in range(G)]
+    out = torch.empty(total, dtype=keys_local.dtype, device=keys_local.device)
+    counts, pos = [], 0
+    for i in range(0, G, 2):
+        (pa, na), (pb, nb) = runs[i], runs[i + 1] if i + 1 < G else (0, 0)
+        ops.merge_ptrs(pa, na, pb, nb, out.data_ptr() + pos * kb, code)
+        counts.append(na + nb)
+        pos += na + nb
+    return merge_runs(out, counts, ops)
 
 
 def merge_runs(buf, counts, ops):
@@ -325,31 +503,54 @@ def distributed_reduce_totals(x_local, dist):
 # ---------------------------------------------------------------------------
 # Benchmark (bench.py, N > 1)
 # ---------------------------------------------------------------------------
-def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak):
-    """Weak-scaling benchmark of distributed_sort_keys: 2^k uniform u32 keys
-    per rank (rank r holds elements [r n, (r+1) n) of the seed-0 stream).
-    Device time per step is the max over ranks."""
+def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak, seed=0, zipf=False,
+                           metric="Gkeys/s uint32 SortKeys @2^28", scaling="weak"):
+    """Benchmark of distributed_sort_keys: n_local u32 keys per rank (rank r
+    holds elements [r n, (r+1) n) of the `seed` stream, uniform or Zipf(1.1)
+    hashed).  Device time per step is the max over ranks.  Checks on the
+    last warm-up result: every rank's slice is sorted, slices are ordered
+    across ranks and balanced, and the order-independent fingerprints (sum,
+    sum of squares, xor; 64-bit wrapping) of all outputs equal those of all
+    inputs."""
     import torch
 
-    from . import GEN_U32_UNIFORM, KERNEL_SORT_ONESWEEP, diag_timing_enable, diag_timing_read, testgen_fill
+    from . import (GEN_U32_UNIFORM, GEN_U32_ZIPF, KERNEL_SORT_ONESWEEP, diag_timing_enable, diag_timing_read,
+                   testgen_fill)
     G, r = dist.get_world_size(), dist.get_rank()
     dev = torch.device("cuda", torch.cuda.current_device())
     keys = torch.empty(n_local, dtype=torch.uint32, device=dev)
-    testgen_fill(keys, GEN_U32_UNIFORM, seed=0, offset=r * n_local)
+    testgen_fill(keys, GEN_U32_ZIPF if zipf else GEN_U32_UNIFORM, seed=seed, offset=r * n_local)
     ops = GpuOps()
+    out = keys
     for _ in range(warmup):
         out = distributed_sort_keys(keys, dist, ops)
     torch.cuda.synchronize()
     dist.barrier()
-    # correctness of the last warm-up result: locally sorted, ordered across ranks
-    o = out.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
-    ok = bool((o[1:] >= o[:-1]).all()) and out.numel() == n_local
-    edges = torch.tensor([o[0].item(), o[-1].item(), int(ok)], dtype=torch.int64, device=dev)
+
+    # checks in chunks of 2^26 keys (int64 copies of 2^32 keys would not fit)
+    K = 0x9E3779B97F4A7C15 - (1 << 64)  # odd multiplier as a wrapping int64
+
+    def fingerprint(t):
+        f = torch.zeros(4, dtype=torch.int64, device=dev)
+        for c in range(0, t.numel(), 1 << 26):
+            x = t[c:c + (1 << 26)].view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+            f += torch.stack([x.sum(), (x * x).sum(), (x * K).sum(), torch.tensor(x.numel(), device=dev)])
+        return f
+
+    ok = out.numel() == n_local
+    for c in range(0, out.numel(), 1 << 26):
+        x = out[c:c + (1 << 26) + 1].view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+        ok = ok and bool((x[1:] >= x[:-1]).all())
+    lo_hi = (out.view(torch.int32)[[0, -1]].to(torch.int64) & 0xFFFFFFFF if out.numel()
+             else torch.zeros(2, dtype=torch.int64, device=dev))
+    edges = torch.cat([lo_hi, torch.tensor([int(ok)], dtype=torch.int64, device=dev)])
     all_edges = [torch.empty_like(edges) for _ in range(G)]
     dist.all_gather(all_edges, edges)
+    fp = torch.stack([fingerprint(keys), fingerprint(out)])
+    dist.all_reduce(fp)
     e = [t.tolist() for t in all_edges]
     ordered = all(x[2] for x in e) and all(e[i][1] <= e[i + 1][0] for i in range(G - 1))
-
+    same_multiset = bool(torch.equal(fp[0], fp[1]))
     props = torch.cuda.get_device_properties(dev)
     bus = getattr(props, "pci_bus_id", None)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -395,26 +596,40 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
     dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_ms = e2e_ms.item()
 
+    ops.close(dist)
     onesweep = [x[1] for x in recs if x[0] == KERNEL_SORT_ONESWEEP]
     avg_pass = sum(onesweep) / max(1, len(onesweep))
     achieved = 8 * n_local / (avg_pass * 1e-3) / 1e9
     peak_gbs, peak_src = peak
-    # per GPU in HBM: the local sort (4 passes x 8 B/key + 4 B/key histogram read), the
-    # exchange (read + write 8 B/key) and ceil(log2 G) merge levels (8 B/key each);
-    # (G-1)/G of the keys cross NVLink in each direction.
+    # per GPU in HBM: the local sort (4 passes x 8 B/key + 4 B/key histogram read); NCCL
+    # exchange: the all-to-all (read + write 8 B/key) and ceil(log2 G) merge levels (8 B/key
+    # each); peer exchange: the first merge level reads the runs where they lie (this GPU's
+    # buffer is read once, by its owner or a peer: 4 B/key) and writes 4 B/key, then
+    # ceil(log2 G) - 1 local levels.  (G-1)/G of the keys cross NVLink in each direction.
     levels = (G - 1).bit_length()
-    hbm_bytes = (36 + 8 + 8 * levels) * n_local
+    if G == 1:
+        hbm_bytes = 36 * n_local
+    elif ops.peer_capable(dist):
+        hbm_bytes = (36 + 8 + 8 * (levels - 1)) * n_local
+    else:
+        hbm_bytes = (36 + 8 + 8 * levels) * n_local
     nvlink_bytes = (G - 1) / G * 4 * n_local
+    dist_name = "Zipf(1.1) ranks hashed by fmix32" if zipf else "uniform"
     return {
-        "metric": "Gkeys/s uint32 SortKeys @2^28", "value": value, "unit": "Gkeys/s", "n_gpus": G,
-        "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "metric": metric, "value": value, "unit": "Gkeys/s", "n_gpus": G,
+        "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
         "vs_baseline": None, "dtype": "u32",
         "data": "synthetic (splitmix64 counter streams; see include/lcpp_b200_testgen.h)",
-        "config": {"workload": f"distributed SortKeys u32 uniform, 2^{n_local.bit_length() - 1} keys per GPU "
-                               f"(global 2^{(G * n_local).bit_length() - 1})",
+        "config": {"workload": f"distributed SortKeys u32 {dist_name}, seed {seed}, "
+                               f"2^{n_local.bit_length() - 1} keys per GPU (global 2^{(G * n_local).bit_length() - 1})",
                    "items_per_gpu": n_local, "parallelism": f"sort-partitioned over {G} GPUs (NCCL all-to-all)",
-                   "algorithm": "local onesweep -> exact 16-bit-refined splitters (2 all-reduce rounds) -> "
-                                "all-to-all -> pairwise merge-path merge of the G received runs",
+                              "multiset_fingerprint_check": same_multiset,
+                   "algorithm": "local onesweep into a CUDA-IPC exchange buffer -> exact 16-bit-refined splitters "
+                                "(2 all-reduce rounds) -> merge-path merge reading the G runs straight from the "
+                                "owners' memory over NVLink (then local merge levels)"
+                                if ops.peer_capable(dist) else
+                                "local onesweep -> exact 16-bit-refined splitters (2 all-reduce rounds) -> "
+                                "NCCL all-to-all -> pairwise merge-path merge of the G received runs",
                    "l2": "inputs larger than L2; no flush", "globally_sorted_check": ordered},
         "roofline": {"bound": "hbm", "kernel": "onesweep_kernel (one 8-bit pass)", "achieved": achieved,
                      "peak": peak_gbs, "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak_gbs,

@@ -59,7 +59,7 @@ def _worker(rank, world, port, n, q):
     root = Path(__file__).resolve().parent.parent
     sys.path[:0] = [str(root), str(root / "luisacompute-parallelprimitive_b200")]
     import lcpp_b200 as L
-    from lcpp_b200.distributed import distributed_inclusive_sum, distributed_reduce, distributed_sort_keys
+    from lcpp_b200.distributed import GpuOps, distributed_inclusive_sum, distributed_reduce, distributed_sort_keys
     torch.cuda.set_device(rank)
     from datetime import timedelta
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
@@ -68,12 +68,24 @@ def _worker(rank, world, port, n, q):
         keys = torch.empty(n, dtype=torch.uint32, device="cuda")
         L.testgen_fill(keys, L.GEN_U32_ZIPF, seed=7, offset=rank * n)
         out = distributed_sort_keys(keys, dist)
+        out_nccl = distributed_sort_keys(keys, dist, exchange="nccl")
+        # one GpuOps over several steps: the exchange buffers alternate and
+        # are reused; every step's keys differ (and the sizes differ by rank)
+        ops = GpuOps()
+        steps = []
+        for s in range(3):
+            m = n // 2 + 1000 * rank + 7 * s
+            k = torch.empty(m, dtype=torch.uint32, device="cuda")
+            L.testgen_fill(k, L.GEN_U32_UNIFORM if s != 1 else L.GEN_U32_AND3, seed=100 + s, offset=rank * n)
+            steps.append((k.cpu().numpy(), distributed_sort_keys(k, dist, ops).cpu().numpy()))
+        ops.close(dist)
         x = torch.empty(n, dtype=torch.int32, device="cuda")
         L.testgen_fill(x, L.GEN_I32_SCAN, seed=3, offset=rank * n)
         scan = distributed_inclusive_sum(x, dist)
         red = distributed_reduce(x, dist, L.OP_SUM)
         torch.cuda.synchronize()
-        q.put((rank, out.cpu().numpy(), keys.cpu().numpy(), scan.cpu().numpy(), x.cpu().numpy(), red))
+        q.put((rank, out.cpu().numpy(), keys.cpu().numpy(), scan.cpu().numpy(), x.cpu().numpy(), red,
+               out_nccl.cpu().numpy(), steps))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -93,7 +105,15 @@ def test_two_ranks_nccl():
         p.join(timeout=120)
         assert p.exitcode == 0
     allk = np.concatenate([got[r][1] for r in range(world)])
-    np.testing.assert_array_equal(np.concatenate([got[r][0] for r in range(world)]), np.sort(allk))
+    expect = np.sort(allk)
+    # peer exchange (default on one node) and NCCL all-to-all give the same slices
+    np.testing.assert_array_equal(np.concatenate([got[r][0] for r in range(world)]), expect)
+    np.testing.assert_array_equal(np.concatenate([got[r][5] for r in range(world)]), expect)
+    for s in range(3):
+        allk = np.concatenate([got[r][6][s][0] for r in range(world)])
+        N = allk.size
+        for r in range(world):
+            np.testing.assert_array_equal(got[r][6][s][1], np.sort(allk)[r * N // world:(r + 1) * N // world])
     allx = np.concatenate([got[r][3] for r in range(world)]).astype(np.int64)
     np.testing.assert_array_equal(np.concatenate([got[r][2] for r in range(world)]).astype(np.int64),
                                   np.cumsum(allx))
