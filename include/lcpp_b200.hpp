@@ -1,0 +1,447 @@
+/*
+ * lcpp_b200.hpp -- C++ surface of the B200 sort / scan / reduce library,
+ * shaped like the reference's Device-level classes so that a caller of
+ * lcpp::DeviceRadixSort / DeviceScan / DeviceReduce switches by changing
+ * types, not call sites.  Header-only; every call forwards to the C ABI in
+ * lcpp_b200.h.
+ *
+ * Mapping (reference -> here):
+ *   CommandList& cmdlist            -> lcpp_stream_t stream (a cudaStream_t;
+ *                                      work is enqueued, not recorded)
+ *   BufferView<T>                   -> lcpp_b200::BufferView<T> {T* ptr, size}
+ *   BufferView<uint> temp_storage   -> lcpp_b200::BufferView<uint32_t>
+ *                                      (size in 4-byte words, like the
+ *                                      reference's uint temp buffer)
+ *   DoubleBuffer<T>                 -> lcpp_b200::DoubleBuffer<T> (same
+ *                                      members and selector semantics)
+ *   scan / reduce operators         -> SumOp, MinOp, MaxOp tag types (the
+ *                                      reference's thread_operators.h names;
+ *                                      DSL lambdas have no counterpart)
+ *   LUISA_ASSERT on misuse          -> throws lcpp_b200::Error (status code)
+ *
+ * Reference: src/lcpp/device/device_radix_sort.h:351-554 (temp queries,
+ * SortKeys / SortPairs / ...Descending, DoubleBuffer overloads),
+ * src/lcpp/device/device_scan.h:295-420 (GetTempStorageBytes,
+ * ExclusiveScan / InclusiveScan / InclusiveScanInit / ExclusiveSum /
+ * InclusiveSum), src/lcpp/device/device_reduce.h:183-308
+ * (GetTempStorageBytes, Reduce / Sum / Min / Max),
+ * src/lcpp/common/util_type.h:57-74 (DoubleBuffer).
+ */
+#ifndef LCPP_B200_HPP
+#define LCPP_B200_HPP
+
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <type_traits>
+
+#include "lcpp_b200.h"
+
+namespace lcpp_b200 {
+
+// ---------------------------------------------------------------------------
+// Views, double buffers, operators, errors
+// ---------------------------------------------------------------------------
+template <typename T>
+struct BufferView {
+    T* ptr = nullptr;
+    size_t count = 0;  // elements
+
+    BufferView() = default;
+    BufferView(T* p, size_t n) noexcept : ptr(p), count(n) {}
+    [[nodiscard]] size_t size() const noexcept { return count; }
+    [[nodiscard]] size_t size_bytes() const noexcept { return count * sizeof(T); }
+    [[nodiscard]] T* data() const noexcept { return ptr; }
+    [[nodiscard]] BufferView subview(size_t offset, size_t n) const noexcept { return {ptr + offset, n}; }
+};
+
+template <typename T>
+struct DoubleBuffer {
+    BufferView<T> d_buffer[2];
+    int selector = 0;
+
+    DoubleBuffer() = default;
+    DoubleBuffer(BufferView<T> d_current, BufferView<T> d_alternate) noexcept
+        : d_buffer{d_current, d_alternate}, selector{0}
+    {
+    }
+    [[nodiscard]] BufferView<T> current() const noexcept { return d_buffer[selector]; }
+    [[nodiscard]] BufferView<T> alternate() const noexcept { return d_buffer[selector ^ 1]; }
+};
+
+struct SumOp {};
+struct MinOp {};
+struct MaxOp {};
+
+class Error : public std::runtime_error {
+public:
+    Error(lcpp_status s, const std::string& what)
+        : std::runtime_error(what + ": " + lcpp_status_string(s)), status_(s)
+    {
+    }
+    [[nodiscard]] lcpp_status status() const noexcept { return status_; }
+
+private:
+    lcpp_status status_;
+};
+
+namespace detail {
+
+template <typename T>
+constexpr lcpp_dtype dtype_of()
+{
+    if constexpr (std::is_same_v<T, float>)
+        return LCPP_F32;
+    else if constexpr (std::is_same_v<T, double>)
+        return LCPP_F64;
+    else if constexpr (std::is_integral_v<T> && sizeof(T) == 4)
+        return std::is_signed_v<T> ? LCPP_I32 : LCPP_U32;
+    else if constexpr (std::is_integral_v<T> && sizeof(T) == 8)
+        return std::is_signed_v<T> ? LCPP_I64 : LCPP_U64;
+    else
+        return LCPP_NONE;
+}
+
+template <typename T>
+constexpr lcpp_dtype checked_dtype()
+{
+    constexpr lcpp_dtype d = dtype_of<T>();
+    static_assert(d != LCPP_NONE, "element types: 4- or 8-byte integers, float, double");
+    return d;
+}
+
+template <typename Op>
+constexpr lcpp_op op_of()
+{
+    if constexpr (std::is_same_v<Op, SumOp>)
+        return LCPP_OP_SUM;
+    else if constexpr (std::is_same_v<Op, MinOp>)
+        return LCPP_OP_MIN;
+    else {
+        static_assert(std::is_same_v<Op, MaxOp>, "operators: SumOp, MinOp, MaxOp");
+        return LCPP_OP_MAX;
+    }
+}
+
+inline void check(lcpp_status s, const char* what)
+{
+    if (s != LCPP_OK) throw Error(s, what);
+}
+
+inline void require(bool ok, const char* what)
+{
+    if (!ok) throw Error(LCPP_ERR_INVALID_ARG, what);
+}
+
+inline size_t temp_bytes(BufferView<uint32_t> t) { return t.size_bytes(); }
+
+}  // namespace detail
+
+// ---------------------------------------------------------------------------
+// DeviceRadixSort
+// ---------------------------------------------------------------------------
+class DeviceRadixSort {
+public:
+    /// Temp storage bytes for SortPairs / SortPairsDescending (0 for 0 items).
+    template <typename KeyType, typename ValueType>
+    static size_t GetSortPairsTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_radix_sort_pairs_temp_bytes(detail::checked_dtype<KeyType>(),
+                                                       detail::checked_dtype<ValueType>(), num_items, &b),
+                      "GetSortPairsTempStorageBytes");
+        return b;
+    }
+
+    /// Temp storage bytes for SortKeys / SortKeysDescending (0 for 0 items).
+    template <typename KeyType>
+    static size_t GetSortKeysTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_radix_sort_keys_temp_bytes(detail::checked_dtype<KeyType>(), num_items, &b),
+                      "GetSortKeysTempStorageBytes");
+        return b;
+    }
+
+    template <typename KeyType, typename ValueType>
+    void SortPairs(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<KeyType> d_keys_in,
+                   BufferView<KeyType> d_keys_out, BufferView<ValueType> d_values_in,
+                   BufferView<ValueType> d_values_out, uint64_t num_items, int begin_bit = 0,
+                   int end_bit = sizeof(KeyType) * 8)
+    {
+        pairs(stream, temp_storage, d_keys_in, d_keys_out, d_values_in, d_values_out, num_items, begin_bit, end_bit,
+              0);
+    }
+
+    template <typename KeyType, typename ValueType>
+    void SortPairsDescending(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<KeyType> d_keys_in,
+                             BufferView<KeyType> d_keys_out, BufferView<ValueType> d_values_in,
+                             BufferView<ValueType> d_values_out, uint64_t num_items, int begin_bit = 0,
+                             int end_bit = sizeof(KeyType) * 8)
+    {
+        pairs(stream, temp_storage, d_keys_in, d_keys_out, d_values_in, d_values_out, num_items, begin_bit, end_bit,
+              1);
+    }
+
+    template <typename KeyType>
+    void SortKeys(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<KeyType> d_keys_in,
+                  BufferView<KeyType> d_keys_out, uint64_t num_items, int begin_bit = 0,
+                  int end_bit = sizeof(KeyType) * 8)
+    {
+        keys(stream, temp_storage, d_keys_in, d_keys_out, num_items, begin_bit, end_bit, 0);
+    }
+
+    template <typename KeyType>
+    void SortKeysDescending(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<KeyType> d_keys_in,
+                            BufferView<KeyType> d_keys_out, uint64_t num_items, int begin_bit = 0,
+                            int end_bit = sizeof(KeyType) * 8)
+    {
+        keys(stream, temp_storage, d_keys_in, d_keys_out, num_items, begin_bit, end_bit, 1);
+    }
+
+    // DoubleBuffer overloads: the result ends in d_keys.current() (and
+    // d_values.current()); the selector flips once per 8-bit pass and is
+    // unchanged for zero items or begin_bit == end_bit.
+    template <typename KeyType, typename ValueType>
+    void SortPairs(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, DoubleBuffer<KeyType>& d_keys,
+                   DoubleBuffer<ValueType>& d_values, uint64_t num_items, int begin_bit = 0,
+                   int end_bit = sizeof(KeyType) * 8)
+    {
+        pairs_db(stream, temp_storage, d_keys, d_values, num_items, begin_bit, end_bit, 0);
+    }
+
+    template <typename KeyType, typename ValueType>
+    void SortPairsDescending(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, DoubleBuffer<KeyType>& d_keys,
+                             DoubleBuffer<ValueType>& d_values, uint64_t num_items, int begin_bit = 0,
+                             int end_bit = sizeof(KeyType) * 8)
+    {
+        pairs_db(stream, temp_storage, d_keys, d_values, num_items, begin_bit, end_bit, 1);
+    }
+
+    template <typename KeyType>
+    void SortKeys(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, DoubleBuffer<KeyType>& d_keys,
+                  uint64_t num_items, int begin_bit = 0, int end_bit = sizeof(KeyType) * 8)
+    {
+        keys_db(stream, temp_storage, d_keys, num_items, begin_bit, end_bit, 0);
+    }
+
+    template <typename KeyType>
+    void SortKeysDescending(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, DoubleBuffer<KeyType>& d_keys,
+                            uint64_t num_items, int begin_bit = 0, int end_bit = sizeof(KeyType) * 8)
+    {
+        keys_db(stream, temp_storage, d_keys, num_items, begin_bit, end_bit, 1);
+    }
+
+private:
+    template <typename K, typename V>
+    static void pairs(lcpp_stream_t s, BufferView<uint32_t> t, BufferView<K> ki, BufferView<K> ko, BufferView<V> vi,
+                      BufferView<V> vo, uint64_t n, int b, int e, int desc)
+    {
+        detail::require(ki.size() >= n && ko.size() >= n && vi.size() >= n && vo.size() >= n,
+                        "SortPairs: a key or value view is shorter than num_items");
+        detail::check(lcpp_radix_sort_pairs(t.data(), detail::temp_bytes(t), ki.data(), ko.data(), vi.data(),
+                                            vo.data(), n, b, e, desc, detail::checked_dtype<K>(),
+                                            detail::checked_dtype<V>(), s),
+                      "SortPairs");
+    }
+
+    template <typename K>
+    static void keys(lcpp_stream_t s, BufferView<uint32_t> t, BufferView<K> ki, BufferView<K> ko, uint64_t n, int b,
+                     int e, int desc)
+    {
+        detail::require(ki.size() >= n && ko.size() >= n, "SortKeys: a key view is shorter than num_items");
+        detail::check(lcpp_radix_sort_keys(t.data(), detail::temp_bytes(t), ki.data(), ko.data(), n, b, e, desc,
+                                           detail::checked_dtype<K>(), s),
+                      "SortKeys");
+    }
+
+    template <typename K, typename V>
+    static void pairs_db(lcpp_stream_t s, BufferView<uint32_t> t, DoubleBuffer<K>& kd, DoubleBuffer<V>& vd,
+                         uint64_t n, int b, int e, int desc)
+    {
+        detail::require(kd.d_buffer[0].size() >= n && kd.d_buffer[1].size() >= n && vd.d_buffer[0].size() >= n &&
+                            vd.d_buffer[1].size() >= n,
+                        "SortPairs: a double-buffer view is shorter than num_items");
+        detail::require(kd.selector == vd.selector, "SortPairs: key and value selectors differ");
+        void* kb[2] = {kd.d_buffer[0].data(), kd.d_buffer[1].data()};
+        void* vb[2] = {vd.d_buffer[0].data(), vd.d_buffer[1].data()};
+        int sel = kd.selector;
+        detail::check(lcpp_radix_sort_pairs_double_buffer(t.data(), detail::temp_bytes(t), kb, vb, &sel, n, b, e, desc,
+                                                          detail::checked_dtype<K>(), detail::checked_dtype<V>(), s),
+                      "SortPairs");
+        kd.selector = vd.selector = sel;
+    }
+
+    template <typename K>
+    static void keys_db(lcpp_stream_t s, BufferView<uint32_t> t, DoubleBuffer<K>& kd, uint64_t n, int b, int e,
+                        int desc)
+    {
+        detail::require(kd.d_buffer[0].size() >= n && kd.d_buffer[1].size() >= n,
+                        "SortKeys: a double-buffer view is shorter than num_items");
+        void* kb[2] = {kd.d_buffer[0].data(), kd.d_buffer[1].data()};
+        int sel = kd.selector;
+        detail::check(lcpp_radix_sort_keys_double_buffer(t.data(), detail::temp_bytes(t), kb, &sel, n, b, e, desc,
+                                                         detail::checked_dtype<K>(), s),
+                      "SortKeys");
+        kd.selector = sel;
+    }
+};
+
+// ---------------------------------------------------------------------------
+// DeviceScan
+// ---------------------------------------------------------------------------
+class DeviceScan {
+public:
+    /// Temp storage bytes for ExclusiveScan / InclusiveScan / ExclusiveSum /
+    /// InclusiveSum (0 for 0 items).
+    template <typename T>
+    static size_t GetTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_scan_temp_bytes(detail::checked_dtype<T>(), num_items, &b), "GetTempStorageBytes");
+        return b;
+    }
+
+    template <typename T, typename ScanOp>
+    void ExclusiveScan(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in,
+                       BufferView<T> d_out, uint64_t num_items, ScanOp, T initial_value)
+    {
+        views(d_in, d_out, num_items);
+        detail::check(lcpp_scan_exclusive(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                          d_out.data(), num_items, detail::op_of<ScanOp>(), &initial_value,
+                                          detail::checked_dtype<T>(), stream),
+                      "ExclusiveScan");
+    }
+
+    /// Inclusive scan without an initial value (CUB semantics).
+    template <typename T, typename ScanOp>
+    void InclusiveScan(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in,
+                       BufferView<T> d_out, uint64_t num_items, ScanOp)
+    {
+        views(d_in, d_out, num_items);
+        detail::check(lcpp_scan_inclusive(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                          d_out.data(), num_items, detail::op_of<ScanOp>(),
+                                          detail::checked_dtype<T>(), stream),
+                      "InclusiveScan");
+    }
+
+    /// Inclusive scan with the initial value folded in front.
+    template <typename T, typename ScanOp>
+    void InclusiveScan(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in,
+                       BufferView<T> d_out, uint64_t num_items, ScanOp op, T initial_value)
+    {
+        InclusiveScanInit(stream, temp_storage, d_in, d_out, num_items, op, initial_value);
+    }
+
+    template <typename T, typename ScanOp>
+    void InclusiveScanInit(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in,
+                           BufferView<T> d_out, uint64_t num_items, ScanOp, T initial_value)
+    {
+        views(d_in, d_out, num_items);
+        detail::check(lcpp_scan_inclusive_init(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                               d_out.data(), num_items, detail::op_of<ScanOp>(), &initial_value,
+                                               detail::checked_dtype<T>(), stream),
+                      "InclusiveScanInit");
+    }
+
+    template <typename T>
+    void ExclusiveSum(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in,
+                      BufferView<T> d_out, uint64_t num_items)
+    {
+        views(d_in, d_out, num_items);
+        detail::check(lcpp_scan_exclusive_sum(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                              d_out.data(), num_items, detail::checked_dtype<T>(), stream),
+                      "ExclusiveSum");
+    }
+
+    template <typename T>
+    void InclusiveSum(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in,
+                      BufferView<T> d_out, uint64_t num_items)
+    {
+        views(d_in, d_out, num_items);
+        detail::check(lcpp_scan_inclusive_sum(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                              d_out.data(), num_items, detail::checked_dtype<T>(), stream),
+                      "InclusiveSum");
+    }
+
+private:
+    template <typename T>
+    static void views(BufferView<T> i, BufferView<T> o, uint64_t n)
+    {
+        detail::require(i.size() >= n && o.size() >= n, "DeviceScan: a view is shorter than num_items");
+    }
+};
+
+// ---------------------------------------------------------------------------
+// DeviceReduce
+// ---------------------------------------------------------------------------
+class DeviceReduce {
+public:
+    /// Temp storage bytes for Reduce / Sum / Min / Max.
+    template <typename T>
+    static size_t GetTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_reduce_temp_bytes(detail::checked_dtype<T>(), num_items, &b), "GetTempStorageBytes");
+        return b;
+    }
+
+    /// d_out[0] = initial_value op d_in[0] op ... (initial_value alone for 0 items).
+    template <typename T, typename ReduceOp>
+    void Reduce(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in, BufferView<T> d_out,
+                uint64_t num_items, ReduceOp, T initial_value)
+    {
+        views(d_in, d_out, num_items);
+        detail::check(lcpp_reduce(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(), d_out.data(),
+                                  num_items, detail::op_of<ReduceOp>(), &initial_value, detail::checked_dtype<T>(),
+                                  stream),
+                      "Reduce");
+    }
+
+    template <typename T>
+    void Sum(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in, BufferView<T> d_out,
+             uint64_t num_items)
+    {
+        views(d_in, d_out, num_items);
+        detail::check(lcpp_reduce_sum(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                      d_out.data(), num_items, detail::checked_dtype<T>(), stream),
+                      "Sum");
+    }
+
+    template <typename T>
+    void Min(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in, BufferView<T> d_out,
+             uint64_t num_items)
+    {
+        views(d_in, d_out, num_items);
+        detail::check(lcpp_reduce_min(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                      d_out.data(), num_items, detail::checked_dtype<T>(), stream),
+                      "Min");
+    }
+
+    template <typename T>
+    void Max(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in, BufferView<T> d_out,
+             uint64_t num_items)
+    {
+        views(d_in, d_out, num_items);
+        detail::check(lcpp_reduce_max(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                      d_out.data(), num_items, detail::checked_dtype<T>(), stream),
+                      "Max");
+    }
+
+private:
+    template <typename T>
+    static void views(BufferView<T> i, BufferView<T> o, uint64_t n)
+    {
+        detail::require(i.size() >= n && o.size() >= 1, "DeviceReduce: the input view is shorter than num_items "
+                                                        "or the output view is empty");
+    }
+};
+
+/// Words of a uint32 temp buffer that hold `bytes` (the reference's
+/// bytes_to_uint_count).
+inline size_t bytes_to_uint_count(size_t bytes) { return (bytes + 3) / 4; }
+
+}  // namespace lcpp_b200
+
+#endif /* LCPP_B200_HPP */

@@ -1,0 +1,264 @@
+// C++ caller of include/lcpp_b200.hpp, written like the reference's own
+// tests (tests/device_radix_sort_one_sweep.cpp, tests/device_scan_test.cpp,
+// tests/device_reduce_test.cpp): device results against std:: host
+// algorithms.  Built and run by tests/test_cpp_api.py on a GPU box; also
+// compiled (not run) on the CPU.  Prints "OK <checks>" and exits 0 on success.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstdio>
+#include <limits>
+#include <numeric>
+#include <random>
+#include <vector>
+
+#include "lcpp_b200.hpp"
+
+using namespace lcpp_b200;
+
+namespace {
+
+int g_checks = 0;
+
+#define CHECK(cond)                                                                  \
+    do {                                                                             \
+        ++g_checks;                                                                  \
+        if (!(cond)) {                                                               \
+            std::fprintf(stderr, "FAILED %s at %s:%d\n", #cond, __FILE__, __LINE__); \
+            std::exit(1);                                                            \
+        }                                                                            \
+    } while (0)
+
+#define CUDA(call) CHECK((call) == cudaSuccess)
+
+template <typename T>
+struct DeviceArray {
+    T* p = nullptr;
+    size_t n = 0;
+    explicit DeviceArray(size_t count) : n(count) { CUDA(cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T))); }
+    ~DeviceArray() { cudaFree(p); }
+    BufferView<T> view() const { return {p, n}; }
+    void upload(const std::vector<T>& h) { CUDA(cudaMemcpy(p, h.data(), h.size() * sizeof(T), cudaMemcpyHostToDevice)); }
+    std::vector<T> download() const
+    {
+        std::vector<T> h(n);
+        CUDA(cudaMemcpy(h.data(), p, n * sizeof(T), cudaMemcpyDeviceToHost));
+        return h;
+    }
+};
+
+DeviceArray<uint32_t> temp_for(size_t bytes) { return DeviceArray<uint32_t>(bytes_to_uint_count(bytes)); }
+
+void sort_keys_float(lcpp_stream_t s)
+{
+    // device_radix_sort_one_sweep.cpp: float keys U[0,1), mt19937(114521), asc and desc
+    for (size_t n : {size_t(1) << 5, size_t(1) << 16, size_t(1) << 20}) {
+        std::mt19937 rng(114521);
+        std::uniform_real_distribution<float> dist(0.f, 1.f);
+        std::vector<float> h(n);
+        for (auto& x : h) x = dist(rng);
+        DeviceArray<float> in(n), out(n);
+        in.upload(h);
+        auto temp = temp_for(DeviceRadixSort::GetSortKeysTempStorageBytes<float>(n));
+        DeviceRadixSort rs;
+        rs.SortKeys(s, temp.view(), in.view(), out.view(), n);
+        CUDA(cudaStreamSynchronize(s));
+        auto expect = h;
+        std::sort(expect.begin(), expect.end());
+        CHECK(out.download() == expect);
+        rs.SortKeysDescending(s, temp.view(), in.view(), out.view(), n);
+        CUDA(cudaStreamSynchronize(s));
+        std::sort(expect.begin(), expect.end(), std::greater<float>());
+        CHECK(out.download() == expect);
+    }
+}
+
+void sort_pairs_shuffled(lcpp_stream_t s)
+{
+    // shuffled permutation keys with float values, asc and desc
+    const size_t n = 524288;
+    std::vector<uint32_t> keys(n);
+    std::iota(keys.begin(), keys.end(), 0u);
+    std::shuffle(keys.begin(), keys.end(), std::mt19937(114521));
+    std::vector<float> vals(n);
+    for (size_t i = 0; i < n; ++i) vals[i] = float(keys[i]) * 0.5f;
+    DeviceArray<uint32_t> ki(n), ko(n);
+    DeviceArray<float> vi(n), vo(n);
+    ki.upload(keys);
+    vi.upload(vals);
+    auto temp = temp_for(DeviceRadixSort::GetSortPairsTempStorageBytes<uint32_t, float>(n));
+    DeviceRadixSort rs;
+    for (int desc = 0; desc < 2; ++desc) {
+        if (desc)
+            rs.SortPairsDescending(s, temp.view(), ki.view(), ko.view(), vi.view(), vo.view(), n);
+        else
+            rs.SortPairs(s, temp.view(), ki.view(), ko.view(), vi.view(), vo.view(), n);
+        CUDA(cudaStreamSynchronize(s));
+        auto k = ko.download();
+        auto v = vo.download();
+        for (size_t i = 0; i < n; ++i) {
+            CHECK(k[i] == (desc ? uint32_t(n - 1 - i) : uint32_t(i)));
+            CHECK(v[i] == float(k[i]) * 0.5f);
+            if (!(k[i] == (desc ? uint32_t(n - 1 - i) : uint32_t(i)))) break;
+        }
+    }
+}
+
+void sort_bits_stable_double_buffer(lcpp_stream_t s)
+{
+    // device_radix_sort_interface_test.cpp: 257 keys, bits [1,6), stable; DoubleBuffer selector
+    const size_t n = 257;
+    std::vector<uint32_t> keys(n), idx(n);
+    for (size_t i = 0; i < n; ++i) {
+        keys[i] = uint32_t(((i * 53) % 64) | (((i * 17) % 11) << 8));
+        idx[i] = uint32_t(i);
+    }
+    std::vector<size_t> order(n);
+    std::iota(order.begin(), order.end(), 0);
+    auto bits = [](uint32_t k) { return (k >> 1) & 31u; };
+    std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return bits(keys[a]) < bits(keys[b]); });
+    DeviceArray<uint32_t> k0(n), k1(n), v0(n), v1(n);
+    k0.upload(keys);
+    v0.upload(idx);
+    DoubleBuffer<uint32_t> dk(k0.view(), k1.view());
+    DoubleBuffer<uint32_t> dv(v0.view(), v1.view());
+    auto temp = temp_for(DeviceRadixSort::GetSortPairsTempStorageBytes<uint32_t, uint32_t>(n));
+    DeviceRadixSort rs;
+    rs.SortPairs(s, temp.view(), dk, dv, n, 1, 6);
+    CUDA(cudaStreamSynchronize(s));
+    CHECK(dk.selector == 1 && dv.selector == 1);  // one 5-bit pass
+    const auto& kc = dk.selector ? k1 : k0;
+    const auto& vc = dv.selector ? v1 : v0;
+    auto k = kc.download();
+    auto v = vc.download();
+    for (size_t i = 0; i < n; ++i) {
+        CHECK(v[i] == uint32_t(order[i]));
+        CHECK(k[i] == keys[order[i]]);
+    }
+    // zero-width range: selector unchanged
+    rs.SortKeys(s, temp.view(), dk, n, 3, 3);
+    CHECK(dk.selector == 1);
+}
+
+void scans(lcpp_stream_t s)
+{
+    // device_scan_test.cpp: (i % 7) - 3 at 320*25*3+17 items; wrapping int arithmetic
+    const size_t n = 320 * 25 * 3 + 17;
+    std::vector<int32_t> h(n);
+    for (size_t i = 0; i < n; ++i) h[i] = int32_t(i % 7) - 3;
+    DeviceArray<int32_t> in(n), out(n);
+    in.upload(h);
+    auto temp = temp_for(DeviceScan::GetTempStorageBytes<int32_t>(n));
+    DeviceScan sc;
+    std::vector<int32_t> expect(n);
+    sc.InclusiveSum(s, temp.view(), in.view(), out.view(), n);
+    CUDA(cudaStreamSynchronize(s));
+    std::inclusive_scan(h.begin(), h.end(), expect.begin());
+    CHECK(out.download() == expect);
+    sc.ExclusiveSum(s, temp.view(), in.view(), out.view(), n);
+    CUDA(cudaStreamSynchronize(s));
+    std::exclusive_scan(h.begin(), h.end(), expect.begin(), 0);
+    CHECK(out.download() == expect);
+    sc.InclusiveScanInit(s, temp.view(), in.view(), out.view(), n, SumOp{}, int32_t(100));
+    CUDA(cudaStreamSynchronize(s));
+    std::inclusive_scan(h.begin(), h.end(), expect.begin(), std::plus<int32_t>(), 100);
+    CHECK(out.download() == expect);
+    sc.ExclusiveScan(s, temp.view(), in.view(), out.view(), n, MaxOp{}, std::numeric_limits<int32_t>::lowest());
+    CUDA(cudaStreamSynchronize(s));
+    int32_t run = std::numeric_limits<int32_t>::lowest();
+    for (size_t i = 0; i < n; ++i) {
+        expect[i] = run;
+        run = std::max(run, h[i]);
+    }
+    CHECK(out.download() == expect);
+    sc.InclusiveScan(s, temp.view(), in.view(), out.view(), n, MinOp{});
+    CUDA(cudaStreamSynchronize(s));
+    run = std::numeric_limits<int32_t>::max();
+    for (size_t i = 0; i < n; ++i) expect[i] = run = std::min(run, h[i]);
+    CHECK(out.download() == expect);
+}
+
+void reductions(lcpp_stream_t s)
+{
+    // device_reduce_test.cpp: ones at 2^k + 1; float max identity on empty input
+    for (int k : {0, 10, 20}) {
+        const size_t n = (size_t(1) << k) + 1;
+        std::vector<int32_t> h(n, 1);
+        DeviceArray<int32_t> in(n), out(1);
+        in.upload(h);
+        auto temp = temp_for(DeviceReduce::GetTempStorageBytes<int32_t>(n));
+        DeviceReduce rd;
+        rd.Sum(s, temp.view(), in.view(), out.view(), n);
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(out.download()[0] == int32_t(n));
+    }
+    {
+        DeviceArray<float> in(1), out(1);
+        auto temp = temp_for(std::max<size_t>(DeviceReduce::GetTempStorageBytes<float>(0), 4));
+        DeviceReduce rd;
+        rd.Max(s, temp.view(), in.view(), out.view(), 0);
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(out.download()[0] == std::numeric_limits<float>::lowest());
+    }
+    {
+        const size_t n = 1000003;
+        std::vector<int64_t> h(n);
+        std::mt19937_64 rng(7);
+        for (auto& x : h) x = int64_t(rng());
+        DeviceArray<int64_t> in(n), out(1);
+        in.upload(h);
+        auto temp = temp_for(DeviceReduce::GetTempStorageBytes<int64_t>(n));
+        DeviceReduce rd;
+        rd.Reduce(s, temp.view(), in.view(), out.view(), n, MinOp{}, std::numeric_limits<int64_t>::max());
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(out.download()[0] == *std::min_element(h.begin(), h.end()));
+    }
+}
+
+void misuse_throws(lcpp_stream_t s)
+{
+    DeviceArray<uint32_t> a(16), b(16);
+    auto temp = temp_for(DeviceRadixSort::GetSortKeysTempStorageBytes<uint32_t>(16));
+    DeviceRadixSort rs;
+    bool threw = false;
+    try {
+        rs.SortKeys(s, temp.view(), a.view(), b.view(), 16, 4, 40);  // end_bit past the key
+    } catch (const Error& e) {
+        threw = e.status() == LCPP_ERR_INVALID_ARG;
+    }
+    CHECK(threw);
+    threw = false;
+    try {
+        rs.SortKeys(s, temp.view().subview(0, 1), a.view(), b.view(), 16);  // temp too small
+    } catch (const Error& e) {
+        threw = e.status() == LCPP_ERR_TEMP_TOO_SMALL;
+    }
+    CHECK(threw);
+    threw = false;
+    try {
+        rs.SortKeys(s, temp.view(), a.view(), b.view().subview(0, 8), 16);  // output view too short
+    } catch (const Error& e) {
+        threw = e.status() == LCPP_ERR_INVALID_ARG;
+    }
+    CHECK(threw);
+    CHECK(DeviceRadixSort::GetSortKeysTempStorageBytes<uint32_t>(0) == 0);
+}
+
+}  // namespace
+
+int main()
+{
+    cudaStream_t stream;
+    CUDA(cudaStreamCreate(&stream));
+    const auto s = reinterpret_cast<lcpp_stream_t>(stream);
+    sort_keys_float(s);
+    sort_pairs_shuffled(s);
+    sort_bits_stable_double_buffer(s);
+    scans(s);
+    reductions(s);
+    misuse_throws(s);
+    CUDA(cudaStreamDestroy(stream));
+    std::printf("OK %d\n", g_checks);
+    return 0;
+}

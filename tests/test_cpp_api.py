@@ -1,0 +1,42 @@
+"""The C++ surface (include/lcpp_b200.hpp): compiled on the CPU; on a GPU the
+C++ test program (tests/cpp/device_api_test.cpp, written like the
+reference's own tests) is built against the library and run."""
+from __future__ import annotations
+
+import shutil
+import subprocess
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+SRC = ROOT / "tests" / "cpp" / "device_api_test.cpp"
+CUDA = Path("/usr/local/cuda")
+LIBDIR = ROOT / "luisacompute-parallelprimitive_b200" / "lcpp_b200"
+
+
+def _gxx():
+    gxx = shutil.which("g++")
+    if gxx is None or not (CUDA / "include" / "cuda_runtime.h").exists():
+        pytest.skip("g++ or the CUDA headers are missing")
+    return gxx
+
+
+def test_header_compiles_cleanly():
+    gxx = _gxx()
+    r = subprocess.run([gxx, "-std=c++17", "-fsyntax-only", "-Wall", "-Wextra", "-Werror", f"-I{ROOT / 'include'}",
+                        f"-I{CUDA / 'include'}", str(SRC)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
+@pytest.mark.gpu
+def test_cpp_program_runs(tmp_path):
+    gxx = _gxx()
+    exe = tmp_path / "device_api_test"
+    r = subprocess.run([gxx, "-std=c++17", "-O2", f"-I{ROOT / 'include'}", f"-I{CUDA / 'include'}", str(SRC),
+                        "-o", str(exe), f"-L{LIBDIR}", "-llcpp_b200", f"-L{CUDA / 'lib64'}", "-lcudart",
+                        f"-Wl,-rpath,{LIBDIR}", f"-Wl,-rpath,{CUDA / 'lib64'}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert run.stdout.startswith("OK "), run.stdout
