@@ -40,6 +40,17 @@ lcpp_status lcpp_dist_merge_temp_bytes(uint64_t total, size_t* temp_bytes);
 lcpp_status lcpp_dist_merge_sorted(void* temp, size_t temp_bytes, const void* a, uint64_t na, const void* b,
                                    uint64_t nb, void* out, lcpp_dtype key_dtype, lcpp_stream_t stream);
 
+/* Batched form: `count` (1..LCPP_MERGE_BATCH_MAX) independent merges
+ * out[i] = merge(a[i][0, na[i]), b[i][0, nb[i])) in one split launch and one
+ * merge launch (one level of a merge tree).  Same ordering, overlap and
+ * alignment rules as lcpp_dist_merge_sorted; the runs may live in another
+ * GPU's memory (pointers from lcpp_dist_ipc_open). */
+#define LCPP_MERGE_BATCH_MAX 32
+lcpp_status lcpp_dist_merge_batch_temp_bytes(int count, const uint64_t* na, const uint64_t* nb, size_t* temp_bytes);
+lcpp_status lcpp_dist_merge_sorted_batch(void* temp, size_t temp_bytes, int count, const void* const* a,
+                                         const uint64_t* na, const void* const* b, const uint64_t* nb,
+                                         void* const* out, lcpp_dtype key_dtype, lcpp_stream_t stream);
+
 /* Exchange buffers shared between the processes of one node (CUDA IPC), so
  * that a rank's merge kernel reads the sorted runs of the other ranks straight
  * from their memory over NVLink (plain loads).  Set-up calls, not hot-path

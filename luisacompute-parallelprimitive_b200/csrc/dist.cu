@@ -96,14 +96,41 @@ __device__ __forceinline__ uint64_t co_rank(uint64_t o, uint64_t na, uint64_t nb
     return lo;
 }
 
+// A batch of independent merges (one level of a merge tree), passed by value.
 template <typename U>
-__global__ void merge_split_kernel(const U* __restrict__ a, uint64_t na, const U* __restrict__ b, uint64_t nb,
-                                   uint64_t* __restrict__ splits, uint64_t nsplits, KeyCodec<U> codec)
+struct MergeBatch {
+    int count;
+    uint64_t block_start[LCPP_MERGE_BATCH_MAX + 1];  // first output block of each merge (prefix sums)
+    uint64_t split_start[LCPP_MERGE_BATCH_MAX + 1];  // first split entry of each merge (blocks + 1 each)
+    const U* a[LCPP_MERGE_BATCH_MAX];
+    const U* b[LCPP_MERGE_BATCH_MAX];
+    U* out[LCPP_MERGE_BATCH_MAX];
+    uint64_t na[LCPP_MERGE_BATCH_MAX];
+    uint64_t nb[LCPP_MERGE_BATCH_MAX];
+};
+
+// Merge of an index (a block or a split entry) in a prefix-sum table.
+__device__ __forceinline__ int batch_slot(const uint64_t* start, int count, uint64_t idx)
 {
-    const uint64_t k = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (k >= nsplits) return;
+    int m = 0;
+    while (m + 1 < count && start[m + 1] <= idx) ++m;
+    return m;
+}
+
+// Split points: for merge m and output block k, the number of a-keys among
+// its first k * kMergeTile outputs (ties: a first).
+template <typename U>
+__global__ void merge_split_kernel(const MergeBatch<U> mb, uint64_t* __restrict__ splits, KeyCodec<U> codec)
+{
+    const uint64_t e = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= mb.split_start[mb.count]) return;
+    const int m = batch_slot(mb.split_start, mb.count, e);
+    const uint64_t k = e - mb.split_start[m];
+    const uint64_t na = mb.na[m], nb = mb.nb[m];
+    const U* a = mb.a[m];
+    const U* b = mb.b[m];
     const uint64_t o = min(k * kMergeTile, na + nb);
-    splits[k] = co_rank<U>(o, na, nb, [&](uint64_t i) { return key_image(a[i], codec); },
+    splits[e] = co_rank<U>(o, na, nb, [&](uint64_t i) { return key_image(a[i], codec); },
                            [&](uint64_t j) { return key_image(b[j], codec); });
 }
 
@@ -124,15 +151,20 @@ __device__ __forceinline__ U merge_image(U k, const KeyCodec<U>& c)
 // with one shared-memory load per output, then the tile is stored coalesced.
 template <typename U, bool PLAIN>
 __global__ void __launch_bounds__(kMergeBlock)
-merge_block_kernel(const U* __restrict__ a, uint64_t na, const U* __restrict__ b, uint64_t nb,
-                   const uint64_t* __restrict__ splits, U* __restrict__ out, KeyCodec<U> codec)
+merge_block_kernel(const MergeBatch<U> mb, const uint64_t* __restrict__ all_splits, KeyCodec<U> codec)
 {
     __shared__ U s[kMergeTile];
     const int tid = threadIdx.x;
-    const uint64_t total = na + nb;
-    const uint64_t o0 = uint64_t(blockIdx.x) * kMergeTile;
+    const int m = batch_slot(mb.block_start, mb.count, blockIdx.x);
+    const uint64_t blk = blockIdx.x - mb.block_start[m];
+    const U* __restrict__ a = mb.a[m];
+    const U* __restrict__ b = mb.b[m];
+    U* __restrict__ out = mb.out[m];
+    const uint64_t* splits = all_splits + mb.split_start[m];
+    const uint64_t total = mb.na[m] + mb.nb[m];
+    const uint64_t o0 = blk * kMergeTile;
     const uint64_t o1 = min(o0 + kMergeTile, total);
-    const uint64_t i0 = splits[blockIdx.x], i1 = splits[blockIdx.x + 1];
+    const uint64_t i0 = splits[blk], i1 = splits[blk + 1];
     const uint64_t j0 = o0 - i0, j1 = o1 - i1;
     const int la = int(i1 - i0), lb = int(j1 - j0), len = int(o1 - o0);
     // Gather: all of a thread's loads are issued before any is stored, so
@@ -203,52 +235,104 @@ inline uint64_t merge_blocks(uint64_t total) { return ceil_div(total, kMergeTile
 }  // namespace dist
 }  // namespace lcpp
 
-extern "C" lcpp_status lcpp_dist_merge_temp_bytes(uint64_t total, size_t* temp_bytes)
+namespace lcpp {
+namespace dist {
+namespace {
+
+// Split entries (blocks + 1) of every merge of a batch, in order.
+bool batch_layout(int count, const uint64_t* na, const uint64_t* nb, uint64_t* block_start, uint64_t* split_start)
 {
-    if (!temp_bytes) return LCPP_ERR_INVALID_ARG;
-    *temp_bytes = total ? lcpp::align_up(size_t(lcpp::dist::merge_blocks(total) + 1) * 8, lcpp::kTempAlign) : 0;
+    block_start[0] = split_start[0] = 0;
+    for (int m = 0; m < count; ++m) {
+        const uint64_t blocks = merge_blocks(na[m] + nb[m]);
+        block_start[m + 1] = block_start[m] + blocks;
+        split_start[m + 1] = split_start[m] + blocks + 1;
+    }
+    return block_start[count] <= 0x7fffffffull && split_start[count] <= 0x7fffffffull * 256;
+}
+
+}  // namespace
+}  // namespace dist
+}  // namespace lcpp
+
+extern "C" lcpp_status lcpp_dist_merge_batch_temp_bytes(int count, const uint64_t* na, const uint64_t* nb,
+                                                        size_t* temp_bytes)
+{
+    using namespace lcpp;
+    if (!temp_bytes || count < 0 || count > LCPP_MERGE_BATCH_MAX || (count && (!na || !nb)))
+        return LCPP_ERR_INVALID_ARG;
+    uint64_t bs[LCPP_MERGE_BATCH_MAX + 1], ss[LCPP_MERGE_BATCH_MAX + 1];
+    if (!dist::batch_layout(count, na, nb, bs, ss)) return LCPP_ERR_INVALID_ARG;
+    *temp_bytes = count ? align_up(size_t(ss[count]) * 8, kTempAlign) : 0;
     return LCPP_OK;
 }
 
-extern "C" lcpp_status lcpp_dist_merge_sorted(void* temp, size_t temp_bytes, const void* a, uint64_t na,
-                                              const void* b, uint64_t nb, void* out, lcpp_dtype key_dtype,
-                                              lcpp_stream_t stream)
+extern "C" lcpp_status lcpp_dist_merge_sorted_batch(void* temp, size_t temp_bytes, int count, const void* const* a,
+                                                    const uint64_t* na, const void* const* b, const uint64_t* nb,
+                                                    void* const* out, lcpp_dtype key_dtype, lcpp_stream_t stream)
 {
     using namespace lcpp;
     using namespace lcpp::dist;
     const int kb = dtype_bytes(key_dtype);
     if (!kb) return LCPP_ERR_UNSUPPORTED_DTYPE;
-    const uint64_t total = na + nb;
-    if (total == 0) return LCPP_OK;
-    if (!out || (na && !a) || (nb && !b)) return LCPP_ERR_INVALID_ARG;
+    if (count < 0 || count > LCPP_MERGE_BATCH_MAX) return LCPP_ERR_INVALID_ARG;
+    if (count == 0) return LCPP_OK;
+    if (!a || !na || !b || !nb || !out) return LCPP_ERR_INVALID_ARG;
+    uint64_t grand = 0;
+    for (int m = 0; m < count; ++m) {
+        if ((na[m] && !a[m]) || (nb[m] && !b[m]) || (na[m] + nb[m] && !out[m])) return LCPP_ERR_INVALID_ARG;
+        grand += na[m] + nb[m];
+    }
+    if (grand == 0) return LCPP_OK;
     size_t need = 0;
-    lcpp_dist_merge_temp_bytes(total, &need);
+    lcpp_status st = lcpp_dist_merge_batch_temp_bytes(count, na, nb, &need);
+    if (st != LCPP_OK) return st;
     if (!temp || (reinterpret_cast<uintptr_t>(temp) & (kTempAlign - 1))) return LCPP_ERR_INVALID_ARG;
     if (temp_bytes < need) return LCPP_ERR_TEMP_TOO_SMALL;
-    const uint64_t blocks = merge_blocks(total);
-    if (blocks + 1 > 0x7fffffffull * 256) return LCPP_ERR_INVALID_ARG;
     uint64_t* splits = static_cast<uint64_t*>(temp);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    const unsigned sgrid = unsigned(ceil_div(blocks + 1, 256));
     const bool plain = key_dtype == LCPP_U32 || key_dtype == LCPP_U64;
     auto go = [&](auto tag) {
         using U = decltype(tag);
+        MergeBatch<U> mb{};
+        mb.count = count;
+        batch_layout(count, na, nb, mb.block_start, mb.split_start);
+        for (int m = 0; m < count; ++m) {
+            mb.a[m] = static_cast<const U*>(a[m]);
+            mb.b[m] = static_cast<const U*>(b[m]);
+            mb.out[m] = static_cast<U*>(out[m]);
+            mb.na[m] = na[m];
+            mb.nb[m] = nb[m];
+        }
         const auto c = make_codec<U>(key_dtype, false);
-        const U* pa = static_cast<const U*>(a);
-        const U* pb = static_cast<const U*>(b);
-        merge_split_kernel<U><<<sgrid, 256, 0, s>>>(pa, na, pb, nb, splits, blocks + 1, c);
+        const unsigned sgrid = unsigned(ceil_div(mb.split_start[count], 256));
+        merge_split_kernel<U><<<sgrid, 256, 0, s>>>(mb, splits, c);
+        const unsigned grid = unsigned(mb.block_start[count]);
+        if (grid == 0) return;
         if (plain)
-            merge_block_kernel<U, true><<<unsigned(blocks), kMergeBlock, 0, s>>>(pa, na, pb, nb, splits,
-                                                                              static_cast<U*>(out), c);
+            merge_block_kernel<U, true><<<grid, kMergeBlock, 0, s>>>(mb, splits, c);
         else
-            merge_block_kernel<U, false><<<unsigned(blocks), kMergeBlock, 0, s>>>(pa, na, pb, nb, splits,
-                                                                               static_cast<U*>(out), c);
+            merge_block_kernel<U, false><<<grid, kMergeBlock, 0, s>>>(mb, splits, c);
     };
     if (kb == 4)
         go(uint32_t{});
     else
         go(uint64_t{});
     return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;
+}
+
+extern "C" lcpp_status lcpp_dist_merge_temp_bytes(uint64_t total, size_t* temp_bytes)
+{
+    if (!temp_bytes) return LCPP_ERR_INVALID_ARG;
+    const uint64_t zero = 0;
+    return lcpp_dist_merge_batch_temp_bytes(total ? 1 : 0, &total, &zero, temp_bytes);
+}
+
+extern "C" lcpp_status lcpp_dist_merge_sorted(void* temp, size_t temp_bytes, const void* a, uint64_t na,
+                                              const void* b, uint64_t nb, void* out, lcpp_dtype key_dtype,
+                                              lcpp_stream_t stream)
+{
+    return lcpp_dist_merge_sorted_batch(temp, temp_bytes, 1, &a, &na, &b, &nb, &out, key_dtype, stream);
 }
 
 // ---------------------------------------------------------------------------

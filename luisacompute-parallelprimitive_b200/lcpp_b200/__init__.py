@@ -88,6 +88,9 @@ def lib() -> ctypes.CDLL:
         "lcpp_dist_search_sorted": ([vp, u64, vp, u64, i, vp, i, vp], i),
         "lcpp_dist_merge_temp_bytes": ([u64, szp], i),
         "lcpp_dist_merge_sorted": ([vp, sz, vp, u64, vp, u64, vp, i, vp], i),
+        "lcpp_dist_merge_batch_temp_bytes": ([i, ctypes.POINTER(u64), ctypes.POINTER(u64), szp], i),
+        "lcpp_dist_merge_sorted_batch": ([vp, sz, i, ctypes.POINTER(vp), ctypes.POINTER(u64), ctypes.POINTER(vp),
+                                          ctypes.POINTER(u64), ctypes.POINTER(vp), i, vp], i),
         "lcpp_dist_ipc_alloc": ([sz, ctypes.POINTER(ctypes.c_void_p), vp], i),
         "lcpp_dist_ipc_open": ([vp, ctypes.POINTER(ctypes.c_void_p)], i),
         "lcpp_dist_ipc_close": ([vp], i),

@@ -114,20 +114,35 @@ class GpuOps:
             ctypes.c_void_p(out_ptr), n, 0, keys.element_size() * 8, 0, code,
             ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)), "lcpp_radix_sort_keys")
 
-    def merge_ptrs(self, a_ptr, na, b_ptr, nb, out_ptr, code):
-        """Stable merge of two sorted runs given as device pointers (local or
-        mapped from a peer)."""
-        total = na + nb
-        if total == 0:
+    def merge_batch(self, items, code):
+        """One merge level: items = [(a_ptr, na, b_ptr, nb, out_ptr), ...],
+        stable merges of sorted runs given as device pointers (local or mapped
+        from a peer), all in one split launch and one merge launch (per 32)."""
+        items = [it for it in items if it[1] + it[3] > 0]
+        stream = ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)
+        for c0 in range(0, len(items), 32):
+            chunk = items[c0:c0 + 32]
+            k = len(chunk)
+            pa = (ctypes.c_void_p * k)(*[it[0] for it in chunk])
+            na = (ctypes.c_uint64 * k)(*[it[1] for it in chunk])
+            pb = (ctypes.c_void_p * k)(*[it[2] for it in chunk])
+            nb = (ctypes.c_uint64 * k)(*[it[3] for it in chunk])
+            po = (ctypes.c_void_p * k)(*[it[4] for it in chunk])
+            nbytes = ctypes.c_size_t(0)
+            check(lib().lcpp_dist_merge_batch_temp_bytes(k, na, nb, ctypes.byref(nbytes)),
+                  "lcpp_dist_merge_batch_temp_bytes")
+            temp = self._temp("merge", nbytes.value)
+            self.launches += 2
+            check(lib().lcpp_dist_merge_sorted_batch(ctypes.c_void_p(temp.data_ptr()), temp.numel(), k, pa, na, pb,
+                                                     nb, po, code, stream), "lcpp_dist_merge_sorted_batch")
+
+    def merge_level(self, pairs):
+        """pairs = [(a, b, out), ...] of tensors (b may be None: copy a)."""
+        if not pairs:
             return
-        nbytes = ctypes.c_size_t(0)
-        check(lib().lcpp_dist_merge_temp_bytes(total, ctypes.byref(nbytes)), "lcpp_dist_merge_temp_bytes")
-        temp = self._temp("merge", nbytes.value)
-        self.launches += 2
-        check(lib().lcpp_dist_merge_sorted(
-            ctypes.c_void_p(temp.data_ptr()), temp.numel(), ctypes.c_void_p(a_ptr), na, ctypes.c_void_p(b_ptr), nb,
-            ctypes.c_void_p(out_ptr), code, ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)),
-            "lcpp_dist_merge_sorted")
+        self.merge_batch([(a.data_ptr(), a.numel(), b.data_ptr() if b is not None else 0,
+                           b.numel() if b is not None else 0, o.data_ptr()) for a, b, o in pairs],
+                         dtype_code(pairs[0][0]))
 
     def peer_capable(self, dist):
         """Whether every pair of ranks shares a node and has GPU peer access
@@ -169,18 +184,7 @@ class GpuOps:
 
     def merge(self, a, b, out):
         """out[:a.numel() + b.numel()] = stable merge of sorted runs a, b."""
-        torch = self.torch
-        total = a.numel() + b.numel()
-        if total == 0:
-            return
-        nbytes = ctypes.c_size_t(0)
-        check(lib().lcpp_dist_merge_temp_bytes(total, ctypes.byref(nbytes)), "lcpp_dist_merge_temp_bytes")
-        temp = self._temp("merge", nbytes.value)
-        self.launches += 2
-        check(lib().lcpp_dist_merge_sorted(
-            ctypes.c_void_p(temp.data_ptr()), temp.numel(), ctypes.c_void_p(a.data_ptr()), a.numel(),
-            ctypes.c_void_p(b.data_ptr()), b.numel(), ctypes.c_void_p(out.data_ptr()), dtype_code(a),
-            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "lcpp_dist_merge_sorted")
+        self.merge_level([(a, b, out)])
 
     def empty_like(self, t):
         return self.torch.empty_like(t)
@@ -379,20 +383,22 @@ def distributed_sort_keys(keys_local, dist, ops=None, exchange="auto"):
     # keys rank i sends here, in rank order), into `out`
     runs = [(ex.ptrs[i][slot] + idx[i][r] * kb, idx[i][r + 1] - idx[i][r]) for i in range(G)]
     out = torch.empty(total, dtype=keys_local.dtype, device=keys_local.device)
-    counts, pos = [], 0
+    counts, items, pos = [], [], 0
     for i in range(0, G, 2):
         (pa, na), (pb, nb) = runs[i], runs[i + 1] if i + 1 < G else (0, 0)
-        ops.merge_ptrs(pa, na, pb, nb, out.data_ptr() + pos * kb, code)
+        items.append((pa, na, pb, nb, out.data_ptr() + pos * kb))
         counts.append(na + nb)
         pos += na + nb
+    ops.merge_batch(items, code)
     return merge_runs(out, counts, ops)
 
 
 def merge_runs(buf, counts, ops):
     """Merge the consecutive sorted runs of `buf` (lengths `counts`, in rank
     order) into one sorted run: pairwise merge-path levels ping-ponging
-    between `buf` and one scratch buffer.  Merging adjacent runs with ties
-    taken from the left run keeps equal keys in rank order."""
+    between `buf` and one scratch buffer, each level one batch of merges (a
+    run without a partner is copied).  Merging adjacent runs with ties taken
+    from the left run keeps equal keys in rank order."""
     bounds = [0]
     for c in counts:
         bounds.append(bounds[-1] + int(c))
@@ -401,16 +407,17 @@ def merge_runs(buf, counts, ops):
     while len(runs) > 1:
         if dst is None:
             dst = ops.empty_like(buf)
-        nxt = []
+        nxt, level = [], []
         for i in range(0, len(runs), 2):
             if i + 1 == len(runs):
                 s0, s1 = runs[i]
-                dst[s0:s1].copy_(src[s0:s1])
+                level.append((src[s0:s1], None, dst[s0:s1]))
                 nxt.append(runs[i])
                 continue
             (a0, a1), (b0, b1) = runs[i], runs[i + 1]
-            ops.merge(src[a0:a1], src[b0:b1], dst[a0:b1])
+            level.append((src[a0:a1], src[b0:b1], dst[a0:b1]))
             nxt.append((a0, b1))
+        ops.merge_level(level)
         runs = nxt
         src, dst = dst, src
     return src

@@ -34,6 +34,13 @@ class NumpyOps:
         ab = np.concatenate([a.numpy(), b.numpy()])
         out.copy_(torch.from_numpy(ab[np.argsort(key_images_np(ab), kind="stable")].copy()))
 
+    def merge_level(self, pairs):
+        for a, b, out in pairs:
+            if b is None:
+                out.copy_(a)
+            else:
+                self.merge(a, b, out)
+
     def empty_like(self, t):
         return torch.empty_like(t)
 

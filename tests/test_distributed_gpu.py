@@ -91,9 +91,14 @@ def _worker(rank, world, port, n, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_ranks_nccl():
-    world, n = 2, 1 << 21
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+def test_multi_rank(world):
+    """One process per GPU over NCCL: the distributed sort (peer exchange and
+    NCCL all-to-all), repeated calls on one set of exchange buffers, scan and
+    reduce, against host references."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    n = 1 << 21
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -117,7 +122,7 @@ def test_two_ranks_nccl():
     allx = np.concatenate([got[r][3] for r in range(world)]).astype(np.int64)
     np.testing.assert_array_equal(np.concatenate([got[r][2] for r in range(world)]).astype(np.int64),
                                   np.cumsum(allx))
-    assert got[0][4] == got[1][4] == int(allx.sum())
+    assert all(got[r][4] == int(allx.sum()) for r in range(world))
 
 
 def _stable_merge_np(a, b):
@@ -189,3 +194,23 @@ def test_merge_runs_tree(counts):
     allk = np.concatenate(runs)
     res = merge_runs(torch.from_numpy(allk).cuda(), counts, GpuOps())
     np.testing.assert_array_equal(res.cpu().numpy(), allk[np.argsort(key_images_np(allk), kind="stable")])
+
+
+def test_merge_batch_parity():
+    """One batched merge level (lcpp_dist_merge_sorted_batch): independent
+    pairs of different sizes, empty ones and a copy (empty b) included."""
+    from lcpp_b200.distributed import GpuOps
+    rng = np.random.default_rng(5)
+    sizes = [(1000, 3), (0, 0), (4096, 0), (0, 77), (300_000, 123_457), (3840, 3840), (5, 100_000)]
+    ops = GpuOps()
+    pairs, expect = [], []
+    for na, nb in sizes:
+        a = _sorted_run(rng, na, np.uint32, "ties")
+        b = _sorted_run(rng, nb, np.uint32, "uniform")
+        ta, tb = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+        out = torch.full((na + nb,), 0xAB, dtype=torch.uint32, device="cuda")
+        pairs.append((ta, tb if nb else None, out))
+        expect.append(_stable_merge_np(a, b))
+    ops.merge_level(pairs)
+    for (_, _, out), e in zip(pairs, expect):
+        np.testing.assert_array_equal(out.cpu().numpy(), e)
