@@ -74,6 +74,14 @@ OPS = {
                    workload="DeviceReduce::Sum f32 U[0,1), seed 1", bytes=4, kbytes=4, kernel="reduce_kernel"),
     "reduce_max": dict(metric="Gitems/s int64 Reduce Max @2^30", unit="Gitems/s", log2n=30, dtype="i64",
                        workload="DeviceReduce::Max i64 uniform, seed 1", bytes=8, kbytes=8, kernel="reduce_kernel"),
+    # DeviceSegmentedRadixSort (SURVEY next-row widening): 2^27 u32 keys in
+    # segments of 1..2047 keys (sizes uniform, seed 1), contiguous.
+    # Algorithmic bytes counted like SortKeys (k(1+2P), P = 4); the dominant
+    # launch is an onesweep pass over the composite keys (8 B) and indices
+    # (4 B): 24 B per item.
+    "segsort": dict(metric="Gkeys/s uint32 SegmentedRadixSort SortKeys @2^27", unit="Gkeys/s", log2n=27,
+                    dtype="u32", workload="SegmentedRadixSort SortKeys u32 uniform, segments of 1..2047 keys, seed 1",
+                    bytes=36, kbytes=24, kernel="onesweep_kernel (one 8-bit pass of the segment|key composite)"),
     # Distributed SortKeys of 2^32 keys in total (seed 7), sharded evenly:
     # strong scaling over N GPUs (N = 1 is the 1-GPU-equivalent run).
     "dist": dict(metric="Gkeys/s uint32 distributed SortKeys @2^32", unit="Gkeys/s", log2n=32, dtype="u32",
@@ -204,6 +212,15 @@ class Workload:
             self.inputs = [fill(kdt, kdist, 1), fill(vdt, L.GEN_U32_INDEX, 1)]
             self.outputs = [T.empty_like(self.inputs[0]), T.empty_like(self.inputs[1])]
             self.temp = L.alloc_temp(L.DeviceRadixSort.GetSortPairsTempStorageBytes(kc, vc, n))
+        elif op == "segsort":
+            import numpy as np
+            self.inputs = [fill(T.uint32, L.GEN_U32_UNIFORM, 1)]
+            self.outputs = [T.empty_like(self.inputs[0])]
+            b, e = segsort_offsets(n)
+            self.seg = (T.from_numpy(b).to(dev), T.from_numpy(e).to(dev), int(b.size))
+            self.temp = L.alloc_temp(L.DeviceSegmentedRadixSort.GetSortKeysTempStorageBytes(L.U32, n))
+            self.ss = L.DeviceSegmentedRadixSort()
+            del np
         elif op == "scan":
             self.inputs = [fill(T.int32, L.GEN_I32_SCAN, 1)]
             self.outputs = [T.empty_like(self.inputs[0])]
@@ -226,6 +243,9 @@ class Workload:
             self.rs.SortKeys(t, i[0], o[0], n, 8, 24)
         elif op.startswith("pairs"):
             self.rs.SortPairs(t, i[0], o[0], i[1], o[1], n)
+        elif op == "segsort":
+            b, e, nseg = self.seg
+            self.ss.SortKeys(t, i[0], o[0], n, nseg, b, e)
         elif op == "scan":
             self.sc.InclusiveSum(t, i[0], o[0], n)
         elif op == "reduce":
@@ -242,10 +262,24 @@ class Workload:
         return L.KERNEL_SORT_ONESWEEP
 
 
+def segsort_offsets(n: int):
+    """Contiguous segments of 1..2047 keys covering [0, n) (seed 1)."""
+    import numpy as np
+    rng = np.random.default_rng(1)
+    sizes = rng.integers(1, 2048, n // 1024 + 2)
+    cum = np.concatenate([[0], np.cumsum(sizes)])
+    cum = cum[cum < n]
+    return cum.astype(np.uint32), np.concatenate([cum[1:], [n]]).astype(np.uint32)
+
+
 def cpu_fn(op: str, n_sample: int, threads: int):
     """One run of the oracle port on a bounded sample of the workload (the
     reference tests' host algorithms restated)."""
     from oracle import oracle as O
+    if op == "segsort":
+        x = O.generate(O.GEN_U32_UNIFORM, n_sample, seed=1)
+        b, e = segsort_offsets(n_sample)
+        return lambda: O.segmented_radix_sort(x, None, b, e)
     if op.startswith("dist"):
         # LSD radix sort time does not depend on the key distribution: the
         # uniform seed-7 stream stands in for both distributed workloads
@@ -288,6 +322,7 @@ def cpu_threads_for(op: str) -> int:
     from oracle import oracle as O
     # the sort restatement is multi-threaded; the scan / reduce host
     # references of the reference's tests are sequential
+    # (the segmented restatement is a single-threaded numpy stable sort)
     return O.cpu_threads() if (op in ("sort", "bits") or op.startswith(("pairs", "dist"))) else 1
 
 
@@ -298,7 +333,7 @@ def run_reference(args):
     cfg = OPS[args.op]
     log2n = args.log2n or cfg["log2n"]
     threads = cpu_threads_for(args.op)
-    n_sample = 1 << 22
+    n_sample = 1 << (20 if args.op == "segsort" else 22)
     fn = cpu_fn(args.op, n_sample, threads)
     for _ in range(args.warmup):
         fn()
@@ -307,7 +342,7 @@ def run_reference(args):
         fn()
     el = time.perf_counter() - t0
     v = n_sample * args.steps / el / 1e9
-    sample = (f"2^22 items of the {cfg['workload']} stream per step; "
+    sample = (f"2^{n_sample.bit_length() - 1} items of the {cfg['workload']} stream per step; "
               + ("multi-threaded LSD restatement of the onesweep semantics" if threads > 1
                  else "sequential host reference of the reference's tests"))
     line = {

@@ -223,6 +223,65 @@ lcpp_status lcpp_reduce_max(void* temp, size_t temp_bytes, const void* d_in, voi
                             uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * DeviceSegmentedRadixSort  (src/lcpp/device/device_segmented_radix_sort.h)
+ *
+ * Stable sort of every segment by the key bits [begin_bit, end_bit) after the
+ * radix bijection (unsigned as is, signed with the high bit flipped, floats
+ * sign-dependent; here +0.0 and -0.0 are different keys, as in the
+ * reference's comparator, device_segmented_radix_sort.h:216-243), ascending
+ * or descending.  begin_offsets / end_offsets are device arrays of
+ * num_segments uint32; item i belongs to the last segment s with
+ * begin_offsets[s] <= i, when i < end_offsets[s] and
+ * begin_offsets[s] <= end_offsets[s] <= num_items (the reference's rule,
+ * device_segmented_sort.h:753-775): segments are expected in ascending order
+ * of begin offset and not to overlap.  Items outside every segment are not
+ * written.  num_items and num_segments are at most 2^32 - 1.  The temp size
+ * depends on num_items only; lcpp_device_status(temp, stream) reports the
+ * device error word of the sorting passes.
+ * ---------------------------------------------------------------------- */
+
+/* Replace DeviceSegmentedRadixSort::GetSortKeysTempStorageBytes /
+ * GetSortPairsTempStorageBytes (device_segmented_radix_sort.h:28-38). */
+lcpp_status lcpp_segmented_radix_sort_keys_temp_bytes(lcpp_dtype key_dtype, uint64_t num_items, size_t* temp_bytes);
+lcpp_status lcpp_segmented_radix_sort_pairs_temp_bytes(lcpp_dtype key_dtype, lcpp_dtype value_dtype,
+                                                      uint64_t num_items, size_t* temp_bytes);
+
+/* Replaces SortKeys / SortKeysDescending, copy form
+ * (device_segmented_radix_sort.h:40-56, :80-96). */
+lcpp_status lcpp_segmented_radix_sort_keys(void* temp, size_t temp_bytes, const void* keys_in, void* keys_out,
+                                           uint64_t num_items, uint64_t num_segments,
+                                           const uint32_t* begin_offsets, const uint32_t* end_offsets,
+                                           int begin_bit, int end_bit, int descending, lcpp_dtype key_dtype,
+                                           lcpp_stream_t stream);
+
+/* Replaces SortPairs / SortPairsDescending, copy form
+ * (device_segmented_radix_sort.h:120-138, :163-181). */
+lcpp_status lcpp_segmented_radix_sort_pairs(void* temp, size_t temp_bytes, const void* keys_in, void* keys_out,
+                                            const void* values_in, void* values_out, uint64_t num_items,
+                                            uint64_t num_segments, const uint32_t* begin_offsets,
+                                            const uint32_t* end_offsets, int begin_bit, int end_bit, int descending,
+                                            lcpp_dtype key_dtype, lcpp_dtype value_dtype, lcpp_stream_t stream);
+
+/* Replace the DoubleBuffer forms (device_segmented_radix_sort.h:58-78,
+ * :98-118, :140-161, :183-204).  As in the reference's segmented merge sort
+ * (device_segmented_sort.h:229-246), the selector flips once per merge pass,
+ * ceil(log2(num_items)) times, and key_buffers[*selector] holds the result on
+ * return; nothing happens (selector unchanged) for num_items <= 1, no
+ * segments or begin_bit == end_bit.  Positions outside every segment keep
+ * what the result slot held. */
+lcpp_status lcpp_segmented_radix_sort_keys_double_buffer(void* temp, size_t temp_bytes, void* key_buffers[2],
+                                                         int* selector, uint64_t num_items, uint64_t num_segments,
+                                                         const uint32_t* begin_offsets, const uint32_t* end_offsets,
+                                                         int begin_bit, int end_bit, int descending,
+                                                         lcpp_dtype key_dtype, lcpp_stream_t stream);
+lcpp_status lcpp_segmented_radix_sort_pairs_double_buffer(void* temp, size_t temp_bytes, void* key_buffers[2],
+                                                          void* value_buffers[2], int* selector, uint64_t num_items,
+                                                          uint64_t num_segments, const uint32_t* begin_offsets,
+                                                          const uint32_t* end_offsets, int begin_bit, int end_bit,
+                                                          int descending, lcpp_dtype key_dtype,
+                                                          lcpp_dtype value_dtype, lcpp_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Device diagnostics (no reference counterpart: the reference's look-back
  * spins are unbounded, src/lcpp/agent/agent_radix_sort_onesweep.h:324-334).
  *

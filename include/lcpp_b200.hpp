@@ -25,7 +25,9 @@
  * ExclusiveScan / InclusiveScan / InclusiveScanInit / ExclusiveSum /
  * InclusiveSum), src/lcpp/device/device_reduce.h:183-308
  * (GetTempStorageBytes, Reduce / Sum / Min / Max),
- * src/lcpp/common/util_type.h:57-74 (DoubleBuffer).
+ * src/lcpp/common/util_type.h:57-74 (DoubleBuffer),
+ * src/lcpp/device/device_segmented_radix_sort.h:28-204
+ * (DeviceSegmentedRadixSort).
  */
 #ifndef LCPP_B200_HPP
 #define LCPP_B200_HPP
@@ -285,6 +287,181 @@ private:
                                                          detail::checked_dtype<K>(), s),
                       "SortKeys");
         kd.selector = sel;
+    }
+};
+
+// ---------------------------------------------------------------------------
+// DeviceSegmentedRadixSort (src/lcpp/device/device_segmented_radix_sort.h)
+// ---------------------------------------------------------------------------
+class DeviceSegmentedRadixSort {
+public:
+    template <typename KeyType>
+    static size_t GetSortKeysTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_segmented_radix_sort_keys_temp_bytes(detail::checked_dtype<KeyType>(), num_items, &b),
+                      "GetSortKeysTempStorageBytes");
+        return b;
+    }
+
+    template <typename KeyType, typename ValueType>
+    static size_t GetSortPairsTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_segmented_radix_sort_pairs_temp_bytes(detail::checked_dtype<KeyType>(),
+                                                                 detail::checked_dtype<ValueType>(), num_items, &b),
+                      "GetSortPairsTempStorageBytes");
+        return b;
+    }
+
+    template <typename KeyType>
+    void SortKeys(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<KeyType> keys_input,
+                  BufferView<KeyType> keys_output, uint64_t num_items, uint64_t num_segments,
+                  BufferView<uint32_t> begin_offsets, BufferView<uint32_t> end_offsets, int begin_bit = 0,
+                  int end_bit = sizeof(KeyType) * 8)
+    {
+        keys(stream, temp_storage, keys_input, keys_output, num_items, num_segments, begin_offsets, end_offsets,
+             begin_bit, end_bit, 0);
+    }
+
+    template <typename KeyType>
+    void SortKeysDescending(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<KeyType> keys_input,
+                            BufferView<KeyType> keys_output, uint64_t num_items, uint64_t num_segments,
+                            BufferView<uint32_t> begin_offsets, BufferView<uint32_t> end_offsets, int begin_bit = 0,
+                            int end_bit = sizeof(KeyType) * 8)
+    {
+        keys(stream, temp_storage, keys_input, keys_output, num_items, num_segments, begin_offsets, end_offsets,
+             begin_bit, end_bit, 1);
+    }
+
+    template <typename KeyType, typename ValueType>
+    void SortPairs(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<KeyType> keys_input,
+                   BufferView<KeyType> keys_output, BufferView<ValueType> values_input,
+                   BufferView<ValueType> values_output, uint64_t num_items, uint64_t num_segments,
+                   BufferView<uint32_t> begin_offsets, BufferView<uint32_t> end_offsets, int begin_bit = 0,
+                   int end_bit = sizeof(KeyType) * 8)
+    {
+        pairs(stream, temp_storage, keys_input, keys_output, values_input, values_output, num_items, num_segments,
+              begin_offsets, end_offsets, begin_bit, end_bit, 0);
+    }
+
+    template <typename KeyType, typename ValueType>
+    void SortPairsDescending(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<KeyType> keys_input,
+                             BufferView<KeyType> keys_output, BufferView<ValueType> values_input,
+                             BufferView<ValueType> values_output, uint64_t num_items, uint64_t num_segments,
+                             BufferView<uint32_t> begin_offsets, BufferView<uint32_t> end_offsets, int begin_bit = 0,
+                             int end_bit = sizeof(KeyType) * 8)
+    {
+        pairs(stream, temp_storage, keys_input, keys_output, values_input, values_output, num_items, num_segments,
+              begin_offsets, end_offsets, begin_bit, end_bit, 1);
+    }
+
+    // DoubleBuffer forms: the selector flips ceil(log2 num_items) times, as
+    // in the reference's segmented merge sort.
+    template <typename KeyType>
+    void SortKeys(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, DoubleBuffer<KeyType>& keys_db,
+                  uint64_t num_items, uint64_t num_segments, BufferView<uint32_t> begin_offsets,
+                  BufferView<uint32_t> end_offsets, int begin_bit = 0, int end_bit = sizeof(KeyType) * 8)
+    {
+        keys_db_(stream, temp_storage, keys_db, num_items, num_segments, begin_offsets, end_offsets, begin_bit,
+                 end_bit, 0);
+    }
+
+    template <typename KeyType>
+    void SortKeysDescending(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, DoubleBuffer<KeyType>& keys_db,
+                            uint64_t num_items, uint64_t num_segments, BufferView<uint32_t> begin_offsets,
+                            BufferView<uint32_t> end_offsets, int begin_bit = 0, int end_bit = sizeof(KeyType) * 8)
+    {
+        keys_db_(stream, temp_storage, keys_db, num_items, num_segments, begin_offsets, end_offsets, begin_bit,
+                 end_bit, 1);
+    }
+
+    template <typename KeyType, typename ValueType>
+    void SortPairs(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, DoubleBuffer<KeyType>& keys_db,
+                   DoubleBuffer<ValueType>& values_db, uint64_t num_items, uint64_t num_segments,
+                   BufferView<uint32_t> begin_offsets, BufferView<uint32_t> end_offsets, int begin_bit = 0,
+                   int end_bit = sizeof(KeyType) * 8)
+    {
+        pairs_db_(stream, temp_storage, keys_db, values_db, num_items, num_segments, begin_offsets, end_offsets,
+                  begin_bit, end_bit, 0);
+    }
+
+    template <typename KeyType, typename ValueType>
+    void SortPairsDescending(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, DoubleBuffer<KeyType>& keys_db,
+                             DoubleBuffer<ValueType>& values_db, uint64_t num_items, uint64_t num_segments,
+                             BufferView<uint32_t> begin_offsets, BufferView<uint32_t> end_offsets, int begin_bit = 0,
+                             int end_bit = sizeof(KeyType) * 8)
+    {
+        pairs_db_(stream, temp_storage, keys_db, values_db, num_items, num_segments, begin_offsets, end_offsets,
+                  begin_bit, end_bit, 1);
+    }
+
+private:
+    static void offsets(BufferView<uint32_t> b, BufferView<uint32_t> e, uint64_t nseg)
+    {
+        detail::require(b.size() >= nseg && e.size() >= nseg, "segment offset views are shorter than num_segments");
+    }
+
+    template <typename K>
+    static void keys(lcpp_stream_t s, BufferView<uint32_t> t, BufferView<K> ki, BufferView<K> ko, uint64_t n,
+                     uint64_t nseg, BufferView<uint32_t> b, BufferView<uint32_t> e, int bb, int eb, int desc)
+    {
+        offsets(b, e, nseg);
+        detail::require(ki.size() >= n && ko.size() >= n, "SortKeys: a key view is shorter than num_items");
+        detail::check(lcpp_segmented_radix_sort_keys(t.data(), detail::temp_bytes(t), ki.data(), ko.data(), n, nseg,
+                                                     b.data(), e.data(), bb, eb, desc, detail::checked_dtype<K>(), s),
+                      "SortKeys");
+    }
+
+    template <typename K, typename V>
+    static void pairs(lcpp_stream_t s, BufferView<uint32_t> t, BufferView<K> ki, BufferView<K> ko, BufferView<V> vi,
+                      BufferView<V> vo, uint64_t n, uint64_t nseg, BufferView<uint32_t> b, BufferView<uint32_t> e,
+                      int bb, int eb, int desc)
+    {
+        offsets(b, e, nseg);
+        detail::require(ki.size() >= n && ko.size() >= n && vi.size() >= n && vo.size() >= n,
+                        "SortPairs: a key or value view is shorter than num_items");
+        detail::check(lcpp_segmented_radix_sort_pairs(t.data(), detail::temp_bytes(t), ki.data(), ko.data(),
+                                                      vi.data(), vo.data(), n, nseg, b.data(), e.data(), bb, eb, desc,
+                                                      detail::checked_dtype<K>(), detail::checked_dtype<V>(), s),
+                      "SortPairs");
+    }
+
+    template <typename K>
+    static void keys_db_(lcpp_stream_t s, BufferView<uint32_t> t, DoubleBuffer<K>& kd, uint64_t n, uint64_t nseg,
+                         BufferView<uint32_t> b, BufferView<uint32_t> e, int bb, int eb, int desc)
+    {
+        offsets(b, e, nseg);
+        detail::require(kd.d_buffer[0].size() >= n && kd.d_buffer[1].size() >= n,
+                        "SortKeys: a double-buffer view is shorter than num_items");
+        void* kb[2] = {kd.d_buffer[0].data(), kd.d_buffer[1].data()};
+        int sel = kd.selector;
+        detail::check(lcpp_segmented_radix_sort_keys_double_buffer(t.data(), detail::temp_bytes(t), kb, &sel, n,
+                                                                   nseg, b.data(), e.data(), bb, eb, desc,
+                                                                   detail::checked_dtype<K>(), s),
+                      "SortKeys");
+        kd.selector = sel;
+    }
+
+    template <typename K, typename V>
+    static void pairs_db_(lcpp_stream_t s, BufferView<uint32_t> t, DoubleBuffer<K>& kd, DoubleBuffer<V>& vd,
+                          uint64_t n, uint64_t nseg, BufferView<uint32_t> b, BufferView<uint32_t> e, int bb, int eb,
+                          int desc)
+    {
+        offsets(b, e, nseg);
+        detail::require(kd.d_buffer[0].size() >= n && kd.d_buffer[1].size() >= n && vd.d_buffer[0].size() >= n &&
+                            vd.d_buffer[1].size() >= n,
+                        "SortPairs: a double-buffer view is shorter than num_items");
+        detail::require(kd.selector == vd.selector, "SortPairs: key and value selectors differ");
+        void* kb[2] = {kd.d_buffer[0].data(), kd.d_buffer[1].data()};
+        void* vb[2] = {vd.d_buffer[0].data(), vd.d_buffer[1].data()};
+        int sel = kd.selector;
+        detail::check(lcpp_segmented_radix_sort_pairs_double_buffer(t.data(), detail::temp_bytes(t), kb, vb, &sel, n,
+                                                                    nseg, b.data(), e.data(), bb, eb, desc,
+                                                                    detail::checked_dtype<K>(),
+                                                                    detail::checked_dtype<V>(), s),
+                      "SortPairs");
+        kd.selector = vd.selector = sel;
     }
 };
 

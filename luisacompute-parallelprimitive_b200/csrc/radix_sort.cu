@@ -266,8 +266,11 @@ struct OnesweepArgs {
 //     independent, so one __syncwarp covers the group and the chains overlap);
 //   MIN_BLOCKS: resident blocks per SM requested from the register allocator
 //     (0: left to the compiler);
-//   PACK: tile ranks kept as 16-bit pairs (fewer live registers).
-template <int BLOCK, int ITEMS, int PEERS, int WINDOW, int GROUP = 1, int MIN_BLOCKS = 0, bool PACK = false>
+//   PACK: tile ranks kept as 16-bit pairs (fewer live registers);
+//   SLEEP_NS: __nanosleep between polls of a status word that is not
+//     published yet (spinning warps take issue slots from the others).
+template <int BLOCK, int ITEMS, int PEERS, int WINDOW, int GROUP = 1, int MIN_BLOCKS = 0, bool PACK = false,
+          int SLEEP_NS = 32, bool PTX_VOTE = false>
 struct Policy {
     static constexpr int kBlock = BLOCK;
     static constexpr int kItems = ITEMS;
@@ -276,6 +279,8 @@ struct Policy {
     static constexpr int kGroup = GROUP;
     static constexpr int kMinBlocks = MIN_BLOCKS;
     static constexpr bool kPack = PACK;
+    static constexpr int kSleepNs = SLEEP_NS;  // back-off between polls of an unpublished status word
+    static constexpr bool kPtxVote = PTX_VOTE;  // ranking ballots / warp barrier as PTX
     static constexpr int kTile = BLOCK * ITEMS;
     static constexpr int kWarps = BLOCK / kWarp;
     // mask words per warp and mask set; mask sets alternate by group parity
@@ -307,14 +312,14 @@ struct OnesweepSmem {
 // with __nanosleep so that waiting warps leave issue slots to the warps of
 // other tiles on the same SM.  On timeout (or when another thread already
 // reported an error) returns an inclusive zero so that the caller finishes.
-template <typename ST>
+template <int SLEEP_NS, typename ST>
 __device__ __forceinline__ ST wait_status(const ST* p, ST w, uint32_t* error)
 {
     using SB = StatusBits<ST>;
     uint32_t spins = 0;
     uint64_t t0 = 0;
     while ((w & SB::kFlags) == 0) {
-        __nanosleep(32);
+        if constexpr (SLEEP_NS > 0) __nanosleep(SLEEP_NS);
         w = ld_relaxed(p);
         if (++spins == 32) {
             spins = 0;
@@ -334,7 +339,7 @@ __device__ __forceinline__ ST wait_status(const ST* p, ST w, uint32_t* error)
 // Exclusive prefix of one digit over tiles [0, tile): walk back from
 // tile - 1, W tiles per round trip, adding partial counts until an inclusive
 // count is found.  Tile 0 always publishes an inclusive count.
-template <typename ST, typename OffT, int W>
+template <typename ST, typename OffT, int W, int SLEEP_NS>
 __device__ __forceinline__ OffT lookback_digit(const ST* status, uint32_t tile, int digit, uint32_t* error)
 {
     using SB = StatusBits<ST>;
@@ -352,7 +357,7 @@ __device__ __forceinline__ OffT lookback_digit(const ST* status, uint32_t tile, 
         for (int q = 0; q < W; ++q) {
             if (!done) {
                 const int64_t j = base - q;
-                if (j >= 0) w[q] = wait_status(status + uint64_t(j) * kDigits + digit, w[q], error);
+                if (j >= 0) w[q] = wait_status<SLEEP_NS>(status + uint64_t(j) * kDigits + digit, w[q], error);
                 prefix += OffT(w[q] & SB::kValue);
                 done = (w[q] & SB::kInclusive) != 0;
             }
@@ -435,6 +440,29 @@ __device__ __forceinline__ void shared_store_if(bool pred, uint32_t smem_addr, u
 __device__ __forceinline__ void shared_red_add(uint32_t smem_addr, uint32_t inc)
 {
     asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(smem_addr), "r"(inc) : "memory");
+}
+
+// Full-warp ballot and warp barrier written as PTX (vote.sync /
+// bar.warp.sync with the full member mask).
+__device__ __forceinline__ uint32_t warp_ballot(bool pred)
+{
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "vote.sync.ballot.b32 %0, p, 0xffffffff;\n\t}"
+        : "=r"(r)
+        : "r"(uint32_t(pred)));
+    return r;
+}
+
+__device__ __forceinline__ void warp_barrier() { asm volatile("bar.warp.sync 0xffffffff;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t warp_shfl(uint32_t v, int src)
+{
+    uint32_t r;
+    asm volatile("shfl.sync.idx.b32 %0, %1, %2, 0x1f, 0xffffffff;" : "=r"(r) : "r"(v), "r"(src));
+    return r;
 }
 
 // Everything after the tile id is known.  FULL: the tile has kTile keys (all
@@ -577,7 +605,12 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
                     }
                 }
             }
-            if constexpr (PEERS != 0) __syncwarp();
+            if constexpr (PEERS != 0) {
+                if constexpr (P::kPtxVote)
+                    warp_barrier();
+                else
+                    __syncwarp();
+            }
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 if (i0 + g < ITEMS) {
@@ -589,7 +622,7 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
 #pragma unroll
                             for (int b = 5; b < kRadixBits; ++b) {
                                 const bool bit = (d[g] >> b) & 1u;
-                                const uint32_t vote = __ballot_sync(0xffffffffu, bit);
+                                const uint32_t vote = P::kPtxVote ? warp_ballot(bit) : __ballot_sync(0xffffffffu, bit);
                                 peers[g] &= bit ? vote : ~vote;
                             }
                         }
@@ -606,7 +639,8 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 if (i0 + g < ITEMS) {
-                    base[g] = __shfl_sync(0xffffffffu, base[g], 31 - __clz(peers[g]));
+                    base[g] = P::kPtxVote ? warp_shfl(base[g], 31 - __clz(peers[g]))
+                                          : __shfl_sync(0xffffffffu, base[g], 31 - __clz(peers[g]));
                     if constexpr (PEERS == 1) shared_store_if(lane == 31 - __clz(peers[g]), maddr[g], 0u);
                     if constexpr (PEERS == 2) shared_store_if(true, maddr[g], 0u);
                     set_rank(i0 + g, base[g] + __popc(peers[g] & lt));
@@ -620,7 +654,7 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
     // per round trip.
     if (tid < kDigits) {
         OffT prefix = 0;
-        if (tile > 0) prefix = lookback_digit<ST, OffT, P::kWindow>(a.status, tile, tid, a.error);
+        if (tile > 0) prefix = lookback_digit<ST, OffT, P::kWindow, P::kSleepNs>(a.status, tile, tid, a.error);
         finish_digit(tid, prefix);
     }
 
@@ -878,6 +912,11 @@ lcpp_status run_kind(const Layout& L, unsigned char* temp, const SortCall& c, ui
             case 4: return LCPP_PASSES(256, 24, 2, 8, 4);  // slots ranked in fours
             case 5: return LCPP_PASSES(256, 24, 2, 8, 1, 4, true);  // 4 blocks per SM, 16-bit ranks
             case 6: return LCPP_PASSES(256, 24, 2, 8, 1, 1);        // 2 blocks per SM (116 registers)
+            case 7: return LCPP_PASSES(256, 24, 2, 8, 1, 0, false, 0);    // look-back polls without back-off
+            case 8: return LCPP_PASSES(256, 24, 2, 8, 1, 0, false, 128);  // 128 ns back-off
+            case 9: return LCPP_PASSES(256, 24, 2, 8, 1, 0, false, 400);  // 400 ns back-off
+            case 10: return LCPP_PASSES(256, 24, 2, 8, 1, 0, false, 32, true);  // PTX vote / warp barrier
+            case 14: return LCPP_PASSES(256, 24, 2, 8, 2, 0, false, 32, true);
             default: break;
             }
         }

@@ -71,6 +71,13 @@ def lib() -> ctypes.CDLL:
         "lcpp_radix_sort_pairs": ([vp, sz, vp, vp, vp, vp, u64, i, i, i, i, i, vp], i),
         "lcpp_radix_sort_keys_double_buffer": ([vp, sz, vpa, ip, u64, i, i, i, i, vp], i),
         "lcpp_radix_sort_pairs_double_buffer": ([vp, sz, vpa, vpa, ip, u64, i, i, i, i, i, vp], i),
+        "lcpp_segmented_radix_sort_keys_temp_bytes": ([i, u64, szp], i),
+        "lcpp_segmented_radix_sort_pairs_temp_bytes": ([i, i, u64, szp], i),
+        "lcpp_segmented_radix_sort_keys": ([vp, sz, vp, vp, u64, u64, vp, vp, i, i, i, i, vp], i),
+        "lcpp_segmented_radix_sort_pairs": ([vp, sz, vp, vp, vp, vp, u64, u64, vp, vp, i, i, i, i, i, vp], i),
+        "lcpp_segmented_radix_sort_keys_double_buffer": ([vp, sz, vpa, ip, u64, u64, vp, vp, i, i, i, i, vp], i),
+        "lcpp_segmented_radix_sort_pairs_double_buffer": ([vp, sz, vpa, vpa, ip, u64, u64, vp, vp, i, i, i, i, i,
+                                                           vp], i),
         "lcpp_scan_temp_bytes": ([i, u64, szp], i),
         "lcpp_scan_exclusive": ([vp, sz, vp, vp, u64, i, vp, i, vp], i),
         "lcpp_scan_inclusive": ([vp, sz, vp, vp, u64, i, i, vp], i),
@@ -268,6 +275,86 @@ class DeviceRadixSort:
             _ptr(temp), temp.numel() if temp is not None else 0, kb, vb, ctypes.byref(sel), n,
             begin, end, int(desc), kd, vd, _stream(stream)), "SortPairs(DoubleBuffer)")
         kdb.selector = vdb.selector = sel.value
+
+
+class DeviceSegmentedRadixSort:
+    """Mirror of lcpp::DeviceSegmentedRadixSort
+    (src/lcpp/device/device_segmented_radix_sort.h:16-246): copy form
+    (temp, keys_in, keys_out, n, num_segments, begin_offsets, end_offsets,
+    begin_bit, end_bit) and DoubleBuffer form (temp, keys_db, n, num_segments,
+    begin_offsets, end_offsets, begin_bit, end_bit); offsets are uint32 device
+    tensors."""
+
+    @staticmethod
+    def GetSortKeysTempStorageBytes(key_dtype: int, num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_segmented_radix_sort_keys_temp_bytes(key_dtype, num_items, ctypes.byref(out)),
+              "GetSortKeysTempStorageBytes")
+        return out.value
+
+    @staticmethod
+    def GetSortPairsTempStorageBytes(key_dtype: int, value_dtype: int, num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_segmented_radix_sort_pairs_temp_bytes(key_dtype, value_dtype, num_items,
+                                                               ctypes.byref(out)), "GetSortPairsTempStorageBytes")
+        return out.value
+
+    def SortKeys(self, temp, *args, stream=None):
+        self._keys(temp, args, False, stream)
+
+    def SortKeysDescending(self, temp, *args, stream=None):
+        self._keys(temp, args, True, stream)
+
+    def SortPairs(self, temp, *args, stream=None):
+        self._pairs(temp, args, False, stream)
+
+    def SortPairsDescending(self, temp, *args, stream=None):
+        self._pairs(temp, args, True, stream)
+
+    def _keys(self, temp, args, desc, stream):
+        tb = temp.numel() if temp is not None else 0
+        if isinstance(args[0], DoubleBuffer):
+            db, n, nseg, bo, eo, *rest = args
+            begin, end = _bit_range(rest)
+            k0 = db.d_buffers[0]
+            end = k0.element_size() * 8 if end is None else end
+            bufs = (ctypes.c_void_p * 2)(db.d_buffers[0].data_ptr(), db.d_buffers[1].data_ptr())
+            sel = ctypes.c_int(db.selector)
+            check(lib().lcpp_segmented_radix_sort_keys_double_buffer(
+                _ptr(temp), tb, bufs, ctypes.byref(sel), n, nseg, _ptr(bo), _ptr(eo), begin, end, int(desc),
+                dtype_code(k0), _stream(stream)), "SortKeys(DoubleBuffer)")
+            db.selector = sel.value
+            return
+        kin, kout, n, nseg, bo, eo, *rest = args
+        begin, end = _bit_range(rest)
+        end = kin.element_size() * 8 if end is None else end
+        check(lib().lcpp_segmented_radix_sort_keys(_ptr(temp), tb, _ptr(kin), _ptr(kout), n, nseg, _ptr(bo),
+                                                   _ptr(eo), begin, end, int(desc), dtype_code(kin),
+                                                   _stream(stream)), "SortKeys")
+
+    def _pairs(self, temp, args, desc, stream):
+        tb = temp.numel() if temp is not None else 0
+        if isinstance(args[0], DoubleBuffer):
+            kdb, vdb, n, nseg, bo, eo, *rest = args
+            if kdb.selector != vdb.selector:
+                raise LcppError(ERR_INVALID_ARG, "key and value DoubleBuffer selectors must match")
+            begin, end = _bit_range(rest)
+            k0, v0 = kdb.d_buffers[0], vdb.d_buffers[0]
+            end = k0.element_size() * 8 if end is None else end
+            kb = (ctypes.c_void_p * 2)(kdb.d_buffers[0].data_ptr(), kdb.d_buffers[1].data_ptr())
+            vb = (ctypes.c_void_p * 2)(vdb.d_buffers[0].data_ptr(), vdb.d_buffers[1].data_ptr())
+            sel = ctypes.c_int(kdb.selector)
+            check(lib().lcpp_segmented_radix_sort_pairs_double_buffer(
+                _ptr(temp), tb, kb, vb, ctypes.byref(sel), n, nseg, _ptr(bo), _ptr(eo), begin, end, int(desc),
+                dtype_code(k0), dtype_code(v0), _stream(stream)), "SortPairs(DoubleBuffer)")
+            kdb.selector = vdb.selector = sel.value
+            return
+        kin, kout, vin, vout, n, nseg, bo, eo, *rest = args
+        begin, end = _bit_range(rest)
+        end = kin.element_size() * 8 if end is None else end
+        check(lib().lcpp_segmented_radix_sort_pairs(_ptr(temp), tb, _ptr(kin), _ptr(kout), _ptr(vin), _ptr(vout),
+                                                    n, nseg, _ptr(bo), _ptr(eo), begin, end, int(desc),
+                                                    dtype_code(kin), dtype_code(vin), _stream(stream)), "SortPairs")
 
 
 class DeviceScan:

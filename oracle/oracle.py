@@ -145,3 +145,55 @@ def generate(dist: int, n: int, seed: int, offset: int = 0) -> np.ndarray:
 
 def cpu_threads() -> int:
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def segmented_radix_sort(keys: np.ndarray, values: np.ndarray | None, begin_offsets: np.ndarray,
+                         end_offsets: np.ndarray, begin_bit: int = 0, end_bit: int | None = None,
+                         descending: bool = False, out_keys: np.ndarray | None = None,
+                         out_values: np.ndarray | None = None):
+    """DeviceSegmentedRadixSort restated (numpy).
+
+    Order: the key bits [begin_bit, end_bit) after the radix bijection --
+    Traits<T>::TwiddleIn, no +-0.0 fold -- compared with < (ascending) or >
+    (descending) in a stable sort (src/lcpp/device/device_segmented_radix_sort.h:216-243,
+    src/lcpp/common/util_type.h:97-175).  Segment rule: item i belongs to the
+    last segment s with begin[s] <= i, when i < end[s] and
+    begin[s] <= end[s] <= n (src/lcpp/device/device_segmented_sort.h:753-775);
+    other positions of the outputs keep their contents.  Returns
+    (out_keys, out_values); outputs default to copies of the inputs.
+    """
+    n = keys.size
+    bits = keys.dtype.itemsize * 8
+    end_bit = bits if end_bit is None else end_bit
+    ok = out_keys if out_keys is not None else keys.copy()
+    ov = None
+    if values is not None:
+        ov = out_values if out_values is not None else values.copy()
+    if n == 0 or begin_offsets.size == 0:
+        return ok, ov
+    u = keys.view(np.uint32 if bits == 32 else np.uint64).astype(np.uint64)
+    full = np.uint64((1 << bits) - 1)
+    high = np.uint64(1 << (bits - 1))
+    if keys.dtype.kind == "i":
+        t = u ^ high
+    elif keys.dtype.kind == "f":
+        t = np.where((u & high) != 0, (~u) & full, u ^ high)
+    else:
+        t = u
+    width = end_bit - begin_bit
+    fmask = np.uint64((1 << width) - 1) if width < 64 else np.uint64(0xFFFFFFFFFFFFFFFF)
+    field = (t >> np.uint64(begin_bit)) & fmask if width else np.zeros(n, dtype=np.uint64)
+    if descending:
+        field = fmask - field
+    pos = np.arange(n, dtype=np.int64)
+    b = begin_offsets.astype(np.int64)
+    e = end_offsets.astype(np.int64)
+    seg = np.searchsorted(b, pos, side="right") - 1
+    sc = np.clip(seg, 0, None)
+    valid = (seg >= 0) & (pos >= b[sc]) & (pos < e[sc]) & (b[sc] <= e[sc]) & (e[sc] <= n)
+    members = pos[valid]
+    order = members[np.lexsort((field[valid], seg[valid]))]  # stable: by segment, then field
+    ok[members] = keys[order]
+    if ov is not None:
+        ov[members] = values[order]
+    return ok, ov

@@ -216,6 +216,41 @@ void reductions(lcpp_stream_t s)
     }
 }
 
+void segmented(lcpp_stream_t s)
+{
+    // device_segmented_sort_test.cpp: 19 items, segments [1,4) [5,5) [5,9) [10,19)
+    const size_t n = 19, nseg = 4;
+    const std::vector<uint32_t> begin{1u, 5u, 5u, 10u}, end{4u, 5u, 9u, 19u};
+    std::vector<int32_t> keys{91, 3, -2, 3, 92, 8, 1, 8, 4, 93, 5, -1, 5, 2, -1, 7, 2, 5, 0};
+    std::vector<uint32_t> vals(n);
+    std::iota(vals.begin(), vals.end(), 0u);
+    std::vector<int32_t> expect_k(n, -777);
+    std::vector<uint32_t> expect_v(n, 0xffffffffu);
+    for (size_t g = 0; g < nseg; ++g) {
+        std::vector<uint32_t> o(end[g] - begin[g]);
+        std::iota(o.begin(), o.end(), begin[g]);
+        std::stable_sort(o.begin(), o.end(), [&](uint32_t l, uint32_t r) { return keys[l] > keys[r]; });
+        for (size_t i = 0; i < o.size(); ++i) {
+            expect_k[begin[g] + i] = keys[o[i]];
+            expect_v[begin[g] + i] = vals[o[i]];
+        }
+    }
+    DeviceArray<int32_t> ki(n), ko(n);
+    DeviceArray<uint32_t> vi(n), vo(n), db(nseg), de(nseg);
+    ki.upload(keys);
+    vi.upload(vals);
+    ko.upload(std::vector<int32_t>(n, -777));
+    vo.upload(std::vector<uint32_t>(n, 0xffffffffu));
+    db.upload(begin);
+    de.upload(end);
+    auto temp = temp_for(DeviceSegmentedRadixSort::GetSortPairsTempStorageBytes<int32_t, uint32_t>(n));
+    DeviceSegmentedRadixSort ss;
+    ss.SortPairsDescending(s, temp.view(), ki.view(), ko.view(), vi.view(), vo.view(), n, nseg, db.view(), de.view());
+    CUDA(cudaStreamSynchronize(s));
+    CHECK(ko.download() == expect_k);
+    CHECK(vo.download() == expect_v);
+}
+
 void misuse_throws(lcpp_stream_t s)
 {
     DeviceArray<uint32_t> a(16), b(16);
@@ -257,6 +292,7 @@ int main()
     sort_bits_stable_double_buffer(s);
     scans(s);
     reductions(s);
+    segmented(s);
     misuse_throws(s);
     CUDA(cudaStreamDestroy(stream));
     std::printf("OK %d\n", g_checks);

@@ -220,6 +220,47 @@ static void reduce_cases()
     emit("reduce_shuffled_minmax", mm);
 }
 
+// tests/device_segmented_sort_test.cpp:22-56 and :260-268 -- 19 items in
+// segments [1,4) [5,5) [5,9) [10,19); keys outside every segment are -777
+// and their values UINT_MAX; expected = std::stable_sort per segment with
+// std::less / std::greater (the reference's segmented_order helper).
+static void segmented_cases()
+{
+    const unsigned n = 19, segments = 4;
+    const std::vector<uint32_t> begin{1u, 5u, 5u, 10u}, end{4u, 5u, 9u, 19u};
+    std::vector<int32_t> keys{91, 3, -2, 3, 92, 8, 1, 8, 4, 93, 5, -1, 5, 2, -1, 7, 2, 5, 0};
+    std::vector<uint32_t> vals(n);
+    std::iota(vals.begin(), vals.end(), 0u);
+    auto in_segment = [&](unsigned i) {
+        for (unsigned s = 0; s < segments; ++s)
+            if (i >= begin[s] && i < end[s]) return true;
+        return false;
+    };
+    for (unsigned i = 0; i < n; ++i)
+        if (!in_segment(i)) {
+            keys[i] = -777;
+            vals[i] = 0xffffffffu;
+        }
+    auto order = [&](bool desc) {
+        std::vector<uint32_t> ord(n, 0xffffffffu);
+        for (unsigned s = 0; s < segments; ++s) {
+            std::vector<uint32_t> o(end[s] - begin[s]);
+            std::iota(o.begin(), o.end(), begin[s]);
+            std::stable_sort(o.begin(), o.end(), [&](uint32_t l, uint32_t r) {
+                return desc ? keys[l] > keys[r] : keys[l] < keys[r];
+            });
+            std::copy(o.begin(), o.end(), ord.begin() + begin[s]);
+        }
+        return ord;
+    };
+    emit("segmented_keys", keys);
+    emit("segmented_vals", vals);
+    emit("segmented_begin", begin);
+    emit("segmented_end", end);
+    emit("segmented_asc_order", order(false));
+    emit("segmented_desc_order", order(true));
+}
+
 int main(int argc, char** argv)
 {
     if (argc != 2) {
@@ -235,6 +276,7 @@ int main(int argc, char** argv)
     interface_cases();
     scan_cases();
     reduce_cases();
+    segmented_cases();
     std::fclose(g_index);
     return 0;
 }

@@ -212,3 +212,69 @@ def test_generators_match_numpy(oracle):
                                   ((r[0] & r[1] & r[2]) & np.uint64(0xFFFFFFFF)).astype(np.uint32))
     np.testing.assert_array_equal(oracle.generate(oracle.GEN_I32_SCAN, 1000, 1, 1000),
                                   ((r[0] % np.uint64(2001)).astype(np.int64) - 1000).astype(np.int32))
+
+
+def test_segmented_oracle_matches_golden(golden):
+    from oracle import oracle as O
+    keys, vals = golden["segmented_keys"], golden["segmented_vals"]
+    b, e = golden["segmented_begin"], golden["segmented_end"]
+    for desc, name in ((False, "segmented_asc_order"), (True, "segmented_desc_order")):
+        order = golden[name]
+        sentinel_k = np.full_like(keys, -777)
+        sentinel_v = np.full_like(vals, 0xFFFFFFFF)
+        ok, ov = O.segmented_radix_sort(keys, vals, b, e, descending=desc, out_keys=sentinel_k,
+                                        out_values=sentinel_v)
+        inside = order != 0xFFFFFFFF
+        np.testing.assert_array_equal(ok[inside], keys[order[inside]])
+        np.testing.assert_array_equal(ov[inside], vals[order[inside]])
+        assert (ok[~inside] == -777).all() and (ov[~inside] == 0xFFFFFFFF).all()
+
+
+def _segmented_by_python(keys, b, e, begin_bit, end_bit, desc):
+    """Independent pure-Python restatement for small cases."""
+    bits = keys.dtype.itemsize * 8
+    ubits = keys.view(np.uint32 if bits == 32 else np.uint64)
+
+    def field(i):
+        u = int(ubits[i])
+        if keys.dtype.kind == "i":
+            u ^= 1 << (bits - 1)
+        elif keys.dtype.kind == "f":
+            u = (~u & ((1 << bits) - 1)) if u >> (bits - 1) else u ^ (1 << (bits - 1))
+        return (u >> begin_bit) & ((1 << (end_bit - begin_bit)) - 1)
+
+    out = keys.copy()
+    n = keys.size
+    for i_s in range(len(b)):
+        nb = int(b[i_s + 1]) if i_s + 1 < len(b) else None
+        lo, hi = int(b[i_s]), int(e[i_s])
+        if not (lo <= hi <= n):
+            continue
+        members = [i for i in range(lo, hi) if nb is None or i < nb]
+        order = sorted(members, key=field, reverse=False)
+        if desc:
+            order = sorted(members, key=lambda i: -field(i))
+        for p, q in zip(members, order):
+            out[p] = keys[q]
+    return out
+
+
+@pytest.mark.parametrize("dt", [np.uint32, np.int32, np.float32, np.uint64, np.int64, np.float64])
+@pytest.mark.parametrize("desc", [False, True])
+def test_segmented_oracle_vs_python(dt, desc):
+    from oracle import oracle as O
+    rng = np.random.default_rng(3)
+    n = 300
+    if np.dtype(dt).kind == "f":
+        keys = rng.standard_normal(n).astype(dt)
+        keys[::7] = 0.0
+        keys[3::7] = -0.0
+    else:
+        keys = rng.integers(0, 50, n).astype(dt) if np.dtype(dt).kind == "u" else rng.integers(-25, 25, n).astype(dt)
+    b = np.array([0, 10, 10, 57, 120, 250], dtype=np.uint32)
+    e = np.array([7, 10, 50, 120, 240, 300], dtype=np.uint32)
+    bits = np.dtype(dt).itemsize * 8
+    for begin_bit, end_bit in ((0, bits), (1, 6), (3, 3)):
+        ok, _ = O.segmented_radix_sort(keys, None, b, e, begin_bit, end_bit, desc)
+        exp = _segmented_by_python(keys, b, e, begin_bit, end_bit, desc)
+        np.testing.assert_array_equal(ok.view(np.uint8), exp.view(np.uint8))
