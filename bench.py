@@ -352,7 +352,7 @@ def run_reference(args):
         "dtype": cfg["dtype"], "data": DATA,
         "config": {"workload": f"{cfg['workload']}, 2^{log2n} items " + ("in total" if cfg.get("distributed") else "per GPU")
                    + "; each step runs a bounded "
-                               f"2^22-item sample of it on the host"},
+                               f"2^{n_sample.bit_length() - 1}-item sample of it on the host"},
         "cpu_baseline": {"value": v, "unit": cfg["unit"], "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": cfg["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

@@ -908,22 +908,21 @@ lcpp_status run_kind(const Layout& L, unsigned char* temp, const SortCall& c, ui
             switch (onesweep_variant()) {
             case 1: return LCPP_PASSES(384, 20, 0, 8);  // 8 ballots per digit
             case 2: return LCPP_PASSES(256, 24, 1, 8);  // shared-memory peer masks
-            case 3: return LCPP_PASSES(256, 24, 2, 8, 2);  // slots ranked in pairs
-            case 4: return LCPP_PASSES(256, 24, 2, 8, 4);  // slots ranked in fours
-            case 5: return LCPP_PASSES(256, 24, 2, 8, 1, 4, true);  // 4 blocks per SM, 16-bit ranks
-            case 6: return LCPP_PASSES(256, 24, 2, 8, 1, 1);        // 2 blocks per SM (116 registers)
-            case 7: return LCPP_PASSES(256, 24, 2, 8, 1, 0, false, 0);    // look-back polls without back-off
-            case 8: return LCPP_PASSES(256, 24, 2, 8, 1, 0, false, 128);  // 128 ns back-off
-            case 9: return LCPP_PASSES(256, 24, 2, 8, 1, 0, false, 400);  // 400 ns back-off
-            case 10: return LCPP_PASSES(256, 24, 2, 8, 1, 0, false, 32, true);  // PTX vote / warp barrier
-            case 14: return LCPP_PASSES(256, 24, 2, 8, 2, 0, false, 32, true);
+            case 3: return LCPP_PASSES(256, 24, 2, 8);  // slots ranked one at a time, CUDA intrinsics
+            case 4: return LCPP_PASSES(256, 24, 2, 8, 4, 0, false, 32, true);      // slots ranked in fours
+            case 5: return LCPP_PASSES(256, 24, 2, 8, 2, 4, true, 32, true);       // 4 blocks per SM, 16-bit ranks
+            case 6: return LCPP_PASSES(256, 24, 2, 8, 2, 1, false, 32, true);      // 2 blocks per SM
+            case 7: return LCPP_PASSES(256, 24, 2, 8, 2, 0, false, 0, true);       // look-back without back-off
+            case 8: return LCPP_PASSES(256, 24, 2, 8, 2, 0, false, 400, true);     // 400 ns back-off
             default: break;
             }
         }
         // Measured best on B200 for 4-byte keys: 256 x 24 keys per tile,
-        // peers from low-5-bit shared masks plus 3 ballots, 3 blocks per SM
-        // (80 registers).  Variants 3-6 were within 1.5 % of it or slower.
-        return LCPP_PASSES(256, 24, 2, 8);
+        // peers from low-5-bit shared masks plus 3 ballots, slots ranked in
+        // pairs, votes / shuffles / warp barrier as PTX, 3 blocks per SM
+        // (80 registers).  Variants 1-8 were within 1.5 % of it or slower;
+        // the look-back back-off made no difference.
+        return LCPP_PASSES(256, 24, 2, 8, 2, 0, false, 32, true);
     } else if constexpr (sizeof(U) == 4 && sizeof(V) == 4) {
         switch (onesweep_variant()) {
         case 11: return LCPP_PASSES(384, 15, 0, 8);  // 8 ballots per digit
