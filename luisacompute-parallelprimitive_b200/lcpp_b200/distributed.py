@@ -510,6 +510,17 @@ def distributed_reduce_totals(x_local, dist):
 # ---------------------------------------------------------------------------
 # Benchmark (bench.py, N > 1)
 # ---------------------------------------------------------------------------
+class _NoSampler:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+    def summary(self):
+        return None
+
+
 def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak, seed=0, zipf=False,
                            metric="Gkeys/s uint32 SortKeys @2^28", scaling="weak"):
     """Benchmark of distributed_sort_keys: n_local u32 keys per rank (rank r
@@ -562,7 +573,10 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
     bus = getattr(props, "pci_bus_id", None)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stream = torch.cuda.current_stream()
-    with clock_sampler_cls(f"{bus:02x}:00.0" if isinstance(bus, int) else None) as clocks:
+    # one nvidia-smi sampler (rank 0) for the whole job: a sampler per rank
+    # adds NVML queries of every GPU while the ranks are being timed
+    sampler = clock_sampler_cls(f"{bus:02x}:00.0" if isinstance(bus, int) else None) if r == 0 else _NoSampler()
+    with sampler as clocks:
         diag_timing_enable(True)
         dist.barrier()
         torch.cuda.synchronize()
