@@ -75,13 +75,13 @@ OPS = {
     "reduce_max": dict(metric="Gitems/s int64 Reduce Max @2^30", unit="Gitems/s", log2n=30, dtype="i64",
                        workload="DeviceReduce::Max i64 uniform, seed 1", bytes=8, kbytes=8, kernel="reduce_kernel"),
     # DeviceSegmentedRadixSort (SURVEY next-row widening): 2^27 u32 keys in
-    # segments of 1..2047 keys (sizes uniform, seed 1), contiguous.
-    # Algorithmic bytes counted like SortKeys (k(1+2P), P = 4); the dominant
-    # launch is an onesweep pass over the composite keys (8 B) and indices
-    # (4 B): 24 B per item.
+    # segments of 1..2047 keys (sizes uniform, seed 1), contiguous.  All
+    # segments are short, so the one-block-per-segment kernel does the whole
+    # sort: it reads and writes every key once (8 B per item, the op's and
+    # the kernel's algorithmic bytes).
     "segsort": dict(metric="Gkeys/s uint32 SegmentedRadixSort SortKeys @2^27", unit="Gkeys/s", log2n=27,
                     dtype="u32", workload="SegmentedRadixSort SortKeys u32 uniform, segments of 1..2047 keys, seed 1",
-                    bytes=36, kbytes=24, kernel="onesweep_kernel (one 8-bit pass of the segment|key composite)"),
+                    bytes=8, kbytes=8, kernel="small_segment_kernel (one block per segment, shared-memory LSD)"),
     # Distributed SortKeys of 2^32 keys in total (seed 7), sharded evenly:
     # strong scaling over N GPUs (N = 1 is the 1-GPU-equivalent run).
     "dist": dict(metric="Gkeys/s uint32 distributed SortKeys @2^32", unit="Gkeys/s", log2n=32, dtype="u32",
@@ -259,6 +259,8 @@ class Workload:
             return L.KERNEL_SCAN
         if self.op.startswith("reduce"):
             return L.KERNEL_REDUCE
+        if self.op == "segsort":
+            return L.KERNEL_SEGMENT_BLOCK
         return L.KERNEL_SORT_ONESWEEP
 
 

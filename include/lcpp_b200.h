@@ -237,7 +237,10 @@ lcpp_status lcpp_reduce_max(void* temp, size_t temp_bytes, const void* d_in, voi
  * of begin offset and not to overlap.  Items outside every segment are not
  * written.  num_items and num_segments are at most 2^32 - 1.  The temp size
  * depends on num_items only; lcpp_device_status(temp, stream) reports the
- * device error word of the sorting passes.
+ * device error word of the sorting passes.  Segments of up to 2048 items are
+ * sorted by one block each in shared memory; if longer segments exist, the
+ * call reads their item count back (it synchronises `stream` once) and sorts
+ * them with the onesweep sort of a (segment, key) composite. 
  * ---------------------------------------------------------------------- */
 
 /* Replace DeviceSegmentedRadixSort::GetSortKeysTempStorageBytes /

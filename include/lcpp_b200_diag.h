@@ -21,7 +21,8 @@ typedef enum lcpp_kernel_kind {
     LCPP_KERNEL_SORT_HISTOGRAM = 0, /* all-pass digit histogram + digit offsets */
     LCPP_KERNEL_SORT_ONESWEEP = 1,  /* one 8-bit onesweep pass */
     LCPP_KERNEL_SCAN = 2,           /* decoupled look-back scan */
-    LCPP_KERNEL_REDUCE = 3          /* two-level reduce */
+    LCPP_KERNEL_REDUCE = 3,         /* two-level reduce */
+    LCPP_KERNEL_SEGMENT_BLOCK = 4   /* segmented sort: one block per short segment */
 } lcpp_kernel_kind;
 
 typedef struct lcpp_kernel_time {

@@ -9,8 +9,12 @@
 // begin[s] <= end[s] <= num_items; other items are not written.  Unlike
 // DeviceRadixSort, +0.0 and -0.0 are different keys here (no fold).
 //
-// B200 design: every segment is sorted by one onesweep sort of the whole
-// array.
+// B200 design.  Segments of at most kSmallMax (2048) items: one block each
+// sorts its segment in shared memory (stable 8-bit LSD passes), reading and
+// writing every key once.  Longer segments, when the blocks found any (their
+// item count is read back: one host sync), are sorted together by one
+// onesweep sort of the whole array, in which the items of short segments
+// count as inactive:
 //   1. build: one thread per item finds its segment by binary search over
 //      the begin offsets and writes the composite key
 //      (segment << kb) | key_bits (inactive items get segment =
@@ -24,6 +28,7 @@
 //      (through a stash when the output buffer is the input buffer).
 // Temp storage depends on num_items only (as the reference's query).
 #include <cstdint>
+#include <type_traits>
 
 #include "../../include/lcpp_b200.h"
 #include "common.cuh"
@@ -35,9 +40,33 @@ namespace seg {
 
 constexpr int kBlock = 256;
 
-// Segment of item i under the reference's rule, or num_segments.
+constexpr int kSmallBlock = 256;
+constexpr int kSmallItems = 8;
+constexpr int kSmallMax = kSmallBlock * kSmallItems;  // keys of a segment sorted by one block
+
+// Members of segment s under the reference's rule, for segments in
+// ascending order of begin offset: [begin[s], min(end[s], begin[s + 1]))
+// when begin[s] <= end[s] <= n, else none.
+__device__ __forceinline__ void segment_members(uint32_t s, const uint32_t* __restrict__ begin,
+                                                const uint32_t* __restrict__ end, uint32_t num_segments, uint64_t n,
+                                                uint64_t& lo, uint64_t& hi)
+{
+    lo = begin[s];
+    const uint64_t e = end[s];
+    if (!(lo <= e && e <= n)) {
+        hi = lo;
+        return;
+    }
+    const uint64_t next = s + 1 < num_segments ? uint64_t(begin[s + 1]) : e;
+    hi = next < e ? (next > lo ? next : lo) : e;
+}
+
+// Segment of item i under the reference's rule, or num_segments.  With
+// `large_only`, segments of at most kSmallMax members (sorted by the
+// one-block kernel) count as no segment.
 __device__ __forceinline__ uint32_t segment_of(uint64_t i, const uint32_t* __restrict__ begin,
-                                               const uint32_t* __restrict__ end, uint32_t num_segments, uint64_t n)
+                                               const uint32_t* __restrict__ end, uint32_t num_segments, uint64_t n,
+                                               bool large_only = false)
 {
     uint32_t lo = 0, hi = num_segments;  // number of segments with begin <= i
     while (lo < hi) {
@@ -50,7 +79,13 @@ __device__ __forceinline__ uint32_t segment_of(uint64_t i, const uint32_t* __res
     if (lo == 0) return num_segments;
     const uint32_t s = lo - 1;
     const uint64_t b = begin[s], e = end[s];
-    return (b <= i && i < e && b <= e && e <= n) ? s : num_segments;
+    if (!(b <= i && i < e && b <= e && e <= n)) return num_segments;
+    if (large_only) {
+        uint64_t mlo, mhi;
+        segment_members(s, begin, end, num_segments, n, mlo, mhi);
+        if (mhi - mlo <= uint64_t(kSmallMax)) return num_segments;
+    }
+    return s;
 }
 
 // Key bits [begin_bit, begin_bit + kb) of the radix bijection (no +-0 fold),
@@ -69,12 +104,12 @@ __device__ __forceinline__ uint64_t key_field(U k, const KeyCodec<U>& c, int beg
 template <typename U, typename CT>
 __global__ void build_kernel(const U* __restrict__ keys, uint64_t n, const uint32_t* __restrict__ begin,
                              const uint32_t* __restrict__ end, uint32_t num_segments, KeyCodec<U> codec,
-                             int begin_bit, uint64_t mask, int key_bits, int desc, int with_segment,
+                             int begin_bit, uint64_t mask, int key_bits, int desc, int with_segment, int large_only,
                              CT* __restrict__ comp, uint32_t* __restrict__ idx)
 {
     for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += uint64_t(gridDim.x) * blockDim.x) {
         uint64_t c = key_bits ? key_field(keys[i], codec, begin_bit, mask, desc != 0) : 0;
-        if (with_segment) c |= uint64_t(segment_of(i, begin, end, num_segments, n)) << key_bits;
+        if (with_segment) c |= uint64_t(segment_of(i, begin, end, num_segments, n, large_only != 0)) << key_bits;
         comp[i] = CT(c);
         idx[i] = uint32_t(i);
     }
@@ -82,11 +117,135 @@ __global__ void build_kernel(const U* __restrict__ keys, uint64_t n, const uint3
 
 // Second key of the two-sort path: the segment of each (key-sorted) item.
 __global__ void segment_key_kernel(const uint32_t* __restrict__ idx, uint64_t n, const uint32_t* __restrict__ begin,
-                                   const uint32_t* __restrict__ end, uint32_t num_segments,
+                                   const uint32_t* __restrict__ end, uint32_t num_segments, int large_only,
                                    uint64_t* __restrict__ comp)
 {
     for (uint64_t j = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += uint64_t(gridDim.x) * blockDim.x)
-        comp[j] = segment_of(idx[j], begin, end, num_segments, n);
+        comp[j] = segment_of(idx[j], begin, end, num_segments, n, large_only != 0);
+}
+
+// ---------------------------------------------------------------------------
+// Short segments: one block sorts a segment of at most kSmallMax keys in
+// shared memory -- a stable LSD radix sort over the key field, 8 bits per
+// pass, ranked like the onesweep tile (8 ballots per slot for the lanes
+// holding the same digit, per-warp digit counters, a block scan over digits
+// and warps), so every key is read and written once in global memory.
+// Blocks of longer segments only add their length to *large_items.
+// ---------------------------------------------------------------------------
+template <typename U, typename V, bool PAIRS>
+__global__ void __launch_bounds__(kSmallBlock)
+small_segment_kernel(const U* __restrict__ keys_in, U* __restrict__ keys_out, const V* __restrict__ vals_in,
+                     V* __restrict__ vals_out, uint64_t n, const uint32_t* __restrict__ begin,
+                     const uint32_t* __restrict__ end, uint32_t num_segments, KeyCodec<U> codec, int begin_bit,
+                     int key_bits, int desc, unsigned long long* __restrict__ large_items)
+{
+    constexpr int kWarps = kSmallBlock / 32;
+    __shared__ U s_keys[kSmallMax];
+    __shared__ V s_vals[PAIRS ? kSmallMax : 1];
+    __shared__ uint32_t s_count[kWarps][256];
+    __shared__ uint32_t s_warp_sum[kWarps];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint64_t mask = key_bits >= 64 ? ~uint64_t(0) : ((uint64_t(1) << key_bits) - 1);
+    const int passes = (key_bits + 7) / 8;
+    const uint32_t lt = (1u << lane) - 1u;
+
+    for (uint64_t seg = blockIdx.x; seg < num_segments; seg += gridDim.x) {
+        uint64_t lo, hi;
+        segment_members(uint32_t(seg), begin, end, num_segments, n, lo, hi);
+        const int len = int(hi - lo > uint64_t(kSmallMax) ? kSmallMax + 1 : hi - lo);
+        if (len > kSmallMax) {
+            if (tid == 0) atomicAdd(large_items, (unsigned long long)(hi - lo));
+            continue;
+        }
+        if (len == 0) continue;
+        // load: slot i of lane l of warp w is position w * 8 * 32 + i * 32 + l
+        U k[kSmallItems];
+        V v[PAIRS ? kSmallItems : 1];
+#pragma unroll
+        for (int i = 0; i < kSmallItems; ++i) {
+            const int p = warp * kSmallItems * 32 + i * 32 + lane;
+            if (p < len) {
+                k[i] = keys_in[lo + p];
+                if constexpr (PAIRS) v[i] = vals_in[lo + p];
+            }
+        }
+        for (int pass = 0; pass < passes && len > 1; ++pass) {
+            for (int d = tid; d < kWarps * 256; d += kSmallBlock) (&s_count[0][0])[d] = 0;
+            __syncthreads();
+            uint32_t dig[kSmallItems], rank[kSmallItems];
+#pragma unroll
+            for (int i = 0; i < kSmallItems; ++i) {
+                const int slot = warp * kSmallItems * 32 + i * 32;  // first position of this warp slot
+                const int p = slot + lane;
+                rank[i] = 0;
+                dig[i] = 0;
+                if (slot >= len) continue;  // warp-uniform: no key of this slot exists
+                // positions past the end take digit 255 and rank after every key
+                dig[i] = p < len ? uint32_t(key_field(k[i], codec, begin_bit, mask, desc != 0) >> (8 * pass)) & 0xffu
+                                 : 0xffu;
+                uint32_t peers = 0xffffffffu;
+#pragma unroll
+                for (int b = 0; b < 8; ++b) {
+                    const bool bit = (dig[i] >> b) & 1u;
+                    const uint32_t vote = __ballot_sync(0xffffffffu, bit);
+                    peers &= bit ? vote : ~vote;
+                }
+                const int leader = 31 - __clz(peers);
+                uint32_t base = 0;
+                if (lane == leader) base = atomicAdd(&s_count[warp][dig[i]], uint32_t(__popc(peers)));
+                base = __shfl_sync(0xffffffffu, base, leader);
+                rank[i] = base + __popc(peers & lt);
+            }
+            __syncthreads();
+            // digit d (one per thread): exclusive prefix over digits, then over warps
+            {
+                uint32_t tot = 0;
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) tot += s_count[w][tid];
+                uint32_t incl = tot;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                if (lane == 31) s_warp_sum[warp] = incl;
+                __syncthreads();
+                uint32_t run = incl - tot;
+                for (int w = 0; w < warp; ++w) run += s_warp_sum[w];
+#pragma unroll
+                for (int w = 0; w < kWarps; ++w) {
+                    const uint32_t c = s_count[w][tid];
+                    s_count[w][tid] = run;
+                    run += c;
+                }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int i = 0; i < kSmallItems; ++i) {
+                if (warp * kSmallItems * 32 + i * 32 >= len) continue;
+                const uint32_t r = s_count[warp][dig[i]] + rank[i];
+                s_keys[r] = k[i];
+                if constexpr (PAIRS) s_vals[r] = v[i];
+            }
+            __syncthreads();
+#pragma unroll
+            for (int i = 0; i < kSmallItems; ++i) {
+                const int p = warp * kSmallItems * 32 + i * 32 + lane;
+                if (p - lane >= len) continue;
+                k[i] = s_keys[p];
+                if constexpr (PAIRS) v[i] = s_vals[p];
+            }
+            __syncthreads();
+        }
+#pragma unroll
+        for (int i = 0; i < kSmallItems; ++i) {
+            const int p = warp * kSmallItems * 32 + i * 32 + lane;
+            if (p < len) {
+                keys_out[lo + p] = k[i];
+                if constexpr (PAIRS) vals_out[lo + p] = v[i];
+            }
+        }
+    }
 }
 
 // heads[j] = j where a segment's run starts in sorted order, else 0.
@@ -121,7 +280,7 @@ __global__ void scatter_kernel(const T* __restrict__ src, const uint32_t* __rest
 }
 
 struct Layout {
-    size_t comp0, comp1, idx0, idx1, heads, first, stash_k, stash_v, scan, sort, total;
+    size_t comp0, comp1, idx0, idx1, heads, first, stash_k, stash_v, scan, sort, large, total;
 };
 
 Layout make_layout(int kb, int vb, uint64_t n)
@@ -143,6 +302,7 @@ Layout make_layout(int kb, int vb, uint64_t n)
     L.stash_k = take(size_t(n) * kb);
     L.stash_v = take(size_t(n) * vb);
     L.scan = take(scan::temp_bytes(LCPP_U32, n));
+    L.large = take(sizeof(unsigned long long));  // items in segments too long for one block
     L.total = off;
     return L;
 }
@@ -187,18 +347,32 @@ void launch_scatter(int eb, const void* src, const uint32_t* idx, const CT* comp
 template <typename U>
 void launch_build(const void* keys, uint64_t n, const uint32_t* begin, const uint32_t* end, uint32_t num_segments,
                   lcpp_dtype kdt, int begin_bit, int key_bits, int desc, bool with_segment, bool wide,
-                  void* comp, uint32_t* idx, cudaStream_t s)
+                  void* comp, uint32_t* idx, cudaStream_t s, int large_only)
 {
     const KeyCodec<U> codec = make_codec<U>(kdt, false);
     const uint64_t mask = key_bits >= 64 ? ~uint64_t(0) : ((uint64_t(1) << key_bits) - 1);
     if (wide)
         build_kernel<U, uint64_t><<<grid_for(n), kBlock, 0, s>>>(
             static_cast<const U*>(keys), n, begin, end, num_segments, codec, begin_bit, mask, key_bits, desc,
-            with_segment, static_cast<uint64_t*>(comp), idx);
+            with_segment, large_only, static_cast<uint64_t*>(comp), idx);
     else
         build_kernel<U, uint32_t><<<grid_for(n), kBlock, 0, s>>>(
             static_cast<const U*>(keys), n, begin, end, num_segments, codec, begin_bit, mask, key_bits, desc,
-            with_segment, static_cast<uint32_t*>(comp), idx);
+            with_segment, large_only, static_cast<uint32_t*>(comp), idx);
+}
+
+template <typename U, typename V, bool PAIRS>
+void launch_small(const void* kin, void* kout, const void* vin, void* vout, uint64_t n, const uint32_t* begin,
+                  const uint32_t* end, uint32_t num_segments, lcpp_dtype kdt, int begin_bit, int key_bits, int desc,
+                  unsigned long long* large, cudaStream_t s)
+{
+    const KeyCodec<U> codec = make_codec<U>(kdt, false);
+    const uint64_t cap = uint64_t(device_sm_count()) * 8;
+    const unsigned grid = unsigned(num_segments < cap ? num_segments : cap);
+    diag::KernelTimer timer(4 /* LCPP_KERNEL_SEGMENT_BLOCK */, n, s);
+    small_segment_kernel<U, V, PAIRS><<<grid, kSmallBlock, 0, s>>>(
+        static_cast<const U*>(kin), static_cast<U*>(kout), static_cast<const V*>(vin), static_cast<V*>(vout), n,
+        begin, end, num_segments, codec, begin_bit, key_bits, desc, large);
 }
 
 }  // namespace seg
@@ -257,6 +431,36 @@ lcpp_status segmented_sort(void* temp, size_t temp_bytes_given, const void* keys
     const lcpp_dtype comp_dt = wide ? LCPP_U64 : LCPP_U32;
     int csel = 0;
 
+    // Short segments: one block each, straight from input to output.
+    unsigned long long* large = reinterpret_cast<unsigned long long*>(t + L.large);
+    LCPP_CUDA_TRY(cudaMemsetAsync(large, 0, sizeof(unsigned long long), stream));
+    {
+        auto small = [&](auto ktag, auto vtag, auto pairs_tag) {
+            using U = decltype(ktag);
+            using V = decltype(vtag);
+            launch_small<U, V, decltype(pairs_tag)::value>(kin, kout, vin, vout, n, begin_offsets, end_offsets, nseg,
+                                                           kdt, begin_bit, key_bits, descending, large, stream);
+        };
+        using T_ = std::true_type;
+        using F_ = std::false_type;
+        if (!pairs)
+            kb == 4 ? small(uint32_t{}, uint32_t{}, F_{}) : small(uint64_t{}, uint32_t{}, F_{});
+        else if (kb == 4)
+            vb == 4 ? small(uint32_t{}, uint32_t{}, T_{}) : small(uint32_t{}, uint64_t{}, T_{});
+        else
+            vb == 4 ? small(uint64_t{}, uint32_t{}, T_{}) : small(uint64_t{}, uint64_t{}, T_{});
+    }
+    // Longer segments (if any): the composite sort below, restricted to
+    // them.  Reading their item count back is the call's one host sync.
+    unsigned long long large_items = 0;
+    LCPP_CUDA_TRY(cudaMemcpyAsync(&large_items, large, sizeof(large_items), cudaMemcpyDeviceToHost, stream));
+    LCPP_CUDA_TRY(cudaStreamSynchronize(stream));
+    if (large_items == 0) {
+        if (cudaGetLastError() != cudaSuccess) return LCPP_ERR_CUDA;
+        if (double_buffer) *selector ^= (flips & 1);
+        return LCPP_OK;
+    }
+    
     auto run_sort = [&](int bits) -> lcpp_status {
         return radix::sort(t + L.sort, radix::temp_bytes(8, 4, n), nullptr, nullptr, nullptr, nullptr, comp, idx,
                            &csel, n, 0, bits, 0, comp_dt, LCPP_U32, true, true, stream);
@@ -265,24 +469,24 @@ lcpp_status segmented_sort(void* temp, size_t temp_bytes_given, const void* keys
     if (one_sort) {
         if (kb == 4)
             launch_build<uint32_t>(kin, n, begin_offsets, end_offsets, nseg, kdt, begin_bit, key_bits, descending,
-                                   true, wide, comp[0], static_cast<uint32_t*>(idx[0]), stream);
+                                   true, wide, comp[0], static_cast<uint32_t*>(idx[0]), stream, 1);
         else
             launch_build<uint64_t>(kin, n, begin_offsets, end_offsets, nseg, kdt, begin_bit, key_bits, descending,
-                                   true, wide, comp[0], static_cast<uint32_t*>(idx[0]), stream);
+                                   true, wide, comp[0], static_cast<uint32_t*>(idx[0]), stream, 1);
         lcpp_status st = run_sort(total_bits);
         if (st != LCPP_OK) return st;
     } else {
         // key bits first, then a stable sort by segment
         if (kb == 4)
             launch_build<uint32_t>(kin, n, begin_offsets, end_offsets, nseg, kdt, begin_bit, key_bits, descending,
-                                   false, true, comp[0], static_cast<uint32_t*>(idx[0]), stream);
+                                   false, true, comp[0], static_cast<uint32_t*>(idx[0]), stream, 1);
         else
             launch_build<uint64_t>(kin, n, begin_offsets, end_offsets, nseg, kdt, begin_bit, key_bits, descending,
-                                   false, true, comp[0], static_cast<uint32_t*>(idx[0]), stream);
+                                   false, true, comp[0], static_cast<uint32_t*>(idx[0]), stream, 1);
         lcpp_status st = run_sort(key_bits);
         if (st != LCPP_OK) return st;
         segment_key_kernel<<<grid_for(n), kBlock, 0, stream>>>(static_cast<const uint32_t*>(idx[csel]), n,
-                                                              begin_offsets, end_offsets, nseg,
+                                                              begin_offsets, end_offsets, nseg, 1,
                                                               static_cast<uint64_t*>(comp[csel]));
         st = run_sort(seg_bits);
         if (st != LCPP_OK) return st;

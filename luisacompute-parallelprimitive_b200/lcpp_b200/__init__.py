@@ -32,7 +32,7 @@ GEN_I32_SCAN, GEN_F32_UNIT, GEN_I64_UNIFORM, GEN_U32_INDEX = 4, 5, 6, 7
 GEN_F32_NORMAL, GEN_U32_ZIPF = 8, 9
 
 # lcpp_kernel_kind
-KERNEL_SORT_HISTOGRAM, KERNEL_SORT_ONESWEEP, KERNEL_SCAN, KERNEL_REDUCE = 0, 1, 2, 3
+KERNEL_SORT_HISTOGRAM, KERNEL_SORT_ONESWEEP, KERNEL_SCAN, KERNEL_REDUCE, KERNEL_SEGMENT_BLOCK = 0, 1, 2, 3, 4
 
 _lib = None
 

@@ -171,7 +171,9 @@ def test_two_sort_path_and_narrow_composite(lcpp, oracle):
     n = 100_000
     keys = rng.integers(0, 2**64 - 1, n, dtype=np.uint64)
     keys[::3] = keys[5]
-    b, e = _segments(rng, n, "many")
+    # long segments (composite sort) mixed with short ones (one block each)
+    b = np.array([0, 5000, 5100, 70000, 70001], np.uint32)
+    e = np.array([5000, 5100, 70000, 70001, n], np.uint32)
     for desc in (False, True):
         ok, _, _ = _run(lcpp, keys, None, b, e, 0, 64, desc, "copy")
         exp, _ = oracle.segmented_radix_sort(keys, None, b, e, 0, 64, desc)
@@ -181,6 +183,27 @@ def test_two_sort_path_and_narrow_composite(lcpp, oracle):
     ok, _, _ = _run(lcpp, k32, None, b, e, 8, 16, True, "copy")
     exp, _ = oracle.segmented_radix_sort(k32, None, b, e, 8, 16, True)
     np.testing.assert_array_equal(ok, exp)
+
+
+@pytest.mark.parametrize("kdt,vdt", [(np.uint32, None), (np.int32, np.uint32), (np.float64, np.uint64),
+                                     (np.uint64, np.uint32)])
+def test_short_segment_kernel_boundaries(lcpp, oracle, kdt, vdt):
+    """Segment lengths around the one-block limit (2048): 0, 1, 2, 2047, 2048
+    (one block) and 2049 (composite sort), in one call."""
+    rng = np.random.default_rng(17)
+    sizes = [0, 1, 2, 31, 33, 2047, 2048, 2049, 5, 4096, 2048]
+    cum = np.concatenate([[0], np.cumsum(sizes)]).astype(np.uint32)
+    n = int(cum[-1]) + 10  # trailing items outside every segment
+    keys = _keys_for(rng, kdt, n, "ties")
+    vals = None if vdt is None else np.arange(n).astype(vdt)
+    for desc in (False, True):
+        ok, ov, _ = _run(lcpp, keys, vals, cum[:-1], cum[1:], 0, np.dtype(kdt).itemsize * 8, desc, "copy")
+        exp_k, exp_v = oracle.segmented_radix_sort(keys, vals, cum[:-1], cum[1:], 0, None, desc)
+        m = int(cum[-1])
+        np.testing.assert_array_equal(_bits(ok)[:m], _bits(exp_k)[:m])
+        assert (_bits(ok)[m:] == _bits(np.full(10, SENT[keys.dtype], keys.dtype))).all()
+        if vals is not None:
+            np.testing.assert_array_equal(ov[:m], exp_v[:m])
 
 
 def test_large(lcpp, oracle):
