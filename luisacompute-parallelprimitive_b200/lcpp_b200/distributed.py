@@ -11,7 +11,8 @@ Sort (keys only), per rank:
      rank counts its sorted keys per 16-bit sub-bucket of each boundary's
      current prefix (device binary searches), the counts are all-reduced,
      and the sub-bucket holding P_j extends the prefix; after key_bits/16
-     rounds the prefix is the exact boundary key k_j;
+     rounds the prefix is the exact boundary key k_j (for 32-bit keys all
+     of it in device tensors, one host wait at the end);
   3. keys equal to k_j are split between the ranks below and above the
      boundary in rank order, so every rank receives exactly its share even
      when one key value fills several ranks (heavy hitters);
@@ -99,6 +100,19 @@ class GpuOps:
             check(lib().lcpp_dist_search_sorted(
                 ctypes.c_void_p(sorted_keys.data_ptr()), sorted_keys.numel(), ctypes.c_void_p(q.data_ptr()),
                 q.numel(), int(upper), ctypes.c_void_p(out.data_ptr()), dtype_code(sorted_keys),
+                ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "lcpp_dist_search_sorted")
+        return out
+
+    def search_bits(self, sorted_keys, queries, upper: bool):
+        """search() with the queries already a device tensor holding key images
+        of the key width (int32 / int64 with the image's bits)."""
+        torch = self.torch
+        out = torch.empty(queries.numel(), dtype=torch.int64, device=self.device)
+        if queries.numel():
+            self.launches += 1
+            check(lib().lcpp_dist_search_sorted(
+                ctypes.c_void_p(sorted_keys.data_ptr()), sorted_keys.numel(), ctypes.c_void_p(queries.data_ptr()),
+                queries.numel(), int(upper), ctypes.c_void_p(out.data_ptr()), dtype_code(sorted_keys),
                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "lcpp_dist_search_sorted")
         return out
 
@@ -268,11 +282,86 @@ def _all_gather_int64(dist, values, device):
     return [o.tolist() for o in out]
 
 
+def _split_indices(G, sizes, P, below, lo_hi):
+    """idx[r][j]: split index of rank r before destination j.  Keys equal to
+    boundary key k_j go below the boundary in rank order until the boundary
+    holds exactly P_j keys.  lo_hi[r] = lo (G-1 values) ++ hi (G-1 values):
+    counts of rank r's keys with image < k_j and <= k_j."""
+    idx = [[0] * (G + 1) for _ in range(G)]
+    for rr in range(G):
+        idx[rr][G] = sizes[rr]
+    for j in range(G - 1):
+        remaining = P[j] - below[j]  # keys equal to k_j that go below boundary j, in rank order
+        for rr in range(G):
+            lo_r, hi_r = lo_hi[rr][j], lo_hi[rr][G - 1 + j]
+            take = min(hi_r - lo_r, remaining)
+            idx[rr][j + 1] = lo_r + take
+            remaining -= take
+        if remaining != 0:
+            raise LcppError(7, "distributed splitter selection is inconsistent")
+    return idx
+
+
+def _exact_splits_32(sorted_keys, dist, ops):
+    """exact_splits for 32-bit keys with every step on the device: the
+    queries, counts, histograms, cumulative sums and prefix updates stay in
+    device tensors, and the host waits once, for the final all-gather."""
+    import torch
+    G, r = dist.get_world_size(), dist.get_rank()
+    dev = ops.device
+    n_local = sorted_keys.numel()
+    mine = torch.tensor([n_local], dtype=torch.int64, device=dev)
+    parts = [torch.empty_like(mine) for _ in range(G)]
+    dist.all_gather(parts, mine)
+    sizes_t = torch.cat(parts)
+    P = torch.arange(1, G, dtype=torch.int64, device=dev) * sizes_t.sum() // G
+    prefix = torch.zeros(G - 1, dtype=torch.int64, device=dev)
+    below = torch.zeros(G - 1, dtype=torch.int64, device=dev)
+    sub = 1 << SUB_BITS
+    l_all = torch.arange(sub + 1, dtype=torch.int64, device=dev)
+
+    def as_bits(q):  # values in [0, 2^32) as the int32 with the same bits
+        return torch.where(q >= (1 << 31), q - (1 << 32), q).to(torch.int32)
+
+    for rnd in range(32 // SUB_BITS):
+        shift = 32 - SUB_BITS * (rnd + 1)
+        # query ((prefix << 16) | l) << shift for l in [0, 2^16]; 2^32 (the end
+        # of the last prefix range) stands for the key count
+        q = ((prefix[:, None] << SUB_BITS) + l_all[None, :]) << shift
+        over = q >= (1 << 32)
+        counts = ops.search_bits(sorted_keys, as_bits(torch.where(over, torch.zeros_like(q), q)).reshape(-1),
+                                 upper=False).view(G - 1, sub + 1)
+        counts = torch.where(over, torch.full_like(counts, n_local), counts)
+        hist = (counts[:, 1:] - counts[:, :-1]).contiguous()
+        dist.all_reduce(hist)
+        cum = torch.cumsum(hist, dim=1)
+        # first sub-bucket whose cumulative count exceeds the residual rank
+        l = torch.searchsorted(cum, (P - below).unsqueeze(1), right=True).squeeze(1)
+        below = below + torch.where(l > 0, cum.gather(1, (l - 1).clamp_min(0).unsqueeze(1)).squeeze(1),
+                                    torch.zeros_like(l))
+        prefix = (prefix << SUB_BITS) | l
+    kq = as_bits(prefix)
+    lo = ops.search_bits(sorted_keys, kq, upper=False)
+    hi = ops.search_bits(sorted_keys, kq, upper=True)
+    row = torch.cat([lo, hi, below, P, sizes_t])
+    parts = [torch.empty_like(row) for _ in range(G)]
+    dist.all_gather(parts, row)
+    rows = torch.stack(parts).tolist()  # the one host wait
+    m = G - 1
+    below_l, P_l, sizes = rows[0][2 * m:3 * m], rows[0][3 * m:4 * m], rows[0][4 * m:]
+    idx = _split_indices(G, sizes, P_l, below_l, [rw[:2 * m] for rw in rows])
+    send = [idx[r][j + 1] - idx[r][j] for j in range(G)]
+    recv = [idx[i][r + 1] - idx[i][r] for i in range(G)]
+    return send, recv, idx
+
+
 def exact_splits(sorted_keys, dist, ops):
     """Split indices of this rank's sorted keys so that rank j receives global
     sorted positions [P_j, P_{j+1}).  Returns (send_counts, recv_counts, idx)
     where idx[r][j] is the split index of rank r before destination j."""
     import torch
+    if sorted_keys.element_size() == 4 and hasattr(ops, "search_bits"):
+        return _exact_splits_32(sorted_keys, dist, ops)
     G, r = dist.get_world_size(), dist.get_rank()
     device = ops.device
     n_local = sorted_keys.numel()
@@ -319,18 +408,7 @@ def exact_splits(sorted_keys, dist, ops):
     lo = ops.search(sorted_keys, kq, upper=False).tolist()
     hi = ops.search(sorted_keys, kq, upper=True).tolist()
     gathered = _all_gather_int64(dist, lo + hi, device)
-    idx = [[0] * (G + 1) for _ in range(G)]
-    for rr in range(G):
-        idx[rr][G] = sizes[rr]
-    for j in range(G - 1):
-        remaining = P[j] - below[j]  # keys equal to k_j that go below boundary j, in rank order
-        for rr in range(G):
-            lo_r, hi_r = gathered[rr][j], gathered[rr][G - 1 + j]
-            take = min(hi_r - lo_r, remaining)
-            idx[rr][j + 1] = lo_r + take
-            remaining -= take
-        if remaining != 0:
-            raise LcppError(7, "distributed splitter selection is inconsistent")
+    idx = _split_indices(G, sizes, P, below, gathered)
     send = [idx[r][j + 1] - idx[r][j] for j in range(G)]
     recv = [idx[i][r + 1] - idx[i][r] for i in range(G)]
     return send, recv, idx

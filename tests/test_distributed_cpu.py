@@ -30,6 +30,10 @@ class NumpyOps:
         q = queries.astype(np.uint64)
         return torch.from_numpy(np.searchsorted(img, q, side="right" if upper else "left").astype(np.int64))
 
+    def search_bits(self, sorted_keys, queries, upper):
+        q = queries.numpy().view(np.uint32 if queries.element_size() == 4 else np.uint64)
+        return self.search(sorted_keys, q, upper)
+
     def merge(self, a, b, out):
         ab = np.concatenate([a.numpy(), b.numpy()])
         out.copy_(torch.from_numpy(ab[np.argsort(key_images_np(ab), kind="stable")].copy()))
