@@ -82,6 +82,12 @@ OPS = {
     "segsort": dict(metric="Gkeys/s uint32 SegmentedRadixSort SortKeys @2^27", unit="Gkeys/s", log2n=27,
                     dtype="u32", workload="SegmentedRadixSort SortKeys u32 uniform, segments of 1..2047 keys, seed 1",
                     bytes=8, kbytes=8, kernel="small_segment_kernel (one block per segment, shared-memory LSD)"),
+    # Merge path of the distributed sort (lcpp_dist_merge_sorted): two sorted
+    # runs of 2^27 u32 keys (uniform, seed 1) into 2^28; reads and writes
+    # every key once (8 B per output key).
+    "merge": dict(metric="Gkeys/s uint32 merge of two sorted runs @2^28", unit="Gkeys/s", log2n=28, dtype="u32",
+                  workload="merge path of two sorted u32 runs of 2^27 keys, uniform, seed 1", bytes=8, kbytes=8,
+                  kernel="merge_block_kernel"),
     # Distributed SortKeys of 2^32 keys in total (seed 7), sharded evenly:
     # strong scaling over N GPUs (N = 1 is the 1-GPU-equivalent run).
     "dist": dict(metric="Gkeys/s uint32 distributed SortKeys @2^32", unit="Gkeys/s", log2n=32, dtype="u32",
@@ -221,6 +227,15 @@ class Workload:
             self.temp = L.alloc_temp(L.DeviceSegmentedRadixSort.GetSortKeysTempStorageBytes(L.U32, n))
             self.ss = L.DeviceSegmentedRadixSort()
             del np
+        elif op == "merge":
+            from lcpp_b200.distributed import GpuOps
+            self.gops = GpuOps()
+            half = n // 2
+            keys = fill(T.uint32, L.GEN_U32_UNIFORM, 1)
+            self.inputs = [self.gops.local_sort(keys[:half].clone()), self.gops.local_sort(keys[half:].clone())]
+            self.outputs = [T.empty(n, dtype=T.uint32, device=dev)]
+            self.temp = None
+            del keys
         elif op == "scan":
             self.inputs = [fill(T.int32, L.GEN_I32_SCAN, 1)]
             self.outputs = [T.empty_like(self.inputs[0])]
@@ -243,6 +258,8 @@ class Workload:
             self.rs.SortKeys(t, i[0], o[0], n, 8, 24)
         elif op.startswith("pairs"):
             self.rs.SortPairs(t, i[0], o[0], i[1], o[1], n)
+        elif op == "merge":
+            self.gops.merge(i[0], i[1], o[0])
         elif op == "segsort":
             b, e, nseg = self.seg
             self.ss.SortKeys(t, i[0], o[0], n, nseg, b, e)
@@ -261,6 +278,8 @@ class Workload:
             return L.KERNEL_REDUCE
         if self.op == "segsort":
             return L.KERNEL_SEGMENT_BLOCK
+        if self.op == "merge":
+            return L.KERNEL_MERGE
         return L.KERNEL_SORT_ONESWEEP
 
 
@@ -278,6 +297,12 @@ def cpu_fn(op: str, n_sample: int, threads: int):
     """One run of the oracle port on a bounded sample of the workload (the
     reference tests' host algorithms restated)."""
     from oracle import oracle as O
+    if op == "merge":
+        import numpy as np
+        x = O.generate(O.GEN_U32_UNIFORM, n_sample, seed=1)
+        a, b = np.sort(x[: n_sample // 2]), np.sort(x[n_sample // 2:])
+        # the reference tests' host merge: std::merge (ties from the first run)
+        return lambda: np.concatenate([a, b])[np.argsort(np.concatenate([a, b]), kind="stable")]
     if op == "segsort":
         x = O.generate(O.GEN_U32_UNIFORM, n_sample, seed=1)
         b, e = segsort_offsets(n_sample)
@@ -426,7 +451,8 @@ def run_ours(args):
     for _ in range(args.warmup):
         w.step()
     torch.cuda.synchronize()
-    assert L.device_status(w.temp) == L.OK
+    if w.temp is not None:
+        assert L.device_status(w.temp) == L.OK
 
     props = torch.cuda.get_device_properties(local)
     bus = getattr(props, "pci_bus_id", None)
@@ -443,7 +469,8 @@ def run_ours(args):
         recs = L.diag_timing_read()
         L.diag_timing_enable(False)
     ms = e0.elapsed_time(e1) / args.steps
-    assert L.device_status(w.temp) == L.OK
+    if w.temp is not None:
+        assert L.device_status(w.temp) == L.OK
     value = n / (ms * 1e-3) / 1e9
     clk = clocks.summary()
 
@@ -516,7 +543,7 @@ def run_ours(args):
            "steps": k_e2e, "ms_per_step": e2e_ms,
            "pipeline": "3 streams: H2D of step s+1 and D2H of step s-1 overlap the op of step s"}
     host_out = host_out[(k_e2e - 1) % 2]
-    if args.op in ("sort", "bits"):  # sanity: what came back is ordered
+    if args.op in ("sort", "bits", "merge"):  # sanity: what came back is ordered
         ho = host_out[0].numpy()
         if args.op == "bits":
             ho = (ho >> 8) & 0xFFFF

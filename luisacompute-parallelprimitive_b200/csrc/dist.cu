@@ -309,6 +309,7 @@ extern "C" lcpp_status lcpp_dist_merge_sorted_batch(void* temp, size_t temp_byte
         merge_split_kernel<U><<<sgrid, 256, 0, s>>>(mb, splits, c);
         const unsigned grid = unsigned(mb.block_start[count]);
         if (grid == 0) return;
+        diag::KernelTimer timer(5 /* LCPP_KERNEL_MERGE */, mb.split_start[count] - count, s);
         if (plain)
             merge_block_kernel<U, true><<<grid, kMergeBlock, 0, s>>>(mb, splits, c);
         else

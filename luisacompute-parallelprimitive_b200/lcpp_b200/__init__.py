@@ -33,6 +33,7 @@ GEN_F32_NORMAL, GEN_U32_ZIPF = 8, 9
 
 # lcpp_kernel_kind
 KERNEL_SORT_HISTOGRAM, KERNEL_SORT_ONESWEEP, KERNEL_SCAN, KERNEL_REDUCE, KERNEL_SEGMENT_BLOCK = 0, 1, 2, 3, 4
+KERNEL_MERGE = 5
 
 _lib = None
 
