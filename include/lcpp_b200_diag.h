@@ -40,6 +40,16 @@ lcpp_status lcpp_diag_timing_enable(int enable);
  * launch order) to `out`; *count receives the number of records held. */
 lcpp_status lcpp_diag_timing_read(lcpp_kernel_time* out, int capacity, int* count);
 
+/* Wait-timeout probe (no reference counterpart: the reference's look-back
+ * spins are unbounded, src/lcpp/agent/agent_radix_sort_onesweep.h:324-334).
+ * One device thread waits on a status word that nothing publishes, with the
+ * same bounded wait routine as the onesweep look-back but a limit of
+ * `limit_ns` (at most 4 s).  The wait runs out, records
+ * LCPP_ERR_LOOKBACK_TIMEOUT in temp's error word and the kernel returns, so
+ * lcpp_device_status(temp, stream) reports the timeout and the context stays
+ * usable.  temp: 256-byte aligned, at least 256 bytes. */
+lcpp_status lcpp_diag_wait_timeout_probe(void* temp, size_t temp_bytes, uint64_t limit_ns, lcpp_stream_t stream);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -133,6 +133,75 @@ inline KeyCodec<U> make_codec(lcpp_dtype dt, bool descending)
     return c;
 }
 
+// ---------------------------------------------------------------------------
+// Shared-memory and warp primitives of the ranking loops (inline PTX).
+// ---------------------------------------------------------------------------
+// Predicated shared-memory atomic add: returns the old value when `pred`,
+// else 0, without a branch.
+__device__ __forceinline__ uint32_t shared_add_if(bool pred, uint32_t smem_addr, uint32_t inc)
+{
+    uint32_t old = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "@p atom.shared.add.u32 %0, [%2], %3;\n\t}"
+        : "+r"(old)
+        : "r"(uint32_t(pred)), "r"(smem_addr), "r"(inc)
+        : "memory");
+    return old;
+}
+
+// Fire-and-forget shared-memory OR.
+__device__ __forceinline__ void shared_red_or(uint32_t smem_addr, uint32_t bits)
+{
+    asm volatile("red.shared.or.b32 [%0], %1;" ::"r"(smem_addr), "r"(bits) : "memory");
+}
+
+__device__ __forceinline__ uint32_t shared_load(uint32_t smem_addr)
+{
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void shared_store_if(bool pred, uint32_t smem_addr, uint32_t v)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.u32 p, %0, 0;\n\t"
+        "@p st.shared.u32 [%1], %2;\n\t}" ::"r"(uint32_t(pred)), "r"(smem_addr), "r"(v)
+        : "memory");
+}
+
+// Fire-and-forget shared-memory add.
+__device__ __forceinline__ void shared_red_add(uint32_t smem_addr, uint32_t inc)
+{
+    asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(smem_addr), "r"(inc) : "memory");
+}
+
+// Full-warp ballot and warp barrier written as PTX (vote.sync /
+// bar.warp.sync with the full member mask).
+__device__ __forceinline__ uint32_t warp_ballot(bool pred)
+{
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "vote.sync.ballot.b32 %0, p, 0xffffffff;\n\t}"
+        : "=r"(r)
+        : "r"(uint32_t(pred)));
+    return r;
+}
+
+__device__ __forceinline__ void warp_barrier() { asm volatile("bar.warp.sync 0xffffffff;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t warp_shfl(uint32_t v, int src)
+{
+    uint32_t r;
+    asm volatile("shfl.sync.idx.b32 %0, %1, %2, 0x1f, 0xffffffff;" : "=r"(r) : "r"(v), "r"(src));
+    return r;
+}
+
 // Cached per-device SM count (grid sizing in multiples of the SM count).
 int device_sm_count();
 

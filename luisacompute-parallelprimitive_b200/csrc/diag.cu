@@ -5,6 +5,7 @@
 
 #include "../../include/lcpp_b200_diag.h"
 #include "common.cuh"
+#include "radix_sort.cuh"
 
 namespace lcpp {
 namespace diag {
@@ -91,4 +92,10 @@ extern "C" lcpp_status lcpp_diag_timing_read(lcpp_kernel_time* out, int capacity
         out[i].items = r.items;
     }
     return LCPP_OK;
+}
+
+extern "C" lcpp_status lcpp_diag_wait_timeout_probe(void* temp, size_t temp_bytes, uint64_t limit_ns,
+                                                   lcpp_stream_t stream)
+{
+    return lcpp::radix::wait_timeout_probe(temp, temp_bytes, limit_ns, reinterpret_cast<cudaStream_t>(stream));
 }

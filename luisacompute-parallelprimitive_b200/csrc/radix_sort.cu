@@ -313,7 +313,7 @@ struct OnesweepSmem {
 // other tiles on the same SM.  On timeout (or when another thread already
 // reported an error) returns an inclusive zero so that the caller finishes.
 template <int SLEEP_NS, typename ST>
-__device__ __forceinline__ ST wait_status(const ST* p, ST w, uint32_t* error)
+__device__ __forceinline__ ST wait_status(const ST* p, ST w, uint32_t* error, uint64_t limit_ns = kWaitLimitNs)
 {
     using SB = StatusBits<ST>;
     uint32_t spins = 0;
@@ -326,7 +326,7 @@ __device__ __forceinline__ ST wait_status(const ST* p, ST w, uint32_t* error)
             const uint64_t now = global_timer_ns();
             if (t0 == 0) {
                 t0 = now;
-            } else if (now - t0 > kWaitLimitNs) {
+            } else if (now - t0 > limit_ns) {
                 report_error(error, kDevErrTimeout);
                 return SB::kInclusive;
             }
@@ -367,20 +367,6 @@ __device__ __forceinline__ OffT lookback_digit(const ST* status, uint32_t tile, 
     }
 }
 
-// Predicated shared-memory atomic add: returns the old value when `pred`,
-// else 0, without a branch.
-__device__ __forceinline__ uint32_t shared_add_if(bool pred, uint32_t smem_addr, uint32_t inc)
-{
-    uint32_t old = 0;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "@p atom.shared.add.u32 %0, [%2], %3;\n\t}"
-        : "+r"(old)
-        : "r"(uint32_t(pred)), "r"(smem_addr), "r"(inc)
-        : "memory");
-    return old;
-}
 
 // Lanes of the warp holding the same 8-bit digit: one ballot per digit bit
 // narrows the set (warp-level multisplit, Ashkiani et al., PPoPP 2016).  On
@@ -414,56 +400,10 @@ __device__ __forceinline__ uint32_t pass_digit(U t, int shift, uint32_t mask, ui
     }
 }
 
-// Fire-and-forget shared-memory OR.
-__device__ __forceinline__ void shared_red_or(uint32_t smem_addr, uint32_t bits)
-{
-    asm volatile("red.shared.or.b32 [%0], %1;" ::"r"(smem_addr), "r"(bits) : "memory");
-}
 
-__device__ __forceinline__ uint32_t shared_load(uint32_t smem_addr)
-{
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr) : "memory");
-    return v;
-}
 
-__device__ __forceinline__ void shared_store_if(bool pred, uint32_t smem_addr, uint32_t v)
-{
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.u32 p, %0, 0;\n\t"
-        "@p st.shared.u32 [%1], %2;\n\t}" ::"r"(uint32_t(pred)), "r"(smem_addr), "r"(v)
-        : "memory");
-}
 
-// Fire-and-forget shared-memory add.
-__device__ __forceinline__ void shared_red_add(uint32_t smem_addr, uint32_t inc)
-{
-    asm volatile("red.shared.add.u32 [%0], %1;" ::"r"(smem_addr), "r"(inc) : "memory");
-}
 
-// Full-warp ballot and warp barrier written as PTX (vote.sync /
-// bar.warp.sync with the full member mask).
-__device__ __forceinline__ uint32_t warp_ballot(bool pred)
-{
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "vote.sync.ballot.b32 %0, p, 0xffffffff;\n\t}"
-        : "=r"(r)
-        : "r"(uint32_t(pred)));
-    return r;
-}
-
-__device__ __forceinline__ void warp_barrier() { asm volatile("bar.warp.sync 0xffffffff;" ::: "memory"); }
-
-__device__ __forceinline__ uint32_t warp_shfl(uint32_t v, int src)
-{
-    uint32_t r;
-    asm volatile("shfl.sync.idx.b32 %0, %1, %2, 0x1f, 0xffffffff;" : "=r"(r) : "r"(v), "r"(src));
-    return r;
-}
 
 // Everything after the tile id is known.  FULL: the tile has kTile keys (all
 // but possibly the last tile), compiled without any per-key bounds logic.
@@ -725,6 +665,14 @@ onesweep_kernel(OnesweepArgs<U, V, ST, OffT> a)
         process_tile<true, BYTE, P, U, V, PAIRS, KIND, ST, OffT>(a, s, tile, kTile);
     else
         process_tile<false, BYTE, P, U, V, PAIRS, KIND, ST, OffT>(a, s, tile, int(a.n - tile_base));
+}
+
+// Wait-timeout probe: one thread waits, with the look-back's bounded wait
+// routine, on a status word that nothing publishes.  The wait runs out after
+// limit_ns, records LCPP_ERR_LOOKBACK_TIMEOUT and the kernel returns.
+__global__ void wait_timeout_probe_kernel(const uint32_t* never_published, uint32_t* error, uint64_t limit_ns)
+{
+    if (threadIdx.x == 0 && blockIdx.x == 0) wait_status<32>(never_published, 0u, error, limit_ns);
 }
 
 // ---------------------------------------------------------------------------
@@ -1062,6 +1010,25 @@ lcpp_status sort(void* temp, size_t temp_bytes_given, const void* keys_in, void*
 }
 
 size_t error_word_offset() { return offsetof(Ctrl, error); }
+
+}  // namespace radix
+}  // namespace lcpp
+
+namespace lcpp {
+namespace radix {
+
+lcpp_status wait_timeout_probe(void* temp, size_t temp_bytes, uint64_t limit_ns, cudaStream_t stream)
+{
+    if (!temp || (reinterpret_cast<uintptr_t>(temp) & (kTempAlign - 1)) || temp_bytes < kTempAlign)
+        return LCPP_ERR_INVALID_ARG;
+    if (limit_ns > kWaitLimitNs) return LCPP_ERR_INVALID_ARG;
+    // word 0: the status word nothing publishes; word 1: the error word (the
+    // offset lcpp_device_status reads)
+    uint32_t* words = static_cast<uint32_t*>(temp);
+    LCPP_CUDA_TRY(cudaMemsetAsync(words, 0, 2 * sizeof(uint32_t), stream));
+    wait_timeout_probe_kernel<<<1, 32, 0, stream>>>(words, words + 1, limit_ns);
+    return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;
+}
 
 }  // namespace radix
 }  // namespace lcpp

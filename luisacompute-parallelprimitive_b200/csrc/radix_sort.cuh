@@ -23,5 +23,9 @@ lcpp_status sort(void* temp, size_t temp_bytes, const void* keys_in, void* keys_
 // Byte offset of the device error word inside the sort's temp storage.
 size_t error_word_offset();
 
+// Runs the look-back's bounded wait on a status word nothing publishes
+// (lcpp_diag_wait_timeout_probe).
+lcpp_status wait_timeout_probe(void* temp, size_t temp_bytes, uint64_t limit_ns, cudaStream_t stream);
+
 }  // namespace radix
 }  // namespace lcpp

@@ -127,9 +127,10 @@ __global__ void segment_key_kernel(const uint32_t* __restrict__ idx, uint64_t n,
 // ---------------------------------------------------------------------------
 // Short segments: one block sorts a segment of at most kSmallMax keys in
 // shared memory -- a stable LSD radix sort over the key field, 8 bits per
-// pass, ranked like the onesweep tile (8 ballots per slot for the lanes
-// holding the same digit, per-warp digit counters, a block scan over digits
-// and warps), so every key is read and written once in global memory.
+// pass, ranked like the onesweep tile (lanes holding the same digit from
+// low-5-bit shared mask words and 3 ballots, per-warp digit counters, a
+// block scan over digits and warps), so every key is read and written once
+// in global memory.
 // Blocks of longer segments only add their length to *large_items.
 // ---------------------------------------------------------------------------
 template <typename U, typename V, bool PAIRS>
@@ -143,11 +144,19 @@ small_segment_kernel(const U* __restrict__ keys_in, U* __restrict__ keys_out, co
     __shared__ U s_keys[kSmallMax];
     __shared__ V s_vals[PAIRS ? kSmallMax : 1];
     __shared__ uint32_t s_count[kWarps][256];
+    __shared__ uint32_t s_masks[2][kWarps][32];  // per slot parity: lanes of each low-5-bit digit class
     __shared__ uint32_t s_warp_sum[kWarps];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint64_t mask = key_bits >= 64 ? ~uint64_t(0) : ((uint64_t(1) << key_bits) - 1);
     const int passes = (key_bits + 7) / 8;
     const uint32_t lt = (1u << lane) - 1u;
+    const uint32_t counters_base = static_cast<uint32_t>(__cvta_generic_to_shared(&s_count[warp][0]));
+    const uint32_t masks_base = static_cast<uint32_t>(__cvta_generic_to_shared(&s_masks[0][warp][0]));
+    constexpr uint32_t kSetBytes = kWarps * 32 * 4;
+
+    for (int d = tid; d < kWarps * 256; d += kSmallBlock) (&s_count[0][0])[d] = 0;
+    for (int d = tid; d < 2 * kWarps * 32; d += kSmallBlock) (&s_masks[0][0][0])[d] = 0;
+    __syncthreads();
 
     for (uint64_t seg = blockIdx.x; seg < num_segments; seg += gridDim.x) {
         uint64_t lo, hi;
@@ -169,9 +178,9 @@ small_segment_kernel(const U* __restrict__ keys_in, U* __restrict__ keys_out, co
                 if constexpr (PAIRS) v[i] = vals_in[lo + p];
             }
         }
+        // The digit counters are zero here (zeroed at start and after every
+        // pass's scatter).
         for (int pass = 0; pass < passes && len > 1; ++pass) {
-            for (int d = tid; d < kWarps * 256; d += kSmallBlock) (&s_count[0][0])[d] = 0;
-            __syncthreads();
             uint32_t dig[kSmallItems], rank[kSmallItems];
 #pragma unroll
             for (int i = 0; i < kSmallItems; ++i) {
@@ -183,17 +192,25 @@ small_segment_kernel(const U* __restrict__ keys_in, U* __restrict__ keys_out, co
                 // positions past the end take digit 255 and rank after every key
                 dig[i] = p < len ? uint32_t(key_field(k[i], codec, begin_bit, mask, desc != 0) >> (8 * pass)) & 0xffu
                                  : 0xffu;
-                uint32_t peers = 0xffffffffu;
+                // lanes of the same digit: a shared mask word per low-5-bit
+                // class (one per bank), narrowed by 3 ballots; the word is
+                // cleared once every lane has read it (the shuffle below
+                // depends on every lane's read), and the other parity's words
+                // serve the next slot
+                const uint32_t maddr = masks_base + uint32_t(i & 1) * kSetBytes + (dig[i] & 31u) * 4u;
+                shared_red_or(maddr, 1u << lane);
+                warp_barrier();
+                uint32_t peers = shared_load(maddr);
 #pragma unroll
-                for (int b = 0; b < 8; ++b) {
+                for (int b = 5; b < 8; ++b) {
                     const bool bit = (dig[i] >> b) & 1u;
-                    const uint32_t vote = __ballot_sync(0xffffffffu, bit);
+                    const uint32_t vote = warp_ballot(bit);
                     peers &= bit ? vote : ~vote;
                 }
                 const int leader = 31 - __clz(peers);
-                uint32_t base = 0;
-                if (lane == leader) base = atomicAdd(&s_count[warp][dig[i]], uint32_t(__popc(peers)));
-                base = __shfl_sync(0xffffffffu, base, leader);
+                uint32_t base = shared_add_if(lane == leader, counters_base + dig[i] * 4u, uint32_t(__popc(peers)));
+                base = warp_shfl(base, leader);
+                shared_store_if(true, maddr, 0u);
                 rank[i] = base + __popc(peers & lt);
             }
             __syncthreads();
@@ -228,6 +245,9 @@ small_segment_kernel(const U* __restrict__ keys_in, U* __restrict__ keys_out, co
                 if constexpr (PAIRS) s_vals[r] = v[i];
             }
             __syncthreads();
+            // reload in the new order; the counters are free again
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) s_count[w][tid] = 0;
 #pragma unroll
             for (int i = 0; i < kSmallItems; ++i) {
                 const int p = warp * kSmallItems * 32 + i * 32 + lane;

@@ -104,6 +104,7 @@ def lib() -> ctypes.CDLL:
         "lcpp_dist_ipc_close": ([vp], i),
         "lcpp_dist_ipc_free": ([vp], i),
         "lcpp_diag_timing_enable": ([i], i),
+        "lcpp_diag_wait_timeout_probe": ([vp, sz, u64, vp], i),
         "lcpp_diag_timing_read": ([ctypes.POINTER(KernelTime), i, ip], i),
     }
     for name, (args, res) in sigs.items():
