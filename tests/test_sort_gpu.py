@@ -340,3 +340,32 @@ def test_partial_bits_2p27(lcpp, oracle):
     ks = host(keys[:m])
     got = gpu_sort(ks, begin_bit=8, end_bit=24)
     np.testing.assert_array_equal(got, oracle.radix_sort(ks, begin_bit=8, end_bit=24, threads=8))
+
+
+def test_wide_layout_above_2p30(lcpp):
+    """n >= 2^30 switches the sort to 64-bit look-back status words and
+    offsets: SortKeys of 2^30 + 12345 u32 keys against torch.sort (exact),
+    plus SortPairs stability on the same size (values = index)."""
+    n = (1 << 30) + 12345
+    keys = torch.empty(n, dtype=torch.uint32, device="cuda")
+    lcpp.testgen_fill(keys, lcpp.GEN_U32_AND3, seed=5)  # low entropy: many ties
+    out = torch.empty_like(keys)
+    rs = lcpp.DeviceRadixSort()
+    temp = lcpp.alloc_temp(lcpp.DeviceRadixSort.GetSortPairsTempStorageBytes(lcpp.U32, lcpp.U32, n))
+    rs.SortKeys(temp, keys, out, n)
+    assert lcpp.device_status(temp) == lcpp.OK
+    k64 = keys.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    o64 = out.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    assert torch.equal(o64, torch.sort(k64).values)
+    del o64
+    vals = torch.arange(n, dtype=torch.int32, device="cuda")
+    vout = torch.empty_like(vals)
+    rs.SortPairs(temp, keys, out, vals, vout, n)
+    assert lcpp.device_status(temp) == lcpp.OK
+    o64 = out.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    assert torch.equal(o64, torch.sort(k64).values)
+    # stable: the keys gathered by the value permutation are the output, and
+    # equal keys keep ascending indices
+    assert torch.equal(k64[vout.to(torch.int64)], o64)
+    same = o64[1:] == o64[:-1]
+    assert bool((vout[1:][same] > vout[:-1][same]).all())
