@@ -82,6 +82,14 @@ OPS = {
     "segsort": dict(metric="Gkeys/s uint32 SegmentedRadixSort SortKeys @2^27", unit="Gkeys/s", log2n=27,
                     dtype="u32", workload="SegmentedRadixSort SortKeys u32 uniform, segments of 1..2047 keys, seed 1",
                     bytes=8, kbytes=8, kernel="small_segment_kernel (one block per segment, shared-memory LSD)"),
+    # DeviceRadixSort over decomposed keys (the decomposer overloads): 2^27
+    # structs {u32 primary; i32 secondary} (uniform, seed 1), full 64-bit
+    # window.  Algorithmic bytes as SortKeys of 8-byte keys (k(1+2P), P = 8);
+    # the dominant launch is an onesweep pass over the 64-bit composite and
+    # the 32-bit index: 24 B per item.
+    "decomposed": dict(metric="Gkeys/s {u32,i32} decomposed SortKeys @2^27", unit="Gkeys/s", log2n=27,
+                       dtype="u32+i32", workload="SortKeys of {u32 primary, i32 secondary} structs, uniform, seed 1",
+                       bytes=136, kbytes=24, kernel="onesweep_kernel (one 8-bit pass of the 64-bit composite)"),
     # Merge path of the distributed sort (lcpp_dist_merge_sorted): two sorted
     # runs of 2^27 u32 keys (uniform, seed 1) into 2^28; reads and writes
     # every key once (8 B per output key).
@@ -227,6 +235,14 @@ class Workload:
             self.temp = L.alloc_temp(L.DeviceSegmentedRadixSort.GetSortKeysTempStorageBytes(L.U32, n))
             self.ss = L.DeviceSegmentedRadixSort()
             del np
+        elif op == "decomposed":
+            words = fill(T.uint32, L.GEN_U32_UNIFORM, 1)
+            more = fill(T.uint32, L.GEN_U32_UNIFORM, 2)
+            self.inputs = [T.stack([words, more], dim=1).contiguous()]  # n structs of 8 bytes
+            del words, more
+            self.outputs = [T.empty_like(self.inputs[0])]
+            self.dec = L.Decomposer(8, [(0, L.U32), (4, L.I32)])
+            self.temp = L.alloc_temp(L.DeviceRadixSort.GetDecomposedTempStorageBytes(n))
         elif op == "merge":
             from lcpp_b200.distributed import GpuOps
             self.gops = GpuOps()
@@ -260,6 +276,8 @@ class Workload:
             self.rs.SortPairs(t, i[0], o[0], i[1], o[1], n)
         elif op == "merge":
             self.gops.merge(i[0], i[1], o[0])
+        elif op == "decomposed":
+            self.rs.SortKeys(t, i[0], o[0], n, self.dec)
         elif op == "segsort":
             b, e, nseg = self.seg
             self.ss.SortKeys(t, i[0], o[0], n, nseg, b, e)
@@ -297,6 +315,11 @@ def cpu_fn(op: str, n_sample: int, threads: int):
     """One run of the oracle port on a bounded sample of the workload (the
     reference tests' host algorithms restated)."""
     from oracle import oracle as O
+    if op == "decomposed":
+        p = O.generate(O.GEN_U32_UNIFORM, n_sample, seed=1)
+        s = O.generate(O.GEN_U32_UNIFORM, n_sample, seed=2).view("int32")
+        # the reference tests' host oracle: std::stable_sort by (primary, secondary)
+        return lambda: O.decomposed_sort_order([p, s])
     if op == "merge":
         import numpy as np
         x = O.generate(O.GEN_U32_UNIFORM, n_sample, seed=1)

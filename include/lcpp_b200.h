@@ -223,6 +223,54 @@ lcpp_status lcpp_reduce_max(void* temp, size_t temp_bytes, const void* d_in, voi
                             uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * DeviceRadixSort over decomposed keys (the decomposer overloads,
+ * src/lcpp/device/device_radix_sort.h:556-940)
+ *
+ * Keys are structs of key_bytes bytes; `members` (host array, at most
+ * LCPP_MAX_KEY_MEMBERS) lists the members the reference's decomposer returns,
+ * most significant first, by byte offset and dtype.  Keys are ordered by the
+ * concatenation of the members' order-preserving bits (unsigned as is,
+ * signed with the high bit flipped, floats sign-dependent with -0.0 sorted as
+ * +0.0; the last member occupies bits [0, its width),
+ * src/lcpp/block/block_radix_sort.h:251-318), compared on the bit window
+ * [begin_bit, end_bit) only (end_bit at most the members' total width), in a
+ * stable sort, ascending or descending.  Input and output must not overlap.
+ * The DoubleBuffer forms read slot *selector, write the other slot and flip
+ * *selector once (device_radix_sort.h:833-837); begin_bit == end_bit leaves
+ * them unchanged and makes the copy forms copy.
+ * ---------------------------------------------------------------------- */
+#define LCPP_MAX_KEY_MEMBERS 8
+typedef struct lcpp_key_member {
+    uint32_t offset;  /* byte offset of the member in the key struct */
+    lcpp_dtype dtype; /* LCPP_U32 ... LCPP_F64 */
+} lcpp_key_member;
+
+/* Temp bytes of the decomposed-key sorts for num_items keys (any key struct,
+ * with or without values). */
+lcpp_status lcpp_radix_sort_decomposed_temp_bytes(uint64_t num_items, size_t* temp_bytes);
+
+lcpp_status lcpp_radix_sort_decomposed_keys(void* temp, size_t temp_bytes, const void* keys_in, void* keys_out,
+                                            uint64_t num_items, uint32_t key_bytes, const lcpp_key_member* members,
+                                            int num_members, int begin_bit, int end_bit, int descending,
+                                            lcpp_stream_t stream);
+lcpp_status lcpp_radix_sort_decomposed_pairs(void* temp, size_t temp_bytes, const void* keys_in, void* keys_out,
+                                             const void* values_in, void* values_out, uint64_t num_items,
+                                             uint32_t key_bytes, const lcpp_key_member* members, int num_members,
+                                             int begin_bit, int end_bit, int descending, lcpp_dtype value_dtype,
+                                             lcpp_stream_t stream);
+lcpp_status lcpp_radix_sort_decomposed_keys_double_buffer(void* temp, size_t temp_bytes, void* key_buffers[2],
+                                                          int* selector, uint64_t num_items, uint32_t key_bytes,
+                                                          const lcpp_key_member* members, int num_members,
+                                                          int begin_bit, int end_bit, int descending,
+                                                          lcpp_stream_t stream);
+lcpp_status lcpp_radix_sort_decomposed_pairs_double_buffer(void* temp, size_t temp_bytes, void* key_buffers[2],
+                                                           void* value_buffers[2], int* selector, uint64_t num_items,
+                                                           uint32_t key_bytes, const lcpp_key_member* members,
+                                                           int num_members, int begin_bit, int end_bit,
+                                                           int descending, lcpp_dtype value_dtype,
+                                                           lcpp_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * DeviceSegmentedRadixSort  (src/lcpp/device/device_segmented_radix_sort.h)
  *
  * Stable sort of every segment by the key bits [begin_bit, end_bit) after the

@@ -141,10 +141,98 @@ inline size_t temp_bytes(BufferView<uint32_t> t) { return t.size_bytes(); }
 }  // namespace detail
 
 // ---------------------------------------------------------------------------
+// Decomposed (struct) keys: the reference's decomposer returns a tuple of
+// the key's members, most significant first; here `members(&Key::a,
+// &Key::b, ...)` names the same members by pointer-to-member.
+// ---------------------------------------------------------------------------
+template <typename Key>
+struct Decomposer {
+    lcpp_key_member member[LCPP_MAX_KEY_MEMBERS];
+    int count = 0;
+    int bits = 0;  // total width of the members (the default end_bit)
+};
+
+template <typename Key, typename... M>
+Decomposer<Key> members(M Key::*... ptrs)
+{
+    static_assert(sizeof...(M) >= 1 && sizeof...(M) <= LCPP_MAX_KEY_MEMBERS, "1 to 8 key members");
+    static_assert(std::is_default_constructible_v<Key>, "the key struct must be default constructible");
+    Decomposer<Key> d{};
+    const Key probe{};
+    auto add = [&](auto ptr) {
+        using T = std::remove_cv_t<std::remove_reference_t<decltype(probe.*ptr)>>;
+        const auto offset = reinterpret_cast<const char*>(&(probe.*ptr)) - reinterpret_cast<const char*>(&probe);
+        d.member[d.count++] = lcpp_key_member{uint32_t(offset), detail::checked_dtype<T>()};
+        d.bits += int(sizeof(T) * 8);
+    };
+    (add(ptrs), ...);
+    return d;
+}
+
+// ---------------------------------------------------------------------------
 // DeviceRadixSort
 // ---------------------------------------------------------------------------
 class DeviceRadixSort {
 public:
+    /// Temp storage bytes for the decomposed-key sorts.
+    static size_t GetDecomposedTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_radix_sort_decomposed_temp_bytes(num_items, &b), "GetDecomposedTempStorageBytes");
+        return b;
+    }
+
+    // Decomposer overloads (device_radix_sort.h:556-940): end_bit = -1 means
+    // the members' total width.
+    template <typename Key>
+    void SortKeys(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<Key> d_keys_in,
+                  BufferView<Key> d_keys_out, uint64_t num_items, const Decomposer<Key>& decomposer,
+                  int begin_bit = 0, int end_bit = -1)
+    {
+        dec_keys(stream, temp_storage, d_keys_in, d_keys_out, num_items, decomposer, begin_bit, end_bit, 0);
+    }
+
+    template <typename Key>
+    void SortKeysDescending(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<Key> d_keys_in,
+                            BufferView<Key> d_keys_out, uint64_t num_items, const Decomposer<Key>& decomposer,
+                            int begin_bit = 0, int end_bit = -1)
+    {
+        dec_keys(stream, temp_storage, d_keys_in, d_keys_out, num_items, decomposer, begin_bit, end_bit, 1);
+    }
+
+    template <typename Key, typename ValueType>
+    void SortPairs(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<Key> d_keys_in,
+                   BufferView<Key> d_keys_out, BufferView<ValueType> d_values_in, BufferView<ValueType> d_values_out,
+                   uint64_t num_items, const Decomposer<Key>& decomposer, int begin_bit = 0, int end_bit = -1)
+    {
+        dec_pairs(stream, temp_storage, d_keys_in, d_keys_out, d_values_in, d_values_out, num_items, decomposer,
+                  begin_bit, end_bit, 0);
+    }
+
+    template <typename Key, typename ValueType>
+    void SortPairsDescending(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<Key> d_keys_in,
+                             BufferView<Key> d_keys_out, BufferView<ValueType> d_values_in,
+                             BufferView<ValueType> d_values_out, uint64_t num_items,
+                             const Decomposer<Key>& decomposer, int begin_bit = 0, int end_bit = -1)
+    {
+        dec_pairs(stream, temp_storage, d_keys_in, d_keys_out, d_values_in, d_values_out, num_items, decomposer,
+                  begin_bit, end_bit, 1);
+    }
+
+    template <typename Key>
+    void SortKeys(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, DoubleBuffer<Key>& d_keys,
+                  uint64_t num_items, const Decomposer<Key>& decomposer, int begin_bit = 0, int end_bit = -1)
+    {
+        dec_keys_db(stream, temp_storage, d_keys, num_items, decomposer, begin_bit, end_bit, 0);
+    }
+
+    template <typename Key>
+    void SortKeysDescending(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, DoubleBuffer<Key>& d_keys,
+                            uint64_t num_items, const Decomposer<Key>& decomposer, int begin_bit = 0, int end_bit = -1)
+    {
+        dec_keys_db(stream, temp_storage, d_keys, num_items, decomposer, begin_bit, end_bit, 1);
+    }
+
     /// Temp storage bytes for SortPairs / SortPairsDescending (0 for 0 items).
     template <typename KeyType, typename ValueType>
     static size_t GetSortPairsTempStorageBytes(uint64_t num_items)
@@ -236,6 +324,46 @@ public:
     }
 
 private:
+    template <typename Key>
+    static void dec_keys(lcpp_stream_t s, BufferView<uint32_t> t, BufferView<Key> ki, BufferView<Key> ko, uint64_t n,
+                         const Decomposer<Key>& d, int b, int e, int desc)
+    {
+        detail::require(ki.size() >= n && ko.size() >= n, "SortKeys: a key view is shorter than num_items");
+        detail::check(lcpp_radix_sort_decomposed_keys(t.data(), detail::temp_bytes(t), ki.data(), ko.data(), n,
+                                                      uint32_t(sizeof(Key)), d.member, d.count, b,
+                                                      e < 0 ? d.bits : e, desc, s),
+                      "SortKeys(decomposer)");
+    }
+
+    template <typename Key, typename V>
+    static void dec_pairs(lcpp_stream_t s, BufferView<uint32_t> t, BufferView<Key> ki, BufferView<Key> ko,
+                          BufferView<V> vi, BufferView<V> vo, uint64_t n, const Decomposer<Key>& d, int b, int e,
+                          int desc)
+    {
+        detail::require(ki.size() >= n && ko.size() >= n && vi.size() >= n && vo.size() >= n,
+                        "SortPairs: a key or value view is shorter than num_items");
+        detail::check(lcpp_radix_sort_decomposed_pairs(t.data(), detail::temp_bytes(t), ki.data(), ko.data(),
+                                                       vi.data(), vo.data(), n, uint32_t(sizeof(Key)), d.member,
+                                                       d.count, b, e < 0 ? d.bits : e, desc,
+                                                       detail::checked_dtype<V>(), s),
+                      "SortPairs(decomposer)");
+    }
+
+    template <typename Key>
+    static void dec_keys_db(lcpp_stream_t s, BufferView<uint32_t> t, DoubleBuffer<Key>& kd, uint64_t n,
+                            const Decomposer<Key>& d, int b, int e, int desc)
+    {
+        detail::require(kd.d_buffer[0].size() >= n && kd.d_buffer[1].size() >= n,
+                        "SortKeys: a double-buffer view is shorter than num_items");
+        void* kb[2] = {kd.d_buffer[0].data(), kd.d_buffer[1].data()};
+        int sel = kd.selector;
+        detail::check(lcpp_radix_sort_decomposed_keys_double_buffer(t.data(), detail::temp_bytes(t), kb, &sel, n,
+                                                                    uint32_t(sizeof(Key)), d.member, d.count, b,
+                                                                    e < 0 ? d.bits : e, desc, s),
+                      "SortKeys(decomposer)");
+        kd.selector = sel;
+    }
+
     template <typename K, typename V>
     static void pairs(lcpp_stream_t s, BufferView<uint32_t> t, BufferView<K> ki, BufferView<K> ko, BufferView<V> vi,
                       BufferView<V> vo, uint64_t n, int b, int e, int desc)

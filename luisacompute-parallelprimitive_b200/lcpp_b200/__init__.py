@@ -72,6 +72,14 @@ def lib() -> ctypes.CDLL:
         "lcpp_radix_sort_pairs": ([vp, sz, vp, vp, vp, vp, u64, i, i, i, i, i, vp], i),
         "lcpp_radix_sort_keys_double_buffer": ([vp, sz, vpa, ip, u64, i, i, i, i, vp], i),
         "lcpp_radix_sort_pairs_double_buffer": ([vp, sz, vpa, vpa, ip, u64, i, i, i, i, i, vp], i),
+        "lcpp_radix_sort_decomposed_temp_bytes": ([u64, szp], i),
+        "lcpp_radix_sort_decomposed_keys": ([vp, sz, vp, vp, u64, ctypes.c_uint32, vp, i, i, i, i, vp], i),
+        "lcpp_radix_sort_decomposed_pairs": ([vp, sz, vp, vp, vp, vp, u64, ctypes.c_uint32, vp, i, i, i, i, i, vp],
+                                             i),
+        "lcpp_radix_sort_decomposed_keys_double_buffer": ([vp, sz, vpa, ip, u64, ctypes.c_uint32, vp, i, i, i, i, vp],
+                                                          i),
+        "lcpp_radix_sort_decomposed_pairs_double_buffer": ([vp, sz, vpa, vpa, ip, u64, ctypes.c_uint32, vp, i, i, i,
+                                                            i, i, vp], i),
         "lcpp_segmented_radix_sort_keys_temp_bytes": ([i, u64, szp], i),
         "lcpp_segmented_radix_sort_pairs_temp_bytes": ([i, i, u64, szp], i),
         "lcpp_segmented_radix_sort_keys": ([vp, sz, vp, vp, u64, u64, vp, vp, i, i, i, i, vp], i),
@@ -188,8 +196,32 @@ def _bit_range(rest):
     return begin, end
 
 
+class KeyMember(ctypes.Structure):
+    _fields_ = [("offset", ctypes.c_uint32), ("dtype", ctypes.c_int)]
+
+
+class Decomposer:
+    """The reference's decomposer for struct keys (device_radix_sort.h:556-940):
+    the key struct's size in bytes and its members, most significant first, as
+    (byte offset, dtype code) pairs."""
+
+    def __init__(self, key_bytes: int, members):
+        self.key_bytes = int(key_bytes)
+        self.members = [(int(o), int(d)) for o, d in members]
+        self.bits = sum(8 * (4 if d in (U32, I32, F32) else 8) for _, d in self.members)
+        arr = (KeyMember * len(self.members))(*[KeyMember(o, d) for o, d in self.members])
+        self._arr = arr
+
+
 class DeviceRadixSort:
     """Mirror of lcpp::DeviceRadixSort (src/lcpp/device/device_radix_sort.h:50-1489)."""
+
+    @staticmethod
+    def GetDecomposedTempStorageBytes(num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_radix_sort_decomposed_temp_bytes(num_items, ctypes.byref(out)),
+              "GetDecomposedTempStorageBytes")
+        return out.value
 
     @staticmethod
     def GetSortKeysTempStorageBytes(key_dtype: int, num_items: int) -> int:
@@ -236,7 +268,50 @@ class DeviceRadixSort:
     def SortPairsDescending(self, temp, *args, stream=None):
         self._dispatch_pairs(temp, args, True, stream)
 
+    def _decomposed(self, temp, args, desc, stream, pairs):
+        tb = temp.numel() if temp is not None else 0
+        st = _stream(stream)
+        if isinstance(args[0], DoubleBuffer):
+            if pairs:
+                kdb, vdb, n, dec, *rest = args
+                if kdb.selector != vdb.selector:
+                    raise LcppError(ERR_INVALID_ARG, "key and value DoubleBuffer selectors must match")
+            else:
+                kdb, n, dec, *rest = args
+            begin, end = _bit_range(rest)
+            end = dec.bits if end is None else end
+            kb = (ctypes.c_void_p * 2)(kdb.d_buffers[0].data_ptr(), kdb.d_buffers[1].data_ptr())
+            sel = ctypes.c_int(kdb.selector)
+            if pairs:
+                vb = (ctypes.c_void_p * 2)(vdb.d_buffers[0].data_ptr(), vdb.d_buffers[1].data_ptr())
+                check(lib().lcpp_radix_sort_decomposed_pairs_double_buffer(
+                    _ptr(temp), tb, kb, vb, ctypes.byref(sel), n, dec.key_bytes, dec._arr, len(dec.members), begin,
+                    end, int(desc), dtype_code(vdb.d_buffers[0]), st), "SortPairs(decomposed, DoubleBuffer)")
+                vdb.selector = sel.value
+            else:
+                check(lib().lcpp_radix_sort_decomposed_keys_double_buffer(
+                    _ptr(temp), tb, kb, ctypes.byref(sel), n, dec.key_bytes, dec._arr, len(dec.members), begin, end,
+                    int(desc), st), "SortKeys(decomposed, DoubleBuffer)")
+            kdb.selector = sel.value
+            return
+        if pairs:
+            kin, kout, vin, vout, n, dec, *rest = args
+        else:
+            kin, kout, n, dec, *rest = args
+        begin, end = _bit_range(rest)
+        end = dec.bits if end is None else end
+        if pairs:
+            check(lib().lcpp_radix_sort_decomposed_pairs(
+                _ptr(temp), tb, _ptr(kin), _ptr(kout), _ptr(vin), _ptr(vout), n, dec.key_bytes, dec._arr,
+                len(dec.members), begin, end, int(desc), dtype_code(vin), st), "SortPairs(decomposed)")
+        else:
+            check(lib().lcpp_radix_sort_decomposed_keys(
+                _ptr(temp), tb, _ptr(kin), _ptr(kout), n, dec.key_bytes, dec._arr, len(dec.members), begin, end,
+                int(desc), st), "SortKeys(decomposed)")
+
     def _dispatch_keys(self, temp, args, desc, stream):
+        if any(isinstance(a, Decomposer) for a in args):
+            return self._decomposed(temp, args, desc, stream, False)
         if isinstance(args[0], DoubleBuffer):
             db, n, *rest = args
             begin, end = _bit_range(rest)
@@ -246,6 +321,8 @@ class DeviceRadixSort:
         self._keys(temp, kin, kout, n, begin, end, desc, stream)
 
     def _dispatch_pairs(self, temp, args, desc, stream):
+        if any(isinstance(a, Decomposer) for a in args):
+            return self._decomposed(temp, args, desc, stream, True)
         if isinstance(args[0], DoubleBuffer):
             kdb, vdb, n, *rest = args
             begin, end = _bit_range(rest)

@@ -197,3 +197,54 @@ def segmented_radix_sort(keys: np.ndarray, values: np.ndarray | None, begin_offs
     if ov is not None:
         ov[members] = values[order]
     return ok, ov
+
+
+def _ordered_bits(col: np.ndarray) -> np.ndarray:
+    """Order-preserving bits of one member column (uint64): unsigned as is,
+    signed with the high bit flipped, floats sign-dependent with -0.0 as +0.0
+    (src/lcpp/block/block_radix_sort.h:264-272)."""
+    bits = col.dtype.itemsize * 8
+    u = col.view(np.uint32 if bits == 32 else np.uint64).astype(np.uint64)
+    high = np.uint64(1 << (bits - 1))
+    full = np.uint64((1 << bits) - 1)
+    if col.dtype.kind == "i":
+        return u ^ high
+    if col.dtype.kind == "f":
+        t = np.where((u & high) != 0, (~u) & full, u ^ high)
+        return np.where(t == high - np.uint64(1), high, t)
+    return u
+
+
+def decomposed_sort_order(members: list[np.ndarray], begin_bit: int = 0, end_bit: int | None = None,
+                          descending: bool = False) -> np.ndarray:
+    """Stable order of keys decomposed into member columns (most significant
+    first), compared on the bit window [begin_bit, end_bit) of the
+    concatenation of the members' ordered bits
+    (src/lcpp/block/block_radix_sort.h:251-318,
+    src/lcpp/device/device_radix_sort.h:788-823).  Returns the permutation."""
+    n = members[0].size
+    widths = [m.dtype.itemsize * 8 for m in members]
+    total = sum(widths)
+    end_bit = total if end_bit is None else end_bit
+    lows, acc = [0] * len(members), 0
+    for k in range(len(members) - 1, -1, -1):
+        lows[k] = acc
+        acc += widths[k]
+    obits = [_ordered_bits(m) for m in members]
+    chunks = []  # least significant first
+    for lo in range(begin_bit, end_bit, 64):
+        w = min(64, end_bit - lo)
+        c = np.zeros(n, dtype=np.uint64)
+        for k, b in enumerate(obits):
+            olo, ohi = max(lows[k], lo), min(lows[k] + widths[k], lo + w)
+            if olo >= ohi:
+                continue
+            ow = ohi - olo
+            part = (b >> np.uint64(olo - lows[k])) & np.uint64((1 << ow) - 1 if ow < 64 else 0xFFFFFFFFFFFFFFFF)
+            c |= part << np.uint64(olo - lo)
+        if descending:
+            c = np.uint64((1 << w) - 1 if w < 64 else 0xFFFFFFFFFFFFFFFF) - c
+        chunks.append(c)
+    if not chunks:
+        return np.arange(n)
+    return np.lexsort(chunks)  # the last key (most significant chunk) is primary; stable

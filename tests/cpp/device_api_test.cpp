@@ -11,6 +11,7 @@
 #include <limits>
 #include <numeric>
 #include <random>
+#include <tuple>
 #include <vector>
 
 #include "lcpp_b200.hpp"
@@ -251,6 +252,41 @@ void segmented(lcpp_stream_t s)
     CHECK(vo.download() == expect_v);
 }
 
+struct RadixCompositeKey {
+    uint32_t primary;
+    int32_t secondary;
+    bool operator==(const RadixCompositeKey& o) const { return primary == o.primary && secondary == o.secondary; }
+};
+
+void decomposed(lcpp_stream_t s)
+{
+    // device_radix_sort_interface_test.cpp:285-330: decomposed as (primary, secondary)
+    const std::vector<RadixCompositeKey> keys{{1u, -1}, {0u, 7}, {1u, -1}, {2u, -8}, {0u, 3}, {1u, 4}, {2u, 0}, {0u, 7}};
+    const size_t n = keys.size();
+    std::vector<RadixCompositeKey> expect = keys;
+    std::stable_sort(expect.begin(), expect.end(), [](const RadixCompositeKey& l, const RadixCompositeKey& r) {
+        return std::tie(l.primary, l.secondary) < std::tie(r.primary, r.secondary);
+    });
+    DeviceArray<RadixCompositeKey> in(n), out(n);
+    in.upload(keys);
+    auto temp = temp_for(DeviceRadixSort::GetDecomposedTempStorageBytes(n));
+    DeviceRadixSort rs;
+    const auto dec = members(&RadixCompositeKey::primary, &RadixCompositeKey::secondary);
+    CHECK(dec.bits == 64);
+    rs.SortKeys(s, temp.view(), in.view(), out.view(), n, dec);
+    CUDA(cudaStreamSynchronize(s));
+    CHECK(out.download() == expect);
+    DeviceArray<RadixCompositeKey> alt(n);
+    DoubleBuffer<RadixCompositeKey> db(in.view(), alt.view());
+    rs.SortKeysDescending(s, temp.view(), db, n, dec);
+    CUDA(cudaStreamSynchronize(s));
+    CHECK(db.selector == 1);
+    std::stable_sort(expect.begin(), expect.end(), [](const RadixCompositeKey& l, const RadixCompositeKey& r) {
+        return std::tie(l.primary, l.secondary) > std::tie(r.primary, r.secondary);
+    });
+    CHECK(alt.download() == expect);
+}
+
 void misuse_throws(lcpp_stream_t s)
 {
     DeviceArray<uint32_t> a(16), b(16);
@@ -293,6 +329,7 @@ int main()
     scans(s);
     reductions(s);
     segmented(s);
+    decomposed(s);
     misuse_throws(s);
     CUDA(cudaStreamDestroy(stream));
     std::printf("OK %d\n", g_checks);

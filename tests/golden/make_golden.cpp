@@ -18,6 +18,7 @@
 #include <cstdio>
 #include <functional>
 #include <numeric>
+#include <tuple>
 #include <random>
 #include <string>
 #include <vector>
@@ -261,6 +262,37 @@ static void segmented_cases()
     emit("segmented_desc_order", order(true));
 }
 
+// tests/device_radix_sort_interface_test.cpp:285-330 -- 8 keys
+// {uint primary; int secondary}, decomposed as (primary, secondary); full
+// stable orders by std::tie and the window [28, 36) (low 4 bits of primary,
+// top 4 bits of the twiddled secondary).
+static void decomposed_cases()
+{
+    const std::vector<uint32_t> primary{1u, 0u, 1u, 2u, 0u, 1u, 2u, 0u};
+    const std::vector<int32_t> secondary{-1, 7, -1, -8, 3, 4, 0, 7};
+    const unsigned n = 8;
+    auto cross = [&](unsigned i) {
+        const uint32_t sb = static_cast<uint32_t>(secondary[i]) ^ 0x80000000u;
+        return ((primary[i] & 0x0fu) << 4u) | ((sb >> 28u) & 0x0fu);
+    };
+    auto order = [&](auto less) {
+        std::vector<uint32_t> o(n);
+        std::iota(o.begin(), o.end(), 0u);
+        std::stable_sort(o.begin(), o.end(), less);
+        return o;
+    };
+    emit("decomposed_primary", primary);
+    emit("decomposed_secondary", secondary);
+    emit("decomposed_full_asc_order", order([&](uint32_t l, uint32_t r) {
+        return std::tie(primary[l], secondary[l]) < std::tie(primary[r], secondary[r]);
+    }));
+    emit("decomposed_full_desc_order", order([&](uint32_t l, uint32_t r) {
+        return std::tie(primary[l], secondary[l]) > std::tie(primary[r], secondary[r]);
+    }));
+    emit("decomposed_window_asc_order", order([&](uint32_t l, uint32_t r) { return cross(l) < cross(r); }));
+    emit("decomposed_window_desc_order", order([&](uint32_t l, uint32_t r) { return cross(l) > cross(r); }));
+}
+
 int main(int argc, char** argv)
 {
     if (argc != 2) {
@@ -277,6 +309,7 @@ int main(int argc, char** argv)
     scan_cases();
     reduce_cases();
     segmented_cases();
+    decomposed_cases();
     std::fclose(g_index);
     return 0;
 }

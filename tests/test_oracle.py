@@ -278,3 +278,53 @@ def test_segmented_oracle_vs_python(dt, desc):
         ok, _ = O.segmented_radix_sort(keys, None, b, e, begin_bit, end_bit, desc)
         exp = _segmented_by_python(keys, b, e, begin_bit, end_bit, desc)
         np.testing.assert_array_equal(ok.view(np.uint8), exp.view(np.uint8))
+
+
+def test_decomposed_oracle_matches_golden(golden):
+    from oracle import oracle as O
+    p, s = golden["decomposed_primary"], golden["decomposed_secondary"]
+    cases = [("decomposed_full_asc_order", 0, 64, False), ("decomposed_full_desc_order", 0, 64, True),
+             ("decomposed_window_asc_order", 28, 36, False), ("decomposed_window_desc_order", 28, 36, True)]
+    for name, b, e, desc in cases:
+        np.testing.assert_array_equal(O.decomposed_sort_order([p, s], b, e, desc), golden[name])
+
+
+def test_decomposed_oracle_vs_python():
+    """Members of every dtype, 3 members (160 bits, three chunks), windows
+    across member boundaries, against a pure-Python sorted() on the bits."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(4)
+    n = 400
+    a = rng.integers(-3, 3, n).astype(np.int64)
+    b = rng.standard_normal(n).astype(np.float32)
+    b[::9] = 0.0
+    b[4::9] = -0.0
+    c = rng.integers(0, 4, n).astype(np.uint64)
+    cols = [a, b, c]
+
+    def ob(x, kind, bits):
+        x = int(x)
+        if kind == "i":
+            return (x & ((1 << bits) - 1)) ^ (1 << (bits - 1))
+        if kind == "f":
+            u = x
+            t = (~u & ((1 << bits) - 1)) if u >> (bits - 1) else u ^ (1 << (bits - 1))
+            return (1 << (bits - 1)) if t == (1 << (bits - 1)) - 1 else t
+        return x
+
+    ubits = [a.view(np.uint64), b.view(np.uint32), c]
+    kinds = ["i", "f", "u"]
+    widths = [64, 32, 64]
+
+    def concat(i):
+        v = 0
+        for col, kind, w in zip(ubits, kinds, widths):
+            v = (v << w) | ob(col[i], kind, w)
+        return v
+
+    full = [concat(i) for i in range(n)]
+    for lo, hi in ((0, 160), (30, 100), (60, 70), (5, 5)):
+        for desc in (False, True):
+            key = [(v >> lo) & ((1 << (hi - lo)) - 1) for v in full]
+            exp = sorted(range(n), key=(lambda i: -key[i]) if desc else (lambda i: key[i]))
+            np.testing.assert_array_equal(O.decomposed_sort_order(cols, lo, hi, desc), exp)
