@@ -74,6 +74,11 @@ OPS = {
                    workload="DeviceReduce::Sum f32 U[0,1), seed 1", bytes=4, kbytes=4, kernel="reduce_kernel"),
     "reduce_max": dict(metric="Gitems/s int64 Reduce Max @2^30", unit="Gitems/s", log2n=30, dtype="i64",
                        workload="DeviceReduce::Max i64 uniform, seed 1", bytes=8, kbytes=8, kernel="reduce_kernel"),
+    # DeviceReduce::ArgMin: one read of every item (4 B), nothing written
+    # but the (value, index) result.
+    "argmin": dict(metric="Gitems/s float32 ArgMin @2^30", unit="Gitems/s", log2n=30, dtype="f32",
+                   workload="DeviceReduce::ArgMin f32 U[0,1) (many tied minima), seed 1", bytes=4, kbytes=4,
+                   kernel="arg_extremum_kernel"),
     # DeviceSegmentedRadixSort (SURVEY next-row widening): 2^27 u32 keys in
     # segments of 1..2047 keys (sizes uniform, seed 1), contiguous.  All
     # segments are short, so the one-block-per-segment kernel does the whole
@@ -260,6 +265,10 @@ class Workload:
             self.inputs = [fill(T.float32, L.GEN_F32_UNIT, 1)]
             self.outputs = [T.empty(1, dtype=T.float32, device=dev)]
             self.temp = L.alloc_temp(L.DeviceReduce.GetTempStorageBytes(L.F32, n))
+        elif op == "argmin":
+            self.inputs = [fill(T.float32, L.GEN_F32_UNIT, 1)]
+            self.outputs = [T.empty(1, dtype=T.float32, device=dev), T.empty(1, dtype=T.int32, device=dev)]
+            self.temp = L.alloc_temp(L.DeviceReduce.GetArgTempStorageBytes(L.F32, n))
         elif op == "reduce_max":
             self.inputs = [fill(T.int64, L.GEN_I64_UNIFORM, 1)]
             self.outputs = [T.empty(1, dtype=T.int64, device=dev)]
@@ -287,6 +296,8 @@ class Workload:
             self.rd.Sum(t, i[0], o[0], n)
         elif op == "reduce_max":
             self.rd.Max(t, i[0], o[0], n)
+        elif op == "argmin":
+            self.rd.ArgMin(t, i[0], o[0], o[1], n)
 
     def dominant_kind(self):
         L = self.L
@@ -298,6 +309,8 @@ class Workload:
             return L.KERNEL_SEGMENT_BLOCK
         if self.op == "merge":
             return L.KERNEL_MERGE
+        if self.op == "argmin":
+            return L.KERNEL_ARG_REDUCE
         return L.KERNEL_SORT_ONESWEEP
 
 
@@ -350,6 +363,9 @@ def cpu_fn(op: str, n_sample: int, threads: int):
     if op == "reduce":
         x = O.generate(O.GEN_F32_UNIT, n_sample, seed=1)
         return lambda: O.sum_f64(x)
+    if op == "argmin":
+        x = O.generate(O.GEN_F32_UNIT, n_sample, seed=1)
+        return lambda: O.arg_extremum(x, True)
     x = O.generate(O.GEN_I64_UNIFORM, n_sample, seed=1)
     return lambda: O.reduce(x, O.OP_MAX, -(1 << 63))
 

@@ -332,6 +332,18 @@ lcpp_status lcpp_segmented_radix_sort_pairs_double_buffer(void* temp, size_t tem
                                                           int descending, lcpp_dtype key_dtype,
                                                           lcpp_dtype value_dtype, lcpp_stream_t stream);
 
+/* Replace DeviceReduce::GetArgTempStorageBytes / ArgMin / ArgMax
+ * (device_reduce.h:192-204, :310-436): *d_out = the minimum (maximum) value
+ * and *d_index_out = the first index holding it (ties go to the smaller
+ * index, thread_operators.h:19-47; NaN never wins); zero items write the
+ * numeric max (ArgMin) or lowest (ArgMax) value and index 1 (:318-323).
+ * num_items at most 2^32 - 1 (uint32 indices, as the reference). */
+lcpp_status lcpp_reduce_arg_temp_bytes(lcpp_dtype dtype, uint64_t num_items, size_t* temp_bytes);
+lcpp_status lcpp_reduce_argmin(void* temp, size_t temp_bytes, const void* d_in, void* d_out, uint32_t* d_index_out,
+                               uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
+lcpp_status lcpp_reduce_argmax(void* temp, size_t temp_bytes, const void* d_in, void* d_out, uint32_t* d_index_out,
+                               uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Device diagnostics (no reference counterpart: the reference's look-back
  * spins are unbounded, src/lcpp/agent/agent_radix_sort_onesweep.h:324-334).

@@ -39,6 +39,9 @@
 #include <type_traits>
 
 #include "lcpp_b200.h"
+#ifdef __CUDACC__
+#include "lcpp_b200_device.cuh"
+#endif
 
 namespace lcpp_b200 {
 
@@ -137,6 +140,14 @@ inline void require(bool ok, const char* what)
 }
 
 inline size_t temp_bytes(BufferView<uint32_t> t) { return t.size_bytes(); }
+
+#ifdef __CUDACC__
+inline void check_cuda(cudaError_t e, const char* what)
+{
+    if (e == cudaErrorInvalidValue) throw Error(LCPP_ERR_INVALID_ARG, what);
+    if (e != cudaSuccess) throw Error(LCPP_ERR_CUDA, what);
+}
+#endif
 
 }  // namespace detail
 
@@ -734,12 +745,84 @@ public:
                       "Max");
     }
 
+    /// Temp storage bytes for ArgMin / ArgMax (the reference's
+    /// GetArgTempStorageBytes, device_reduce.h:192-204).
+    template <typename T>
+    static size_t GetArgTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_reduce_arg_temp_bytes(detail::checked_dtype<T>(), num_items, &b), "GetArgTempStorageBytes");
+        return b;
+    }
+
+    /// d_out[0] = the minimum, d_index_out[0] = the first index holding it;
+    /// 0 items: max() and index 1 (device_reduce.h:310-358).
+    template <typename T>
+    void ArgMin(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in, BufferView<T> d_out,
+                BufferView<uint32_t> d_index_out, uint64_t num_items)
+    {
+        arg_views(d_in, d_out, d_index_out, num_items);
+        detail::check(lcpp_reduce_argmin(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                         d_out.data(), d_index_out.data(), num_items, detail::checked_dtype<T>(),
+                                         stream),
+                      "ArgMin");
+    }
+
+    /// d_out[0] = the maximum, d_index_out[0] = the first index holding it;
+    /// 0 items: lowest() and index 1 (device_reduce.h:373-422).
+    template <typename T>
+    void ArgMax(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in, BufferView<T> d_out,
+                BufferView<uint32_t> d_index_out, uint64_t num_items)
+    {
+        arg_views(d_in, d_out, d_index_out, num_items);
+        detail::check(lcpp_reduce_argmax(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                         d_out.data(), d_index_out.data(), num_items, detail::checked_dtype<T>(),
+                                         stream),
+                      "ArgMax");
+    }
+
+#ifdef __CUDACC__
+    /// The comparator overloads (device_reduce.h:360-371, :424-434):
+    /// `compare` is a __device__ callable "a orders before b"; the result is
+    /// the first index of the extreme equivalence class.  Needs nvcc; the
+    /// kernel is instantiated in the caller's translation unit
+    /// (lcpp_b200_device.cuh).
+    template <typename T, typename Compare>
+    void ArgMin(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in, BufferView<T> d_out,
+                BufferView<uint32_t> d_index_out, uint64_t num_items, Compare compare)
+    {
+        arg_views(d_in, d_out, d_index_out, num_items);
+        detail::check_cuda(device::ArgMin(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                          d_out.data(), d_index_out.data(), num_items, compare,
+                                          reinterpret_cast<cudaStream_t>(stream)),
+                           "ArgMin");
+    }
+
+    template <typename T, typename Compare>
+    void ArgMax(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in, BufferView<T> d_out,
+                BufferView<uint32_t> d_index_out, uint64_t num_items, Compare compare)
+    {
+        arg_views(d_in, d_out, d_index_out, num_items);
+        detail::check_cuda(device::ArgMax(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                          d_out.data(), d_index_out.data(), num_items, compare,
+                                          reinterpret_cast<cudaStream_t>(stream)),
+                           "ArgMax");
+    }
+#endif
+
 private:
     template <typename T>
     static void views(BufferView<T> i, BufferView<T> o, uint64_t n)
     {
         detail::require(i.size() >= n && o.size() >= 1, "DeviceReduce: the input view is shorter than num_items "
                                                         "or the output view is empty");
+    }
+
+    template <typename T>
+    static void arg_views(BufferView<T> i, BufferView<T> o, BufferView<uint32_t> idx, uint64_t n)
+    {
+        detail::require(o.size() >= 1 && idx.size() >= 1, "DeviceReduce: extremum output view is empty");
+        detail::require(i.size() >= n, "DeviceReduce: the input view is shorter than num_items");
     }
 };
 

@@ -23,7 +23,8 @@ typedef enum lcpp_kernel_kind {
     LCPP_KERNEL_SCAN = 2,           /* decoupled look-back scan */
     LCPP_KERNEL_REDUCE = 3,         /* two-level reduce */
     LCPP_KERNEL_SEGMENT_BLOCK = 4,  /* segmented sort: one block per short segment */
-    LCPP_KERNEL_MERGE = 5           /* merge path (lcpp_dist_merge_sorted*) */
+    LCPP_KERNEL_MERGE = 5,          /* merge path (lcpp_dist_merge_sorted*) */
+    LCPP_KERNEL_ARG_REDUCE = 6      /* ArgMin / ArgMax */
 } lcpp_kernel_kind;
 
 typedef struct lcpp_kernel_time {

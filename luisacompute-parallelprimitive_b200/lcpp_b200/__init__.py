@@ -34,6 +34,7 @@ GEN_F32_NORMAL, GEN_U32_ZIPF = 8, 9
 # lcpp_kernel_kind
 KERNEL_SORT_HISTOGRAM, KERNEL_SORT_ONESWEEP, KERNEL_SCAN, KERNEL_REDUCE, KERNEL_SEGMENT_BLOCK = 0, 1, 2, 3, 4
 KERNEL_MERGE = 5
+KERNEL_ARG_REDUCE = 6
 
 _lib = None
 
@@ -95,6 +96,9 @@ def lib() -> ctypes.CDLL:
         "lcpp_scan_inclusive_sum": ([vp, sz, vp, vp, u64, i, vp], i),
         "lcpp_scan_inclusive_sum_noalloc": ([vp, vp, u64, i, vp], i),
         "lcpp_reduce_temp_bytes": ([i, u64, szp], i),
+        "lcpp_reduce_arg_temp_bytes": ([i, u64, szp], i),
+        "lcpp_reduce_argmin": ([vp, sz, vp, vp, vp, u64, i, vp], i),
+        "lcpp_reduce_argmax": ([vp, sz, vp, vp, vp, u64, i, vp], i),
         "lcpp_reduce": ([vp, sz, vp, vp, u64, i, vp, i, vp], i),
         "lcpp_reduce_sum": ([vp, sz, vp, vp, u64, i, vp], i),
         "lcpp_reduce_min": ([vp, sz, vp, vp, u64, i, vp], i),
@@ -500,6 +504,21 @@ class DeviceReduce:
     def _named(self, fn, temp, d_in, d_out, num_items, stream, what):
         check(fn(_ptr(temp), temp.numel() if temp is not None else 0, _ptr(d_in), _ptr(d_out),
                  num_items, dtype_code(d_out), _stream(stream)), what)
+
+    @staticmethod
+    def GetArgTempStorageBytes(dtype: int, num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_reduce_arg_temp_bytes(dtype, num_items, ctypes.byref(out)), "GetArgTempStorageBytes")
+        return out.value
+
+    def ArgMin(self, temp, d_in, d_out, d_index_out, num_items, stream=None):
+        """d_out[0] = min value, d_index_out[0] = its first index (uint32 / int32 tensor)."""
+        check(lib().lcpp_reduce_argmin(_ptr(temp), temp.numel() if temp is not None else 0, _ptr(d_in), _ptr(d_out),
+                                       _ptr(d_index_out), num_items, dtype_code(d_out), _stream(stream)), "ArgMin")
+
+    def ArgMax(self, temp, d_in, d_out, d_index_out, num_items, stream=None):
+        check(lib().lcpp_reduce_argmax(_ptr(temp), temp.numel() if temp is not None else 0, _ptr(d_in), _ptr(d_out),
+                                       _ptr(d_index_out), num_items, dtype_code(d_out), _stream(stream)), "ArgMax")
 
     def Sum(self, temp, d_in, d_out, num_items, stream=None):
         self._named(lib().lcpp_reduce_sum, temp, d_in, d_out, num_items, stream, "Sum")

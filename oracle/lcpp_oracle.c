@@ -17,6 +17,7 @@
  */
 #include <math.h>
 #include <pthread.h>
+#include <float.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -351,6 +352,64 @@ int oracle_reduce(const void* vin, void* vout, uint64_t n, int dtype, int op, co
         if (op == OP_SUM) RED_BODY(double, long double, C_SUM);
         else if (op == OP_MIN) RED_BODY(double, double, C_MIN);
         else RED_BODY(double, double, C_MAX);
+        return 0;
+    default:
+        return -1;
+    }
+}
+
+/* ArgMin / ArgMax: the reference's fold with ArgMinOp / ArgMaxOp
+ * (src/lcpp/common/thread_operators.h:19-47) from the identity pair
+ * {UINT_MAX, max() or lowest()} (src/lcpp/device/device_reduce.h:346-353,
+ * :412-418), taken in index order: item i replaces the best when its value
+ * is smaller (larger), or equal with a smaller index -- so the result is the
+ * first index of the extreme value.  A NaN compares false both ways and never
+ * replaces the best (the reference's tree may keep a NaN it met first; NaN
+ * inputs are outside the parity domain).  n == 0 writes the empty-input
+ * sentinels max() / lowest() and index 1 (:318-323). */
+#define ARG_BODY(T, IS_MIN, EMPTY)                                                   \
+    do {                                                                             \
+        const T* in = (const T*)vin;                                                 \
+        T best = (EMPTY);                                                            \
+        uint32_t bi = 0xffffffffu;                                                   \
+        if (n == 0) {                                                                \
+            *(T*)vout = best;                                                        \
+            *index_out = 1u;                                                         \
+            return 0;                                                                \
+        }                                                                            \
+        for (uint64_t i = 0; i < n; ++i) {                                           \
+            const T x = in[i];                                                       \
+            const int strictly = (IS_MIN) ? (x < best) : (x > best);                 \
+            if (strictly || (x == best && (uint32_t)i < bi)) {                       \
+                best = x;                                                            \
+                bi = (uint32_t)i;                                                    \
+            }                                                                        \
+        }                                                                            \
+        *(T*)vout = best;                                                            \
+        *index_out = bi;                                                             \
+    } while (0)
+
+int oracle_arg_extremum(const void* vin, void* vout, uint32_t* index_out, uint64_t n, int dtype, int is_min)
+{
+    if (!vout || !index_out || n > 0xffffffffull) return -1;
+    switch (dtype) {
+    case DT_I32:
+        if (is_min) ARG_BODY(int32_t, 1, INT32_MAX); else ARG_BODY(int32_t, 0, INT32_MIN);
+        return 0;
+    case DT_U32:
+        if (is_min) ARG_BODY(uint32_t, 1, UINT32_MAX); else ARG_BODY(uint32_t, 0, 0u);
+        return 0;
+    case DT_I64:
+        if (is_min) ARG_BODY(int64_t, 1, INT64_MAX); else ARG_BODY(int64_t, 0, INT64_MIN);
+        return 0;
+    case DT_U64:
+        if (is_min) ARG_BODY(uint64_t, 1, UINT64_MAX); else ARG_BODY(uint64_t, 0, 0ull);
+        return 0;
+    case DT_F32:
+        if (is_min) ARG_BODY(float, 1, FLT_MAX); else ARG_BODY(float, 0, -FLT_MAX);
+        return 0;
+    case DT_F64:
+        if (is_min) ARG_BODY(double, 1, DBL_MAX); else ARG_BODY(double, 0, -DBL_MAX);
         return 0;
     default:
         return -1;

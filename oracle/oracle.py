@@ -66,6 +66,8 @@ def lib() -> ctypes.CDLL:
         l.oracle_scan.restype = i
         l.oracle_reduce.argtypes = [vp, vp, u64, i, i, vp]
         l.oracle_reduce.restype = i
+        l.oracle_arg_extremum.argtypes = [vp, vp, vp, u64, i, i]
+        l.oracle_arg_extremum.restype = i
         l.oracle_sum_f64.argtypes = [vp, u64, i]
         l.oracle_sum_f64.restype = ctypes.c_double
         l.oracle_generate.argtypes = [vp, u64, u64, u64, i]
@@ -128,6 +130,35 @@ def reduce(x: np.ndarray, op: int, init):
     if rc != 0:
         raise ValueError(f"oracle_reduce failed with {rc}")
     return out[0]
+
+
+def arg_extremum(x: np.ndarray, is_min: bool):
+    """(value, index) of DeviceReduce::ArgMin / ArgMax (lcpp_oracle.c:
+    oracle_arg_extremum, after src/lcpp/device/device_reduce.h:310-436)."""
+    x = np.ascontiguousarray(x)
+    out = np.empty(1, dtype=x.dtype)
+    idx = np.empty(1, dtype=np.uint32)
+    rc = lib().oracle_arg_extremum(_ptr(x), _ptr(out), _ptr(idx), x.size, NP_TO_DTYPE[x.dtype], int(is_min))
+    if rc != 0:
+        raise ValueError(f"oracle_arg_extremum failed with {rc}")
+    return out[0], int(idx[0])
+
+
+def arg_extremum_compare(x, is_min: bool, compare):
+    """The comparator overloads (src/lcpp/device/device_reduce.h:539-605): one
+    walk from item 0 where item i replaces the best when compare(item, best)
+    (ArgMin) or compare(best, item) (ArgMax); 0 items give max() / lowest()
+    and index 1.  Pure Python: small inputs only."""
+    x = np.asarray(x)
+    if x.size == 0:
+        info = np.finfo(x.dtype) if x.dtype.kind == "f" else np.iinfo(x.dtype)
+        return (x.dtype.type(info.max) if is_min else x.dtype.type(info.min)), 1
+    best, bi = x[0], 0
+    for i in range(1, x.size):
+        c = x[i]
+        if (compare(c, best) if is_min else compare(best, c)):
+            best, bi = c, i
+    return best, bi
 
 
 def sum_f64(x: np.ndarray) -> float:

@@ -180,6 +180,63 @@ void scans(lcpp_stream_t s)
     CHECK(out.download() == expect);
 }
 
+void arg_reductions(lcpp_stream_t s)
+{
+    // device_reduce_test.cpp:238-288: first of equal maxima; negative floats
+    {
+        const std::vector<int32_t> h{1, 9, 4, 9, 3};
+        DeviceArray<int32_t> in(h.size()), value(1);
+        DeviceArray<uint32_t> index(1);
+        in.upload(h);
+        auto temp = temp_for(DeviceReduce::GetArgTempStorageBytes<int32_t>(h.size()));
+        DeviceReduce rd;
+        rd.ArgMax(s, temp.view(), in.view(), value.view(), index.view(), h.size());
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(value.download()[0] == 9 && index.download()[0] == 1u);
+    }
+    {
+        const std::vector<float> h{-7.0f, -3.0f, -5.0f};
+        DeviceArray<float> in(h.size()), value(1);
+        DeviceArray<uint32_t> index(1);
+        in.upload(h);
+        auto temp = temp_for(DeviceReduce::GetArgTempStorageBytes<float>(h.size()));
+        DeviceReduce rd;
+        rd.ArgMax(s, temp.view(), in.view(), value.view(), index.view(), h.size());
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(value.download()[0] == -3.0f && index.download()[0] == 1u);
+    }
+    // empty input: max() / lowest() and index 1 (device_reduce.h:318-323)
+    {
+        DeviceArray<int64_t> in(0), value(1);
+        DeviceArray<uint32_t> index(1);
+        DeviceReduce rd;
+        rd.ArgMin(s, BufferView<uint32_t>{}, in.view(), value.view(), index.view(), 0);
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(value.download()[0] == std::numeric_limits<int64_t>::max() && index.download()[0] == 1u);
+    }
+    // random doubles against std::min_element / std::max_element (first index)
+    {
+        const size_t n = 3000017;
+        std::vector<double> h(n);
+        std::mt19937_64 rng(11);
+        std::uniform_int_distribution<int> dist(-500, 500);
+        for (auto& x : h) x = dist(rng) * 0.25;
+        DeviceArray<double> in(n), value(1);
+        DeviceArray<uint32_t> index(1);
+        in.upload(h);
+        auto temp = temp_for(DeviceReduce::GetArgTempStorageBytes<double>(n));
+        DeviceReduce rd;
+        const auto mn = std::min_element(h.begin(), h.end());
+        const auto mx = std::max_element(h.begin(), h.end());
+        rd.ArgMin(s, temp.view(), in.view(), value.view(), index.view(), n);
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(value.download()[0] == *mn && index.download()[0] == uint32_t(mn - h.begin()));
+        rd.ArgMax(s, temp.view(), in.view(), value.view(), index.view(), n);
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(value.download()[0] == *mx && index.download()[0] == uint32_t(mx - h.begin()));
+    }
+}
+
 void reductions(lcpp_stream_t s)
 {
     // device_reduce_test.cpp: ones at 2^k + 1; float max identity on empty input
@@ -328,6 +385,7 @@ int main()
     sort_bits_stable_double_buffer(s);
     scans(s);
     reductions(s);
+    arg_reductions(s);
     segmented(s);
     decomposed(s);
     misuse_throws(s);

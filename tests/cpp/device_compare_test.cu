@@ -1,0 +1,170 @@
+// CUDA caller of the comparator overloads of DeviceReduce::ArgMin / ArgMax
+// (include/lcpp_b200.hpp with nvcc, kernels from lcpp_b200_device.cuh),
+// written like the reference's tests/device_reduce_test.cpp:290-345: device
+// results against the reference's sequential comparator fold
+// (src/lcpp/device/device_reduce.h:580-603) on the host.  Built and run by
+// tests/test_cpp_api.py on a GPU box; compiled (not run) on the CPU.  Prints
+// "OK <checks>" and exits 0 on success.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <limits>
+#include <random>
+#include <utility>
+#include <vector>
+
+#include "lcpp_b200.hpp"
+
+using namespace lcpp_b200;
+
+namespace {
+
+int g_checks = 0;
+
+#define CHECK(cond)                                                                  \
+    do {                                                                             \
+        ++g_checks;                                                                  \
+        if (!(cond)) {                                                               \
+            std::fprintf(stderr, "FAILED %s at %s:%d\n", #cond, __FILE__, __LINE__); \
+            std::exit(1);                                                            \
+        }                                                                            \
+    } while (0)
+
+#define CUDA(call) CHECK((call) == cudaSuccess)
+
+template <typename T>
+struct DeviceArray {
+    T* p = nullptr;
+    size_t n = 0;
+    explicit DeviceArray(size_t count) : n(count) { CUDA(cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T))); }
+    ~DeviceArray() { cudaFree(p); }
+    BufferView<T> view() const { return {p, n}; }
+    void upload(const std::vector<T>& h) { CUDA(cudaMemcpy(p, h.data(), h.size() * sizeof(T), cudaMemcpyHostToDevice)); }
+    T first() const
+    {
+        T v;
+        CUDA(cudaMemcpy(&v, p, sizeof(T), cudaMemcpyDeviceToHost));
+        return v;
+    }
+};
+
+DeviceArray<uint32_t> temp_for(size_t bytes) { return DeviceArray<uint32_t>(bytes_to_uint_count(std::max<size_t>(bytes, 4))); }
+
+struct LastDigitLess {
+    __host__ __device__ bool operator()(int a, int b) const { return a % 10 < b % 10; }
+};
+
+// |a| < |b| with a modulus carried in the functor (a stateful comparator).
+struct ModAbsLess {
+    int64_t m;
+    __host__ __device__ bool operator()(int64_t a, int64_t b) const
+    {
+        const int64_t x = (a < 0 ? -a : a) % m, y = (b < 0 ? -b : b) % m;
+        return x < y;
+    }
+};
+
+// The reference's comparator fold: item i replaces the best when
+// compare(item, best) (ArgMin) or compare(best, item) (ArgMax).
+template <typename T, typename C>
+std::pair<T, uint32_t> fold(const std::vector<T>& h, bool is_min, C c)
+{
+    T best = h[0];
+    uint32_t bi = 0;
+    for (size_t i = 1; i < h.size(); ++i)
+        if (is_min ? c(h[i], best) : c(best, h[i])) {
+            best = h[i];
+            bi = uint32_t(i);
+        }
+    return {best, bi};
+}
+
+template <typename T, typename C>
+void check_both(lcpp_stream_t s, const std::vector<T>& h, C c, size_t offset = 0)
+{
+    const size_t n = h.size() - offset;
+    DeviceArray<T> in(h.size()), value(1);
+    DeviceArray<uint32_t> index(1);
+    in.upload(h);
+    auto temp = temp_for(DeviceReduce::GetArgTempStorageBytes<T>(n));
+    BufferView<T> view{in.p + offset, n};
+    const std::vector<T> sub(h.begin() + offset, h.end());
+    DeviceReduce rd;
+    rd.ArgMin(s, temp.view(), view, value.view(), index.view(), n, c);
+    CUDA(cudaStreamSynchronize(s));
+    auto want = fold(sub, true, c);
+    CHECK(value.first() == want.first && index.first() == want.second);
+    rd.ArgMax(s, temp.view(), view, value.view(), index.view(), n, c);
+    CUDA(cudaStreamSynchronize(s));
+    want = fold(sub, false, c);
+    CHECK(value.first() == want.first && index.first() == want.second);
+}
+
+void reference_case(lcpp_stream_t s)
+{
+    // device_reduce_test.cpp:290-330: last-digit comparator, first ties
+    const std::vector<int> h{21, 11, 33, 23, 8, 28};
+    DeviceArray<int> in(h.size()), mn(1), mx(1);
+    DeviceArray<uint32_t> mni(1), mxi(1);
+    in.upload(h);
+    auto temp = temp_for(DeviceReduce::GetArgTempStorageBytes<int>(h.size()));
+    DeviceReduce rd;
+    rd.ArgMin(s, temp.view(), in.view(), mn.view(), mni.view(), h.size(), LastDigitLess{});
+    rd.ArgMax(s, temp.view(), in.view(), mx.view(), mxi.view(), h.size(), LastDigitLess{});
+    CUDA(cudaStreamSynchronize(s));
+    CHECK(mn.first() == 21 && mni.first() == 0u);
+    CHECK(mx.first() == 8 && mxi.first() == 4u);
+}
+
+void empty_sentinels(lcpp_stream_t s)
+{
+    // device_reduce_test.cpp:332-345: the comparator forms keep the sentinels
+    DeviceArray<int> in(0), mn(1), mx(1);
+    DeviceArray<uint32_t> mni(1), mxi(1);
+    DeviceReduce rd;
+    rd.ArgMin(s, BufferView<uint32_t>{}, in.view(), mn.view(), mni.view(), 0, LastDigitLess{});
+    rd.ArgMax(s, BufferView<uint32_t>{}, in.view(), mx.view(), mxi.view(), 0, LastDigitLess{});
+    CUDA(cudaStreamSynchronize(s));
+    CHECK(mn.first() == std::numeric_limits<int>::max() && mni.first() == 1u);
+    CHECK(mx.first() == std::numeric_limits<int>::lowest() && mxi.first() == 1u);
+}
+
+void random_cases(lcpp_stream_t s)
+{
+    std::mt19937 rng(114521);
+    for (size_t n : {size_t(1), size_t(7), size_t(2049), size_t(1000003), size_t(20000003)}) {
+        std::vector<int> h(n);
+        for (auto& x : h) x = int(rng() % 2000001) - 1000000;
+        check_both(s, h, LastDigitLess{});
+        if (n > 8) check_both(s, h, LastDigitLess{}, 3);  // misaligned start
+    }
+    std::mt19937_64 rng64(7);
+    std::vector<int64_t> h(3000001);
+    for (auto& x : h) x = int64_t(rng64());
+    check_both(s, h, ModAbsLess{1000});
+    check_both(s, h, ModAbsLess{1000}, 1);
+#ifdef __CUDACC_EXTENDED_LAMBDA__
+    std::vector<float> f(1000003);
+    std::normal_distribution<float> nd;
+    for (auto& x : f) x = std::round(nd(rng) * 8.0f);
+    check_both(s, f, [] __host__ __device__(float a, float b) { return std::fabs(a) < std::fabs(b); });
+#endif
+}
+
+}  // namespace
+
+int main()
+{
+    cudaStream_t stream;
+    CUDA(cudaStreamCreate(&stream));
+    const auto s = reinterpret_cast<lcpp_stream_t>(stream);
+    reference_case(s);
+    empty_sentinels(s);
+    random_cases(s);
+    CUDA(cudaStreamDestroy(stream));
+    std::printf("OK %d\n", g_checks);
+    return 0;
+}

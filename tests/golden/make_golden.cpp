@@ -221,6 +221,30 @@ static void reduce_cases()
     emit("reduce_shuffled_minmax", mm);
 }
 
+// tests/device_reduce_test.cpp:238-330 -- ArgMax of {1, 9, 4, 9, 3} is
+// (9, 1) (first of equal maxima); float ArgMax of {-7, -3, -5} is (-3, 1);
+// with the comparator "last decimal digit less", {21, 11, 33, 23, 8, 28}
+// gives ArgMin (21, 0) and ArgMax (8, 4).  Expected pairs come from a
+// first-index scan with std::min_element / std::max_element semantics.
+static void arg_cases()
+{
+    const std::vector<int32_t> ties{1, 9, 4, 9, 3};
+    emit("arg_ties_in", ties);
+    const auto mx = std::max_element(ties.begin(), ties.end());  // first of equal maxima
+    emit("arg_ties_max", std::vector<int32_t>{*mx, int32_t(mx - ties.begin())});
+    const std::vector<float> neg{-7.0f, -3.0f, -5.0f};
+    emit("arg_negative_in", neg);
+    const auto nmx = std::max_element(neg.begin(), neg.end());
+    emit("arg_negative_max", std::vector<float>{*nmx, float(nmx - neg.begin())});
+    const std::vector<int32_t> digits{21, 11, 33, 23, 8, 28};
+    emit("arg_digit_in", digits);
+    auto last_digit_less = [](int32_t l, int32_t r) { return l % 10 < r % 10; };
+    const auto dmn = std::min_element(digits.begin(), digits.end(), last_digit_less);
+    const auto dmx = std::max_element(digits.begin(), digits.end(), last_digit_less);
+    emit("arg_digit_minmax", std::vector<int32_t>{*dmn, int32_t(dmn - digits.begin()), *dmx,
+                                                  int32_t(dmx - digits.begin())});
+}
+
 // tests/device_segmented_sort_test.cpp:22-56 and :260-268 -- 19 items in
 // segments [1,4) [5,5) [5,9) [10,19); keys outside every segment are -777
 // and their values UINT_MAX; expected = std::stable_sort per segment with
@@ -308,6 +332,7 @@ int main(int argc, char** argv)
     interface_cases();
     scan_cases();
     reduce_cases();
+    arg_cases();
     segmented_cases();
     decomposed_cases();
     std::fclose(g_index);

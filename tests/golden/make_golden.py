@@ -28,7 +28,7 @@ def is_expected_output(name: str) -> bool:
 
 
 def main() -> int:
-    with tempfile.TemporaryDirectory() as tmp:
+    with tempfile.TemporaryDirectory(dir=HERE) as tmp:
         exe = Path(tmp) / "make_golden"
         subprocess.run(["g++", "-O2", "-std=c++17", str(HERE / "make_golden.cpp"), "-o", str(exe)],
                        check=True)

@@ -11,6 +11,7 @@ import pytest
 
 ROOT = Path(__file__).resolve().parent.parent
 SRC = ROOT / "tests" / "cpp" / "device_api_test.cpp"
+CU_SRC = ROOT / "tests" / "cpp" / "device_compare_test.cu"
 CUDA = Path("/usr/local/cuda")
 LIBDIR = ROOT / "luisacompute-parallelprimitive_b200" / "lcpp_b200"
 
@@ -36,6 +37,33 @@ def test_cpp_program_runs(tmp_path):
     r = subprocess.run([gxx, "-std=c++17", "-O2", f"-I{ROOT / 'include'}", f"-I{CUDA / 'include'}", str(SRC),
                         "-o", str(exe), f"-L{LIBDIR}", "-llcpp_b200", f"-L{CUDA / 'lib64'}", "-lcudart",
                         f"-Wl,-rpath,{LIBDIR}", f"-Wl,-rpath,{CUDA / 'lib64'}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert run.stdout.startswith("OK "), run.stdout
+
+
+def _nvcc_cmd(out: Path, compile_only: bool):
+    nvcc = CUDA / "bin" / "nvcc"
+    if not nvcc.exists():
+        pytest.skip("nvcc is missing")
+    cmd = [str(nvcc), "-std=c++17", "-O2", "-gencode", "arch=compute_100a,code=sm_100a", "--extended-lambda",
+           f"-I{ROOT / 'include'}", str(CU_SRC), "-o", str(out)]
+    if compile_only:
+        return cmd[:-3] + ["-c", str(CU_SRC), "-o", str(out)]
+    return cmd + [f"-L{LIBDIR}", "-llcpp_b200", f"-Xlinker=-rpath,{LIBDIR}"]
+
+
+def test_comparator_header_compiles(tmp_path):
+    """The comparator overloads (lcpp_b200_device.cuh through lcpp_b200.hpp) build with nvcc."""
+    r = subprocess.run(_nvcc_cmd(tmp_path / "cmp.o", True), capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
+@pytest.mark.gpu
+def test_comparator_program_runs(tmp_path):
+    exe = tmp_path / "device_compare_test"
+    r = subprocess.run(_nvcc_cmd(exe, False), capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     assert run.returncode == 0, run.stdout + run.stderr

@@ -179,6 +179,45 @@ def test_reduce_shuffled_golden(oracle, golden):
     assert oracle.reduce(x, oracle.OP_MAX, np.iinfo(np.int32).min) == mx
 
 
+def test_arg_extremum_golden(oracle, golden):
+    """device_reduce_test.cpp:238-288: first of equal maxima; negative floats."""
+    v, i = oracle.arg_extremum(golden["arg_ties_in"], False)
+    assert (v, i) == tuple(golden["arg_ties_max"])
+    v, i = oracle.arg_extremum(golden["arg_negative_in"], False)
+    assert v == golden["arg_negative_max"][0] and i == int(golden["arg_negative_max"][1])
+
+
+def test_arg_extremum_comparator_golden(oracle, golden):
+    """device_reduce_test.cpp:290-330: last-digit comparator, first ties."""
+    x = golden["arg_digit_in"]
+    mn, mni, mx, mxi = golden["arg_digit_minmax"]
+    def less(a, b):
+        return a % 10 < b % 10
+    assert oracle.arg_extremum_compare(x, True, less) == (mn, mni)
+    assert oracle.arg_extremum_compare(x, False, less) == (mx, mxi)
+
+
+@pytest.mark.parametrize("dtype", [np.int32, np.uint32, np.float32, np.int64, np.uint64, np.float64])
+def test_arg_extremum_vs_numpy(oracle, dtype):
+    """First index of the extreme (numpy argmin / argmax keep the first), the
+    empty-input sentinels (device_reduce.h:318-323), NaN never wins."""
+    rng = np.random.default_rng(5)
+    x = rng.integers(0, 50, size=10_007).astype(dtype)
+    assert oracle.arg_extremum(x, True) == (x.min(), int(np.argmin(x)))
+    assert oracle.arg_extremum(x, False) == (x.max(), int(np.argmax(x)))
+    info = np.finfo(dtype) if np.dtype(dtype).kind == "f" else np.iinfo(dtype)
+    assert oracle.arg_extremum(np.zeros(0, dtype), True) == (info.max, 1)
+    assert oracle.arg_extremum(np.zeros(0, dtype), False) == (info.min, 1)
+    if np.dtype(dtype).kind == "f":
+        x[::3] = np.nan
+        assert oracle.arg_extremum(x, True)[1] == int(np.nanargmin(x))
+        assert oracle.arg_extremum(x, False)[1] == int(np.nanargmax(x))
+    # the comparator walk with "<" is the same fold for NaN-free input
+    y = rng.integers(0, 9, size=2000).astype(dtype)
+    assert oracle.arg_extremum_compare(y, True, lambda a, b: a < b) == oracle.arg_extremum(y, True)
+    assert oracle.arg_extremum_compare(y, False, lambda a, b: a < b) == oracle.arg_extremum(y, False)
+
+
 def test_reduce_identities(oracle):
     """device_reduce_test.cpp:95-118 (ones, 2^k+1) and :220-236 (float max identity)."""
     for k in range(0, 16):
