@@ -79,6 +79,16 @@ OPS = {
     "argmin": dict(metric="Gitems/s float32 ArgMin @2^30", unit="Gitems/s", log2n=30, dtype="f32",
                    workload="DeviceReduce::ArgMin f32 U[0,1) (many tied minima), seed 1", bytes=4, kbytes=4,
                    kernel="arg_extremum_kernel"),
+    # By-key family, keys i / 100 (segments of 100 as in the reference's
+    # by-key tests), i32 values from the scan stream.  InclusiveSumByKey reads
+    # keys and values and writes the output (12 B per item); ReduceByKey reads
+    # both and writes one (key, aggregate) pair per 100 items (8.08 B).
+    "scan_by_key": dict(metric="Gitems/s i32 by i32 InclusiveSumByKey @2^30", unit="Gitems/s", log2n=30,
+                        dtype="i32", workload="InclusiveSumByKey i32 values by keys i/100, seed 1", bytes=12,
+                        kbytes=12, kernel="by_key_kernel"),
+    "reduce_by_key": dict(metric="Gitems/s i32 by i32 ReduceByKey Sum @2^30", unit="Gitems/s", log2n=30,
+                          dtype="i32", workload="ReduceByKey Sum of i32 values by keys i/100, seed 1",
+                          bytes=8.08, kbytes=8.08, kernel="by_key_kernel"),
     # DeviceSegmentedRadixSort (SURVEY next-row widening): 2^27 u32 keys in
     # segments of 1..2047 keys (sizes uniform, seed 1), contiguous.  All
     # segments are short, so the one-block-per-segment kernel does the whole
@@ -265,6 +275,17 @@ class Workload:
             self.inputs = [fill(T.float32, L.GEN_F32_UNIT, 1)]
             self.outputs = [T.empty(1, dtype=T.float32, device=dev)]
             self.temp = L.alloc_temp(L.DeviceReduce.GetTempStorageBytes(L.F32, n))
+        elif op in ("scan_by_key", "reduce_by_key"):
+            keys = T.arange(n, dtype=T.int64, device=dev).div_(100, rounding_mode="floor").to(T.int32)
+            self.inputs = [keys, fill(T.int32, L.GEN_I32_SCAN, 1)]
+            if op == "scan_by_key":
+                self.outputs = [T.empty_like(self.inputs[1])]
+                self.temp = L.alloc_temp(L.DeviceScan.GetScanByKeyTempStorageBytes(L.I32, L.I32, n))
+            else:
+                runs = (n + 99) // 100
+                self.outputs = [T.empty(runs, dtype=T.int32, device=dev), T.empty(runs, dtype=T.int32, device=dev),
+                                T.empty(1, dtype=T.int32, device=dev)]
+                self.temp = L.alloc_temp(L.DeviceReduce.GetReduceByKeyTempStorageBytes(L.I32, L.I32, n))
         elif op == "argmin":
             self.inputs = [fill(T.float32, L.GEN_F32_UNIT, 1)]
             self.outputs = [T.empty(1, dtype=T.float32, device=dev), T.empty(1, dtype=T.int32, device=dev)]
@@ -298,6 +319,10 @@ class Workload:
             self.rd.Max(t, i[0], o[0], n)
         elif op == "argmin":
             self.rd.ArgMin(t, i[0], o[0], o[1], n)
+        elif op == "scan_by_key":
+            self.sc.InclusiveSumByKey(t, i[0], i[1], o[0], n)
+        elif op == "reduce_by_key":
+            self.rd.ReduceByKey(t, i[0], i[1], o[0], o[1], o[2], self.L.OP_SUM, n)
 
     def dominant_kind(self):
         L = self.L
@@ -311,6 +336,8 @@ class Workload:
             return L.KERNEL_MERGE
         if self.op == "argmin":
             return L.KERNEL_ARG_REDUCE
+        if self.op.endswith("by_key"):
+            return L.KERNEL_BY_KEY
         return L.KERNEL_SORT_ONESWEEP
 
 
@@ -366,6 +393,13 @@ def cpu_fn(op: str, n_sample: int, threads: int):
     if op == "argmin":
         x = O.generate(O.GEN_F32_UNIT, n_sample, seed=1)
         return lambda: O.arg_extremum(x, True)
+    if op in ("scan_by_key", "reduce_by_key"):
+        import numpy as np
+        k = (np.arange(n_sample, dtype=np.int64) // 100).astype(np.int32)
+        v = O.generate(O.GEN_I32_SCAN, n_sample, seed=1)
+        if op == "scan_by_key":
+            return lambda: O.scan_by_key(k, v, "inclusive")
+        return lambda: O.reduce_by_key(k, v, O.OP_SUM)
     x = O.generate(O.GEN_I64_UNIFORM, n_sample, seed=1)
     return lambda: O.reduce(x, O.OP_MAX, -(1 << 63))
 

@@ -178,6 +178,39 @@ lcpp_status lcpp_scan_exclusive_sum(void* temp, size_t temp_bytes, const void* d
 lcpp_status lcpp_scan_inclusive_sum(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
                                     uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
 
+/* By-key scans: DeviceScan::GetScanByKeyTempStorageBytes,
+ * ExclusiveScanByKey, InclusiveScanByKey (with and without an initial
+ * value), ExclusiveSumByKey, InclusiveSumByKey (device_scan.h:310-597).
+ * Segments are maximal runs of consecutive equal keys (== on the key type:
+ * -0.0 equals +0.0, NaN starts a new run; signed and unsigned keys of one
+ * width compare alike).  Within a segment starting at h:
+ *   exclusive:      out[i] = init (i == h), init (+) v[h] (+) ... (+) v[i-1]
+ *   inclusive:      out[i] = v[h] (+) ... (+) v[i]
+ *   inclusive init: out[i] = init (+) v[h] (+) ... (+) v[i]
+ * Keys and values may be of different types; d_values_out may equal
+ * d_values_in.  `init` points to one host value of value_dtype.  Zero items
+ * do nothing.  The Sum forms are op = SUM with a zero init. */
+lcpp_status lcpp_scan_by_key_temp_bytes(lcpp_dtype key_dtype, lcpp_dtype value_dtype, uint64_t num_items,
+                                        size_t* temp_bytes);
+lcpp_status lcpp_scan_exclusive_by_key(void* temp, size_t temp_bytes, const void* d_keys_in,
+                                       const void* d_values_in, void* d_values_out, uint64_t num_items,
+                                       lcpp_op op, const void* init, lcpp_dtype key_dtype,
+                                       lcpp_dtype value_dtype, lcpp_stream_t stream);
+lcpp_status lcpp_scan_inclusive_by_key(void* temp, size_t temp_bytes, const void* d_keys_in,
+                                       const void* d_values_in, void* d_values_out, uint64_t num_items,
+                                       lcpp_op op, lcpp_dtype key_dtype, lcpp_dtype value_dtype,
+                                       lcpp_stream_t stream);
+lcpp_status lcpp_scan_inclusive_by_key_init(void* temp, size_t temp_bytes, const void* d_keys_in,
+                                            const void* d_values_in, void* d_values_out, uint64_t num_items,
+                                            lcpp_op op, const void* init, lcpp_dtype key_dtype,
+                                            lcpp_dtype value_dtype, lcpp_stream_t stream);
+lcpp_status lcpp_scan_exclusive_sum_by_key(void* temp, size_t temp_bytes, const void* d_keys_in,
+                                           const void* d_values_in, void* d_values_out, uint64_t num_items,
+                                           lcpp_dtype key_dtype, lcpp_dtype value_dtype, lcpp_stream_t stream);
+lcpp_status lcpp_scan_inclusive_sum_by_key(void* temp, size_t temp_bytes, const void* d_keys_in,
+                                           const void* d_values_in, void* d_values_out, uint64_t num_items,
+                                           lcpp_dtype key_dtype, lcpp_dtype value_dtype, lcpp_stream_t stream);
+
 /* No counterpart in the reference.  InclusiveSum for callers that cannot
  * allocate device memory when they scan (code running inside an allocator or
  * a memory-pool callback, a plugin host that hands out fixed buffers only, a
@@ -343,6 +376,19 @@ lcpp_status lcpp_reduce_argmin(void* temp, size_t temp_bytes, const void* d_in, 
                                uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
 lcpp_status lcpp_reduce_argmax(void* temp, size_t temp_bytes, const void* d_in, void* d_out, uint32_t* d_index_out,
                                uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
+
+/* Replace DeviceReduce::GetReduceByKeyTempStorageBytes / ReduceByKey
+ * (device_reduce.h:208-223, :437-491): for every maximal run of consecutive
+ * equal keys (as in the by-key scans) d_unique_out[r] = the run's first key,
+ * d_aggregates_out[r] = v[first] (+) ... (+) v[last], and *d_num_runs_out =
+ * the number of runs (uint32; zero items write 0 and nothing else).
+ * num_items at most 2^32 - 1; d_unique_out must not overlap d_keys_in. */
+lcpp_status lcpp_reduce_by_key_temp_bytes(lcpp_dtype key_dtype, lcpp_dtype value_dtype, uint64_t num_items,
+                                          size_t* temp_bytes);
+lcpp_status lcpp_reduce_by_key(void* temp, size_t temp_bytes, const void* d_keys_in, const void* d_values_in,
+                               void* d_unique_out, void* d_aggregates_out, uint32_t* d_num_runs_out,
+                               uint64_t num_items, lcpp_op op, lcpp_dtype key_dtype, lcpp_dtype value_dtype,
+                               lcpp_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Device diagnostics (no reference counterpart: the reference's look-back

@@ -75,9 +75,33 @@ struct DoubleBuffer {
     [[nodiscard]] BufferView<T> alternate() const noexcept { return d_buffer[selector ^ 1]; }
 };
 
-struct SumOp {};
-struct MinOp {};
-struct MaxOp {};
+#ifdef __CUDACC__
+#define LCPP_B200_HD __host__ __device__
+#else
+#define LCPP_B200_HD
+#endif
+
+/// The reference's SumOp / MinOp / MaxOp (thread_operators.h:49-75): tags
+/// for the C ABI operators, and callable (also on the device under nvcc) for
+/// the template paths.  Integer sums wrap.
+struct SumOp {
+    template <typename T>
+    LCPP_B200_HD T operator()(T a, T b) const
+    {
+        if constexpr (std::is_integral_v<T>)
+            return T(std::make_unsigned_t<T>(a) + std::make_unsigned_t<T>(b));
+        else
+            return a + b;
+    }
+};
+struct MinOp {
+    template <typename T>
+    LCPP_B200_HD T operator()(T a, T b) const { return b < a ? b : a; }
+};
+struct MaxOp {
+    template <typename T>
+    LCPP_B200_HD T operator()(T a, T b) const { return a < b ? b : a; }
+};
 
 class Error : public std::runtime_error {
 public:
@@ -117,6 +141,9 @@ constexpr lcpp_dtype checked_dtype()
 }
 
 template <typename Op>
+constexpr bool is_builtin_op = std::is_same_v<Op, SumOp> || std::is_same_v<Op, MinOp> || std::is_same_v<Op, MaxOp>;
+
+template <typename Op>
 constexpr lcpp_op op_of()
 {
     if constexpr (std::is_same_v<Op, SumOp>)
@@ -140,6 +167,10 @@ inline void require(bool ok, const char* what)
 }
 
 inline size_t temp_bytes(BufferView<uint32_t> t) { return t.size_bytes(); }
+
+// "keys equal by ==" for the by-key scans (selects the C ABI)
+struct KeyEq {};
+constexpr const KeyEq* kKeyEq = nullptr;
 
 #ifdef __CUDACC__
 inline void check_cuda(cudaError_t e, const char* what)
@@ -681,7 +712,156 @@ public:
                       "InclusiveSum");
     }
 
+    // ---- by key (device_scan.h:310-597; argument order as the reference's).
+    // ScanOp: SumOp / MinOp / MaxOp through the C ABI; under nvcc also any
+    // __device__ callable, and the overloads with an EqualityOp (a
+    // __device__ callable "same segment"), through lcpp_b200_device.cuh.
+
+    template <typename K, typename V>
+    static size_t GetScanByKeyTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_scan_by_key_temp_bytes(detail::checked_dtype<K>(), detail::checked_dtype<V>(), num_items,
+                                                  &b),
+                      "GetScanByKeyTempStorageBytes");
+        return b;
+    }
+
+    template <typename K, typename V, typename ScanOp>
+    void ExclusiveScanByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> d_keys_in,
+                            BufferView<V> d_values_in, BufferView<V> d_values_out, ScanOp scan_op, uint64_t num_items,
+                            V initial_value)
+    {
+        by_key(stream, temp_storage, d_keys_in, d_values_in, d_values_out, scan_op, num_items, 0, initial_value,
+               detail::kKeyEq, "ExclusiveScanByKey");
+    }
+
+    template <typename K, typename V, typename ScanOp>
+    void InclusiveScanByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> d_keys_in,
+                            BufferView<V> d_values_in, BufferView<V> d_values_out, ScanOp scan_op, uint64_t num_items)
+    {
+        by_key(stream, temp_storage, d_keys_in, d_values_in, d_values_out, scan_op, num_items, 1, V{},
+               detail::kKeyEq, "InclusiveScanByKey");
+    }
+
+    /// The reference's extension: init prepended to every segment.
+    template <typename K, typename V, typename ScanOp>
+    void InclusiveScanByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> d_keys_in,
+                            BufferView<V> d_values_in, BufferView<V> d_values_out, ScanOp scan_op, uint64_t num_items,
+                            V initial_value)
+    {
+        by_key(stream, temp_storage, d_keys_in, d_values_in, d_values_out, scan_op, num_items, 2, initial_value,
+               detail::kKeyEq, "InclusiveScanByKey");
+    }
+
+    template <typename K, typename V>
+    void ExclusiveSumByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> d_keys_in,
+                           BufferView<V> d_values_in, BufferView<V> d_values_out, uint64_t num_items)
+    {
+        ExclusiveScanByKey(stream, temp_storage, d_keys_in, d_values_in, d_values_out, SumOp{}, num_items, V(0));
+    }
+
+    template <typename K, typename V>
+    void InclusiveSumByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> d_keys_in,
+                           BufferView<V> d_values_in, BufferView<V> d_values_out, uint64_t num_items)
+    {
+        InclusiveScanByKey(stream, temp_storage, d_keys_in, d_values_in, d_values_out, SumOp{}, num_items);
+    }
+
+#ifdef __CUDACC__
+    template <typename K, typename V, typename ScanOp, typename EqualityOp>
+    void ExclusiveScanByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> d_keys_in,
+                            BufferView<V> d_values_in, BufferView<V> d_values_out, ScanOp scan_op, uint64_t num_items,
+                            V initial_value, EqualityOp equality_op)
+    {
+        by_key(stream, temp_storage, d_keys_in, d_values_in, d_values_out, scan_op, num_items, 0, initial_value,
+               &equality_op, "ExclusiveScanByKey");
+    }
+
+    template <typename K, typename V, typename ScanOp, typename EqualityOp,
+              typename = std::enable_if_t<!std::is_arithmetic_v<EqualityOp>>>
+    void InclusiveScanByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> d_keys_in,
+                            BufferView<V> d_values_in, BufferView<V> d_values_out, ScanOp scan_op, uint64_t num_items,
+                            EqualityOp equality_op)
+    {
+        by_key(stream, temp_storage, d_keys_in, d_values_in, d_values_out, scan_op, num_items, 1, V{}, &equality_op,
+               "InclusiveScanByKey");
+    }
+
+    template <typename K, typename V, typename ScanOp, typename EqualityOp>
+    void InclusiveScanByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> d_keys_in,
+                            BufferView<V> d_values_in, BufferView<V> d_values_out, ScanOp scan_op, uint64_t num_items,
+                            V initial_value, EqualityOp equality_op)
+    {
+        by_key(stream, temp_storage, d_keys_in, d_values_in, d_values_out, scan_op, num_items, 2, initial_value,
+               &equality_op, "InclusiveScanByKey");
+    }
+
+    template <typename K, typename V, typename EqualityOp>
+    void ExclusiveSumByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> d_keys_in,
+                           BufferView<V> d_values_in, BufferView<V> d_values_out, uint64_t num_items,
+                           EqualityOp equality_op)
+    {
+        ExclusiveScanByKey(stream, temp_storage, d_keys_in, d_values_in, d_values_out, SumOp{}, num_items, V(0),
+                           equality_op);
+    }
+
+    template <typename K, typename V, typename EqualityOp>
+    void InclusiveSumByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> d_keys_in,
+                           BufferView<V> d_values_in, BufferView<V> d_values_out, uint64_t num_items,
+                           EqualityOp equality_op)
+    {
+        InclusiveScanByKey(stream, temp_storage, d_keys_in, d_values_in, d_values_out, SumOp{}, num_items,
+                           equality_op);
+    }
+#endif
+
 private:
+    // mode 0 exclusive, 1 inclusive, 2 inclusive with init; eq: a
+    // detail::KeyEq pointer for == (the C ABI), else the user's equality.
+    template <typename K, typename V, typename ScanOp, typename EqualityOp>
+    void by_key(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> keys, BufferView<V> vin,
+                BufferView<V> vout, ScanOp scan_op, uint64_t n, int mode, V init, const EqualityOp* eq,
+                const char* what)
+    {
+        detail::require(keys.size() >= n && vin.size() >= n && vout.size() >= n,
+                        "DeviceScan: a key or value view is shorter than num_items");
+        constexpr bool custom_eq = !std::is_same_v<EqualityOp, detail::KeyEq>;
+        if constexpr (detail::is_builtin_op<ScanOp> && !custom_eq) {
+            (void)scan_op;
+            (void)eq;
+            const void* tb = temp_storage.data();
+            const size_t nb = detail::temp_bytes(temp_storage);
+            const lcpp_dtype kd = detail::checked_dtype<K>(), vd = detail::checked_dtype<V>();
+            const lcpp_op op = detail::op_of<ScanOp>();
+            lcpp_status s;
+            if (mode == 0)
+                s = lcpp_scan_exclusive_by_key(const_cast<void*>(tb), nb, keys.data(), vin.data(), vout.data(), n, op,
+                                               &init, kd, vd, stream);
+            else if (mode == 1)
+                s = lcpp_scan_inclusive_by_key(const_cast<void*>(tb), nb, keys.data(), vin.data(), vout.data(), n, op,
+                                               kd, vd, stream);
+            else
+                s = lcpp_scan_inclusive_by_key_init(const_cast<void*>(tb), nb, keys.data(), vin.data(), vout.data(),
+                                                    n, op, &init, kd, vd, stream);
+            detail::check(s, what);
+        } else {
+#ifdef __CUDACC__
+            const auto st = reinterpret_cast<cudaStream_t>(stream);
+            cudaError_t e;
+            if constexpr (custom_eq)
+                e = device::scan_by_key(temp_storage.data(), detail::temp_bytes(temp_storage), keys.data(), vin.data(),
+                                        vout.data(), n, mode, init, scan_op, *eq, st);
+            else
+                e = device::scan_by_key(temp_storage.data(), detail::temp_bytes(temp_storage), keys.data(), vin.data(),
+                                        vout.data(), n, mode, init, scan_op, device::EqualTo{}, st);
+            detail::check_cuda(e, what);
+#else
+            static_assert(detail::is_builtin_op<ScanOp>, "custom scan operators need nvcc (lcpp_b200_device.cuh)");
+#endif
+        }
+    }
+
     template <typename T>
     static void views(BufferView<T> i, BufferView<T> o, uint64_t n)
     {
@@ -743,6 +923,51 @@ public:
         detail::check(lcpp_reduce_max(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
                                       d_out.data(), num_items, detail::checked_dtype<T>(), stream),
                       "Max");
+    }
+
+    /// Temp storage bytes for ReduceByKey (device_reduce.h:208-223).
+    template <typename K, typename V>
+    static size_t GetReduceByKeyTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_reduce_by_key_temp_bytes(detail::checked_dtype<K>(), detail::checked_dtype<V>(),
+                                                    num_items, &b),
+                      "GetReduceByKeyTempStorageBytes");
+        return b;
+    }
+
+    /// One (first key, aggregate) per run of equal consecutive keys, and the
+    /// run count (device_reduce.h:437-491).  ReduceOp: SumOp / MinOp / MaxOp,
+    /// or under nvcc any __device__ callable.
+    template <typename K, typename V, typename ReduceOp>
+    void ReduceByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> d_keys_in,
+                     BufferView<V> d_values_in, BufferView<K> d_unique_out, BufferView<V> d_aggregates_out,
+                     BufferView<uint32_t> d_num_runs_out, ReduceOp reduce_op, uint64_t num_elements)
+    {
+        detail::require(d_keys_in.size() >= num_elements && d_values_in.size() >= num_elements &&
+                            d_num_runs_out.size() >= 1,
+                        "DeviceReduce: a by-key input view is shorter than num_elements, or no run-count view");
+        detail::require(num_elements == 0 || (d_unique_out.size() >= 1 && d_aggregates_out.size() >= 1),
+                        "DeviceReduce: a by-key output view is empty");
+        if constexpr (detail::is_builtin_op<ReduceOp>) {
+            (void)reduce_op;
+            detail::check(lcpp_reduce_by_key(temp_storage.data(), detail::temp_bytes(temp_storage), d_keys_in.data(),
+                                             d_values_in.data(), d_unique_out.data(), d_aggregates_out.data(),
+                                             d_num_runs_out.data(), num_elements, detail::op_of<ReduceOp>(),
+                                             detail::checked_dtype<K>(), detail::checked_dtype<V>(), stream),
+                          "ReduceByKey");
+        } else {
+#ifdef __CUDACC__
+            detail::check_cuda(device::reduce_by_key(temp_storage.data(), detail::temp_bytes(temp_storage),
+                                                     d_keys_in.data(), d_values_in.data(), d_unique_out.data(),
+                                                     d_aggregates_out.data(), d_num_runs_out.data(), num_elements,
+                                                     reduce_op, device::EqualTo{},
+                                                     reinterpret_cast<cudaStream_t>(stream)),
+                               "ReduceByKey");
+#else
+            static_assert(detail::is_builtin_op<ReduceOp>, "custom reduce operators need nvcc (lcpp_b200_device.cuh)");
+#endif
+        }
     }
 
     /// Temp storage bytes for ArgMin / ArgMax (the reference's

@@ -317,6 +317,445 @@ cudaError_t ArgMax(void* temp, size_t temp_bytes, const T* d_in, T* d_out, uint3
                                stream);
 }
 
+
+/* ---------------------------------------------------------------------------
+ * Scans and reductions by key.
+ *
+ * DeviceScan::ExclusiveScanByKey / InclusiveScanByKey (and the ...SumByKey
+ * forms; src/lcpp/device/device_scan.h:425-597) and
+ * DeviceReduce::ReduceByKey (src/lcpp/device/device_reduce.h:437-491,
+ * details/reduce_by_key.h).  A segment (run) is a maximal stretch of
+ * consecutive items whose keys compare equal with `equal` (default ==, so
+ * -0.0 and +0.0 share a run and every NaN starts one).  Per item i of a
+ * segment starting at h:
+ *   exclusive:       out[i] = init                          (i == h)
+ *                             init op v[h] op ... op v[i-1]  (i > h)
+ *   inclusive:       out[i] = v[h] op ... op v[i]
+ *   inclusive init:  out[i] = init op v[h] op ... op v[i]
+ *   reduce by key:   unique_out[r] = key[h_r], aggregates_out[r] = the fold of
+ *                    run r, *num_runs_out = number of runs (0 for no items).
+ *
+ * One decoupled look-back pass scans (count, value) pairs under
+ * (c1, v1) + (c2, v2) = (c1 + c2, c2 ? v2 : v1 op v2), where c counts segment
+ * heads; the pair operator is associative whenever `op` is, so tiles, warps
+ * and lanes combine in any grouping with left-to-right operand order.  The
+ * count gives ReduceByKey each head's run index (its unique key and the
+ * previous run's aggregate are written at the head; the last item writes the
+ * last run and the run count).  The scans only need "some head", so their
+ * look-back stops at the nearest predecessor tile that holds a head.
+ * Tile = 256 threads x 4 groups x 4 consecutive items (4096 items); a lane's
+ * group is one 16-byte load for 4-byte types (two for 8-byte types) when
+ * keys, values and output are 16-byte aligned.  Tiles take ids from an atomic
+ * counter in launch order, so a tile's predecessors are always running or
+ * done; every wait is bounded by %globaltimer (4 s) and records error 5
+ * (LCPP_ERR_LOOKBACK_TIMEOUT) at byte 4 of temp storage.
+ * ------------------------------------------------------------------------- */
+
+/* key equality (the reference's default `lhs == rhs`) */
+struct EqualTo {
+    template <typename K>
+    __device__ __forceinline__ bool operator()(K a, K b) const { return a == b; }
+};
+
+namespace bykey_detail {
+
+constexpr int kBlock = 256;
+constexpr int kWarps = kBlock / 32;
+constexpr int kChunks = 4;
+constexpr int kGroup = 4;
+constexpr uint64_t kTileItems = uint64_t(kBlock) * kChunks * kGroup;
+constexpr uint64_t kWaitLimitNs = 4000000000ull;
+constexpr unsigned int kErrTimeout = 5;
+constexpr size_t kAlign = 256;
+enum : uint32_t { kInvalid = 0, kPartial = 1, kInclusive = 2 };
+enum : int { kModeExclusive = 0, kModeInclusive = 1, kModeInclusiveInit = 2, kModeReduce = 3 };
+
+struct Ctrl {
+    unsigned int tile_counter;
+    unsigned int error;  // byte 4 of temp storage
+};
+
+/* A (head count, value) pair, or nothing (has == false). */
+template <typename V>
+struct Acc {
+    uint32_t c;
+    uint32_t has;
+    V v;
+};
+
+template <bool COUNT, typename V, typename Op>
+__device__ __forceinline__ Acc<V> seg(const Acc<V>& a, const Acc<V>& b, const Op& op)
+{
+    if (!a.has) return b;
+    if (!b.has) return a;
+    Acc<V> r;
+    r.c = COUNT ? a.c + b.c : (a.c | b.c);
+    r.has = 1;
+    r.v = b.c ? b.v : op(a.v, b.v);
+    return r;
+}
+
+template <typename V>
+__device__ __forceinline__ Acc<V> shfl_acc(const Acc<V>& a, int src)
+{
+    return {__shfl_sync(0xffffffffu, a.c, src), __shfl_sync(0xffffffffu, a.has, src),
+            __shfl_sync(0xffffffffu, a.v, src)};
+}
+template <typename V>
+__device__ __forceinline__ Acc<V> shfl_up_acc(const Acc<V>& a, int d)
+{
+    return {__shfl_up_sync(0xffffffffu, a.c, d), __shfl_up_sync(0xffffffffu, a.has, d),
+            __shfl_up_sync(0xffffffffu, a.v, d)};
+}
+template <typename V>
+__device__ __forceinline__ Acc<V> shfl_down_acc(const Acc<V>& a, int d)
+{
+    return {__shfl_down_sync(0xffffffffu, a.c, d), __shfl_down_sync(0xffffffffu, a.has, d),
+            __shfl_down_sync(0xffffffffu, a.v, d)};
+}
+
+__device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t* p)
+{
+    uint64_t v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_u64(uint64_t* p, uint64_t v)
+{
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+/* Tile status: meta[t] = (head count << 32) | status, released after the
+ * value it announces (partial[t] or inclusive[t]) is stored. */
+template <typename V>
+struct TileStatus {
+    uint64_t* meta;
+    V* partial;
+    V* inclusive;
+    __device__ __forceinline__ void publish(uint64_t t, uint32_t status, const Acc<V>& a) const
+    {
+        *static_cast<volatile V*>(status == kPartial ? partial + t : inclusive + t) = a.v;
+        st_release_u64(meta + t, (uint64_t(a.c) << 32) | status);
+    }
+};
+
+/* Exclusive prefix of `tile` (> 0), run by one whole warp: lane l inspects
+ * tile base - l; the walk ends at the nearest inclusive tile (or, for the
+ * scans, the nearest tile holding a head). */
+template <bool COUNT, typename V, typename Op>
+__device__ __forceinline__ Acc<V> look_back(uint64_t tile, const TileStatus<V>& ts, Ctrl* ctrl, const Op& op)
+{
+    const int lane = threadIdx.x & 31;
+    Acc<V> prefix{0, 0, V{}};
+    int64_t base = int64_t(tile) - 1;
+    while (true) {
+        const int64_t j = base - lane;
+        Acc<V> val{0, 0, V{}};
+        uint32_t status = kInclusive;  // lanes before tile 0 end the walk
+        if (j >= 0) {
+            uint64_t m;
+            uint32_t spins = 0;
+            uint64_t t0 = 0;
+            bool gave_up = false;
+            while (((m = ld_acquire_u64(ts.meta + j)) & 3u) == kInvalid) {
+                if (++spins == 64) {
+                    spins = 0;
+                    const uint64_t now = global_ns();
+                    if (t0 == 0) {
+                        t0 = now;
+                    } else if (now - t0 > kWaitLimitNs || *static_cast<volatile unsigned int*>(&ctrl->error)) {
+                        atomicCAS(&ctrl->error, 0u, kErrTimeout);
+                        gave_up = true;  // stop here, contributing nothing
+                        break;
+                    }
+                }
+            }
+            if (!gave_up) {
+                status = uint32_t(m & 3u);
+                val.c = uint32_t(m >> 32);
+                val.has = 1;
+                val.v = *static_cast<const volatile V*>(status == kPartial ? ts.partial + j : ts.inclusive + j);
+            }
+        }
+        const bool stop = status == kInclusive || (!COUNT && val.has && val.c != 0);
+        const uint32_t mask = __ballot_sync(0xffffffffu, stop);
+        const int last = mask ? __ffs(mask) - 1 : 31;
+        Acc<V> x = lane <= last ? val : Acc<V>{0, 0, V{}};
+        /* ordered fold of lanes 0..last: farther tiles (higher lanes) first */
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const Acc<V> y = shfl_down_acc(x, d);
+            if (lane + d < 32) x = seg<COUNT>(y, x, op);
+        }
+        prefix = seg<COUNT>(shfl_acc(x, 0), prefix, op);
+        if (mask) return prefix;
+        base -= 32;
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void load_group(const T* p, uint64_t n, uint64_t g, bool vector, T (&x)[kGroup])
+{
+    if (vector && g + kGroup <= n) {
+        constexpr int W = int(sizeof(T)) * kGroup / 16;
+        const uint4* q = reinterpret_cast<const uint4*>(p + g);
+        uint4 w[W];
+#pragma unroll
+        for (int i = 0; i < W; ++i) w[i] = q[i];
+        memcpy(x, w, sizeof(x));
+    } else {
+#pragma unroll
+        for (int e = 0; e < kGroup; ++e) x[e] = g + e < n ? p[g + e] : T{};
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_group(T* p, uint64_t n, uint64_t g, bool vector, const T (&x)[kGroup])
+{
+    if (vector && g + kGroup <= n) {
+        constexpr int W = int(sizeof(T)) * kGroup / 16;
+        uint4 w[W];
+        memcpy(w, x, sizeof(x));
+        uint4* q = reinterpret_cast<uint4*>(p + g);
+#pragma unroll
+        for (int i = 0; i < W; ++i) q[i] = w[i];
+    } else {
+#pragma unroll
+        for (int e = 0; e < kGroup; ++e)
+            if (g + e < n) p[g + e] = x[e];
+    }
+}
+
+/* One tile per block.  mode: kModeExclusive / kModeInclusive /
+ * kModeInclusiveInit write out[]; kModeReduce writes unique_out[],
+ * out[] (= the aggregates) and *num_runs. */
+template <typename K, typename V, bool COUNT, typename Equal, typename Op>
+__global__ void __launch_bounds__(kBlock)
+by_key_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* num_runs, uint64_t n, int mode,
+              V init, bool vector, Ctrl* ctrl, TileStatus<V> ts, Equal equal, Op op)
+{
+    __shared__ uint32_t s_tile;
+    __shared__ Acc<V> s_total[kWarps];
+    __shared__ Acc<V> s_excl[kWarps];
+    __shared__ Acc<V> s_prefix;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) s_tile = atomicAdd(&ctrl->tile_counter, 1u);
+    __syncthreads();
+    const uint64_t tile = s_tile;
+    const uint64_t warp_base = tile * kTileItems + uint64_t(warp) * (32 * kChunks * kGroup);
+
+    K k[kChunks][kGroup];
+    V v[kChunks][kGroup];
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+        const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
+        load_group(keys, n, g, vector, k[j]);
+        load_group(values, n, g, vector, v[j]);
+    }
+
+    /* head flags: bit j * kGroup + e; padding past n is a head of its own */
+    uint32_t heads = 0;
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+        const K prev_lane = __shfl_up_sync(0xffffffffu, k[j][kGroup - 1], 1);
+        const K prev_chunk = __shfl_sync(0xffffffffu, k[j > 0 ? j - 1 : 0][kGroup - 1], 31);
+        const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
+#pragma unroll
+        for (int e = 0; e < kGroup; ++e) {
+            const uint64_t i = g + e;
+            bool h;
+            if (i >= n)
+                h = true;
+            else if (e > 0)
+                h = !equal(k[j][e - 1], k[j][e]);
+            else if (lane > 0)
+                h = !equal(prev_lane, k[j][0]);
+            else if (j > 0)
+                h = !equal(prev_chunk, k[j][0]);
+            else
+                h = i == 0 || !equal(keys[i - 1], k[j][0]);
+            heads |= uint32_t(h) << (j * kGroup + e);
+        }
+    }
+
+    /* per-lane group folds, then warp scans chunk by chunk */
+    Acc<V> pre[kChunks];
+    Acc<V> carry{0, 0, V{}};
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+        Acc<V> x{(heads >> (j * kGroup)) & 1u, 1, v[j][0]};
+#pragma unroll
+        for (int e = 1; e < kGroup; ++e) {
+            if ((heads >> (j * kGroup + e)) & 1u) {
+                x.c = COUNT ? x.c + 1 : 1;
+                x.v = v[j][e];
+            } else {
+                x.v = op(x.v, v[j][e]);
+            }
+        }
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const Acc<V> y = shfl_up_acc(x, d);
+            if (lane >= d) x = seg<COUNT>(y, x, op);
+        }
+        Acc<V> ex = shfl_up_acc(x, 1);
+        if (lane == 0) ex.has = 0;
+        pre[j] = seg<COUNT>(carry, ex, op);
+        carry = seg<COUNT>(carry, shfl_acc(x, 31), op);
+    }
+    if (lane == 0) s_total[warp] = carry;
+    __syncthreads();
+
+    if (warp == 0) {
+        Acc<V> x = lane < kWarps ? s_total[lane] : Acc<V>{0, 0, V{}};
+#pragma unroll
+        for (int d = 1; d < kWarps; d <<= 1) {
+            const Acc<V> y = shfl_up_acc(x, d);
+            if (lane >= d) x = seg<COUNT>(y, x, op);
+        }
+        Acc<V> ex = shfl_up_acc(x, 1);
+        if (lane == 0) ex.has = 0;
+        if (lane < kWarps) s_excl[lane] = ex;
+        const Acc<V> aggregate = shfl_acc(x, kWarps - 1);
+        Acc<V> prefix{0, 0, V{}};
+        if (tile == 0) {
+            if (lane == 0) ts.publish(0, kInclusive, aggregate);
+        } else {
+            if (lane == 0) ts.publish(tile, kPartial, aggregate);
+            prefix = look_back<COUNT>(tile, ts, ctrl, op);
+            if (lane == 0) ts.publish(tile, kInclusive, seg<COUNT>(prefix, aggregate, op));
+        }
+        if (lane == 0) s_prefix = prefix;
+    }
+    __syncthreads();
+
+    const Acc<V> warp_prefix = seg<COUNT>(s_prefix, s_excl[warp], op);
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+        const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
+        Acc<V> E = seg<COUNT>(warp_prefix, pre[j], op);
+        V o[kGroup];
+#pragma unroll
+        for (int e = 0; e < kGroup; ++e) {
+            const uint64_t i = g + e;
+            const bool h = (heads >> (j * kGroup + e)) & 1u;
+            Acc<V> P;
+            P.has = 1;
+            if (h || !E.has) {
+                P.c = COUNT ? E.c + uint32_t(h) : uint32_t(h);
+                P.v = v[j][e];
+            } else {
+                P.c = E.c;
+                P.v = op(E.v, v[j][e]);
+            }
+            if (mode == kModeExclusive) {
+                o[e] = h ? init : op(init, E.v);
+            } else if (mode == kModeInclusive) {
+                o[e] = P.v;
+            } else if (mode == kModeInclusiveInit) {
+                o[e] = op(init, P.v);
+            } else if (i < n) {
+                if (h) {
+                    const uint32_t r = P.c - 1;
+                    unique_out[r] = k[j][e];
+                    if (r > 0) out[r - 1] = E.v;
+                }
+                if (i == n - 1) {
+                    out[P.c - 1] = P.v;
+                    *num_runs = P.c;
+                }
+            }
+            E = P;
+        }
+        if (mode != kModeReduce) store_group(out, n, g, vector, o);
+    }
+}
+
+struct Layout {
+    size_t ctrl, meta, partial, inclusive, total;
+    uint64_t tiles;
+};
+
+inline Layout layout(uint64_t n, size_t value_bytes)
+{
+    Layout L{};
+    L.tiles = n ? (n + kTileItems - 1) / kTileItems : 0;
+    auto up = [](size_t x) { return (x + kAlign - 1) / kAlign * kAlign; };
+    L.ctrl = 0;
+    L.meta = kAlign;
+    L.partial = up(L.meta + size_t(L.tiles) * 8);
+    L.inclusive = up(L.partial + size_t(L.tiles) * value_bytes);
+    L.total = up(L.inclusive + size_t(L.tiles) * value_bytes);
+    return L;
+}
+
+inline bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+template <bool COUNT, typename K, typename V, typename Equal, typename Op>
+cudaError_t launch(void* temp, size_t temp_bytes, const K* keys, const V* values, V* out, K* unique_out,
+                   uint32_t* num_runs, uint64_t n, int mode, V init, Equal equal, Op op, cudaStream_t stream)
+{
+    const Layout L = layout(n, sizeof(V));
+    if (!keys || !values || !out || !temp || reinterpret_cast<uintptr_t>(temp) % kAlign || temp_bytes < L.total)
+        return cudaErrorInvalidValue;
+    if (L.tiles > 0xffffffffull) return cudaErrorInvalidValue;
+    unsigned char* t = static_cast<unsigned char*>(temp);
+    cudaError_t e = cudaMemsetAsync(t, 0, L.meta + size_t(L.tiles) * 8, stream);
+    if (e != cudaSuccess) return e;
+    TileStatus<V> ts{reinterpret_cast<uint64_t*>(t + L.meta), reinterpret_cast<V*>(t + L.partial),
+                     reinterpret_cast<V*>(t + L.inclusive)};
+    const bool vector = aligned16(keys) && aligned16(values) && (mode == kModeReduce || aligned16(out));
+    by_key_kernel<K, V, COUNT><<<unsigned(L.tiles), kBlock, 0, stream>>>(
+        keys, values, out, unique_out, num_runs, n, mode, init, vector, reinterpret_cast<Ctrl*>(t), ts, equal, op);
+    return cudaGetLastError();
+}
+
+}  // namespace bykey_detail
+
+/* Temp storage bytes of the by-key scans and ReduceByKey (any key type). */
+inline size_t by_key_temp_bytes(uint64_t num_items, size_t value_bytes)
+{
+    return num_items ? bykey_detail::layout(num_items, value_bytes).total : 0;
+}
+
+/* mode: 0 exclusive (init), 1 inclusive, 2 inclusive with init.  Values may
+ * be scanned in place (d_values_out == d_values_in).  No items: nothing. */
+template <typename K, typename V, typename Op, typename Equal = EqualTo>
+cudaError_t scan_by_key(void* temp, size_t temp_bytes, const K* d_keys_in, const V* d_values_in, V* d_values_out,
+                        uint64_t num_items, int mode, V init, Op op, Equal equal = Equal{}, cudaStream_t stream = 0)
+{
+    static_assert(sizeof(K) == 4 || sizeof(K) == 8, "keys: 4- or 8-byte types");
+    static_assert(sizeof(V) == 4 || sizeof(V) == 8, "values: 4- or 8-byte types");
+    if (mode < 0 || mode > 2) return cudaErrorInvalidValue;
+    if (num_items == 0) return cudaSuccess;
+    return bykey_detail::launch<false>(temp, temp_bytes, d_keys_in, d_values_in, d_values_out,
+                                       static_cast<K*>(nullptr), nullptr, num_items, mode, init, equal, op, stream);
+}
+
+/* ReduceByKey; num_items < 2^32 (the run count is a uint32, as the
+ * reference's); d_unique_out must not overlap d_keys_in.  No items: writes
+ * *d_num_runs_out = 0. */
+template <typename K, typename V, typename Op, typename Equal = EqualTo>
+cudaError_t reduce_by_key(void* temp, size_t temp_bytes, const K* d_keys_in, const V* d_values_in, K* d_unique_out,
+                          V* d_aggregates_out, uint32_t* d_num_runs_out, uint64_t num_items, Op op,
+                          Equal equal = Equal{}, cudaStream_t stream = 0)
+{
+    static_assert(sizeof(K) == 4 || sizeof(K) == 8, "keys: 4- or 8-byte types");
+    static_assert(sizeof(V) == 4 || sizeof(V) == 8, "values: 4- or 8-byte types");
+    if (!d_num_runs_out || num_items > 0xffffffffull) return cudaErrorInvalidValue;
+    if (num_items == 0) return cudaMemsetAsync(d_num_runs_out, 0, sizeof(uint32_t), stream);
+    if (!d_unique_out || static_cast<const void*>(d_unique_out) == static_cast<const void*>(d_keys_in))
+        return cudaErrorInvalidValue;
+    return bykey_detail::launch<true>(temp, temp_bytes, d_keys_in, d_values_in, d_aggregates_out, d_unique_out,
+                                      d_num_runs_out, num_items, bykey_detail::kModeReduce, V{}, equal, op, stream);
+}
+
 }  // namespace device
 }  // namespace lcpp_b200
 

@@ -33,7 +33,8 @@ NVCC_FLAGS = [
 def _needs_rebuild(obj: Path, src: Path) -> bool:
     if not obj.exists():
         return True
-    deps = [src, *CSRC.glob("*.cuh"), *(PKG.parent / "include").glob("*.h"), Path(__file__)]
+    deps = [src, *CSRC.glob("*.cuh"), *(PKG.parent / "include").glob("*.h"), *(PKG.parent / "include").glob("*.cuh"),
+            Path(__file__)]
     return any(d.stat().st_mtime > obj.stat().st_mtime for d in deps)
 
 

@@ -35,6 +35,7 @@ GEN_F32_NORMAL, GEN_U32_ZIPF = 8, 9
 KERNEL_SORT_HISTOGRAM, KERNEL_SORT_ONESWEEP, KERNEL_SCAN, KERNEL_REDUCE, KERNEL_SEGMENT_BLOCK = 0, 1, 2, 3, 4
 KERNEL_MERGE = 5
 KERNEL_ARG_REDUCE = 6
+KERNEL_BY_KEY = 7
 
 _lib = None
 
@@ -97,6 +98,14 @@ def lib() -> ctypes.CDLL:
         "lcpp_scan_inclusive_sum_noalloc": ([vp, vp, u64, i, vp], i),
         "lcpp_reduce_temp_bytes": ([i, u64, szp], i),
         "lcpp_reduce_arg_temp_bytes": ([i, u64, szp], i),
+        "lcpp_scan_by_key_temp_bytes": ([i, i, u64, szp], i),
+        "lcpp_scan_exclusive_by_key": ([vp, sz, vp, vp, vp, u64, i, vp, i, i, vp], i),
+        "lcpp_scan_inclusive_by_key": ([vp, sz, vp, vp, vp, u64, i, i, i, vp], i),
+        "lcpp_scan_inclusive_by_key_init": ([vp, sz, vp, vp, vp, u64, i, vp, i, i, vp], i),
+        "lcpp_scan_exclusive_sum_by_key": ([vp, sz, vp, vp, vp, u64, i, i, vp], i),
+        "lcpp_scan_inclusive_sum_by_key": ([vp, sz, vp, vp, vp, u64, i, i, vp], i),
+        "lcpp_reduce_by_key_temp_bytes": ([i, i, u64, szp], i),
+        "lcpp_reduce_by_key": ([vp, sz, vp, vp, vp, vp, vp, u64, i, i, i, vp], i),
         "lcpp_reduce_argmin": ([vp, sz, vp, vp, vp, u64, i, vp], i),
         "lcpp_reduce_argmax": ([vp, sz, vp, vp, vp, u64, i, vp], i),
         "lcpp_reduce": ([vp, sz, vp, vp, u64, i, vp, i, vp], i),
@@ -484,6 +493,50 @@ class DeviceScan:
                                              _stream(stream)), "InclusiveScanInit")
         del keep
 
+    # ---- by key (device_scan.h:310-597): argument order as the reference's
+    @staticmethod
+    def GetScanByKeyTempStorageBytes(key_dtype: int, value_dtype: int, num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_scan_by_key_temp_bytes(key_dtype, value_dtype, num_items, ctypes.byref(out)),
+              "GetScanByKeyTempStorageBytes")
+        return out.value
+
+    def ExclusiveScanByKey(self, temp, d_keys_in, d_values_in, d_values_out, scan_op, num_items, initial_value,
+                           stream=None):
+        vc = dtype_code(d_values_in)
+        keep, init = _host_scalar(initial_value, vc)
+        check(lib().lcpp_scan_exclusive_by_key(_ptr(temp), temp.numel() if temp is not None else 0,
+                                               _ptr(d_keys_in), _ptr(d_values_in), _ptr(d_values_out), num_items,
+                                               scan_op, init, dtype_code(d_keys_in), vc, _stream(stream)),
+              "ExclusiveScanByKey")
+        del keep
+
+    def InclusiveScanByKey(self, temp, d_keys_in, d_values_in, d_values_out, scan_op, num_items,
+                           initial_value=None, stream=None):
+        vc = dtype_code(d_values_in)
+        t = (_ptr(temp), temp.numel() if temp is not None else 0, _ptr(d_keys_in), _ptr(d_values_in),
+             _ptr(d_values_out), num_items, scan_op)
+        if initial_value is None:
+            check(lib().lcpp_scan_inclusive_by_key(*t, dtype_code(d_keys_in), vc, _stream(stream)),
+                  "InclusiveScanByKey")
+        else:
+            keep, init = _host_scalar(initial_value, vc)
+            check(lib().lcpp_scan_inclusive_by_key_init(*t, init, dtype_code(d_keys_in), vc, _stream(stream)),
+                  "InclusiveScanByKey")
+            del keep
+
+    def ExclusiveSumByKey(self, temp, d_keys_in, d_values_in, d_values_out, num_items, stream=None):
+        check(lib().lcpp_scan_exclusive_sum_by_key(_ptr(temp), temp.numel() if temp is not None else 0,
+                                                   _ptr(d_keys_in), _ptr(d_values_in), _ptr(d_values_out),
+                                                   num_items, dtype_code(d_keys_in), dtype_code(d_values_in),
+                                                   _stream(stream)), "ExclusiveSumByKey")
+
+    def InclusiveSumByKey(self, temp, d_keys_in, d_values_in, d_values_out, num_items, stream=None):
+        check(lib().lcpp_scan_inclusive_sum_by_key(_ptr(temp), temp.numel() if temp is not None else 0,
+                                                   _ptr(d_keys_in), _ptr(d_values_in), _ptr(d_values_out),
+                                                   num_items, dtype_code(d_keys_in), dtype_code(d_values_in),
+                                                   _stream(stream)), "InclusiveSumByKey")
+
 
 class DeviceReduce:
     """Mirror of lcpp::DeviceReduce (src/lcpp/device/device_reduce.h:102-1187)."""
@@ -504,6 +557,22 @@ class DeviceReduce:
     def _named(self, fn, temp, d_in, d_out, num_items, stream, what):
         check(fn(_ptr(temp), temp.numel() if temp is not None else 0, _ptr(d_in), _ptr(d_out),
                  num_items, dtype_code(d_out), _stream(stream)), what)
+
+    @staticmethod
+    def GetReduceByKeyTempStorageBytes(key_dtype: int, value_dtype: int, num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_reduce_by_key_temp_bytes(key_dtype, value_dtype, num_items, ctypes.byref(out)),
+              "GetReduceByKeyTempStorageBytes")
+        return out.value
+
+    def ReduceByKey(self, temp, d_keys_in, d_values_in, d_unique_out, d_aggregates_out, d_num_runs_out,
+                    reduce_op, num_elements, stream=None):
+        """device_reduce.h:437-491 (argument order as the reference's);
+        d_num_runs_out: a one-element 4-byte tensor (uint32 run count)."""
+        check(lib().lcpp_reduce_by_key(_ptr(temp), temp.numel() if temp is not None else 0, _ptr(d_keys_in),
+                                       _ptr(d_values_in), _ptr(d_unique_out), _ptr(d_aggregates_out),
+                                       _ptr(d_num_runs_out), num_elements, reduce_op, dtype_code(d_keys_in),
+                                       dtype_code(d_values_in), _stream(stream)), "ReduceByKey")
 
     @staticmethod
     def GetArgTempStorageBytes(dtype: int, num_items: int) -> int:

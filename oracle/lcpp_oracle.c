@@ -416,6 +416,131 @@ int oracle_arg_extremum(const void* vin, void* vout, uint32_t* index_out, uint64
     }
 }
 
+/* Scans and reductions by key (src/lcpp/device/device_scan.h:425-597,
+ * src/lcpp/device/device_reduce.h:437-491), sequentially: a segment (run) is
+ * a maximal stretch of consecutive items whose keys compare equal with ==
+ * at the key's type (BlockDiscontinuity::FlagHeads with `a != b`,
+ * details/reduce_by_key.h).  Integer sums wrap (computed unsigned). */
+static void key_heads(const void* keys, int kdt, uint64_t n, uint8_t* heads)
+{
+    for (uint64_t i = 0; i < n; ++i) {
+        int h = i == 0;
+        if (!h) {
+            switch (kdt) {
+            case DT_U32: case DT_I32: h = ((const uint32_t*)keys)[i] != ((const uint32_t*)keys)[i - 1]; break;
+            case DT_U64: case DT_I64: h = ((const uint64_t*)keys)[i] != ((const uint64_t*)keys)[i - 1]; break;
+            case DT_F32: h = ((const float*)keys)[i] != ((const float*)keys)[i - 1]; break;
+            default: h = ((const double*)keys)[i] != ((const double*)keys)[i - 1]; break;
+            }
+        }
+        heads[i] = (uint8_t)h;
+    }
+}
+
+/* mode 0: exclusive with init, 1: inclusive, 2: inclusive with init */
+#define SBK_BODY(T, ACC_T, COMBINE)                                                   \
+    do {                                                                              \
+        const T* in = (const T*)vin;                                                  \
+        T* out = (T*)vout;                                                            \
+        const ACC_T init = init_p ? (ACC_T)(*(const T*)init_p) : (ACC_T)0;            \
+        ACC_T run = 0;                                                                \
+        for (uint64_t i = 0; i < n; ++i) {                                            \
+            const ACC_T x = (ACC_T)in[i];                                             \
+            if (mode == 0) {                                                          \
+                if (heads[i]) { out[i] = (T)init; run = x; }                          \
+                else { out[i] = (T)COMBINE(init, run); run = COMBINE(run, x); }       \
+            } else {                                                                  \
+                run = heads[i] ? x : COMBINE(run, x);                                 \
+                out[i] = (T)(mode == 2 ? COMBINE(init, run) : run);                   \
+            }                                                                         \
+        }                                                                             \
+    } while (0)
+
+#define BY_VALUE_TYPE(BODY)                                                           \
+    switch (vdt) {                                                                    \
+    case DT_I32:                                                                      \
+        if (op == OP_SUM) BODY(uint32_t, uint32_t, C_SUM);                            \
+        else if (op == OP_MIN) BODY(int32_t, int32_t, C_MIN);                         \
+        else BODY(int32_t, int32_t, C_MAX);                                           \
+        break;                                                                        \
+    case DT_U32:                                                                      \
+        if (op == OP_SUM) BODY(uint32_t, uint32_t, C_SUM);                            \
+        else if (op == OP_MIN) BODY(uint32_t, uint32_t, C_MIN);                       \
+        else BODY(uint32_t, uint32_t, C_MAX);                                         \
+        break;                                                                        \
+    case DT_I64:                                                                      \
+        if (op == OP_SUM) BODY(uint64_t, uint64_t, C_SUM);                            \
+        else if (op == OP_MIN) BODY(int64_t, int64_t, C_MIN);                         \
+        else BODY(int64_t, int64_t, C_MAX);                                           \
+        break;                                                                        \
+    case DT_U64:                                                                      \
+        if (op == OP_SUM) BODY(uint64_t, uint64_t, C_SUM);                            \
+        else if (op == OP_MIN) BODY(uint64_t, uint64_t, C_MIN);                       \
+        else BODY(uint64_t, uint64_t, C_MAX);                                         \
+        break;                                                                        \
+    case DT_F32:                                                                      \
+        if (op == OP_SUM) BODY(float, float, C_SUM);                                  \
+        else if (op == OP_MIN) BODY(float, float, C_MIN);                             \
+        else BODY(float, float, C_MAX);                                               \
+        break;                                                                        \
+    default:                                                                          \
+        if (op == OP_SUM) BODY(double, double, C_SUM);                                \
+        else if (op == OP_MIN) BODY(double, double, C_MIN);                           \
+        else BODY(double, double, C_MAX);                                             \
+        break;                                                                        \
+    }
+
+int oracle_scan_by_key(const void* keys, const void* vin, void* vout, uint64_t n, int kdt, int vdt, int op,
+                       int mode, const void* init_p)
+{
+    if (kdt < 0 || kdt > 5 || vdt < 0 || vdt > 5 || op < 0 || op > 2 || mode < 0 || mode > 2) return -1;
+    if (mode != 1 && !init_p) return -1;
+    if (n == 0) return 0;
+    uint8_t* heads = (uint8_t*)malloc(n);
+    if (!heads) return -2;
+    key_heads(keys, kdt, n, heads);
+    BY_VALUE_TYPE(SBK_BODY)
+    free(heads);
+    return 0;
+}
+
+#define RBK_BODY(T, ACC_T, COMBINE)                                                   \
+    do {                                                                              \
+        const T* in = (const T*)vin;                                                  \
+        T* agg = (T*)vagg;                                                            \
+        ACC_T run = 0;                                                                \
+        uint64_t r = 0;                                                               \
+        for (uint64_t i = 0; i < n; ++i) {                                            \
+            const ACC_T x = (ACC_T)in[i];                                             \
+            if (heads[i]) {                                                           \
+                if (i > 0) agg[r++] = (T)run;                                         \
+                memcpy((unsigned char*)unique_out + r * kb, (const unsigned char*)keys + i * kb, kb); \
+                run = x;                                                              \
+            } else {                                                                  \
+                run = COMBINE(run, x);                                                \
+            }                                                                         \
+        }                                                                             \
+        agg[r++] = (T)run;                                                            \
+        *num_runs = (uint32_t)r;                                                      \
+    } while (0)
+
+int oracle_reduce_by_key(const void* keys, const void* vin, void* unique_out, void* vagg, uint32_t* num_runs,
+                         uint64_t n, int kdt, int vdt, int op)
+{
+    if (kdt < 0 || kdt > 5 || vdt < 0 || vdt > 5 || op < 0 || op > 2 || !num_runs) return -1;
+    if (n == 0) {
+        *num_runs = 0;
+        return 0;
+    }
+    const size_t kb = (kdt == DT_U32 || kdt == DT_I32 || kdt == DT_F32) ? 4 : 8;
+    uint8_t* heads = (uint8_t*)malloc(n);
+    if (!heads) return -2;
+    key_heads(keys, kdt, n, heads);
+    BY_VALUE_TYPE(RBK_BODY)
+    free(heads);
+    return 0;
+}
+
 /* fp64 sum of a float32 or float64 array: the reference value for the float
  * reduce tolerance 1e-6 * log2(n) (relative). */
 double oracle_sum_f64(const void* vin, uint64_t n, int dtype)

@@ -68,6 +68,10 @@ def lib() -> ctypes.CDLL:
         l.oracle_reduce.restype = i
         l.oracle_arg_extremum.argtypes = [vp, vp, vp, u64, i, i]
         l.oracle_arg_extremum.restype = i
+        l.oracle_scan_by_key.argtypes = [vp, vp, vp, u64, i, i, i, i, vp]
+        l.oracle_scan_by_key.restype = i
+        l.oracle_reduce_by_key.argtypes = [vp, vp, vp, vp, vp, u64, i, i, i]
+        l.oracle_reduce_by_key.restype = i
         l.oracle_sum_f64.argtypes = [vp, u64, i]
         l.oracle_sum_f64.restype = ctypes.c_double
         l.oracle_generate.argtypes = [vp, u64, u64, u64, i]
@@ -159,6 +163,51 @@ def arg_extremum_compare(x, is_min: bool, compare):
         if (compare(c, best) if is_min else compare(best, c)):
             best, bi = c, i
     return best, bi
+
+
+def scan_by_key(keys: np.ndarray, values: np.ndarray, mode: str, op: int = OP_SUM, init=None) -> np.ndarray:
+    """ExclusiveScanByKey / InclusiveScanByKey (lcpp_oracle.c: oracle_scan_by_key,
+    after src/lcpp/device/device_scan.h:425-597).  mode: 'exclusive' (needs
+    init), 'inclusive', 'inclusive_init' (needs init)."""
+    keys, values = np.ascontiguousarray(keys), np.ascontiguousarray(values)
+    out = np.empty_like(values)
+    m = {"exclusive": 0, "inclusive": 1, "inclusive_init": 2}[mode]
+    init_arr = None if init is None else np.array([init], dtype=values.dtype)
+    rc = lib().oracle_scan_by_key(_ptr(keys), _ptr(values), _ptr(out), keys.size, NP_TO_DTYPE[keys.dtype],
+                                  NP_TO_DTYPE[values.dtype], op, m, _ptr(init_arr))
+    if rc != 0:
+        raise ValueError(f"oracle_scan_by_key failed with {rc}")
+    return out
+
+
+def reduce_by_key(keys: np.ndarray, values: np.ndarray, op: int = OP_SUM):
+    """ReduceByKey (lcpp_oracle.c: oracle_reduce_by_key, after
+    src/lcpp/device/device_reduce.h:437-491) -> (unique keys, aggregates)."""
+    keys, values = np.ascontiguousarray(keys), np.ascontiguousarray(values)
+    uniq = np.empty_like(keys)
+    agg = np.empty_like(values)
+    runs = np.zeros(1, np.uint32)
+    rc = lib().oracle_reduce_by_key(_ptr(keys), _ptr(values), _ptr(uniq), _ptr(agg), _ptr(runs), keys.size,
+                                    NP_TO_DTYPE[keys.dtype], NP_TO_DTYPE[values.dtype], op)
+    if rc != 0:
+        raise ValueError(f"oracle_reduce_by_key failed with {rc}")
+    r = int(runs[0])
+    return uniq[:r], agg[:r]
+
+
+def scan_by_key_equal(keys, values, mode: str, equal, op=lambda a, b: a + b, init=None):
+    """The by-key scans with a user key-equality (the reference's EqualityOp
+    overloads, device_scan.h:441-519); pure Python, small inputs only."""
+    out, run = [], None
+    for i, (k, v) in enumerate(zip(keys, values)):
+        head = i == 0 or not equal(keys[i - 1], k)
+        if mode == "exclusive":
+            out.append(init if head else op(init, run))
+            run = v if head else op(run, v)
+        else:
+            run = v if head else op(run, v)
+            out.append(op(init, run) if mode == "inclusive_init" else run)
+    return out
 
 
 def sum_f64(x: np.ndarray) -> float:

@@ -237,6 +237,80 @@ void arg_reductions(lcpp_stream_t s)
     }
 }
 
+void by_key(lcpp_stream_t s)
+{
+    // device_scan_test.cpp:324-380: ExclusiveSumByKey over ones, keys i / 100
+    for (int k : {5, 12, 20}) {
+        const size_t n = size_t(1) << k;
+        std::vector<int32_t> keys(n), ones(n, 1), expect(n);
+        for (size_t i = 0; i < n; ++i) {
+            keys[i] = int32_t(i / 100);
+            expect[i] = int32_t(i % 100);
+        }
+        DeviceArray<int32_t> dk(n), dv(n), out(n);
+        dk.upload(keys);
+        dv.upload(ones);
+        auto temp = temp_for(DeviceScan::GetScanByKeyTempStorageBytes<int32_t, int32_t>(n));
+        DeviceScan sc;
+        sc.ExclusiveSumByKey(s, temp.view(), dk.view(), dv.view(), out.view(), n);
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(out.download() == expect);
+    }
+    // :382-417: int keys, int64 values, segments cut one past each 1024-item tile
+    {
+        const size_t tile = 1024, n = tile * 2 + 2;
+        std::vector<int32_t> keys(n);
+        std::vector<int64_t> ones(n, 1), expect(n);
+        int64_t run = 0;
+        for (size_t i = 0; i < n; ++i) {
+            keys[i] = i < tile + 1 ? 1 : i < tile * 2 + 1 ? 2 : 3;
+            if (i == 0 || keys[i] != keys[i - 1]) run = 0;
+            expect[i] = ++run;
+        }
+        DeviceArray<int32_t> dk(n);
+        DeviceArray<int64_t> dv(n), out(n);
+        dk.upload(keys);
+        dv.upload(ones);
+        auto temp = temp_for(DeviceScan::GetScanByKeyTempStorageBytes<int32_t, int64_t>(n));
+        DeviceScan sc;
+        sc.InclusiveSumByKey(s, temp.view(), dk.view(), dv.view(), out.view(), n);
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(out.download() == expect);
+    }
+    // device_reduce_test.cpp:422-513: ReduceByKey Sum by key i / 100; empty input
+    {
+        const int n = 1 << 12;
+        std::vector<int32_t> keys(n), data(n);
+        for (int i = 0; i < n; ++i) {
+            keys[i] = i / 100;
+            data[i] = i;
+        }
+        std::mt19937 rng(114521);
+        std::shuffle(data.begin(), data.end(), rng);
+        const int runs = (n + 99) / 100;
+        DeviceArray<int32_t> dk(n), dv(n), uniq(runs), agg(runs);
+        DeviceArray<uint32_t> nruns(1);
+        dk.upload(keys);
+        dv.upload(data);
+        auto temp = temp_for(DeviceReduce::GetReduceByKeyTempStorageBytes<int32_t, int32_t>(n));
+        DeviceReduce rd;
+        rd.ReduceByKey(s, temp.view(), dk.view(), dv.view(), uniq.view(), agg.view(), nruns.view(), SumOp{},
+                       uint64_t(n));
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(nruns.download()[0] == uint32_t(runs));
+        const auto u = uniq.download(), a = agg.download();
+        for (int r = 0; r < runs; ++r) {
+            CHECK(u[r] == r);
+            CHECK(a[r] == std::accumulate(data.begin() + r * 100, data.begin() + std::min(r * 100 + 100, n), 0));
+        }
+        nruns.upload({17u});
+        rd.ReduceByKey(s, BufferView<uint32_t>{}, dk.view(), dv.view(), uniq.view(), agg.view(), nruns.view(),
+                       SumOp{}, 0);
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(nruns.download()[0] == 0u);
+    }
+}
+
 void reductions(lcpp_stream_t s)
 {
     // device_reduce_test.cpp: ones at 2^k + 1; float max identity on empty input
@@ -386,6 +460,7 @@ int main()
     scans(s);
     reductions(s);
     arg_reductions(s);
+    by_key(s);
     segmented(s);
     decomposed(s);
     misuse_throws(s);

@@ -1,4 +1,6 @@
-// CUDA caller of the comparator overloads of DeviceReduce::ArgMin / ArgMax
+// CUDA caller of the overloads that take a user callable -- the comparator
+// forms of DeviceReduce::ArgMin / ArgMax, the by-key scans with a key
+// equality and custom operators, ReduceByKey with a custom operator
 // (include/lcpp_b200.hpp with nvcc, kernels from lcpp_b200_device.cuh),
 // written like the reference's tests/device_reduce_test.cpp:290-345: device
 // results against the reference's sequential comparator fold
@@ -154,6 +156,112 @@ void random_cases(lcpp_stream_t s)
 #endif
 }
 
+struct SameParity {
+    __host__ __device__ bool operator()(int a, int b) const { return (a & 1) == (b & 1); }
+};
+
+// a non-commutative associative operator: affine maps x -> a*x + b packed as
+// (a, b) in the two halves of a uint64 (mod 2^32); (f then g)(x) = g(f(x))
+struct Compose {
+    __host__ __device__ uint64_t operator()(uint64_t f, uint64_t g) const
+    {
+        const uint32_t fa = uint32_t(f >> 32), fb = uint32_t(f), ga = uint32_t(g >> 32), gb = uint32_t(g);
+        return (uint64_t(ga * fa) << 32) | uint32_t(ga * fb + gb);
+    }
+};
+
+template <typename K, typename V, typename Op, typename Eq>
+std::vector<V> host_scan_by_key(const std::vector<K>& k, const std::vector<V>& v, int mode, V init, Op op, Eq eq)
+{
+    std::vector<V> out(v.size());
+    V run{};
+    for (size_t i = 0; i < v.size(); ++i) {
+        const bool head = i == 0 || !eq(k[i - 1], k[i]);
+        if (mode == 0) {
+            out[i] = head ? init : op(init, run);
+            run = head ? v[i] : op(run, v[i]);
+        } else {
+            run = head ? v[i] : op(run, v[i]);
+            out[i] = mode == 2 ? op(init, run) : run;
+        }
+    }
+    return out;
+}
+
+void by_key_cases(lcpp_stream_t s)
+{
+    // device_scan_test.cpp:419-446: keys {1, 3, 5, 2, 4} under "same parity"
+    {
+        const std::vector<int> keys{1, 3, 5, 2, 4}, ones(5, 1);
+        DeviceArray<int> dk(5), dv(5), out(5);
+        dk.upload(keys);
+        dv.upload(ones);
+        auto temp = temp_for(DeviceScan::GetScanByKeyTempStorageBytes<int, int>(5));
+        DeviceScan sc;
+        sc.InclusiveSumByKey(s, temp.view(), dk.view(), dv.view(), out.view(), 5, SameParity{});
+        CUDA(cudaStreamSynchronize(s));
+        std::vector<int> got(5);
+        CUDA(cudaMemcpy(got.data(), out.p, 5 * sizeof(int), cudaMemcpyDeviceToHost));
+        CHECK((got == std::vector<int>{1, 2, 3, 1, 2}));
+    }
+    // random keys, parity equality, and a non-commutative operator
+    std::mt19937 rng(7);
+    for (size_t n : {size_t(1), size_t(4097), size_t(1000003)}) {
+        std::vector<int> keys(n);
+        std::vector<uint64_t> maps(n);
+        for (size_t i = 0; i < n; ++i) {
+            keys[i] = int(rng() % 5) * (rng() % 50 == 0 ? 1 : 2);  // mostly even: long parity runs
+            maps[i] = (uint64_t(rng() | 1u) << 32) | rng();
+        }
+        DeviceArray<int> dk(n);
+        DeviceArray<uint64_t> dv(n), out(n);
+        dk.upload(keys);
+        dv.upload(maps);
+        auto temp = temp_for(DeviceScan::GetScanByKeyTempStorageBytes<int, uint64_t>(n));
+        DeviceScan sc;
+        const uint64_t ident_shift = (uint64_t(1) << 32) | 5u;  // x -> x + 5
+        std::vector<uint64_t> got(n);
+        for (int mode = 0; mode < 3; ++mode) {
+            if (mode == 0)
+                sc.ExclusiveScanByKey(s, temp.view(), dk.view(), dv.view(), out.view(), Compose{}, n, ident_shift,
+                                      SameParity{});
+            else if (mode == 1)
+                sc.InclusiveScanByKey(s, temp.view(), dk.view(), dv.view(), out.view(), Compose{}, n, SameParity{});
+            else
+                sc.InclusiveScanByKey(s, temp.view(), dk.view(), dv.view(), out.view(), Compose{}, n, ident_shift,
+                                      SameParity{});
+            CUDA(cudaStreamSynchronize(s));
+            CUDA(cudaMemcpy(got.data(), out.p, n * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+            CHECK(got == host_scan_by_key(keys, maps, mode, ident_shift, Compose{}, SameParity{}));
+        }
+        // ReduceByKey with the non-commutative operator (== on keys)
+        DeviceArray<int> uniq(n);
+        DeviceArray<uint64_t> agg(n);
+        DeviceArray<uint32_t> runs(1);
+        auto rtemp = temp_for(DeviceReduce::GetReduceByKeyTempStorageBytes<int, uint64_t>(n));
+        DeviceReduce rd;
+        rd.ReduceByKey(s, rtemp.view(), dk.view(), dv.view(), uniq.view(), agg.view(), runs.view(), Compose{}, n);
+        CUDA(cudaStreamSynchronize(s));
+        std::vector<int> wu;
+        std::vector<uint64_t> wa;
+        for (size_t i = 0; i < n; ++i) {
+            if (i == 0 || keys[i] != keys[i - 1]) {
+                wu.push_back(keys[i]);
+                wa.push_back(maps[i]);
+            } else {
+                wa.back() = Compose{}(wa.back(), maps[i]);
+            }
+        }
+        CHECK(runs.first() == uint32_t(wu.size()));
+        std::vector<int> gu(wu.size());
+        std::vector<uint64_t> ga(wa.size());
+        CUDA(cudaMemcpy(gu.data(), uniq.p, gu.size() * sizeof(int), cudaMemcpyDeviceToHost));
+        CUDA(cudaMemcpy(ga.data(), agg.p, ga.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+        CHECK(gu == wu);
+        CHECK(ga == wa);
+    }
+}
+
 }  // namespace
 
 int main()
@@ -164,6 +272,7 @@ int main()
     reference_case(s);
     empty_sentinels(s);
     random_cases(s);
+    by_key_cases(s);
     CUDA(cudaStreamDestroy(stream));
     std::printf("OK %d\n", g_checks);
     return 0;

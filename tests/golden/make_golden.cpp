@@ -32,6 +32,7 @@ template <> const char* dtype_name<uint32_t>() { return "u32"; }
 template <> const char* dtype_name<int32_t>() { return "i32"; }
 template <> const char* dtype_name<float>() { return "f32"; }
 template <> const char* dtype_name<uint64_t>() { return "u64"; }
+template <> const char* dtype_name<int64_t>() { return "i64"; }
 
 template <typename T>
 static void emit(const std::string& name, const std::vector<T>& v)
@@ -245,6 +246,53 @@ static void arg_cases()
                                                   int32_t(dmx - digits.begin())});
 }
 
+// tests/device_scan_test.cpp:324-380 -- ExclusiveSumByKey over ones with
+// keys i / 100 (one size of the reference's 2^5..2^23 loop: 2^12); expected
+// = std::exclusive_scan per segment.  :382-417 -- InclusiveSumByKey of int64
+// ones over int keys 1 | 2 | 3 split at one item past each of the
+// reference's 1024-item tiles (2050 items); expected = the running count in
+// each segment.  :419-446 -- keys {1, 3, 5, 2, 4} under "same parity"
+// equality: InclusiveSumByKey of ones = {1, 2, 3, 1, 2}.
+// tests/device_reduce_test.cpp:422-483 -- ReduceByKey (Sum) of the shuffled
+// 0..4095 of reduce_cases over keys i / 100; expected = per-segment sums.
+static void by_key_cases()
+{
+    const int n = 1 << 12, per = 100;
+    std::vector<int32_t> keys(n), ones(n, 1), excl(n);
+    for (int i = 0; i < n; ++i) keys[i] = i / per;
+    for (int s0 = 0; s0 < n; s0 += per)
+        std::exclusive_scan(ones.begin() + s0, ones.begin() + std::min(s0 + per, n), excl.begin() + s0, 0);
+    emit("sbk_segment_keys", keys);
+    emit("sbk_exclusive_sum_out", excl);
+
+    const size_t tile = 256 * 4, m = tile * 2 + 2;
+    std::vector<int32_t> k3(m);
+    std::vector<int64_t> incl(m);
+    int64_t run = 0;
+    for (size_t i = 0; i < m; ++i) {
+        k3[i] = i < tile + 1 ? 1 : i < tile * 2 + 1 ? 2 : 3;
+        if (i == 0 || k3[i] != k3[i - 1]) run = 0;
+        incl[i] = ++run;
+    }
+    emit("sbk_three_tiles_keys", k3);
+    emit("sbk_three_tiles_inclusive_out", incl);
+
+    emit("sbk_parity_keys", std::vector<int32_t>{1, 3, 5, 2, 4});
+    emit("sbk_parity_inclusive_out", std::vector<int32_t>{1, 2, 3, 1, 2});
+
+    std::vector<int32_t> data(n);
+    for (int i = 0; i < n; ++i) data[i] = i;
+    std::mt19937 rng(114521);
+    std::shuffle(data.begin(), data.end(), rng);
+    std::vector<int32_t> uniq, agg;
+    for (int s0 = 0; s0 < n; s0 += per) {
+        uniq.push_back(keys[s0]);
+        agg.push_back(std::accumulate(data.begin() + s0, data.begin() + std::min(s0 + per, n), 0));
+    }
+    emit("rbk_unique_out", uniq);
+    emit("rbk_aggregates_out", agg);
+}
+
 // tests/device_segmented_sort_test.cpp:22-56 and :260-268 -- 19 items in
 // segments [1,4) [5,5) [5,9) [10,19); keys outside every segment are -777
 // and their values UINT_MAX; expected = std::stable_sort per segment with
@@ -333,6 +381,7 @@ int main(int argc, char** argv)
     scan_cases();
     reduce_cases();
     arg_cases();
+    by_key_cases();
     segmented_cases();
     decomposed_cases();
     std::fclose(g_index);

@@ -218,6 +218,53 @@ def test_arg_extremum_vs_numpy(oracle, dtype):
     assert oracle.arg_extremum_compare(y, False, lambda a, b: a < b) == oracle.arg_extremum(y, False)
 
 
+def test_scan_by_key_golden(oracle, golden):
+    """device_scan_test.cpp:324-446: ExclusiveSumByKey over ones, keys i/100;
+    InclusiveSumByKey of int64 ones across three tiles; parity key equality."""
+    keys = golden["sbk_segment_keys"]
+    ones = np.ones(keys.size, np.int32)
+    np.testing.assert_array_equal(oracle.scan_by_key(keys, ones, "exclusive", oracle.OP_SUM, 0),
+                                  golden["sbk_exclusive_sum_out"])
+    k3 = golden["sbk_three_tiles_keys"]
+    np.testing.assert_array_equal(oracle.scan_by_key(k3, np.ones(k3.size, np.int64), "inclusive"),
+                                  golden["sbk_three_tiles_inclusive_out"])
+    pk = golden["sbk_parity_keys"].tolist()
+    assert oracle.scan_by_key_equal(pk, [1] * len(pk), "inclusive",
+                                    lambda a, b: (a & 1) == (b & 1)) == golden["sbk_parity_inclusive_out"].tolist()
+
+
+def test_reduce_by_key_golden(oracle, golden):
+    """device_reduce_test.cpp:422-513: Sum by key i/100 of the shuffled 0..4095; empty input."""
+    keys, vals = golden["sbk_segment_keys"], golden["reduce_shuffled_in"]
+    uniq, agg = oracle.reduce_by_key(keys, vals, oracle.OP_SUM)
+    np.testing.assert_array_equal(uniq, golden["rbk_unique_out"])
+    np.testing.assert_array_equal(agg, golden["rbk_aggregates_out"])
+    u, a = oracle.reduce_by_key(np.zeros(0, np.int32), np.zeros(0, np.int32))
+    assert u.size == 0 and a.size == 0
+
+
+@pytest.mark.parametrize("kdt,vdt", [(np.int32, np.int64), (np.float32, np.float64), (np.uint64, np.int32)])
+def test_by_key_vs_numpy(oracle, kdt, vdt):
+    """The C restatement against a numpy one (split at key changes)."""
+    rng = np.random.default_rng(3)
+    keys = rng.integers(0, 4, size=5000).astype(kdt)
+    vals = rng.integers(-100, 100, size=5000).astype(vdt)
+    cuts = np.flatnonzero(keys[1:] != keys[:-1]) + 1
+    segs = np.split(vals, cuts)
+    np.testing.assert_array_equal(oracle.scan_by_key(keys, vals, "inclusive"),
+                                  np.concatenate([np.cumsum(x, dtype=vdt) for x in segs]))
+    np.testing.assert_array_equal(oracle.scan_by_key(keys, vals, "inclusive", oracle.OP_MAX),
+                                  np.concatenate([np.maximum.accumulate(x) for x in segs]))
+    ex = oracle.scan_by_key(keys, vals, "exclusive", oracle.OP_SUM, 7)
+    np.testing.assert_array_equal(ex, np.concatenate([7 + np.concatenate([[0], np.cumsum(x)[:-1]]).astype(vdt)
+                                                      for x in segs]))
+    ii = oracle.scan_by_key(keys, vals, "inclusive_init", oracle.OP_MIN, 5)
+    np.testing.assert_array_equal(ii, np.concatenate([np.minimum(5, np.minimum.accumulate(x)) for x in segs]))
+    uniq, agg = oracle.reduce_by_key(keys, vals, oracle.OP_SUM)
+    np.testing.assert_array_equal(uniq, keys[np.concatenate([[0], cuts])])
+    np.testing.assert_array_equal(agg, np.array([x.sum() for x in segs], dtype=vdt))
+
+
 def test_reduce_identities(oracle):
     """device_reduce_test.cpp:95-118 (ones, 2^k+1) and :220-236 (float max identity)."""
     for k in range(0, 16):
