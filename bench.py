@@ -89,6 +89,11 @@ OPS = {
     "reduce_by_key": dict(metric="Gitems/s i32 by i32 ReduceByKey Sum @2^30", unit="Gitems/s", log2n=30,
                           dtype="i32", workload="ReduceByKey Sum of i32 values by keys i/100, seed 1",
                           bytes=8.08, kbytes=8.08, kernel="by_key_kernel"),
+    # DeviceSelect::If(x % 2 == 0) over uniform i32: reads every item, writes
+    # the selected half (4 + 2 B per item).
+    "select": dict(metric="Gitems/s i32 DeviceSelect::If(even) @2^30", unit="Gitems/s", log2n=30, dtype="i32",
+                   workload="DeviceSelect::If x % 2 == 0 over uniform i32, seed 1", bytes=6, kbytes=6,
+                   kernel="compact_kernel"),
     # DeviceSegmentedRadixSort (SURVEY next-row widening): 2^27 u32 keys in
     # segments of 1..2047 keys (sizes uniform, seed 1), contiguous.  All
     # segments are short, so the one-block-per-segment kernel does the whole
@@ -286,6 +291,11 @@ class Workload:
                 self.outputs = [T.empty(runs, dtype=T.int32, device=dev), T.empty(runs, dtype=T.int32, device=dev),
                                 T.empty(1, dtype=T.int32, device=dev)]
                 self.temp = L.alloc_temp(L.DeviceReduce.GetReduceByKeyTempStorageBytes(L.I32, L.I32, n))
+        elif op == "select":
+            self.inputs = [fill(T.uint32, L.GEN_U32_UNIFORM, 1).view(T.int32)]
+            self.outputs = [T.empty_like(self.inputs[0]), T.empty(1, dtype=T.int32, device=dev)]
+            self.temp = L.alloc_temp(L.DeviceSelect.GetTempStorageBytes(n))
+            self.pred = L.Pred.mod_eq(2, 0)
         elif op == "argmin":
             self.inputs = [fill(T.float32, L.GEN_F32_UNIT, 1)]
             self.outputs = [T.empty(1, dtype=T.float32, device=dev), T.empty(1, dtype=T.int32, device=dev)]
@@ -295,6 +305,7 @@ class Workload:
             self.outputs = [T.empty(1, dtype=T.int64, device=dev)]
             self.temp = L.alloc_temp(L.DeviceReduce.GetTempStorageBytes(L.I64, n))
         self.rs, self.sc, self.rd = L.DeviceRadixSort(), L.DeviceScan(), L.DeviceReduce()
+        self.sl = L.DeviceSelect()
 
     def step(self, inputs=None, outputs=None):
         op, n, i, o, t = self.op, self.n, inputs or self.inputs, outputs or self.outputs, self.temp
@@ -319,6 +330,8 @@ class Workload:
             self.rd.Max(t, i[0], o[0], n)
         elif op == "argmin":
             self.rd.ArgMin(t, i[0], o[0], o[1], n)
+        elif op == "select":
+            self.sl.If(t, i[0], o[0], o[1], n, self.pred)
         elif op == "scan_by_key":
             self.sc.InclusiveSumByKey(t, i[0], i[1], o[0], n)
         elif op == "reduce_by_key":
@@ -338,6 +351,8 @@ class Workload:
             return L.KERNEL_ARG_REDUCE
         if self.op.endswith("by_key"):
             return L.KERNEL_BY_KEY
+        if self.op == "select":
+            return L.KERNEL_SELECT
         return L.KERNEL_SORT_ONESWEEP
 
 
@@ -393,6 +408,9 @@ def cpu_fn(op: str, n_sample: int, threads: int):
     if op == "argmin":
         x = O.generate(O.GEN_F32_UNIT, n_sample, seed=1)
         return lambda: O.arg_extremum(x, True)
+    if op == "select":
+        x = O.generate(O.GEN_U32_UNIFORM, n_sample, seed=1).view("int32")
+        return lambda: O.select(x, O.clause_mask(x, [(6, 0, 2, 0)]))
     if op in ("scan_by_key", "reduce_by_key"):
         import numpy as np
         k = (np.arange(n_sample, dtype=np.int64) // 100).astype(np.int32)

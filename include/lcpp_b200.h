@@ -52,6 +52,8 @@ typedef enum lcpp_dtype {
     LCPP_U64 = 3,
     LCPP_I64 = 4,
     LCPP_F64 = 5,
+    LCPP_U8 = 6,    /* 1-byte (bool) selection flags of DeviceSelect /
+                       DevicePartition only; every other entry point rejects it */
     LCPP_NONE = 255 /* "no values" (keys-only) */
 } lcpp_dtype;
 
@@ -389,6 +391,103 @@ lcpp_status lcpp_reduce_by_key(void* temp, size_t temp_bytes, const void* d_keys
                                void* d_unique_out, void* d_aggregates_out, uint32_t* d_num_runs_out,
                                uint64_t num_items, lcpp_op op, lcpp_dtype key_dtype, lcpp_dtype value_dtype,
                                lcpp_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * DeviceSelect / DevicePartition  (src/lcpp/device/device_select.h,
+ * src/lcpp/device/device_partition.h)
+ *
+ * The reference takes predicate lambdas; through the C ABI a predicate is
+ * the AND of up to LCPP_MAX_CLAUSES clauses on the tested value (an item, or
+ * a flag for FlaggedIf), each optionally negated.  a and b hold the bit
+ * patterns of values of the tested type (4-byte types in the low half).
+ * Zero clauses select everything.  C++ callers compiled with nvcc can pass
+ * any __device__ callable instead (include/lcpp_b200_device.cuh).
+ * All counts are uint32 (num_items at most 2^32 - 1, as the reference);
+ * zero items write zero count(s) and nothing else.
+ * ------------------------------------------------------------------------ */
+#define LCPP_MAX_CLAUSES 4
+
+typedef enum lcpp_clause_kind {
+    LCPP_CLAUSE_LT = 0,      /* x <  a */
+    LCPP_CLAUSE_LE = 1,      /* x <= a */
+    LCPP_CLAUSE_GT = 2,      /* x >  a */
+    LCPP_CLAUSE_GE = 3,      /* x >= a */
+    LCPP_CLAUSE_EQ = 4,      /* x == a */
+    LCPP_CLAUSE_NE = 5,      /* x != a */
+    LCPP_CLAUSE_MOD_EQ = 6,  /* x % a == b (integer types, a != 0; C remainder) */
+    LCPP_CLAUSE_BITS_ANY = 7 /* (x & a) != 0 (integer types) */
+} lcpp_clause_kind;
+
+typedef struct lcpp_clause {
+    int32_t kind;   /* lcpp_clause_kind */
+    int32_t negate; /* nonzero: the clause's result is inverted */
+    uint64_t a;
+    uint64_t b;
+} lcpp_clause;
+
+/* Replace DeviceSelect::GetTempStorageBytes and DevicePartition::
+ * GetTempStorageBytes / GetThreeWayTempStorageBytes
+ * (device_select.h:56-63, device_partition.h:55-71); item-type independent. */
+lcpp_status lcpp_select_temp_bytes(uint64_t num_items, size_t* temp_bytes);
+lcpp_status lcpp_partition_temp_bytes(uint64_t num_items, size_t* temp_bytes);
+lcpp_status lcpp_partition_three_way_temp_bytes(uint64_t num_items, size_t* temp_bytes);
+
+/* Replace DeviceSelect::Flagged (device_select.h:65-117): the items whose
+ * flag != 0 (at flag_dtype; LCPP_U8 for bool flags), in input order, and
+ * *d_num_selected_out = their count.  d_out may equal d_in (the in-place
+ * overload). */
+lcpp_status lcpp_select_flagged(void* temp, size_t temp_bytes, const void* d_in, const void* d_flags, void* d_out,
+                                uint32_t* d_num_selected_out, uint64_t num_items, lcpp_dtype dtype,
+                                lcpp_dtype flag_dtype, lcpp_stream_t stream);
+
+/* Replace DeviceSelect::FlaggedIf (device_select.h:177-212): the items whose
+ * flag satisfies the clauses (tested at flag_dtype).  d_out may equal d_in. */
+lcpp_status lcpp_select_flagged_if(void* temp, size_t temp_bytes, const void* d_in, const void* d_flags,
+                                   void* d_out, uint32_t* d_num_selected_out, uint64_t num_items, lcpp_dtype dtype,
+                                   lcpp_dtype flag_dtype, const lcpp_clause* clauses, int num_clauses,
+                                   lcpp_stream_t stream);
+
+/* Replace DeviceSelect::If (device_select.h:119-175): the items that satisfy
+ * the clauses.  d_out may equal d_in. */
+lcpp_status lcpp_select_if(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                           uint32_t* d_num_selected_out, uint64_t num_items, lcpp_dtype dtype,
+                           const lcpp_clause* clauses, int num_clauses, lcpp_stream_t stream);
+
+/* Replace DeviceSelect::Unique (device_select.h:214-286): the first item of
+ * every run of consecutive equal items (== at dtype: -0.0 equals +0.0, NaN
+ * never equals).  d_out may equal d_in. */
+lcpp_status lcpp_select_unique(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                               uint32_t* d_num_selected_out, uint64_t num_items, lcpp_dtype dtype,
+                               lcpp_stream_t stream);
+
+/* Replace DeviceSelect::UniqueByKey (device_select.h:288-333): the first
+ * (key, value) of every run of equal consecutive keys. */
+lcpp_status lcpp_select_unique_by_key(void* temp, size_t temp_bytes, const void* d_keys_in, const void* d_values_in,
+                                      void* d_keys_out, void* d_values_out, uint32_t* d_num_selected_out,
+                                      uint64_t num_items, lcpp_dtype key_dtype, lcpp_dtype value_dtype,
+                                      lcpp_stream_t stream);
+
+/* Replace DevicePartition::Flagged / If (device_partition.h:73-155): the
+ * selected items in input order from d_out[0], the rejected ones in REVERSE
+ * input order from d_out[num_items - 1] down; *d_num_selected_out = the
+ * selected count.  d_out must not equal d_in. */
+lcpp_status lcpp_partition_flagged(void* temp, size_t temp_bytes, const void* d_in, const void* d_flags, void* d_out,
+                                   uint32_t* d_num_selected_out, uint64_t num_items, lcpp_dtype dtype,
+                                   lcpp_dtype flag_dtype, lcpp_stream_t stream);
+lcpp_status lcpp_partition_if(void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                              uint32_t* d_num_selected_out, uint64_t num_items, lcpp_dtype dtype,
+                              const lcpp_clause* clauses, int num_clauses, lcpp_stream_t stream);
+
+/* Replace the three-way DevicePartition::If (device_partition.h:157-227):
+ * items satisfying the first clauses go to d_first_out, the others that
+ * satisfy the second clauses to d_second_out (both in input order), the rest
+ * to d_unselected_out in REVERSE input order; d_num_selected_out[0] / [1] =
+ * the first / second counts.  Outputs must not overlap the input. */
+lcpp_status lcpp_partition_if_three_way(void* temp, size_t temp_bytes, const void* d_in, void* d_first_out,
+                                        void* d_second_out, void* d_unselected_out, uint32_t* d_num_selected_out,
+                                        uint64_t num_items, lcpp_dtype dtype, const lcpp_clause* first_clauses,
+                                        int num_first_clauses, const lcpp_clause* second_clauses,
+                                        int num_second_clauses, lcpp_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Device diagnostics (no reference counterpart: the reference's look-back

@@ -28,6 +28,7 @@
 
 #include <algorithm>
 #include <limits>
+#include <type_traits>
 
 namespace lcpp_b200 {
 namespace device {
@@ -754,6 +755,499 @@ cudaError_t reduce_by_key(void* temp, size_t temp_bytes, const K* d_keys_in, con
         return cudaErrorInvalidValue;
     return bykey_detail::launch<true>(temp, temp_bytes, d_keys_in, d_values_in, d_aggregates_out, d_unique_out,
                                       d_num_runs_out, num_items, bykey_detail::kModeReduce, V{}, equal, op, stream);
+}
+
+/* ---------------------------------------------------------------------------
+ * Compaction: DeviceSelect::Flagged / If / FlaggedIf / Unique / UniqueByKey
+ * (src/lcpp/device/device_select.h:56-345) and DevicePartition::Flagged / If
+ * and the three-way If (src/lcpp/device/device_partition.h:55-227).
+ *
+ * Selection per item: Flagged -- flag != 0 at the flag's type (bool flags are
+ * 1-byte); If -- select(item); FlaggedIf -- select(flag); Unique /
+ * UniqueByKey -- item 0 and every item whose key differs from its
+ * predecessor's (`equal`, default ==).  Select writes the selected items in
+ * input order and the count; Partition writes the selected items in order
+ * from the front and the rejected ones in REVERSE order from the back
+ * (output[n - 1 - rejected_before], device_partition.h:531-575); the
+ * three-way form writes items with select_first to first_out, the remaining
+ * ones with select_second to second_out (both in order) and the rest in
+ * reverse order into unselected_out (device_partition.h:582-660), and the two
+ * counts.  Select may run in place (d_out == d_in; Unique too): an item only
+ * ever moves to a lower index, and a tile writes only after its look-back,
+ * i.e. after every lower tile has loaded its items.
+ *
+ * One pass: tiles of 256 threads x 4 groups x 4 consecutive items (4096
+ * items), tile ids from an atomic counter; the per-group selected counts are
+ * scanned across lanes, warps and (decoupled look-back, every wait bounded
+ * by %globaltimer at 4 s, error 5 at byte 4 of temp) tiles; each selected
+ * item is stored at its rank.  The tile status word is
+ * (count << 32) | status; the three-way form keeps its second count in two
+ * more arrays (partial, inclusive) written before the word is released, and
+ * learns both totals from a counting pass first (its unselected output is
+ * placed from the end of a region whose size is n minus both totals).
+ * ------------------------------------------------------------------------- */
+
+/* "no values" for the value arrays of the keys-only forms */
+struct NoValue {};
+
+/* flag != 0 at the flag's type */
+struct NonZero {
+    template <typename F>
+    __device__ __forceinline__ bool operator()(F f) const { return f != F(0); }
+};
+
+namespace select_detail {
+
+constexpr int kBlock = 256;
+constexpr int kWarps = kBlock / 32;
+constexpr int kChunks = 4;
+constexpr int kGroup = 4;
+constexpr uint64_t kTileItems = uint64_t(kBlock) * kChunks * kGroup;
+constexpr uint64_t kWaitLimitNs = 4000000000ull;
+constexpr unsigned int kErrTimeout = 5;
+constexpr size_t kAlign = 256;
+enum : uint32_t { kInvalid = 0, kPartial = 1, kInclusive = 2 };
+enum : int { kSelFlag = 0, kSelIf = 1, kSelUnique = 2 };
+enum : int { kOutSelect = 0, kOutPartition = 1, kOutThreeWay = 2 };
+
+struct Ctrl {
+    unsigned int tile_counter;
+    unsigned int error;      // byte 4 of temp storage
+    unsigned int totals[2];  // three-way: both selected counts (counting pass)
+};
+
+__device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t* p)
+{
+    uint64_t v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_u64(uint64_t* p, uint64_t v)
+{
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+/* 4 consecutive items at g: one 4-, 16- or two 16-byte loads when vector */
+template <typename T>
+__device__ __forceinline__ void load4(const T* p, uint64_t n, uint64_t g, bool vector, T (&x)[kGroup])
+{
+    if (vector && g + kGroup <= n) {
+        if constexpr (sizeof(T) == 1) {
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(p + g);
+            memcpy(x, &w, 4);
+        } else {
+            constexpr int W = int(sizeof(T)) * kGroup / 16;
+            const uint4* q = reinterpret_cast<const uint4*>(p + g);
+            uint4 w[W];
+#pragma unroll
+            for (int i = 0; i < W; ++i) w[i] = q[i];
+            memcpy(x, w, sizeof(x));
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < kGroup; ++e) x[e] = g + e < n ? p[g + e] : T{};
+    }
+}
+
+/* Counts of one range: selected (first) in the low half, second-selected in
+ * the high half.  Both stay below 2^32, so packed sums never carry. */
+__device__ __forceinline__ uint64_t warp_sum(uint64_t v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <bool THREE>
+struct Status {
+    uint64_t* word;       // (first count << 32) | status
+    uint32_t* second_p;   // three-way: second count of the partial
+    uint32_t* second_i;   // three-way: second count of the inclusive prefix
+    __device__ __forceinline__ void publish(uint64_t t, uint32_t status, uint64_t packed) const
+    {
+        if constexpr (THREE)
+            *static_cast<volatile uint32_t*>((status == kPartial ? second_p : second_i) + t) = uint32_t(packed >> 32);
+        st_release_u64(word + t, (uint64_t(uint32_t(packed)) << 32) | status);
+    }
+};
+
+/* Exclusive packed count of `tile` (> 0), run by one whole warp. */
+template <bool THREE>
+__device__ __forceinline__ uint64_t look_back(uint64_t tile, const Status<THREE>& st, Ctrl* ctrl)
+{
+    const int lane = threadIdx.x & 31;
+    uint64_t prefix = 0;
+    int64_t base = int64_t(tile) - 1;
+    while (true) {
+        const int64_t j = base - lane;
+        uint64_t val = 0;
+        uint32_t status = kInclusive;
+        if (j >= 0) {
+            uint64_t m;
+            uint32_t spins = 0;
+            uint64_t t0 = 0;
+            bool gave_up = false;
+            while (((m = ld_acquire_u64(st.word + j)) & 3u) == kInvalid) {
+                if (++spins == 64) {
+                    spins = 0;
+                    const uint64_t now = global_ns();
+                    if (t0 == 0) {
+                        t0 = now;
+                    } else if (now - t0 > kWaitLimitNs || *static_cast<volatile unsigned int*>(&ctrl->error)) {
+                        atomicCAS(&ctrl->error, 0u, kErrTimeout);
+                        gave_up = true;
+                        break;
+                    }
+                }
+            }
+            if (!gave_up) {
+                status = uint32_t(m & 3u);
+                val = m >> 32;
+                if constexpr (THREE)
+                    val |= uint64_t(*static_cast<const volatile uint32_t*>(
+                               (status == kPartial ? st.second_p : st.second_i) + j))
+                           << 32;
+            }
+        }
+        const uint32_t mask = __ballot_sync(0xffffffffu, status == kInclusive);
+        const int last = mask ? __ffs(mask) - 1 : 31;
+        prefix += warp_sum(lane <= last ? val : 0);
+        if (mask) return prefix;
+        base -= 32;
+    }
+}
+
+/* Counting pass of the three-way partition: ctrl->totals[0..1]. */
+template <typename T, typename P1, typename P2>
+__global__ void __launch_bounds__(kBlock) count_kernel(const T* in, uint64_t n, Ctrl* ctrl, P1 first, P2 second)
+{
+    uint32_t c1 = 0, c2 = 0;
+    for (uint64_t i = uint64_t(blockIdx.x) * kBlock + threadIdx.x; i < n; i += uint64_t(gridDim.x) * kBlock) {
+        const T x = in[i];
+        const bool s1 = first(x);
+        c1 += s1;
+        c2 += !s1 && second(x);
+    }
+    const uint64_t w = warp_sum(uint64_t(c1) | (uint64_t(c2) << 32));
+    if ((threadIdx.x & 31) == 0 && w) {
+        atomicAdd(&ctrl->totals[0], uint32_t(w));
+        atomicAdd(&ctrl->totals[1], uint32_t(w >> 32));
+    }
+}
+
+template <typename T, typename F, typename V>
+struct Args {
+    const T* in;
+    const F* flags;
+    const V* vin;
+    T* out;
+    T* out2;
+    T* out3;
+    V* vout;
+    uint32_t* num_selected;
+    uint64_t n;
+    bool vector;
+};
+
+/* SEL: kSelFlag (pick(flag)), kSelIf (pick(item)), kSelUnique (key change by
+ * `equal`); OUT: kOutSelect, kOutPartition, kOutThreeWay (pick = first,
+ * pick2 = second). */
+template <typename T, typename F, typename V, int SEL, int OUT, typename Pick, typename Pick2, typename Equal>
+__global__ void __launch_bounds__(kBlock)
+compact_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st, Pick pick, Pick2 pick2, Equal equal)
+{
+    constexpr bool THREE = OUT == kOutThreeWay;
+    constexpr bool HAS_V = !std::is_same<V, NoValue>::value;
+    __shared__ uint32_t s_tile;
+    __shared__ uint64_t s_total[kWarps];
+    __shared__ uint64_t s_excl[kWarps];
+    __shared__ uint64_t s_prefix;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) s_tile = atomicAdd(&ctrl->tile_counter, 1u);
+    __syncthreads();
+    const uint64_t tile = s_tile;
+    const uint64_t n = a.n;
+    const uint64_t warp_base = tile * kTileItems + uint64_t(warp) * (32 * kChunks * kGroup);
+
+    T x[kChunks][kGroup];
+    uint32_t sel1 = 0, sel2 = 0;  // bit j * kGroup + e
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+        const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
+        load4(a.in, n, g, a.vector, x[j]);
+        if constexpr (SEL == kSelFlag) {
+            F f[kGroup];
+            load4(a.flags, n, g, a.vector, f);
+#pragma unroll
+            for (int e = 0; e < kGroup; ++e)
+                if (g + e < n && pick(f[e])) sel1 |= 1u << (j * kGroup + e);
+        } else if constexpr (SEL == kSelIf) {
+#pragma unroll
+            for (int e = 0; e < kGroup; ++e) {
+                if (g + e >= n) continue;
+                const bool s1 = pick(x[j][e]);
+                if (s1) sel1 |= 1u << (j * kGroup + e);
+                if constexpr (THREE)
+                    if (!s1 && pick2(x[j][e])) sel2 |= 1u << (j * kGroup + e);
+            }
+        }
+    }
+    if constexpr (SEL == kSelUnique) {
+#pragma unroll
+        for (int j = 0; j < kChunks; ++j) {
+            const T prev_lane = __shfl_up_sync(0xffffffffu, x[j][kGroup - 1], 1);
+            const T prev_chunk = __shfl_sync(0xffffffffu, x[j > 0 ? j - 1 : 0][kGroup - 1], 31);
+            const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
+#pragma unroll
+            for (int e = 0; e < kGroup; ++e) {
+                const uint64_t i = g + e;
+                if (i >= n) continue;
+                bool h;
+                if (e > 0)
+                    h = !equal(x[j][e - 1], x[j][e]);
+                else if (lane > 0)
+                    h = !equal(prev_lane, x[j][0]);
+                else if (j > 0)
+                    h = !equal(prev_chunk, x[j][0]);
+                else
+                    h = i == 0 || !equal(a.in[i - 1], x[j][0]);
+                if (h) sel1 |= 1u << (j * kGroup + e);
+            }
+        }
+    }
+
+    /* packed counts: group columns scanned across lanes, carried across columns */
+    uint64_t pre[kChunks];
+    uint64_t carry = 0;
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+        uint64_t c = uint64_t(__popc((sel1 >> (j * kGroup)) & 0xFu));
+        if constexpr (THREE) c |= uint64_t(__popc((sel2 >> (j * kGroup)) & 0xFu)) << 32;
+        uint64_t incl = c;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint64_t y = __shfl_up_sync(0xffffffffu, incl, d);
+            if (lane >= d) incl += y;
+        }
+        pre[j] = carry + incl - c;
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) s_total[warp] = carry;
+    __syncthreads();
+    if (warp == 0) {
+        const uint64_t t = lane < kWarps ? s_total[lane] : 0;
+        uint64_t incl = t;
+#pragma unroll
+        for (int d = 1; d < kWarps; d <<= 1) {
+            const uint64_t y = __shfl_up_sync(0xffffffffu, incl, d);
+            if (lane >= d) incl += y;
+        }
+        if (lane < kWarps) s_excl[lane] = incl - t;
+        const uint64_t aggregate = __shfl_sync(0xffffffffu, incl, kWarps - 1);
+        uint64_t prefix = 0;
+        if (tile == 0) {
+            if (lane == 0) st.publish(0, kInclusive, aggregate);
+        } else {
+            if (lane == 0) st.publish(tile, kPartial, aggregate);
+            prefix = look_back<THREE>(tile, st, ctrl);
+            if (lane == 0) st.publish(tile, kInclusive, prefix + aggregate);
+        }
+        if (lane == 0) {
+            s_prefix = prefix;
+            if (tile == gridDim.x - 1) {
+                a.num_selected[0] = uint32_t(prefix + aggregate);
+                if constexpr (THREE) a.num_selected[1] = uint32_t((prefix + aggregate) >> 32);
+            }
+        }
+    }
+    __syncthreads();
+
+    uint64_t unsel_end = 0;  // three-way: size of the unselected region
+    if constexpr (THREE) unsel_end = n - ctrl->totals[0] - ctrl->totals[1];
+    V v[kGroup];
+    const uint64_t warp_prefix = s_prefix + s_excl[warp];
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+        const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
+        if constexpr (HAS_V) load4(a.vin, n, g, a.vector, v);
+        const uint64_t base = warp_prefix + pre[j];
+        uint64_t pos1 = uint32_t(base), pos2 = base >> 32;
+#pragma unroll
+        for (int e = 0; e < kGroup; ++e) {
+            const uint64_t i = g + e;
+            if (i >= n) continue;
+            const int b = j * kGroup + e;
+            if ((sel1 >> b) & 1u) {
+                a.out[pos1] = x[j][e];
+                if constexpr (HAS_V) a.vout[pos1] = v[e];
+                ++pos1;
+            } else if constexpr (THREE) {
+                if ((sel2 >> b) & 1u) {
+                    a.out2[pos2++] = x[j][e];
+                } else {
+                    a.out3[unsel_end - 1 - (i - pos1 - pos2)] = x[j][e];
+                }
+            } else if constexpr (OUT == kOutPartition) {
+                a.out[n - 1 - (i - pos1)] = x[j][e];
+            }
+        }
+    }
+}
+
+struct Layout {
+    size_t ctrl, word, second_p, second_i, total;
+    uint64_t tiles;
+};
+
+inline Layout layout(uint64_t n, bool three)
+{
+    Layout L{};
+    L.tiles = n ? (n + kTileItems - 1) / kTileItems : 0;
+    auto up = [](size_t x) { return (x + kAlign - 1) / kAlign * kAlign; };
+    L.ctrl = 0;
+    L.word = kAlign;
+    L.second_p = up(L.word + size_t(L.tiles) * 8);
+    L.second_i = up(L.second_p + (three ? size_t(L.tiles) * 4 : 0));
+    L.total = up(L.second_i + (three ? size_t(L.tiles) * 4 : 0));
+    return L;
+}
+
+inline bool aligned16(const void* p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+template <int SEL, int OUT, typename T, typename F, typename V, typename Pick, typename Pick2, typename Equal>
+cudaError_t launch(void* temp, size_t temp_bytes, Args<T, F, V> a, Pick pick, Pick2 pick2, Equal equal,
+                   cudaStream_t stream)
+{
+    constexpr bool THREE = OUT == kOutThreeWay;
+    if (!a.num_selected) return cudaErrorInvalidValue;
+    if (a.n == 0)
+        return cudaMemsetAsync(a.num_selected, 0, (THREE ? 2 : 1) * sizeof(uint32_t), stream);
+    if (a.n > 0xffffffffull || !a.in || !a.out || (THREE && (!a.out2 || !a.out3))) return cudaErrorInvalidValue;
+    if (SEL == kSelFlag && !a.flags) return cudaErrorInvalidValue;
+    const Layout L = layout(a.n, THREE);
+    if (!temp || reinterpret_cast<uintptr_t>(temp) % kAlign || temp_bytes < L.total) return cudaErrorInvalidValue;
+    unsigned char* t = static_cast<unsigned char*>(temp);
+    cudaError_t e = cudaMemsetAsync(t, 0, L.word + size_t(L.tiles) * 8, stream);
+    if (e != cudaSuccess) return e;
+    Ctrl* ctrl = reinterpret_cast<Ctrl*>(t);
+    if constexpr (THREE) {
+        int dev = 0, sms = 0;
+        e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        const uint64_t want = (a.n + kBlock - 1) / kBlock;
+        const unsigned grid = unsigned(std::min<uint64_t>(want, uint64_t(sms > 0 ? sms : 1) * 8));
+        count_kernel<<<grid, kBlock, 0, stream>>>(a.in, a.n, ctrl, pick, pick2);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    a.vector = aligned16(a.in) && aligned16(a.flags) && aligned16(a.vin) && aligned16(a.out) &&
+               aligned16(a.vout) && aligned16(a.out2) && aligned16(a.out3);
+    Status<THREE> st{reinterpret_cast<uint64_t*>(t + L.word), reinterpret_cast<uint32_t*>(t + L.second_p),
+                     reinterpret_cast<uint32_t*>(t + L.second_i)};
+    compact_kernel<T, F, V, SEL, OUT><<<unsigned(L.tiles), kBlock, 0, stream>>>(a, ctrl, st, pick, pick2, equal);
+    return cudaGetLastError();
+}
+
+struct Never {
+    template <typename X>
+    __device__ __forceinline__ bool operator()(X) const { return false; }
+};
+
+}  // namespace select_detail
+
+/* Temp storage bytes of the select / partition forms (any item type);
+ * three_way: the three-way partition. */
+inline size_t select_temp_bytes(uint64_t num_items, bool three_way = false)
+{
+    return num_items ? select_detail::layout(num_items, three_way).total : 0;
+}
+
+/* DeviceSelect / DevicePartition with user callables.  num_items < 2^32
+ * (uint32 counts, as the reference); zero items write zero count(s).
+ * d_out may equal d_in for the select forms. */
+template <typename T, typename F, typename Pick = NonZero>
+cudaError_t select_flagged(void* temp, size_t temp_bytes, const T* d_in, const F* d_flags, T* d_out,
+                           uint32_t* d_num_selected_out, uint64_t num_items, Pick pick = Pick{},
+                           cudaStream_t stream = 0)
+{
+    using namespace select_detail;
+    Args<T, F, NoValue> a{d_in, d_flags, nullptr, d_out, nullptr, nullptr, nullptr, d_num_selected_out, num_items,
+                          false};
+    return launch<kSelFlag, kOutSelect>(temp, temp_bytes, a, pick, Never{}, EqualTo{}, stream);
+}
+
+template <typename T, typename Pick>
+cudaError_t select_if(void* temp, size_t temp_bytes, const T* d_in, T* d_out, uint32_t* d_num_selected_out,
+                      uint64_t num_items, Pick pick, cudaStream_t stream = 0)
+{
+    using namespace select_detail;
+    Args<T, T, NoValue> a{d_in, nullptr, nullptr, d_out, nullptr, nullptr, nullptr, d_num_selected_out, num_items,
+                          false};
+    return launch<kSelIf, kOutSelect>(temp, temp_bytes, a, pick, Never{}, EqualTo{}, stream);
+}
+
+template <typename T, typename Equal = EqualTo>
+cudaError_t select_unique(void* temp, size_t temp_bytes, const T* d_in, T* d_out, uint32_t* d_num_selected_out,
+                          uint64_t num_items, Equal equal = Equal{}, cudaStream_t stream = 0)
+{
+    using namespace select_detail;
+    Args<T, T, NoValue> a{d_in, nullptr, nullptr, d_out, nullptr, nullptr, nullptr, d_num_selected_out, num_items,
+                          false};
+    return launch<kSelUnique, kOutSelect>(temp, temp_bytes, a, Never{}, Never{}, equal, stream);
+}
+
+template <typename K, typename V, typename Equal = EqualTo>
+cudaError_t select_unique_by_key(void* temp, size_t temp_bytes, const K* d_keys_in, const V* d_values_in,
+                                 K* d_keys_out, V* d_values_out, uint32_t* d_num_selected_out, uint64_t num_items,
+                                 Equal equal = Equal{}, cudaStream_t stream = 0)
+{
+    using namespace select_detail;
+    if (num_items && (!d_values_in || !d_values_out)) return cudaErrorInvalidValue;
+    Args<K, K, V> a{d_keys_in, nullptr, d_values_in, d_keys_out, nullptr, nullptr, d_values_out, d_num_selected_out,
+                    num_items, false};
+    return launch<kSelUnique, kOutSelect>(temp, temp_bytes, a, Never{}, Never{}, equal, stream);
+}
+
+template <typename T, typename F, typename Pick = NonZero>
+cudaError_t partition_flagged(void* temp, size_t temp_bytes, const T* d_in, const F* d_flags, T* d_out,
+                              uint32_t* d_num_selected_out, uint64_t num_items, Pick pick = Pick{},
+                              cudaStream_t stream = 0)
+{
+    using namespace select_detail;
+    if (num_items && d_out == d_in) return cudaErrorInvalidValue;
+    Args<T, F, NoValue> a{d_in, d_flags, nullptr, d_out, nullptr, nullptr, nullptr, d_num_selected_out, num_items,
+                          false};
+    return launch<kSelFlag, kOutPartition>(temp, temp_bytes, a, pick, Never{}, EqualTo{}, stream);
+}
+
+template <typename T, typename Pick>
+cudaError_t partition_if(void* temp, size_t temp_bytes, const T* d_in, T* d_out, uint32_t* d_num_selected_out,
+                         uint64_t num_items, Pick pick, cudaStream_t stream = 0)
+{
+    using namespace select_detail;
+    if (num_items && d_out == d_in) return cudaErrorInvalidValue;
+    Args<T, T, NoValue> a{d_in, nullptr, nullptr, d_out, nullptr, nullptr, nullptr, d_num_selected_out, num_items,
+                          false};
+    return launch<kSelIf, kOutPartition>(temp, temp_bytes, a, pick, Never{}, EqualTo{}, stream);
+}
+
+/* d_num_selected_out[0] = first count, [1] = second count. */
+template <typename T, typename Pick1, typename Pick2>
+cudaError_t partition_three_way(void* temp, size_t temp_bytes, const T* d_in, T* d_first_out, T* d_second_out,
+                                T* d_unselected_out, uint32_t* d_num_selected_out, uint64_t num_items,
+                                Pick1 select_first, Pick2 select_second, cudaStream_t stream = 0)
+{
+    using namespace select_detail;
+    Args<T, T, NoValue> a{d_in, nullptr, nullptr, d_first_out, d_second_out, d_unselected_out, nullptr,
+                          d_num_selected_out, num_items, false};
+    return launch<kSelIf, kOutThreeWay>(temp, temp_bytes, a, select_first, select_second, EqualTo{}, stream);
 }
 
 }  // namespace device

@@ -25,7 +25,8 @@ typedef enum lcpp_kernel_kind {
     LCPP_KERNEL_SEGMENT_BLOCK = 4,  /* segmented sort: one block per short segment */
     LCPP_KERNEL_MERGE = 5,          /* merge path (lcpp_dist_merge_sorted*) */
     LCPP_KERNEL_ARG_REDUCE = 6,     /* ArgMin / ArgMax */
-    LCPP_KERNEL_BY_KEY = 7          /* by-key scans and ReduceByKey */
+    LCPP_KERNEL_BY_KEY = 7,         /* by-key scans and ReduceByKey */
+    LCPP_KERNEL_SELECT = 8          /* DeviceSelect / DevicePartition */
 } lcpp_kernel_kind;
 
 typedef struct lcpp_kernel_time {

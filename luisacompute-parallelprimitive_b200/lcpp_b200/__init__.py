@@ -24,6 +24,7 @@ OK, ERR_INVALID_ARG, ERR_TEMP_TOO_SMALL, ERR_UNSUPPORTED_DTYPE = 0, 1, 2, 3
 ERR_CUDA, ERR_LOOKBACK_TIMEOUT, ERR_COMM, ERR_INTERNAL = 4, 5, 6, 7
 # lcpp_dtype
 U32, I32, F32, U64, I64, F64, NONE = 0, 1, 2, 3, 4, 5, 255
+U8 = 6  # 1-byte (bool) selection flags only
 # lcpp_op
 OP_SUM, OP_MIN, OP_MAX = 0, 1, 2
 # lcpp_testgen_dist
@@ -36,6 +37,7 @@ KERNEL_SORT_HISTOGRAM, KERNEL_SORT_ONESWEEP, KERNEL_SCAN, KERNEL_REDUCE, KERNEL_
 KERNEL_MERGE = 5
 KERNEL_ARG_REDUCE = 6
 KERNEL_BY_KEY = 7
+KERNEL_SELECT = 8
 
 _lib = None
 
@@ -106,6 +108,17 @@ def lib() -> ctypes.CDLL:
         "lcpp_scan_inclusive_sum_by_key": ([vp, sz, vp, vp, vp, u64, i, i, vp], i),
         "lcpp_reduce_by_key_temp_bytes": ([i, i, u64, szp], i),
         "lcpp_reduce_by_key": ([vp, sz, vp, vp, vp, vp, vp, u64, i, i, i, vp], i),
+        "lcpp_select_temp_bytes": ([u64, szp], i),
+        "lcpp_partition_temp_bytes": ([u64, szp], i),
+        "lcpp_partition_three_way_temp_bytes": ([u64, szp], i),
+        "lcpp_select_flagged": ([vp, sz, vp, vp, vp, vp, u64, i, i, vp], i),
+        "lcpp_select_flagged_if": ([vp, sz, vp, vp, vp, vp, u64, i, i, vp, i, vp], i),
+        "lcpp_select_if": ([vp, sz, vp, vp, vp, u64, i, vp, i, vp], i),
+        "lcpp_select_unique": ([vp, sz, vp, vp, vp, u64, i, vp], i),
+        "lcpp_select_unique_by_key": ([vp, sz, vp, vp, vp, vp, vp, u64, i, i, vp], i),
+        "lcpp_partition_flagged": ([vp, sz, vp, vp, vp, vp, u64, i, i, vp], i),
+        "lcpp_partition_if": ([vp, sz, vp, vp, vp, u64, i, vp, i, vp], i),
+        "lcpp_partition_if_three_way": ([vp, sz, vp, vp, vp, vp, vp, u64, i, vp, i, vp, i, vp], i),
         "lcpp_reduce_argmin": ([vp, sz, vp, vp, vp, u64, i, vp], i),
         "lcpp_reduce_argmax": ([vp, sz, vp, vp, vp, u64, i, vp], i),
         "lcpp_reduce": ([vp, sz, vp, vp, u64, i, vp, i, vp], i),
@@ -207,6 +220,76 @@ def _bit_range(rest):
     begin = rest[0] if len(rest) >= 1 else 0
     end = rest[1] if len(rest) == 2 else None
     return begin, end
+
+
+class Clause(ctypes.Structure):
+    """One clause of a C-ABI predicate (lcpp_clause in include/lcpp_b200.h)."""
+    _fields_ = [("kind", ctypes.c_int32), ("negate", ctypes.c_int32), ("a", ctypes.c_uint64),
+                ("b", ctypes.c_uint64)]
+
+
+CLAUSE_LT, CLAUSE_LE, CLAUSE_GT, CLAUSE_GE, CLAUSE_EQ, CLAUSE_NE, CLAUSE_MOD_EQ, CLAUSE_BITS_ANY = range(8)
+
+
+def _bits(value, code: int) -> int:
+    import struct
+    if code == F32:
+        return struct.unpack("<I", struct.pack("<f", float(value)))[0]
+    if code == F64:
+        return struct.unpack("<Q", struct.pack("<d", float(value)))[0]
+    width = {U8: 8, U32: 32, I32: 32, U64: 64, I64: 64}[code]
+    return int(value) & ((1 << width) - 1)
+
+
+class Pred:
+    """A predicate for DeviceSelect / DevicePartition through the C ABI: the
+    AND (`&`) of up to 4 clauses, each negatable (`~`).  Examples: the
+    reference tests' `value % 2 == 0` is Pred.mod_eq(2, 0), `value < 7` is
+    Pred.lt(7), `flag > 0 & flag % 2 != 0` is Pred.gt(0) & ~Pred.mod_eq(2, 0)."""
+
+    def __init__(self, clauses=()):
+        self.clauses = list(clauses)  # (kind, negate, a, b)
+
+    def __and__(self, other: "Pred") -> "Pred":
+        return Pred(self.clauses + other.clauses)
+
+    def __invert__(self) -> "Pred":
+        if len(self.clauses) != 1:
+            raise ValueError("~ applies to a single clause")
+        k, n, a, b = self.clauses[0]
+        return Pred([(k, 1 - n, a, b)])
+
+    @staticmethod
+    def lt(a): return Pred([(CLAUSE_LT, 0, a, 0)])
+    @staticmethod
+    def le(a): return Pred([(CLAUSE_LE, 0, a, 0)])
+    @staticmethod
+    def gt(a): return Pred([(CLAUSE_GT, 0, a, 0)])
+    @staticmethod
+    def ge(a): return Pred([(CLAUSE_GE, 0, a, 0)])
+    @staticmethod
+    def eq(a): return Pred([(CLAUSE_EQ, 0, a, 0)])
+    @staticmethod
+    def ne(a): return Pred([(CLAUSE_NE, 0, a, 0)])
+    @staticmethod
+    def mod_eq(m, r): return Pred([(CLAUSE_MOD_EQ, 0, m, r)])
+    @staticmethod
+    def bits_any(mask): return Pred([(CLAUSE_BITS_ANY, 0, mask, 0)])
+
+    def encode(self, code: int):
+        """(ctypes array, count) for values of dtype `code`."""
+        arr = (Clause * max(1, len(self.clauses)))()
+        for j, (k, n, a, b) in enumerate(self.clauses):
+            arr[j] = Clause(k, n, _bits(a, code), _bits(b, code))
+        return arr, len(self.clauses)
+
+
+def flag_code(t) -> int:
+    """dtype code of a selection-flag tensor (bool and uint8 are LCPP_U8)."""
+    torch = _torch()
+    if t.dtype in (torch.bool, torch.uint8):
+        return U8
+    return dtype_code(t)
 
 
 class KeyMember(ctypes.Structure):
@@ -621,3 +704,90 @@ def diag_timing_read() -> list[tuple[int, float, int]]:
     buf = (KernelTime * max(count.value, 1))()
     check(lib().lcpp_diag_timing_read(buf, count.value, ctypes.byref(count)), "diag_timing_read")
     return [(buf[i].kind, buf[i].ms, buf[i].items) for i in range(count.value)]
+
+
+def _tb(temp):
+    return temp.numel() if temp is not None else 0
+
+
+class DeviceSelect:
+    """Mirror of lcpp::DeviceSelect (src/lcpp/device/device_select.h); the
+    predicate arguments are Pred objects.  Passing d_out = d_in (or omitting
+    it in the in-place helpers) compacts in place."""
+
+    @staticmethod
+    def GetTempStorageBytes(num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_select_temp_bytes(num_items, ctypes.byref(out)), "GetTempStorageBytes")
+        return out.value
+
+    def Flagged(self, temp, d_in, d_flags, d_out, d_num_selected_out, num_items, stream=None):
+        check(lib().lcpp_select_flagged(_ptr(temp), _tb(temp), _ptr(d_in), _ptr(d_flags), _ptr(d_out),
+                                        _ptr(d_num_selected_out), num_items, dtype_code(d_in), flag_code(d_flags),
+                                        _stream(stream)), "Flagged")
+
+    def FlaggedIf(self, temp, d_in, d_flags, d_out, d_num_selected_out, num_items, pred: Pred, stream=None):
+        fc = flag_code(d_flags)
+        arr, n = pred.encode(fc)
+        check(lib().lcpp_select_flagged_if(_ptr(temp), _tb(temp), _ptr(d_in), _ptr(d_flags), _ptr(d_out),
+                                           _ptr(d_num_selected_out), num_items, dtype_code(d_in), fc, arr, n,
+                                           _stream(stream)), "FlaggedIf")
+
+    def If(self, temp, d_in, d_out, d_num_selected_out, num_items, pred: Pred, stream=None):
+        code = dtype_code(d_in)
+        arr, n = pred.encode(code)
+        check(lib().lcpp_select_if(_ptr(temp), _tb(temp), _ptr(d_in), _ptr(d_out), _ptr(d_num_selected_out),
+                                   num_items, code, arr, n, _stream(stream)), "If")
+
+    def Unique(self, temp, d_in, d_out, d_num_selected_out, num_items, stream=None):
+        check(lib().lcpp_select_unique(_ptr(temp), _tb(temp), _ptr(d_in), _ptr(d_out), _ptr(d_num_selected_out),
+                                       num_items, dtype_code(d_in), _stream(stream)), "Unique")
+
+    def UniqueByKey(self, temp, d_keys_in, d_values_in, d_keys_out, d_values_out, d_num_selected_out, num_items,
+                    stream=None):
+        check(lib().lcpp_select_unique_by_key(_ptr(temp), _tb(temp), _ptr(d_keys_in), _ptr(d_values_in),
+                                              _ptr(d_keys_out), _ptr(d_values_out), _ptr(d_num_selected_out),
+                                              num_items, dtype_code(d_keys_in), dtype_code(d_values_in),
+                                              _stream(stream)), "UniqueByKey")
+
+
+class DevicePartition:
+    """Mirror of lcpp::DevicePartition (src/lcpp/device/device_partition.h):
+    selected items in order from the front, rejected ones in reverse order
+    from the back."""
+
+    @staticmethod
+    def GetTempStorageBytes(num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_partition_temp_bytes(num_items, ctypes.byref(out)), "GetTempStorageBytes")
+        return out.value
+
+    @staticmethod
+    def GetThreeWayTempStorageBytes(num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_partition_three_way_temp_bytes(num_items, ctypes.byref(out)),
+              "GetThreeWayTempStorageBytes")
+        return out.value
+
+    def Flagged(self, temp, d_in, d_flags, d_out, d_num_selected_out, num_items, stream=None):
+        check(lib().lcpp_partition_flagged(_ptr(temp), _tb(temp), _ptr(d_in), _ptr(d_flags), _ptr(d_out),
+                                           _ptr(d_num_selected_out), num_items, dtype_code(d_in),
+                                           flag_code(d_flags), _stream(stream)), "Flagged")
+
+    def If(self, temp, d_in, d_out, d_num_selected_out, num_items, pred: Pred, stream=None):
+        code = dtype_code(d_in)
+        arr, n = pred.encode(code)
+        check(lib().lcpp_partition_if(_ptr(temp), _tb(temp), _ptr(d_in), _ptr(d_out), _ptr(d_num_selected_out),
+                                      num_items, code, arr, n, _stream(stream)), "If")
+
+    def IfThreeWay(self, temp, d_in, d_first_out, d_second_out, d_unselected_out, d_num_selected_out, num_items,
+                   select_first: Pred, select_second: Pred, stream=None):
+        """The reference's three-way If overload (device_partition.h:157-227);
+        d_num_selected_out holds two counts."""
+        code = dtype_code(d_in)
+        a1, n1 = select_first.encode(code)
+        a2, n2 = select_second.encode(code)
+        check(lib().lcpp_partition_if_three_way(_ptr(temp), _tb(temp), _ptr(d_in), _ptr(d_first_out),
+                                                _ptr(d_second_out), _ptr(d_unselected_out),
+                                                _ptr(d_num_selected_out), num_items, code, a1, n1, a2, n2,
+                                                _stream(stream)), "IfThreeWay")

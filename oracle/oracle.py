@@ -210,6 +210,49 @@ def scan_by_key_equal(keys, values, mode: str, equal, op=lambda a, b: a + b, ini
     return out
 
 
+# ------------------------------------------------------------ select / partition
+def clause_mask(x: np.ndarray, clauses) -> np.ndarray:
+    """The C ABI's predicate (lcpp_clause, include/lcpp_b200.h): the AND of
+    clauses (kind, negate, a, b), a and b given as values of x's type; MOD_EQ
+    uses the C remainder (sign of the dividend), as the reference's `%`."""
+    m = np.ones(x.shape, bool)
+    for kind, negate, a, b in clauses:
+        a, b = x.dtype.type(a), x.dtype.type(b)
+        r = [lambda: x < a, lambda: x <= a, lambda: x > a, lambda: x >= a, lambda: x == a, lambda: x != a,
+             lambda: np.fmod(x, a) == b, lambda: (x & a) != 0][kind]()
+        m &= ~r if negate else r
+    return m
+
+
+def select(items: np.ndarray, mask: np.ndarray) -> np.ndarray:
+    """DeviceSelect::Flagged / If / FlaggedIf (src/lcpp/device/device_select.h:
+    65-212): the selected items in input order."""
+    return items[mask]
+
+
+def unique_mask(keys: np.ndarray) -> np.ndarray:
+    """DeviceSelect::Unique / UniqueByKey (device_select.h:214-333): item 0 and
+    every item that differs (!=, IEEE for floats) from its predecessor."""
+    m = np.ones(keys.shape, bool)
+    if keys.size > 1:
+        m[1:] = keys[1:] != keys[:-1]
+    return m
+
+
+def partition(items: np.ndarray, mask: np.ndarray) -> np.ndarray:
+    """DevicePartition::Flagged / If (src/lcpp/device/device_partition.h:
+    531-575): selected items in order, then the rejected ones in reverse order."""
+    return np.concatenate([items[mask], items[~mask][::-1]])
+
+
+def partition_three_way(items: np.ndarray, first: np.ndarray, second: np.ndarray):
+    """The three-way DevicePartition::If (device_partition.h:582-660): first
+    in order, second (and not first) in order, the rest in reverse order."""
+    second = second & ~first
+    rest = ~(first | second)
+    return items[first], items[second], items[rest][::-1]
+
+
 def sum_f64(x: np.ndarray) -> float:
     x = np.ascontiguousarray(x)
     return float(lib().oracle_sum_f64(_ptr(x), x.size, NP_TO_DTYPE[x.dtype]))

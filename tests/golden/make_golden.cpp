@@ -17,6 +17,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <functional>
+#include <iterator>
 #include <numeric>
 #include <tuple>
 #include <random>
@@ -33,6 +34,7 @@ template <> const char* dtype_name<int32_t>() { return "i32"; }
 template <> const char* dtype_name<float>() { return "f32"; }
 template <> const char* dtype_name<uint64_t>() { return "u64"; }
 template <> const char* dtype_name<int64_t>() { return "i64"; }
+template <> const char* dtype_name<uint8_t>() { return "u8"; }
 
 template <typename T>
 static void emit(const std::string& name, const std::vector<T>& v)
@@ -293,6 +295,128 @@ static void by_key_cases()
     emit("rbk_aggregates_out", agg);
 }
 
+// tests/device_select_test.cpp and tests/device_partition_test.cpp: the
+// select / partition cases with their host expectations (std::copy_if,
+// std::unique, and the reverse walk for rejected items).
+template <typename T, typename P>
+static std::vector<T> keep(const std::vector<T>& v, P p)
+{
+    std::vector<T> out;
+    std::copy_if(v.begin(), v.end(), std::back_inserter(out), p);
+    return out;
+}
+
+static void select_cases()
+{
+    // device_select_test.cpp:254-320: Flagged (flags 7 at i % 3 == 1) and If(even), 17 items
+    std::vector<int32_t> in(17);
+    std::vector<uint32_t> flags(17);
+    for (int i = 0; i < 17; ++i) {
+        in[i] = 100 + i;
+        flags[i] = i % 3 == 1 ? 7u : 0u;
+    }
+    emit("sel_stable_in", in);
+    emit("sel_stable_flags", flags);
+    std::vector<int32_t> fl;
+    for (int i = 0; i < 17; ++i)
+        if (flags[i]) fl.push_back(in[i]);
+    emit("sel_stable_flagged_out", fl);
+    emit("sel_stable_if_even_out", keep(in, [](int32_t x) { return x % 2 == 0; }));
+
+    // :322-372: Unique and UniqueByKey keep the first item of each run
+    const std::vector<int32_t> keys{1, 1, 2, 2, 2, 4, 7, 7, 9}, values{10, 11, 20, 21, 22, 40, 70, 71, 90};
+    emit("sel_unique_keys", keys);
+    emit("sel_unique_values", values);
+    std::vector<int32_t> uk, uv;
+    for (size_t i = 0; i < keys.size(); ++i)
+        if (i == 0 || keys[i] != keys[i - 1]) {
+            uk.push_back(keys[i]);
+            uv.push_back(values[i]);
+        }
+    emit("sel_unique_keys_out", uk);
+    emit("sel_unique_values_out", uv);
+
+    // :374-430: FlaggedIf with "flag > 0 and odd" over flags -3..5
+    std::vector<int32_t> fin(9), ff(9), fif;
+    for (int i = 0; i < 9; ++i) {
+        fin[i] = 100 + i;
+        ff[i] = i - 3;
+        if (ff[i] > 0 && ff[i] % 2 != 0) fif.push_back(fin[i]);
+    }
+    emit("sel_flaggedif_in", fin);
+    emit("sel_flaggedif_flags", ff);
+    emit("sel_flaggedif_out", fif);
+
+    // :432-500: in place -- Flagged with the data as its own flags, If(> 0),
+    // Unique under "same parity" and under ==
+    const std::vector<int32_t> aliased{0, 2, 0, 3, 4, 0, 5, 0}, pred{-3, 4, -1, 6, 0, 2, 7, -8},
+        uniq_par{1, 3, 2, 4, 5, 7, 8, 10}, uniq_def{1, 1, 2, 2, 2, 4, 4, 9};
+    emit("sel_inplace_aliased", aliased);
+    emit("sel_inplace_aliased_out", keep(aliased, [](int32_t x) { return x != 0; }));
+    emit("sel_inplace_pred", pred);
+    emit("sel_inplace_pred_out", keep(pred, [](int32_t x) { return x > 0; }));
+    std::vector<int32_t> up;
+    for (size_t i = 0; i < uniq_par.size(); ++i)
+        if (i == 0 || uniq_par[i] % 2 != uniq_par[i - 1] % 2) up.push_back(uniq_par[i]);
+    emit("sel_inplace_unique_parity", uniq_par);
+    emit("sel_inplace_unique_parity_out", up);
+    std::vector<int32_t> ud = uniq_def;
+    ud.erase(std::unique(ud.begin(), ud.end()), ud.end());
+    emit("sel_inplace_unique", uniq_def);
+    emit("sel_inplace_unique_out", ud);
+
+    // :114-172: wide values (1 << 40 | i / 3) with bool flags (i % 3 == 1)
+    std::vector<uint64_t> wide(17);
+    std::vector<uint8_t> bflags(17);
+    for (int i = 0; i < 17; ++i) {
+        wide[i] = (uint64_t(1) << 40) | uint64_t(i / 3);
+        bflags[i] = i % 3 == 1;
+    }
+    emit("sel_wide_in", wide);
+    emit("sel_wide_flags", bflags);
+    std::vector<uint64_t> wf;
+    for (int i = 0; i < 17; ++i)
+        if (bflags[i]) wf.push_back(wide[i]);
+    emit("sel_wide_flagged_out", wf);
+    emit("sel_wide_if_even_out", keep(wide, [](uint64_t x) { return x % 2 == 0; }));
+    std::vector<uint64_t> wu = wide;
+    wu.erase(std::unique(wu.begin(), wu.end()), wu.end());
+    emit("sel_wide_unique_out", wu);
+
+    // device_partition_test.cpp:122-204: Flagged (i % 3 == 0) and If(< 7) over 0..11,
+    // rejected items in reverse order after the selected ones
+    std::vector<int32_t> pin(12), pf_out, pi_out;
+    std::vector<uint32_t> pflags(12);
+    for (int i = 0; i < 12; ++i) {
+        pin[i] = i;
+        pflags[i] = i % 3 == 0;
+    }
+    for (int i = 0; i < 12; ++i) {
+        if (pflags[i]) pf_out.push_back(pin[i]);
+        if (pin[i] < 7) pi_out.push_back(pin[i]);
+    }
+    for (int i = 12; i-- > 0;) {
+        if (!pflags[i]) pf_out.push_back(pin[i]);
+        if (pin[i] >= 7) pi_out.push_back(pin[i]);
+    }
+    emit("part_in", pin);
+    emit("part_flags", pflags);
+    emit("part_flagged_out", pf_out);
+    emit("part_if_lt7_out", pi_out);
+
+    // :293-353: three-way, first = divisible by 3, second = < 8
+    std::vector<int32_t> first, second, rest;
+    for (int i = 0; i < 12; ++i) {
+        if (i % 3 == 0) first.push_back(i);
+        else if (i < 8) second.push_back(i);
+    }
+    for (int i = 12; i-- > 0;)
+        if (i % 3 != 0 && i >= 8) rest.push_back(i);
+    emit("part3_first_out", first);
+    emit("part3_second_out", second);
+    emit("part3_unselected_out", rest);
+}
+
 // tests/device_segmented_sort_test.cpp:22-56 and :260-268 -- 19 items in
 // segments [1,4) [5,5) [5,9) [10,19); keys outside every segment are -777
 // and their values UINT_MAX; expected = std::stable_sort per segment with
@@ -382,6 +506,7 @@ int main(int argc, char** argv)
     reduce_cases();
     arg_cases();
     by_key_cases();
+    select_cases();
     segmented_cases();
     decomposed_cases();
     std::fclose(g_index);

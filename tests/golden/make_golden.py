@@ -20,7 +20,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 STORE_LIMIT = 4096
-DTYPES = {"u32": np.uint32, "i32": np.int32, "f32": np.float32, "u64": np.uint64, "i64": np.int64}
+DTYPES = {"u32": np.uint32, "i32": np.int32, "f32": np.float32, "u64": np.uint64, "i64": np.int64, "u8": np.uint8}
 
 
 def is_expected_output(name: str) -> bool:

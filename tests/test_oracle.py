@@ -265,6 +265,52 @@ def test_by_key_vs_numpy(oracle, kdt, vdt):
     np.testing.assert_array_equal(agg, np.array([x.sum() for x in segs], dtype=vdt))
 
 
+def test_select_golden(oracle, golden):
+    """device_select_test.cpp:114-500: Flagged, If, FlaggedIf, Unique, UniqueByKey, in-place cases."""
+    g = golden
+    np.testing.assert_array_equal(oracle.select(g["sel_stable_in"], g["sel_stable_flags"] != 0),
+                                  g["sel_stable_flagged_out"])
+    x = g["sel_stable_in"]
+    np.testing.assert_array_equal(oracle.select(x, oracle.clause_mask(x, [(6, 0, 2, 0)])), g["sel_stable_if_even_out"])
+    k, v = g["sel_unique_keys"], g["sel_unique_values"]
+    m = oracle.unique_mask(k)
+    np.testing.assert_array_equal(k[m], g["sel_unique_keys_out"])
+    np.testing.assert_array_equal(v[m], g["sel_unique_values_out"])
+    f = g["sel_flaggedif_flags"]
+    pos_odd = oracle.clause_mask(f, [(2, 0, 0, 0), (6, 1, 2, 0)])  # flag > 0 and not (flag % 2 == 0)
+    np.testing.assert_array_equal(oracle.select(g["sel_flaggedif_in"], pos_odd), g["sel_flaggedif_out"])
+    a = g["sel_inplace_aliased"]
+    np.testing.assert_array_equal(oracle.select(a, a != 0), g["sel_inplace_aliased_out"])
+    p = g["sel_inplace_pred"]
+    np.testing.assert_array_equal(oracle.select(p, oracle.clause_mask(p, [(2, 0, 0, 0)])), g["sel_inplace_pred_out"])
+    u = g["sel_inplace_unique"]
+    np.testing.assert_array_equal(u[oracle.unique_mask(u)], g["sel_inplace_unique_out"])
+    w = g["sel_wide_in"]
+    np.testing.assert_array_equal(oracle.select(w, g["sel_wide_flags"] != 0), g["sel_wide_flagged_out"])
+    np.testing.assert_array_equal(oracle.select(w, oracle.clause_mask(w, [(6, 0, 2, 0)])), g["sel_wide_if_even_out"])
+    np.testing.assert_array_equal(w[oracle.unique_mask(w)], g["sel_wide_unique_out"])
+
+
+def test_partition_golden(oracle, golden):
+    """device_partition_test.cpp:122-353: reversed rejects; three-way category order."""
+    x = golden["part_in"]
+    np.testing.assert_array_equal(oracle.partition(x, golden["part_flags"] != 0), golden["part_flagged_out"])
+    np.testing.assert_array_equal(oracle.partition(x, oracle.clause_mask(x, [(0, 0, 7, 0)])),
+                                  golden["part_if_lt7_out"])
+    f, s2, r = oracle.partition_three_way(x, oracle.clause_mask(x, [(6, 0, 3, 0)]),
+                                          oracle.clause_mask(x, [(0, 0, 8, 0)]))
+    np.testing.assert_array_equal(f, golden["part3_first_out"])
+    np.testing.assert_array_equal(s2, golden["part3_second_out"])
+    np.testing.assert_array_equal(r, golden["part3_unselected_out"])
+
+
+def test_clause_mask_c_remainder(oracle):
+    """MOD_EQ follows C: -3 % 2 == -1, so -3 is neither even nor "% 2 == 1"."""
+    x = np.array([-4, -3, -1, 0, 1, 2, 3], np.int32)
+    np.testing.assert_array_equal(oracle.clause_mask(x, [(6, 0, 2, 0)]), [1, 0, 0, 1, 0, 1, 0])
+    np.testing.assert_array_equal(oracle.clause_mask(x, [(6, 0, 2, 1)]), [0, 0, 0, 0, 1, 0, 1])
+
+
 def test_reduce_identities(oracle):
     """device_reduce_test.cpp:95-118 (ones, 2^k+1) and :220-236 (float max identity)."""
     for k in range(0, 16):
