@@ -34,6 +34,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <cstring>
 #include <stdexcept>
 #include <string>
 #include <type_traits>
@@ -1048,6 +1049,340 @@ private:
     {
         detail::require(o.size() >= 1 && idx.size() >= 1, "DeviceReduce: extremum output view is empty");
         detail::require(i.size() >= n, "DeviceReduce: the input view is shorter than num_items");
+    }
+};
+
+// ---------------------------------------------------------------------------
+// DeviceSelect / DevicePartition
+// ---------------------------------------------------------------------------
+
+/// A predicate that crosses the C ABI: the AND of up to LCPP_MAX_CLAUSES
+/// clauses on a value of type T (lt, le, gt, ge, eq, ne against a constant;
+/// mod_eq(m, r): x % m == r; bits_any(mask): (x & mask) != 0), each negatable
+/// with `!`.  Under nvcc the DeviceSelect / DevicePartition methods also take
+/// any __device__ callable bool(T).
+template <typename T>
+class Predicate {
+public:
+    static Predicate lt(T a) { return one(LCPP_CLAUSE_LT, a); }
+    static Predicate le(T a) { return one(LCPP_CLAUSE_LE, a); }
+    static Predicate gt(T a) { return one(LCPP_CLAUSE_GT, a); }
+    static Predicate ge(T a) { return one(LCPP_CLAUSE_GE, a); }
+    static Predicate eq(T a) { return one(LCPP_CLAUSE_EQ, a); }
+    static Predicate ne(T a) { return one(LCPP_CLAUSE_NE, a); }
+    static Predicate mod_eq(T m, T r) { return one(LCPP_CLAUSE_MOD_EQ, m, r); }
+    static Predicate bits_any(T mask) { return one(LCPP_CLAUSE_BITS_ANY, mask); }
+    static Predicate always() { return Predicate{}; }
+
+    Predicate operator&(const Predicate& o) const
+    {
+        detail::require(n_ + o.n_ <= LCPP_MAX_CLAUSES, "Predicate: too many clauses");
+        Predicate r = *this;
+        for (int i = 0; i < o.n_; ++i) r.c_[r.n_++] = o.c_[i];
+        return r;
+    }
+    Predicate operator!() const
+    {
+        detail::require(n_ == 1, "Predicate: ! applies to a single clause");
+        Predicate r = *this;
+        r.c_[0].negate = !r.c_[0].negate;
+        return r;
+    }
+    const lcpp_clause* data() const { return c_; }
+    int size() const { return n_; }
+
+private:
+    static uint64_t bits(T v)
+    {
+        static_assert(sizeof(T) == 1 || sizeof(T) == 4 || sizeof(T) == 8, "1-, 4- or 8-byte values");
+        uint64_t b = 0;
+        std::memcpy(&b, &v, sizeof(T));
+        return b;
+    }
+    static Predicate one(int kind, T a, T b = T(0))
+    {
+        Predicate p;
+        p.c_[0] = lcpp_clause{kind, 0, bits(a), bits(b)};
+        p.n_ = 1;
+        return p;
+    }
+    lcpp_clause c_[LCPP_MAX_CLAUSES] = {};
+    int n_ = 0;
+};
+
+namespace detail {
+template <typename P>
+struct is_predicate : std::false_type {};
+template <typename T>
+struct is_predicate<Predicate<T>> : std::true_type {};
+
+template <typename F>
+constexpr lcpp_dtype flag_dtype()
+{
+    if constexpr (std::is_same_v<F, bool> || (std::is_integral_v<F> && sizeof(F) == 1))
+        return LCPP_U8;
+    else
+        return checked_dtype<F>();
+}
+
+inline void require_views(bool ok) { require(ok, "a view is shorter than num_items, or a count view is empty"); }
+}  // namespace detail
+
+class DeviceSelect {
+public:
+    static size_t GetTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_select_temp_bytes(num_items, &b), "GetTempStorageBytes");
+        return b;
+    }
+
+    /// Items whose flag != 0, in order (device_select.h:65-104).
+    template <typename T, typename F>
+    void Flagged(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> input,
+                 BufferView<F> selection_flags, BufferView<T> output, BufferView<uint32_t> num_selected_out,
+                 uint64_t num_items)
+    {
+        detail::require_views(input.size() >= num_items && selection_flags.size() >= num_items &&
+                              output.size() >= num_items && num_selected_out.size() >= 1);
+        detail::check(lcpp_select_flagged(temp_storage.data(), detail::temp_bytes(temp_storage), input.data(),
+                                          selection_flags.data(), output.data(), num_selected_out.data(), num_items,
+                                          detail::checked_dtype<T>(), detail::flag_dtype<F>(), stream),
+                      "Flagged");
+    }
+
+    /// In place (device_select.h:106-117).
+    template <typename T, typename F>
+    void Flagged(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> data,
+                 BufferView<F> selection_flags, BufferView<uint32_t> num_selected_out, uint64_t num_items)
+    {
+        Flagged(stream, temp_storage, data, selection_flags, data, num_selected_out, num_items);
+    }
+
+    /// Items with pred(item) (device_select.h:119-158).
+    template <typename T, typename P>
+    void If(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> input, BufferView<T> output,
+            BufferView<uint32_t> num_selected_out, uint64_t num_items, const P& pred)
+    {
+        detail::require_views(input.size() >= num_items && output.size() >= num_items && num_selected_out.size() >= 1);
+        if constexpr (detail::is_predicate<P>::value) {
+            static_assert(std::is_same_v<P, Predicate<T>>, "If: the Predicate's type must be the item type");
+            detail::check(lcpp_select_if(temp_storage.data(), detail::temp_bytes(temp_storage), input.data(),
+                                         output.data(), num_selected_out.data(), num_items,
+                                         detail::checked_dtype<T>(), pred.data(), pred.size(), stream),
+                          "If");
+        } else {
+#ifdef __CUDACC__
+            detail::check_cuda(device::select_if(temp_storage.data(), detail::temp_bytes(temp_storage), input.data(),
+                                                 output.data(), num_selected_out.data(), num_items, pred,
+                                                 reinterpret_cast<cudaStream_t>(stream)),
+                               "If");
+#else
+            static_assert(detail::is_predicate<P>::value, "callable predicates need nvcc (lcpp_b200_device.cuh)");
+#endif
+        }
+    }
+
+    /// In place (device_select.h:160-175).
+    template <typename T, typename P>
+    void If(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> data,
+            BufferView<uint32_t> num_selected_out, uint64_t num_items, const P& pred)
+    {
+        If(stream, temp_storage, data, data, num_selected_out, num_items, pred);
+    }
+
+    /// Items whose flag satisfies pred (device_select.h:177-199).
+    template <typename T, typename F, typename P>
+    void FlaggedIf(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> input,
+                   BufferView<F> selection_flags, BufferView<T> output, BufferView<uint32_t> num_selected_out,
+                   uint64_t num_items, const P& pred)
+    {
+        detail::require_views(input.size() >= num_items && selection_flags.size() >= num_items &&
+                              output.size() >= num_items && num_selected_out.size() >= 1);
+        if constexpr (detail::is_predicate<P>::value) {
+            detail::check(lcpp_select_flagged_if(temp_storage.data(), detail::temp_bytes(temp_storage), input.data(),
+                                                 selection_flags.data(), output.data(), num_selected_out.data(),
+                                                 num_items, detail::checked_dtype<T>(), detail::flag_dtype<F>(),
+                                                 pred.data(), pred.size(), stream),
+                          "FlaggedIf");
+        } else {
+#ifdef __CUDACC__
+            detail::check_cuda(device::select_flagged(temp_storage.data(), detail::temp_bytes(temp_storage),
+                                                      input.data(), selection_flags.data(), output.data(),
+                                                      num_selected_out.data(), num_items, pred,
+                                                      reinterpret_cast<cudaStream_t>(stream)),
+                               "FlaggedIf");
+#else
+            static_assert(detail::is_predicate<P>::value, "callable predicates need nvcc (lcpp_b200_device.cuh)");
+#endif
+        }
+    }
+
+    /// In place (device_select.h:201-212).
+    template <typename T, typename F, typename P>
+    void FlaggedIf(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> data,
+                   BufferView<F> selection_flags, BufferView<uint32_t> num_selected_out, uint64_t num_items,
+                   const P& pred)
+    {
+        FlaggedIf(stream, temp_storage, data, selection_flags, data, num_selected_out, num_items, pred);
+    }
+
+    /// First item of every run of equal items (device_select.h:214-286).
+    template <typename T>
+    void Unique(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> input, BufferView<T> output,
+                BufferView<uint32_t> num_selected_out, uint64_t num_items)
+    {
+        detail::require_views(input.size() >= num_items && output.size() >= num_items && num_selected_out.size() >= 1);
+        detail::check(lcpp_select_unique(temp_storage.data(), detail::temp_bytes(temp_storage), input.data(),
+                                         output.data(), num_selected_out.data(), num_items,
+                                         detail::checked_dtype<T>(), stream),
+                      "Unique");
+    }
+
+    template <typename T>
+    void Unique(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> data,
+                BufferView<uint32_t> num_selected_out, uint64_t num_items)
+    {
+        Unique(stream, temp_storage, data, data, num_selected_out, num_items);
+    }
+
+    /// First (key, value) of every run of equal keys (device_select.h:288-333).
+    template <typename K, typename V>
+    void UniqueByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> keys_input,
+                     BufferView<V> values_input, BufferView<K> keys_output, BufferView<V> values_output,
+                     BufferView<uint32_t> num_selected_out, uint64_t num_items)
+    {
+        detail::require_views(keys_input.size() >= num_items && values_input.size() >= num_items &&
+                              keys_output.size() >= num_items && values_output.size() >= num_items &&
+                              num_selected_out.size() >= 1);
+        detail::check(lcpp_select_unique_by_key(temp_storage.data(), detail::temp_bytes(temp_storage),
+                                                keys_input.data(), values_input.data(), keys_output.data(),
+                                                values_output.data(), num_selected_out.data(), num_items,
+                                                detail::checked_dtype<K>(), detail::checked_dtype<V>(), stream),
+                      "UniqueByKey");
+    }
+
+#ifdef __CUDACC__
+    /// The equality overloads (device_select.h:233-333): `equality` is a
+    /// __device__ callable bool(T, T) "same run".
+    template <typename T, typename Eq, typename = std::enable_if_t<!std::is_arithmetic_v<Eq>>>
+    void Unique(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> input, BufferView<T> output,
+                BufferView<uint32_t> num_selected_out, uint64_t num_items, Eq equality)
+    {
+        detail::require_views(input.size() >= num_items && output.size() >= num_items && num_selected_out.size() >= 1);
+        detail::check_cuda(device::select_unique(temp_storage.data(), detail::temp_bytes(temp_storage), input.data(),
+                                                 output.data(), num_selected_out.data(), num_items, equality,
+                                                 reinterpret_cast<cudaStream_t>(stream)),
+                           "Unique");
+    }
+
+    template <typename T, typename Eq, typename = std::enable_if_t<!std::is_arithmetic_v<Eq>>>
+    void Unique(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> data,
+                BufferView<uint32_t> num_selected_out, uint64_t num_items, Eq equality)
+    {
+        Unique(stream, temp_storage, data, data, num_selected_out, num_items, equality);
+    }
+
+    template <typename K, typename V, typename Eq>
+    void UniqueByKey(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<K> keys_input,
+                     BufferView<V> values_input, BufferView<K> keys_output, BufferView<V> values_output,
+                     BufferView<uint32_t> num_selected_out, uint64_t num_items, Eq equality)
+    {
+        detail::require_views(keys_input.size() >= num_items && values_input.size() >= num_items &&
+                              keys_output.size() >= num_items && values_output.size() >= num_items &&
+                              num_selected_out.size() >= 1);
+        detail::check_cuda(device::select_unique_by_key(temp_storage.data(), detail::temp_bytes(temp_storage),
+                                                        keys_input.data(), values_input.data(), keys_output.data(),
+                                                        values_output.data(), num_selected_out.data(), num_items,
+                                                        equality, reinterpret_cast<cudaStream_t>(stream)),
+                           "UniqueByKey");
+    }
+#endif
+};
+
+class DevicePartition {
+public:
+    static size_t GetTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_partition_temp_bytes(num_items, &b), "GetTempStorageBytes");
+        return b;
+    }
+    static size_t GetThreeWayTempStorageBytes(uint64_t num_items)
+    {
+        size_t b = 0;
+        detail::check(lcpp_partition_three_way_temp_bytes(num_items, &b), "GetThreeWayTempStorageBytes");
+        return b;
+    }
+
+    /// Selected items in order, then the rejected ones in reverse order
+    /// (device_partition.h:73-113).
+    template <typename T, typename F>
+    void Flagged(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> input,
+                 BufferView<F> selection_flags, BufferView<T> output, BufferView<uint32_t> num_selected_out,
+                 uint64_t num_items)
+    {
+        detail::require_views(input.size() >= num_items && selection_flags.size() >= num_items &&
+                              output.size() >= num_items && num_selected_out.size() >= 1);
+        detail::check(lcpp_partition_flagged(temp_storage.data(), detail::temp_bytes(temp_storage), input.data(),
+                                             selection_flags.data(), output.data(), num_selected_out.data(),
+                                             num_items, detail::checked_dtype<T>(), detail::flag_dtype<F>(), stream),
+                      "Flagged");
+    }
+
+    /// device_partition.h:115-155.
+    template <typename T, typename P>
+    void If(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> input, BufferView<T> output,
+            BufferView<uint32_t> num_selected_out, uint64_t num_items, const P& pred)
+    {
+        detail::require_views(input.size() >= num_items && output.size() >= num_items && num_selected_out.size() >= 1);
+        if constexpr (detail::is_predicate<P>::value) {
+            detail::check(lcpp_partition_if(temp_storage.data(), detail::temp_bytes(temp_storage), input.data(),
+                                            output.data(), num_selected_out.data(), num_items,
+                                            detail::checked_dtype<T>(), pred.data(), pred.size(), stream),
+                          "If");
+        } else {
+#ifdef __CUDACC__
+            detail::check_cuda(device::partition_if(temp_storage.data(), detail::temp_bytes(temp_storage),
+                                                    input.data(), output.data(), num_selected_out.data(), num_items,
+                                                    pred, reinterpret_cast<cudaStream_t>(stream)),
+                               "If");
+#else
+            static_assert(detail::is_predicate<P>::value, "callable predicates need nvcc (lcpp_b200_device.cuh)");
+#endif
+        }
+    }
+
+    /// Three-way (device_partition.h:157-227): num_selected_out[0] / [1] =
+    /// the first / second counts; unselected items in reverse order.
+    template <typename T, typename P1, typename P2>
+    void If(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> input, BufferView<T> first_output,
+            BufferView<T> second_output, BufferView<T> unselected_output, BufferView<uint32_t> num_selected_out,
+            uint64_t num_items, const P1& select_first, const P2& select_second)
+    {
+        detail::require_views(input.size() >= num_items && first_output.size() >= num_items &&
+                              second_output.size() >= num_items && unselected_output.size() >= num_items &&
+                              num_selected_out.size() >= 2);
+        if constexpr (detail::is_predicate<P1>::value && detail::is_predicate<P2>::value) {
+            detail::check(lcpp_partition_if_three_way(temp_storage.data(), detail::temp_bytes(temp_storage),
+                                                      input.data(), first_output.data(), second_output.data(),
+                                                      unselected_output.data(), num_selected_out.data(), num_items,
+                                                      detail::checked_dtype<T>(), select_first.data(),
+                                                      select_first.size(), select_second.data(),
+                                                      select_second.size(), stream),
+                          "If");
+        } else {
+#ifdef __CUDACC__
+            detail::check_cuda(device::partition_three_way(temp_storage.data(), detail::temp_bytes(temp_storage),
+                                                           input.data(), first_output.data(), second_output.data(),
+                                                           unselected_output.data(), num_selected_out.data(),
+                                                           num_items, select_first, select_second,
+                                                           reinterpret_cast<cudaStream_t>(stream)),
+                               "If");
+#else
+            static_assert(detail::is_predicate<P1>::value, "callable predicates need nvcc (lcpp_b200_device.cuh)");
+#endif
+        }
     }
 };
 

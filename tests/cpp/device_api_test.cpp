@@ -311,6 +311,102 @@ void by_key(lcpp_stream_t s)
     }
 }
 
+void select_partition(lcpp_stream_t s)
+{
+    // device_select_test.cpp:254-320: Flagged (7 at i % 3 == 1) and If(even)
+    {
+        const size_t n = 17;
+        std::vector<int32_t> in(n);
+        std::vector<uint32_t> flags(n);
+        std::vector<int32_t> want_f, want_e;
+        for (size_t i = 0; i < n; ++i) {
+            in[i] = int32_t(100 + i);
+            flags[i] = i % 3 == 1 ? 7u : 0u;
+            if (flags[i]) want_f.push_back(in[i]);
+            if (in[i] % 2 == 0) want_e.push_back(in[i]);
+        }
+        DeviceArray<int32_t> din(n), out(n);
+        DeviceArray<uint32_t> df(n), cnt(1);
+        din.upload(in);
+        df.upload(flags);
+        auto temp = temp_for(DeviceSelect::GetTempStorageBytes(n));
+        DeviceSelect sel;
+        sel.Flagged(s, temp.view(), din.view(), df.view(), out.view(), cnt.view(), n);
+        CUDA(cudaStreamSynchronize(s));
+        auto got = out.download();
+        CHECK(cnt.download()[0] == want_f.size());
+        CHECK(std::equal(want_f.begin(), want_f.end(), got.begin()));
+        sel.If(s, temp.view(), din.view(), out.view(), cnt.view(), n, Predicate<int32_t>::mod_eq(2, 0));
+        CUDA(cudaStreamSynchronize(s));
+        got = out.download();
+        CHECK(cnt.download()[0] == want_e.size());
+        CHECK(std::equal(want_e.begin(), want_e.end(), got.begin()));
+        // in place: If(> 0 and odd) on the input itself
+        sel.If(s, temp.view(), din.view(), cnt.view(), n, Predicate<int32_t>::gt(0) & !Predicate<int32_t>::mod_eq(2, 0));
+        CUDA(cudaStreamSynchronize(s));
+        got = din.download();
+        CHECK(cnt.download()[0] == 8u);
+        for (int i = 0; i < 8; ++i) CHECK(got[i] == 101 + 2 * i);
+    }
+    // :322-372: Unique / UniqueByKey keep the first item of each run
+    {
+        const std::vector<int32_t> keys{1, 1, 2, 2, 2, 4, 7, 7, 9}, values{10, 11, 20, 21, 22, 40, 70, 71, 90};
+        const size_t n = keys.size();
+        DeviceArray<int32_t> dk(n), dv(n), ko(n), vo(n);
+        DeviceArray<uint32_t> cnt(1);
+        dk.upload(keys);
+        dv.upload(values);
+        auto temp = temp_for(DeviceSelect::GetTempStorageBytes(n));
+        DeviceSelect sel;
+        sel.UniqueByKey(s, temp.view(), dk.view(), dv.view(), ko.view(), vo.view(), cnt.view(), n);
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(cnt.download()[0] == 5u);
+        const auto gk = ko.download(), gv = vo.download();
+        const int32_t ek[5] = {1, 2, 4, 7, 9}, ev[5] = {10, 20, 40, 70, 90};
+        for (int i = 0; i < 5; ++i) CHECK(gk[i] == ek[i] && gv[i] == ev[i]);
+        sel.Unique(s, temp.view(), dk.view(), cnt.view(), n);  // in place
+        CUDA(cudaStreamSynchronize(s));
+        const auto gu = dk.download();
+        CHECK(cnt.download()[0] == 5u);
+        for (int i = 0; i < 5; ++i) CHECK(gu[i] == ek[i]);
+    }
+    // device_partition_test.cpp:122-204 and :293-353
+    {
+        const size_t n = 12;
+        std::vector<int32_t> in(n);
+        std::vector<uint8_t> flags(n);
+        std::vector<int32_t> want;
+        for (size_t i = 0; i < n; ++i) {
+            in[i] = int32_t(i);
+            flags[i] = i % 3 == 0;
+            if (flags[i]) want.push_back(in[i]);
+        }
+        for (size_t i = n; i-- > 0;)
+            if (!flags[i]) want.push_back(in[i]);
+        DeviceArray<int32_t> din(n), out(n), o1(n), o2(n), o3(n);
+        DeviceArray<uint8_t> df(n);
+        DeviceArray<uint32_t> cnt(2);
+        din.upload(in);
+        df.upload(flags);
+        auto temp = temp_for(DevicePartition::GetThreeWayTempStorageBytes(n));
+        DevicePartition part;
+        part.Flagged(s, temp.view(), din.view(), df.view(), out.view(), cnt.view().subview(0, 1), n);
+        CUDA(cudaStreamSynchronize(s));
+        CHECK(cnt.download()[0] == 4u);
+        CHECK(out.download() == want);
+        part.If(s, temp.view(), din.view(), o1.view(), o2.view(), o3.view(), cnt.view(), n,
+                Predicate<int32_t>::mod_eq(3, 0), Predicate<int32_t>::lt(8));
+        CUDA(cudaStreamSynchronize(s));
+        const auto c = cnt.download();
+        CHECK(c[0] == 4u && c[1] == 5u);
+        const auto g1 = o1.download(), g2 = o2.download(), g3 = o3.download();
+        const int32_t e1[4] = {0, 3, 6, 9}, e2[5] = {1, 2, 4, 5, 7}, e3[3] = {11, 10, 8};
+        for (int i = 0; i < 4; ++i) CHECK(g1[i] == e1[i]);
+        for (int i = 0; i < 5; ++i) CHECK(g2[i] == e2[i]);
+        for (int i = 0; i < 3; ++i) CHECK(g3[i] == e3[i]);
+    }
+}
+
 void reductions(lcpp_stream_t s)
 {
     // device_reduce_test.cpp: ones at 2^k + 1; float max identity on empty input
@@ -461,6 +557,7 @@ int main()
     reductions(s);
     arg_reductions(s);
     by_key(s);
+    select_partition(s);
     segmented(s);
     decomposed(s);
     misuse_throws(s);

@@ -9,7 +9,9 @@
 // "OK <checks>" and exits 0 on success.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
+#include <iterator>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -262,6 +264,93 @@ void by_key_cases(lcpp_stream_t s)
     }
 }
 
+struct PositiveOdd {
+    __host__ __device__ bool operator()(int f) const { return f > 0 && f % 2 != 0; }
+};
+struct DivisibleBy {
+    int d;
+    __host__ __device__ bool operator()(int x) const { return x % d == 0; }
+};
+struct Below {
+    int b;
+    __host__ __device__ bool operator()(int x) const { return x < b; }
+};
+
+void select_cases(lcpp_stream_t s)
+{
+    DeviceSelect sel;
+    // device_select_test.cpp:432-500: Unique in place under "same parity"
+    {
+        const std::vector<int> data{1, 3, 2, 4, 5, 7, 8, 10};
+        DeviceArray<int> d(8);
+        DeviceArray<uint32_t> cnt(1);
+        d.upload(data);
+        auto temp = temp_for(DeviceSelect::GetTempStorageBytes(8));
+        sel.Unique(s, temp.view(), d.view(), cnt.view(), 8, SameParity{});
+        CUDA(cudaStreamSynchronize(s));
+        std::vector<int> got(4);
+        CUDA(cudaMemcpy(got.data(), d.p, 4 * sizeof(int), cudaMemcpyDeviceToHost));
+        CHECK(cnt.first() == 4u);
+        CHECK((got == std::vector<int>{1, 2, 5, 8}));
+    }
+    // :374-430: FlaggedIf with a functor over flags -3..5
+    {
+        std::vector<int> in(9), flags(9);
+        for (int i = 0; i < 9; ++i) {
+            in[i] = 100 + i;
+            flags[i] = i - 3;
+        }
+        DeviceArray<int> din(9), df(9), out(9);
+        DeviceArray<uint32_t> cnt(1);
+        din.upload(in);
+        df.upload(flags);
+        auto temp = temp_for(DeviceSelect::GetTempStorageBytes(9));
+        sel.FlaggedIf(s, temp.view(), din.view(), df.view(), out.view(), cnt.view(), 9, PositiveOdd{});
+        CUDA(cudaStreamSynchronize(s));
+        std::vector<int> got(3);
+        CUDA(cudaMemcpy(got.data(), out.p, 3 * sizeof(int), cudaMemcpyDeviceToHost));
+        CHECK(cnt.first() == 3u);
+        CHECK((got == std::vector<int>{104, 106, 108}));
+    }
+    // random: If with a stateful functor vs std::copy_if; partition three-way
+    std::mt19937 rng(5);
+    for (size_t n : {size_t(1), size_t(4097), size_t(1000003)}) {
+        std::vector<int> in(n);
+        for (auto& x : in) x = int(rng() % 1000) - 500;
+        DeviceArray<int> din(n), o1(n), o2(n), o3(n);
+        DeviceArray<uint32_t> cnt(2);
+        din.upload(in);
+        auto temp = temp_for(DevicePartition::GetThreeWayTempStorageBytes(n));
+        sel.If(s, temp.view(), din.view(), o1.view(), cnt.view(), n, DivisibleBy{7});
+        CUDA(cudaStreamSynchronize(s));
+        std::vector<int> want, got(n);
+        std::copy_if(in.begin(), in.end(), std::back_inserter(want), DivisibleBy{7});
+        CHECK(cnt.first() == want.size());
+        CUDA(cudaMemcpy(got.data(), o1.p, n * sizeof(int), cudaMemcpyDeviceToHost));
+        CHECK(std::equal(want.begin(), want.end(), got.begin()));
+        DevicePartition part;
+        part.If(s, temp.view(), din.view(), o1.view(), o2.view(), o3.view(), cnt.view(), n, DivisibleBy{3}, Below{0});
+        CUDA(cudaStreamSynchronize(s));
+        std::vector<int> w1, w2, w3;
+        for (int x : in) {
+            if (x % 3 == 0) w1.push_back(x);
+            else if (x < 0) w2.push_back(x);
+        }
+        for (size_t i = n; i-- > 0;)
+            if (in[i] % 3 != 0 && in[i] >= 0) w3.push_back(in[i]);
+        std::vector<uint32_t> c(2);
+        CUDA(cudaMemcpy(c.data(), cnt.p, 8, cudaMemcpyDeviceToHost));
+        CHECK(c[0] == w1.size() && c[1] == w2.size());
+        std::vector<int> g1(n), g2(n), g3(n);
+        CUDA(cudaMemcpy(g1.data(), o1.p, n * sizeof(int), cudaMemcpyDeviceToHost));
+        CUDA(cudaMemcpy(g2.data(), o2.p, n * sizeof(int), cudaMemcpyDeviceToHost));
+        CUDA(cudaMemcpy(g3.data(), o3.p, n * sizeof(int), cudaMemcpyDeviceToHost));
+        CHECK(std::equal(w1.begin(), w1.end(), g1.begin()));
+        CHECK(std::equal(w2.begin(), w2.end(), g2.begin()));
+        CHECK(std::equal(w3.begin(), w3.end(), g3.begin()));
+    }
+}
+
 }  // namespace
 
 int main()
@@ -273,6 +362,7 @@ int main()
     empty_sentinels(s);
     random_cases(s);
     by_key_cases(s);
+    select_cases(s);
     CUDA(cudaStreamDestroy(stream));
     std::printf("OK %d\n", g_checks);
     return 0;
