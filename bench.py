@@ -341,6 +341,8 @@ class Workload:
         L = self.L
         if self.op in ("scan",):
             return L.KERNEL_SCAN
+        if self.op.endswith("by_key"):
+            return L.KERNEL_BY_KEY
         if self.op.startswith("reduce"):
             return L.KERNEL_REDUCE
         if self.op == "segsort":

@@ -537,7 +537,7 @@ __device__ __forceinline__ void store_group(T* p, uint64_t n, uint64_t g, bool v
  * kModeInclusiveInit write out[]; kModeReduce writes unique_out[],
  * out[] (= the aggregates) and *num_runs. */
 template <typename K, typename V, bool COUNT, typename Equal, typename Op>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock, (sizeof(K) + sizeof(V) <= 8) ? 3 : 2)
 by_key_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* num_runs, uint64_t n, int mode,
               V init, bool vector, Ctrl* ctrl, TileStatus<V> ts, Equal equal, Op op)
 {
@@ -606,7 +606,7 @@ by_key_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* n
             if (lane >= d) x = seg<COUNT>(y, x, op);
         }
         Acc<V> ex = shfl_up_acc(x, 1);
-        if (lane == 0) ex.has = 0;
+        if (lane == 0) ex = Acc<V>{0, 0, V{}};
         pre[j] = seg<COUNT>(carry, ex, op);
         carry = seg<COUNT>(carry, shfl_acc(x, 31), op);
     }
@@ -621,7 +621,7 @@ by_key_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* n
             if (lane >= d) x = seg<COUNT>(y, x, op);
         }
         Acc<V> ex = shfl_up_acc(x, 1);
-        if (lane == 0) ex.has = 0;
+        if (lane == 0) ex = Acc<V>{0, 0, V{}};
         if (lane < kWarps) s_excl[lane] = ex;
         const Acc<V> aggregate = shfl_acc(x, kWarps - 1);
         Acc<V> prefix{0, 0, V{}};
@@ -649,7 +649,7 @@ by_key_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* n
             Acc<V> P;
             P.has = 1;
             if (h || !E.has) {
-                P.c = COUNT ? E.c + uint32_t(h) : uint32_t(h);
+                P.c = COUNT ? (E.has ? E.c : 0u) + uint32_t(h) : uint32_t(h);
                 P.v = v[j][e];
             } else {
                 P.c = E.c;
