@@ -110,3 +110,71 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     monkeypatch.setattr(lcpp_b200, "LIB_PATH", tmp_path / "nope.so")
     with pytest.raises(ImportError):
         lcpp_b200.lib()
+
+
+def test_misuse_new_families_without_device(lcpp):
+    """ArgMin/ArgMax, the by-key scans, ReduceByKey, DeviceSelect and
+    DevicePartition reject bad arguments before any device work."""
+    lib = lcpp.lib()
+    vp = ctypes.c_void_p
+    a, b, c = vp(0x100000), vp(0x200000), vp(0x300000)  # never dereferenced
+    big = 1 << 20
+
+    def clauses(*cl):
+        return (lcpp.Clause * max(1, len(cl)))(*[lcpp.Clause(*x) for x in cl]), len(cl)
+
+    # ArgMin / ArgMax: uint32 indices, 4- and 8-byte types only
+    assert lib.lcpp_reduce_argmin(a, big, b, c, c, 1 << 32, lcpp.I32, None) == lcpp.ERR_INVALID_ARG
+    assert lib.lcpp_reduce_argmax(a, big, b, c, c, 10, lcpp.U8, None) == lcpp.ERR_UNSUPPORTED_DTYPE
+    assert lib.lcpp_reduce_argmin(a, big, b, None, c, 10, lcpp.I32, None) == lcpp.ERR_INVALID_ARG
+    # by-key scans: init required for the exclusive form; temp size; dtypes; operator
+    assert lib.lcpp_scan_exclusive_by_key(a, big, b, c, c, 10, lcpp.OP_SUM, None, lcpp.I32, lcpp.I32,
+                                          None) == lcpp.ERR_INVALID_ARG
+    assert lib.lcpp_scan_inclusive_by_key(a, 16, b, c, c, 10, lcpp.OP_SUM, lcpp.I32, lcpp.I32,
+                                          None) == lcpp.ERR_TEMP_TOO_SMALL
+    assert lib.lcpp_scan_inclusive_by_key(a, big, b, c, c, 10, lcpp.OP_SUM, lcpp.U8, lcpp.I32,
+                                          None) == lcpp.ERR_UNSUPPORTED_DTYPE
+    assert lib.lcpp_scan_inclusive_by_key(a, big, b, c, c, 10, 7, lcpp.I32, lcpp.I32, None) == lcpp.ERR_INVALID_ARG
+    assert lib.lcpp_scan_inclusive_sum_by_key(None, 0, None, None, None, 0, lcpp.I32, lcpp.F64, None) == lcpp.OK
+    # ReduceByKey: run count pointer, uint32 counts, no aliasing of unique_out and keys_in
+    assert lib.lcpp_reduce_by_key(a, big, b, c, vp(0x400000), vp(0x500000), None, 10, lcpp.OP_SUM, lcpp.I32,
+                                  lcpp.I32, None) == lcpp.ERR_INVALID_ARG
+    assert lib.lcpp_reduce_by_key(a, big, b, c, vp(0x400000), vp(0x500000), vp(0x600000), 1 << 32, lcpp.OP_SUM,
+                                  lcpp.I32, lcpp.I32, None) == lcpp.ERR_INVALID_ARG
+    assert lib.lcpp_reduce_by_key(a, big, b, c, b, vp(0x500000), vp(0x600000), 10, lcpp.OP_SUM, lcpp.I32,
+                                  lcpp.I32, None) == lcpp.ERR_INVALID_ARG
+    # DeviceSelect: clause checks (no remainder or bit test on floats, m != 0,
+    # at most LCPP_MAX_CLAUSES, known kinds), item and flag dtypes, count pointer
+    n_sel = vp(0x600000)
+    arr, k = clauses((6, 0, 2, 0))
+    f32_two = 0x40000000
+    assert lib.lcpp_select_if(a, big, b, c, n_sel, 10, lcpp.F32, arr, k, None) == lcpp.ERR_INVALID_ARG
+    arr, k = clauses((7, 0, f32_two, 0))
+    assert lib.lcpp_select_if(a, big, b, c, n_sel, 10, lcpp.F32, arr, k, None) == lcpp.ERR_INVALID_ARG
+    arr, k = clauses((6, 0, 0, 0))
+    assert lib.lcpp_select_if(a, big, b, c, n_sel, 10, lcpp.I32, arr, k, None) == lcpp.ERR_INVALID_ARG
+    arr, k = clauses(*[(0, 0, 1, 0)] * 5)
+    assert lib.lcpp_select_if(a, big, b, c, n_sel, 10, lcpp.I32, arr, k, None) == lcpp.ERR_INVALID_ARG
+    arr, k = clauses((9, 0, 1, 0))
+    assert lib.lcpp_select_if(a, big, b, c, n_sel, 10, lcpp.I32, arr, k, None) == lcpp.ERR_INVALID_ARG
+    assert lib.lcpp_select_if(a, big, b, c, n_sel, 10, lcpp.U8, arr, k, None) == lcpp.ERR_UNSUPPORTED_DTYPE
+    assert lib.lcpp_select_if(a, big, b, c, None, 10, lcpp.I32, arr, k, None) == lcpp.ERR_INVALID_ARG
+    assert lib.lcpp_select_if(a, big, b, c, n_sel, 1 << 32, lcpp.I32, arr, k, None) == lcpp.ERR_INVALID_ARG
+    assert lib.lcpp_select_flagged(a, big, b, c, vp(0x700000), n_sel, 10, lcpp.I32, 99,
+                                   None) == lcpp.ERR_UNSUPPORTED_DTYPE
+    assert lib.lcpp_select_unique(a, 16, b, c, n_sel, 10, lcpp.I64, None) == lcpp.ERR_TEMP_TOO_SMALL
+    # DevicePartition: never in place; three-way outputs must not overlap the
+    # input; the three-way form needs its larger temp storage
+    arr, k = clauses((0, 0, 5, 0))
+    assert lib.lcpp_partition_if(a, big, b, b, n_sel, 10, lcpp.I32, arr, k, None) == lcpp.ERR_INVALID_ARG
+    assert lib.lcpp_partition_flagged(a, big, b, c, b, n_sel, 10, lcpp.I32, lcpp.U8, None) == lcpp.ERR_INVALID_ARG
+    assert lib.lcpp_partition_if_three_way(a, big, b, vp(0x200004), vp(0x800000), vp(0x900000), n_sel, 10,
+                                           lcpp.I32, arr, k, arr, k, None) == lcpp.ERR_INVALID_ARG
+    two, three = ctypes.c_size_t(), ctypes.c_size_t()
+    assert lib.lcpp_partition_temp_bytes(1 << 20, ctypes.byref(two)) == lcpp.OK
+    assert lib.lcpp_partition_three_way_temp_bytes(1 << 20, ctypes.byref(three)) == lcpp.OK
+    assert three.value > two.value > 0
+    assert lib.lcpp_partition_if_three_way(a, two.value, b, vp(0x800000), vp(0x900000), vp(0xA00000), n_sel,
+                                           1 << 20, lcpp.I32, arr, k, arr, k, None) == lcpp.ERR_TEMP_TOO_SMALL
+    zero = ctypes.c_size_t(7)
+    assert lib.lcpp_select_temp_bytes(0, ctypes.byref(zero)) == lcpp.OK and zero.value == 0
