@@ -467,6 +467,20 @@ lcpp_status lcpp_select_unique_by_key(void* temp, size_t temp_bytes, const void*
                                       uint64_t num_items, lcpp_dtype key_dtype, lcpp_dtype value_dtype,
                                       lcpp_stream_t stream);
 
+/* Replace DeviceScan::ExclusiveSumTransform and ExclusiveSumAdjacent
+ * (device_scan.h:387-406; details/scan.h:127-240): d_out[i] (uint32) = the
+ * number of j < i whose item satisfies the clauses (Transform), or that
+ * starts a run of equal items, i.e. j == 0 or d_in[j] != d_in[j - 1]
+ * (Adjacent; == at dtype).  The reference takes 4-byte inputs; 8-byte ones
+ * work too.  Temp storage: lcpp_scan_transform_temp_bytes.  Zero items do
+ * nothing. */
+lcpp_status lcpp_scan_transform_temp_bytes(uint64_t num_items, size_t* temp_bytes);
+lcpp_status lcpp_scan_exclusive_sum_transform(void* temp, size_t temp_bytes, const void* d_in, uint32_t* d_out,
+                                              uint64_t num_items, lcpp_dtype dtype, const lcpp_clause* clauses,
+                                              int num_clauses, lcpp_stream_t stream);
+lcpp_status lcpp_scan_exclusive_sum_adjacent(void* temp, size_t temp_bytes, const void* d_in, uint32_t* d_out,
+                                             uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream);
+
 /* Replace DevicePartition::Flagged / If (device_partition.h:73-155): the
  * selected items in input order from d_out[0], the rejected ones in REVERSE
  * input order from d_out[num_items - 1] down; *d_num_selected_out = the

@@ -808,7 +808,7 @@ constexpr unsigned int kErrTimeout = 5;
 constexpr size_t kAlign = 256;
 enum : uint32_t { kInvalid = 0, kPartial = 1, kInclusive = 2 };
 enum : int { kSelFlag = 0, kSelIf = 1, kSelUnique = 2 };
-enum : int { kOutSelect = 0, kOutPartition = 1, kOutThreeWay = 2 };
+enum : int { kOutSelect = 0, kOutPartition = 1, kOutThreeWay = 2, kOutRanks = 3 };
 
 struct Ctrl {
     unsigned int tile_counter;
@@ -950,9 +950,10 @@ struct Args {
     T* out2;
     T* out3;
     V* vout;
-    uint32_t* num_selected;
+    uint32_t* num_selected;  // may be null for kOutRanks
     uint64_t n;
     bool vector;
+    uint32_t* ranks;  // kOutRanks: the exclusive count of selected items before each item
 };
 
 /* SEL: kSelFlag (pick(flag)), kSelIf (pick(item)), kSelUnique (key change by
@@ -1060,7 +1061,7 @@ compact_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st, Pick
         }
         if (lane == 0) {
             s_prefix = prefix;
-            if (tile == gridDim.x - 1) {
+            if (tile == gridDim.x - 1 && a.num_selected) {
                 a.num_selected[0] = uint32_t(prefix + aggregate);
                 if constexpr (THREE) a.num_selected[1] = uint32_t((prefix + aggregate) >> 32);
             }
@@ -1078,6 +1079,22 @@ compact_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st, Pick
         if constexpr (HAS_V) load4(a.vin, n, g, a.vector, v);
         const uint64_t base = warp_prefix + pre[j];
         uint64_t pos1 = uint32_t(base), pos2 = base >> 32;
+        if constexpr (OUT == kOutRanks) {
+            uint32_t r[kGroup];
+#pragma unroll
+            for (int e = 0; e < kGroup; ++e) {
+                r[e] = uint32_t(pos1);
+                pos1 += (sel1 >> (j * kGroup + e)) & 1u;
+            }
+            if (a.vector && g + kGroup <= n) {
+                *reinterpret_cast<uint4*>(a.ranks + g) = make_uint4(r[0], r[1], r[2], r[3]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < kGroup; ++e)
+                    if (g + e < n) a.ranks[g + e] = r[e];
+            }
+            continue;
+        }
 #pragma unroll
         for (int e = 0; e < kGroup; ++e) {
             const uint64_t i = g + e;
@@ -1125,10 +1142,13 @@ cudaError_t launch(void* temp, size_t temp_bytes, Args<T, F, V> a, Pick pick, Pi
                    cudaStream_t stream)
 {
     constexpr bool THREE = OUT == kOutThreeWay;
-    if (!a.num_selected) return cudaErrorInvalidValue;
+    constexpr bool RANKS = OUT == kOutRanks;
+    if (!a.num_selected && !RANKS) return cudaErrorInvalidValue;
     if (a.n == 0)
-        return cudaMemsetAsync(a.num_selected, 0, (THREE ? 2 : 1) * sizeof(uint32_t), stream);
-    if (a.n > 0xffffffffull || !a.in || !a.out || (THREE && (!a.out2 || !a.out3))) return cudaErrorInvalidValue;
+        return a.num_selected ? cudaMemsetAsync(a.num_selected, 0, (THREE ? 2 : 1) * sizeof(uint32_t), stream)
+                              : cudaSuccess;
+    if (a.n > 0xffffffffull || !a.in || (RANKS ? !a.ranks : !a.out) || (THREE && (!a.out2 || !a.out3)))
+        return cudaErrorInvalidValue;
     if (SEL == kSelFlag && !a.flags) return cudaErrorInvalidValue;
     const Layout L = layout(a.n, THREE);
     if (!temp || reinterpret_cast<uintptr_t>(temp) % kAlign || temp_bytes < L.total) return cudaErrorInvalidValue;
@@ -1148,7 +1168,7 @@ cudaError_t launch(void* temp, size_t temp_bytes, Args<T, F, V> a, Pick pick, Pi
         if (e != cudaSuccess) return e;
     }
     a.vector = aligned16(a.in) && aligned16(a.flags) && aligned16(a.vin) && aligned16(a.out) &&
-               aligned16(a.vout) && aligned16(a.out2) && aligned16(a.out3);
+               aligned16(a.vout) && aligned16(a.out2) && aligned16(a.out3) && aligned16(a.ranks);
     Status<THREE> st{reinterpret_cast<uint64_t*>(t + L.word), reinterpret_cast<uint32_t*>(t + L.second_p),
                      reinterpret_cast<uint32_t*>(t + L.second_i)};
     compact_kernel<T, F, V, SEL, OUT><<<unsigned(L.tiles), kBlock, 0, stream>>>(a, ctrl, st, pick, pick2, equal);
@@ -1179,7 +1199,7 @@ cudaError_t select_flagged(void* temp, size_t temp_bytes, const T* d_in, const F
 {
     using namespace select_detail;
     Args<T, F, NoValue> a{d_in, d_flags, nullptr, d_out, nullptr, nullptr, nullptr, d_num_selected_out, num_items,
-                          false};
+                          false, nullptr};
     return launch<kSelFlag, kOutSelect>(temp, temp_bytes, a, pick, Never{}, EqualTo{}, stream);
 }
 
@@ -1189,7 +1209,7 @@ cudaError_t select_if(void* temp, size_t temp_bytes, const T* d_in, T* d_out, ui
 {
     using namespace select_detail;
     Args<T, T, NoValue> a{d_in, nullptr, nullptr, d_out, nullptr, nullptr, nullptr, d_num_selected_out, num_items,
-                          false};
+                          false, nullptr};
     return launch<kSelIf, kOutSelect>(temp, temp_bytes, a, pick, Never{}, EqualTo{}, stream);
 }
 
@@ -1199,7 +1219,7 @@ cudaError_t select_unique(void* temp, size_t temp_bytes, const T* d_in, T* d_out
 {
     using namespace select_detail;
     Args<T, T, NoValue> a{d_in, nullptr, nullptr, d_out, nullptr, nullptr, nullptr, d_num_selected_out, num_items,
-                          false};
+                          false, nullptr};
     return launch<kSelUnique, kOutSelect>(temp, temp_bytes, a, Never{}, Never{}, equal, stream);
 }
 
@@ -1211,7 +1231,7 @@ cudaError_t select_unique_by_key(void* temp, size_t temp_bytes, const K* d_keys_
     using namespace select_detail;
     if (num_items && (!d_values_in || !d_values_out)) return cudaErrorInvalidValue;
     Args<K, K, V> a{d_keys_in, nullptr, d_values_in, d_keys_out, nullptr, nullptr, d_values_out, d_num_selected_out,
-                    num_items, false};
+                    num_items, false, nullptr};
     return launch<kSelUnique, kOutSelect>(temp, temp_bytes, a, Never{}, Never{}, equal, stream);
 }
 
@@ -1223,7 +1243,7 @@ cudaError_t partition_flagged(void* temp, size_t temp_bytes, const T* d_in, cons
     using namespace select_detail;
     if (num_items && d_out == d_in) return cudaErrorInvalidValue;
     Args<T, F, NoValue> a{d_in, d_flags, nullptr, d_out, nullptr, nullptr, nullptr, d_num_selected_out, num_items,
-                          false};
+                          false, nullptr};
     return launch<kSelFlag, kOutPartition>(temp, temp_bytes, a, pick, Never{}, EqualTo{}, stream);
 }
 
@@ -1234,8 +1254,32 @@ cudaError_t partition_if(void* temp, size_t temp_bytes, const T* d_in, T* d_out,
     using namespace select_detail;
     if (num_items && d_out == d_in) return cudaErrorInvalidValue;
     Args<T, T, NoValue> a{d_in, nullptr, nullptr, d_out, nullptr, nullptr, nullptr, d_num_selected_out, num_items,
-                          false};
+                          false, nullptr};
     return launch<kSelIf, kOutPartition>(temp, temp_bytes, a, pick, Never{}, EqualTo{}, stream);
+}
+
+/* DeviceScan::ExclusiveSumTransform / ExclusiveSumAdjacent
+ * (src/lcpp/device/device_scan.h:387-406, details/scan.h:127-240):
+ * d_out[i] = the number of j < i with pick(d_in[j]), or with j == 0 ||
+ * !equal(d_in[j - 1], d_in[j]).  Temp storage: select_temp_bytes. */
+template <typename T, typename Pick>
+cudaError_t exclusive_sum_transform(void* temp, size_t temp_bytes, const T* d_in, uint32_t* d_out,
+                                    uint64_t num_items, Pick pick, cudaStream_t stream = 0)
+{
+    using namespace select_detail;
+    Args<T, T, NoValue> a{d_in, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, num_items, false,
+                          d_out};
+    return launch<kSelIf, kOutRanks>(temp, temp_bytes, a, pick, Never{}, EqualTo{}, stream);
+}
+
+template <typename T, typename Equal = EqualTo>
+cudaError_t exclusive_sum_adjacent(void* temp, size_t temp_bytes, const T* d_in, uint32_t* d_out,
+                                   uint64_t num_items, Equal equal = Equal{}, cudaStream_t stream = 0)
+{
+    using namespace select_detail;
+    Args<T, T, NoValue> a{d_in, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, num_items, false,
+                          d_out};
+    return launch<kSelUnique, kOutRanks>(temp, temp_bytes, a, Never{}, Never{}, equal, stream);
 }
 
 /* d_num_selected_out[0] = first count, [1] = second count. */
@@ -1246,7 +1290,7 @@ cudaError_t partition_three_way(void* temp, size_t temp_bytes, const T* d_in, T*
 {
     using namespace select_detail;
     Args<T, T, NoValue> a{d_in, nullptr, nullptr, d_first_out, d_second_out, d_unselected_out, nullptr,
-                          d_num_selected_out, num_items, false};
+                          d_num_selected_out, num_items, false, nullptr};
     return launch<kSelIf, kOutThreeWay>(temp, temp_bytes, a, select_first, select_second, EqualTo{}, stream);
 }
 

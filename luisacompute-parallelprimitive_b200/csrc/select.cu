@@ -142,4 +142,48 @@ lcpp_status lcpp_select_unique_by_key(void* temp, size_t temp_bytes, const void*
     });
 }
 
+lcpp_status lcpp_scan_transform_temp_bytes(uint64_t num_items, size_t* temp_bytes)
+{
+    if (!temp_bytes) return LCPP_ERR_INVALID_ARG;
+    *temp_bytes = lcpp_b200::device::select_temp_bytes(num_items, false);
+    return LCPP_OK;
+}
+
+lcpp_status lcpp_scan_exclusive_sum_transform(void* temp, size_t temp_bytes, const void* d_in, uint32_t* d_out,
+                                              uint64_t num_items, lcpp_dtype dtype, const lcpp_clause* clauses,
+                                              int num_clauses, lcpp_stream_t stream)
+{
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    // d_out stands in for the count pointer: non-null and 4-byte aligned
+    lcpp_status st = check(temp, temp_bytes, d_in, dtype_bytes(dtype), d_out, num_items, false);
+    if (st != LCPP_OK || num_items == 0) return st;
+    return with_value_type(dtype, [&](auto t) {
+        using T = decltype(t);
+        ClausePick<T> pick;
+        const lcpp_status ps = make_pick(clauses, num_clauses, pick);
+        if (ps != LCPP_OK) return ps;
+        sd::Args<T, T, NoValue> a{static_cast<const T*>(d_in), nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                  nullptr, num_items, false, d_out};
+        diag::KernelTimer timer(8 /* LCPP_KERNEL_SELECT */, num_items, s);
+        return status_of(sd::launch<sd::kSelIf, sd::kOutRanks>(temp, temp_bytes, a, pick, sd::Never{},
+                                                                lcpp_b200::device::EqualTo{}, s));
+    });
+}
+
+lcpp_status lcpp_scan_exclusive_sum_adjacent(void* temp, size_t temp_bytes, const void* d_in, uint32_t* d_out,
+                                             uint64_t num_items, lcpp_dtype dtype, lcpp_stream_t stream)
+{
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    lcpp_status st = check(temp, temp_bytes, d_in, dtype_bytes(dtype), d_out, num_items, false);
+    if (st != LCPP_OK || num_items == 0) return st;
+    return with_key_type(dtype, [&](auto t) {
+        using T = decltype(t);
+        sd::Args<T, T, NoValue> a{static_cast<const T*>(d_in), nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                                  nullptr, num_items, false, d_out};
+        diag::KernelTimer timer(8 /* LCPP_KERNEL_SELECT */, num_items, s);
+        return status_of(sd::launch<sd::kSelUnique, sd::kOutRanks>(temp, temp_bytes, a, sd::Never{}, sd::Never{},
+                                                                    lcpp_b200::device::EqualTo{}, s));
+    });
+}
+
 }  // extern "C"

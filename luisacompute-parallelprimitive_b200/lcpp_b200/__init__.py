@@ -108,6 +108,9 @@ def lib() -> ctypes.CDLL:
         "lcpp_scan_inclusive_sum_by_key": ([vp, sz, vp, vp, vp, u64, i, i, vp], i),
         "lcpp_reduce_by_key_temp_bytes": ([i, i, u64, szp], i),
         "lcpp_reduce_by_key": ([vp, sz, vp, vp, vp, vp, vp, u64, i, i, i, vp], i),
+        "lcpp_scan_transform_temp_bytes": ([u64, szp], i),
+        "lcpp_scan_exclusive_sum_transform": ([vp, sz, vp, vp, u64, i, vp, i, vp], i),
+        "lcpp_scan_exclusive_sum_adjacent": ([vp, sz, vp, vp, u64, i, vp], i),
         "lcpp_select_temp_bytes": ([u64, szp], i),
         "lcpp_partition_temp_bytes": ([u64, szp], i),
         "lcpp_partition_three_way_temp_bytes": ([u64, szp], i),
@@ -575,6 +578,27 @@ class DeviceScan:
                                              _ptr(d_in), _ptr(d_out), num_items, op, init, code,
                                              _stream(stream)), "InclusiveScanInit")
         del keep
+
+    # ---- counting scans (device_scan.h:387-406)
+    @staticmethod
+    def GetTransformTempStorageBytes(num_items: int) -> int:
+        out = ctypes.c_size_t()
+        check(lib().lcpp_scan_transform_temp_bytes(num_items, ctypes.byref(out)), "GetTransformTempStorageBytes")
+        return out.value
+
+    def ExclusiveSumTransform(self, temp, d_in, d_out, num_items, pred, stream=None):
+        """d_out[i] (4-byte tensor) = how many of d_in[0..i) satisfy pred (a Pred)."""
+        code = dtype_code(d_in)
+        arr, n = pred.encode(code)
+        check(lib().lcpp_scan_exclusive_sum_transform(_ptr(temp), temp.numel() if temp is not None else 0,
+                                                      _ptr(d_in), _ptr(d_out), num_items, code, arr, n,
+                                                      _stream(stream)), "ExclusiveSumTransform")
+
+    def ExclusiveSumAdjacent(self, temp, d_in, d_out, num_items, stream=None):
+        """d_out[i] = how many runs of equal items start before i."""
+        check(lib().lcpp_scan_exclusive_sum_adjacent(_ptr(temp), temp.numel() if temp is not None else 0,
+                                                     _ptr(d_in), _ptr(d_out), num_items, dtype_code(d_in),
+                                                     _stream(stream)), "ExclusiveSumAdjacent")
 
     # ---- by key (device_scan.h:310-597): argument order as the reference's
     @staticmethod

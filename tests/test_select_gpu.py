@@ -284,3 +284,21 @@ def test_argument_errors(lcpp):
     with pytest.raises(lcpp.LcppError) as e:
         sel.If(temp, x, x.clone(), cnt, 1 << 32, lcpp.Pred.gt(0))
     assert e.value.status == lcpp.ERR_INVALID_ARG
+
+
+@pytest.mark.parametrize("dtype", [np.int32, np.float32, np.uint64])
+def test_exclusive_sum_transform_and_adjacent(lcpp, oracle, dtype):
+    """DeviceScan::ExclusiveSumTransform / ExclusiveSumAdjacent (device_scan.h:387-406):
+    exclusive counts of the selected items and of the run heads."""
+    sc = lcpp.DeviceScan()
+    for n in (1, 4095, 4097, 230_413):
+        rng = np.random.default_rng(n)
+        x = np.repeat(rng.integers(0, 9, size=n), rng.integers(1, 4, size=n))[:n].astype(dtype)
+        temp = lcpp.alloc_temp(sc.GetTransformTempStorageBytes(n))
+        out = torch.empty(n, dtype=torch.int32, device="cuda")
+        sc.ExclusiveSumTransform(temp, dev(x), out, n, lcpp.Pred.gt(4))
+        m = oracle.clause_mask(x, [(2, 0, 4, 0)])
+        np.testing.assert_array_equal(host(out).view(np.uint32), np.concatenate([[0], np.cumsum(m)[:-1]]))
+        sc.ExclusiveSumAdjacent(temp, dev(x), out, n)
+        h = oracle.unique_mask(x)
+        np.testing.assert_array_equal(host(out).view(np.uint32), np.concatenate([[0], np.cumsum(h)[:-1]]))
