@@ -32,6 +32,7 @@
 #ifndef LCPP_B200_HPP
 #define LCPP_B200_HPP
 
+#include <algorithm>
 #include <cstddef>
 #include <cstdint>
 #include <cstring>
@@ -648,30 +649,43 @@ public:
     {
         size_t b = 0;
         detail::check(lcpp_scan_temp_bytes(detail::checked_dtype<T>(), num_items, &b), "GetTempStorageBytes");
+#ifdef __CUDACC__
+        b = std::max(b, device::by_key_temp_bytes(num_items, sizeof(T)));  // user operators
+#endif
         return b;
     }
 
+    /// ScanOp: SumOp / MinOp / MaxOp (C ABI), or under nvcc any associative
+    /// __device__ callable (operand order is kept).
     template <typename T, typename ScanOp>
     void ExclusiveScan(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in,
-                       BufferView<T> d_out, uint64_t num_items, ScanOp, T initial_value)
+                       BufferView<T> d_out, uint64_t num_items, ScanOp op, T initial_value)
     {
         views(d_in, d_out, num_items);
-        detail::check(lcpp_scan_exclusive(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
-                                          d_out.data(), num_items, detail::op_of<ScanOp>(), &initial_value,
-                                          detail::checked_dtype<T>(), stream),
-                      "ExclusiveScan");
+        if constexpr (!detail::is_builtin_op<ScanOp>) {
+            user_scan(stream, temp_storage, d_in, d_out, num_items, 0, initial_value, op, "ExclusiveScan");
+        } else {
+            detail::check(lcpp_scan_exclusive(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                              d_out.data(), num_items, detail::op_of<ScanOp>(), &initial_value,
+                                              detail::checked_dtype<T>(), stream),
+                          "ExclusiveScan");
+        }
     }
 
     /// Inclusive scan without an initial value (CUB semantics).
     template <typename T, typename ScanOp>
     void InclusiveScan(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in,
-                       BufferView<T> d_out, uint64_t num_items, ScanOp)
+                       BufferView<T> d_out, uint64_t num_items, ScanOp op)
     {
         views(d_in, d_out, num_items);
-        detail::check(lcpp_scan_inclusive(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
-                                          d_out.data(), num_items, detail::op_of<ScanOp>(),
-                                          detail::checked_dtype<T>(), stream),
-                      "InclusiveScan");
+        if constexpr (!detail::is_builtin_op<ScanOp>) {
+            user_scan(stream, temp_storage, d_in, d_out, num_items, 1, T{}, op, "InclusiveScan");
+        } else {
+            detail::check(lcpp_scan_inclusive(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                              d_out.data(), num_items, detail::op_of<ScanOp>(),
+                                              detail::checked_dtype<T>(), stream),
+                          "InclusiveScan");
+        }
     }
 
     /// Inclusive scan with the initial value folded in front.
@@ -684,13 +698,17 @@ public:
 
     template <typename T, typename ScanOp>
     void InclusiveScanInit(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in,
-                           BufferView<T> d_out, uint64_t num_items, ScanOp, T initial_value)
+                           BufferView<T> d_out, uint64_t num_items, ScanOp op, T initial_value)
     {
         views(d_in, d_out, num_items);
-        detail::check(lcpp_scan_inclusive_init(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
-                                               d_out.data(), num_items, detail::op_of<ScanOp>(), &initial_value,
-                                               detail::checked_dtype<T>(), stream),
-                      "InclusiveScanInit");
+        if constexpr (!detail::is_builtin_op<ScanOp>) {
+            user_scan(stream, temp_storage, d_in, d_out, num_items, 2, initial_value, op, "InclusiveScanInit");
+        } else {
+            detail::check(lcpp_scan_inclusive_init(temp_storage.data(), detail::temp_bytes(temp_storage),
+                                                   d_in.data(), d_out.data(), num_items, detail::op_of<ScanOp>(),
+                                                   &initial_value, detail::checked_dtype<T>(), stream),
+                          "InclusiveScanInit");
+        }
     }
 
     template <typename T>
@@ -818,6 +836,21 @@ public:
 #endif
 
 private:
+    // A user scan operator: the by-key pass over one segment (nvcc only).
+    template <typename T, typename Op>
+    void user_scan(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> in, BufferView<T> out,
+                   uint64_t n, int mode, T init, Op op, const char* what)
+    {
+#ifdef __CUDACC__
+        detail::check_cuda(device::scan(temp_storage.data(), detail::temp_bytes(temp_storage), in.data(), out.data(),
+                                        n, mode, init, op, reinterpret_cast<cudaStream_t>(stream)),
+                           what);
+#else
+        (void)stream, (void)temp_storage, (void)in, (void)out, (void)n, (void)mode, (void)init, (void)op, (void)what;
+        static_assert(detail::is_builtin_op<Op>, "scan operators other than SumOp / MinOp / MaxOp need nvcc");
+#endif
+    }
+
     // mode 0 exclusive, 1 inclusive, 2 inclusive with init; eq: a
     // detail::KeyEq pointer for == (the C ABI), else the user's equality.
     template <typename K, typename V, typename ScanOp, typename EqualityOp>
@@ -881,20 +914,54 @@ public:
     {
         size_t b = 0;
         detail::check(lcpp_reduce_temp_bytes(detail::checked_dtype<T>(), num_items, &b), "GetTempStorageBytes");
+#ifdef __CUDACC__
+        if (num_items) b = std::max(b, device::reduce_temp_bytes(sizeof(T)));  // user operators
+#endif
         return b;
     }
 
-    /// d_out[0] = initial_value op d_in[0] op ... (initial_value alone for 0 items).
+    /// d_out[0] = initial_value op d_in[0] op ... (initial_value alone for 0
+    /// items).  ReduceOp: SumOp / MinOp / MaxOp (C ABI), or under nvcc any
+    /// associative and commutative __device__ callable.
     template <typename T, typename ReduceOp>
     void Reduce(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in, BufferView<T> d_out,
-                uint64_t num_items, ReduceOp, T initial_value)
+                uint64_t num_items, ReduceOp op, T initial_value)
     {
         views(d_in, d_out, num_items);
-        detail::check(lcpp_reduce(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(), d_out.data(),
-                                  num_items, detail::op_of<ReduceOp>(), &initial_value, detail::checked_dtype<T>(),
-                                  stream),
-                      "Reduce");
+        if constexpr (!detail::is_builtin_op<ReduceOp>) {
+#ifdef __CUDACC__
+            detail::check_cuda(device::reduce(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                              d_out.data(), num_items, op, initial_value,
+                                              reinterpret_cast<cudaStream_t>(stream)),
+                               "Reduce");
+#else
+            static_assert(detail::is_builtin_op<ReduceOp>, "reduce operators other than SumOp / MinOp / MaxOp need nvcc");
+#endif
+        } else {
+            (void)op;
+            detail::check(lcpp_reduce(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                      d_out.data(), num_items, detail::op_of<ReduceOp>(), &initial_value,
+                                      detail::checked_dtype<T>(), stream),
+                          "Reduce");
+        }
     }
+
+#ifdef __CUDACC__
+    /// TransformReduce (device_reduce.h:493-516): d_out[0] = initial_value op
+    /// transform(d_in[0]) op ...; transform and op are __device__ callables,
+    /// op associative and commutative.  nvcc only.
+    template <typename T, typename ReduceOp, typename TransformOp>
+    void TransformReduce(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in,
+                         BufferView<T> d_out, uint64_t num_items, ReduceOp reduce_op, TransformOp transform_op,
+                         T initial_value)
+    {
+        views(d_in, d_out, num_items);
+        detail::check_cuda(device::transform_reduce(temp_storage.data(), detail::temp_bytes(temp_storage), d_in.data(),
+                                                    d_out.data(), num_items, reduce_op, transform_op, initial_value,
+                                                    reinterpret_cast<cudaStream_t>(stream)),
+                           "TransformReduce");
+    }
+#endif
 
     template <typename T>
     void Sum(lcpp_stream_t stream, BufferView<uint32_t> temp_storage, BufferView<T> d_in, BufferView<T> d_out,

@@ -1294,6 +1294,169 @@ cudaError_t partition_three_way(void* temp, size_t temp_bytes, const T* d_in, T*
     return launch<kSelIf, kOutThreeWay>(temp, temp_bytes, a, select_first, select_second, EqualTo{}, stream);
 }
 
+/* ---------------------------------------------------------------------------
+ * Reduce / TransformReduce and the plain scans with a user operator
+ * (src/lcpp/device/device_reduce.h:229-308, :493-516; device_scan.h:321-368).
+ *
+ * Reduce: d_out[0] = init op (transform(d_in[0]) op ... op transform(d_in[n-1]));
+ * op must be associative and commutative (the partial results of blocks and
+ * warps combine in a fixed but not left-to-right order).  Two levels as
+ * ArgMin / ArgMax: each block folds an equal contiguous chunk, the last block
+ * to finish folds the partials.  Zero items write init.
+ *
+ * The scans with a user operator run the by-key pass with every key equal
+ * (one segment), so they keep left-to-right operand order: op need only be
+ * associative.  Temp storage: by_key_temp_bytes(num_items, sizeof(T)).
+ * ------------------------------------------------------------------------- */
+
+/* "all keys equal": the by-key pass over one segment is a plain scan */
+struct AlwaysEqual {
+    template <typename K>
+    __device__ __forceinline__ bool operator()(K, K) const { return true; }
+};
+
+struct Identity {
+    template <typename T>
+    __device__ __forceinline__ T operator()(T x) const { return x; }
+};
+
+namespace reduce_detail {
+
+constexpr int kBlock = 256;
+constexpr int kBlocksPerSm = 4;
+constexpr uint64_t kMaxBlocks = 4096;
+constexpr size_t kAlign = 256;
+
+inline size_t temp_bytes(size_t value_bytes) { return kAlign + size_t(kMaxBlocks) * value_bytes; }
+
+template <typename T, typename Op>
+__device__ __forceinline__ T warp_fold(T v, bool has, bool& out_has, const Op& op)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const T ov = __shfl_down_sync(0xffffffffu, v, o);
+        const bool oh = __shfl_down_sync(0xffffffffu, int(has), o) != 0;
+        if ((threadIdx.x & 31) + o < 32 && oh) {
+            v = has ? op(v, ov) : ov;
+            has = true;
+        }
+    }
+    out_has = has;
+    return v;
+}
+
+/* Result in thread 0. */
+template <typename T, typename Op>
+__device__ __forceinline__ T block_fold(T v, bool has, bool& out_has, const Op& op, T* s_v, int* s_h)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_fold(v, has, has, op);
+    if (lane == 0) {
+        s_v[warp] = v;
+        s_h[warp] = has;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const bool h = lane < kBlock / 32 && s_h[lane];
+        v = warp_fold(h ? s_v[lane] : v, h, has, op);
+    }
+    out_has = has;
+    return v;
+}
+
+template <typename T, typename U, typename Op, typename Tr>
+__global__ void __launch_bounds__(kBlock)
+reduce_kernel(const U* in, uint64_t n, uint64_t chunk, T* partials, unsigned int* done, T* out, T init, Op op, Tr tr)
+{
+    __shared__ T s_v[kBlock / 32];
+    __shared__ int s_h[kBlock / 32];
+    __shared__ int s_last;
+    const uint64_t lo = uint64_t(blockIdx.x) * chunk;
+    const uint64_t hi = lo + chunk < n ? lo + chunk : n;
+    T acc{};
+    bool has = false;
+    for (uint64_t i = lo + threadIdx.x; i < hi; i += kBlock) {
+        const T x = tr(in[i]);
+        acc = has ? op(acc, x) : x;
+        has = true;
+    }
+    acc = block_fold(acc, has, has, op, s_v, s_h);
+    if (threadIdx.x == 0) {
+        partials[blockIdx.x] = acc;  // every block holds at least one item
+        __threadfence();
+        s_last = atomicAdd(done, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    T f{};
+    bool fh = false;
+    for (uint32_t b = threadIdx.x; b < gridDim.x; b += kBlock) {
+        const T p = *static_cast<const volatile T*>(partials + b);
+        f = fh ? op(f, p) : p;
+        fh = true;
+    }
+    __syncthreads();
+    f = block_fold(f, fh, fh, op, s_v, s_h);
+    if (threadIdx.x == 0) *out = op(init, f);
+}
+
+template <typename T>
+__global__ void store_kernel(T* out, T v)
+{
+    *out = v;
+}
+
+}  // namespace reduce_detail
+
+/* Temp storage bytes of transform_reduce / reduce (any item count). */
+inline size_t reduce_temp_bytes(size_t value_bytes) { return reduce_detail::temp_bytes(value_bytes); }
+
+template <typename T, typename U, typename Op, typename Transform>
+cudaError_t transform_reduce(void* temp, size_t temp_bytes, const U* d_in, T* d_out, uint64_t num_items, Op op,
+                             Transform transform, T init, cudaStream_t stream = 0)
+{
+    using namespace reduce_detail;
+    if (!d_out) return cudaErrorInvalidValue;
+    if (num_items == 0) {
+        store_kernel<T><<<1, 1, 0, stream>>>(d_out, init);
+        return cudaGetLastError();
+    }
+    if (!d_in || !temp || reinterpret_cast<uintptr_t>(temp) % kAlign || temp_bytes < reduce_detail::temp_bytes(sizeof(T)))
+        return cudaErrorInvalidValue;
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t max_blocks = std::min<uint64_t>(kMaxBlocks, uint64_t(sms > 0 ? sms : 1) * kBlocksPerSm);
+    uint64_t blocks = std::max<uint64_t>(1, std::min<uint64_t>(max_blocks, (num_items + kBlock - 1) / kBlock));
+    const uint64_t chunk = (num_items + blocks - 1) / blocks;
+    blocks = (num_items + chunk - 1) / chunk;
+    unsigned char* t = static_cast<unsigned char*>(temp);
+    e = cudaMemsetAsync(t, 0, sizeof(unsigned int), stream);
+    if (e != cudaSuccess) return e;
+    reduce_kernel<T, U><<<unsigned(blocks), kBlock, 0, stream>>>(d_in, num_items, chunk,
+                                                                 reinterpret_cast<T*>(t + kAlign),
+                                                                 reinterpret_cast<unsigned int*>(t), d_out, init,
+                                                                 op, transform);
+    return cudaGetLastError();
+}
+
+template <typename T, typename Op>
+cudaError_t reduce(void* temp, size_t temp_bytes, const T* d_in, T* d_out, uint64_t num_items, Op op, T init,
+                   cudaStream_t stream = 0)
+{
+    return transform_reduce(temp, temp_bytes, d_in, d_out, num_items, op, Identity{}, init, stream);
+}
+
+/* mode: 0 exclusive (init), 1 inclusive, 2 inclusive with init. */
+template <typename T, typename Op>
+cudaError_t scan(void* temp, size_t temp_bytes, const T* d_in, T* d_out, uint64_t num_items, int mode, T init, Op op,
+                 cudaStream_t stream = 0)
+{
+    return scan_by_key(temp, temp_bytes, d_in, d_in, d_out, num_items, mode, init, op, AlwaysEqual{}, stream);
+}
+
 }  // namespace device
 }  // namespace lcpp_b200
 

@@ -351,6 +351,68 @@ void select_cases(lcpp_stream_t s)
     }
 }
 
+struct Xor {
+    __host__ __device__ uint64_t operator()(uint64_t a, uint64_t b) const { return a ^ b; }
+};
+struct Square {
+    __host__ __device__ int64_t operator()(int64_t x) const { return int64_t(uint64_t(x) * uint64_t(x)); }
+};
+
+void user_operator_cases(lcpp_stream_t s)
+{
+    // Reduce / TransformReduce (device_reduce.h:229-308, :493-516) and the
+    // plain scans (device_scan.h:321-368) with user operators, against host folds
+    std::mt19937_64 rng(17);
+    for (size_t n : {size_t(1), size_t(4097), size_t(1000003)}) {
+        std::vector<uint64_t> maps(n);
+        std::vector<int64_t> ints(n);
+        for (size_t i = 0; i < n; ++i) {
+            maps[i] = (uint64_t(uint32_t(rng()) | 1u) << 32) | uint32_t(rng());
+            ints[i] = int64_t(rng() % 2001) - 1000;
+        }
+        DeviceArray<uint64_t> dm(n), out(n), one(1);
+        DeviceArray<int64_t> di(n), ione(1);
+        dm.upload(maps);
+        di.upload(ints);
+        DeviceReduce rd;
+        auto rtemp = temp_for(DeviceReduce::GetTempStorageBytes<uint64_t>(n));
+        rd.Reduce(s, rtemp.view(), dm.view(), one.view(), n, Xor{}, uint64_t(0x5a5a));
+        CUDA(cudaStreamSynchronize(s));
+        uint64_t x = 0x5a5a;
+        for (uint64_t m : maps) x ^= m;
+        CHECK(one.first() == x);
+        auto itemp = temp_for(DeviceReduce::GetTempStorageBytes<int64_t>(n));
+        rd.TransformReduce(s, itemp.view(), di.view(), ione.view(), n, SumOp{}, Square{}, int64_t(7));
+        CUDA(cudaStreamSynchronize(s));
+        int64_t sq = 7;
+        for (int64_t v : ints) sq += v * v;
+        CHECK(ione.first() == sq);
+
+        DeviceScan sc;
+        auto stemp = temp_for(DeviceScan::GetTempStorageBytes<uint64_t>(n));
+        const uint64_t shift = (uint64_t(1) << 32) | 9u;  // x -> x + 9
+        std::vector<uint64_t> got(n), want(n);
+        for (int mode = 0; mode < 3; ++mode) {
+            if (mode == 0) sc.ExclusiveScan(s, stemp.view(), dm.view(), out.view(), n, Compose{}, shift);
+            else if (mode == 1) sc.InclusiveScan(s, stemp.view(), dm.view(), out.view(), n, Compose{});
+            else sc.InclusiveScanInit(s, stemp.view(), dm.view(), out.view(), n, Compose{}, shift);
+            CUDA(cudaStreamSynchronize(s));
+            CUDA(cudaMemcpy(got.data(), out.p, n * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+            uint64_t run = mode == 1 ? maps[0] : shift;
+            for (size_t i = 0; i < n; ++i) {
+                if (mode == 0) {
+                    want[i] = run;
+                    run = Compose{}(run, maps[i]);
+                } else {
+                    if (mode == 2 || i > 0) run = Compose{}(run, maps[i]);
+                    want[i] = run;
+                }
+            }
+            CHECK(got == want);
+        }
+    }
+}
+
 }  // namespace
 
 int main()
@@ -363,6 +425,7 @@ int main()
     random_cases(s);
     by_key_cases(s);
     select_cases(s);
+    user_operator_cases(s);
     CUDA(cudaStreamDestroy(stream));
     std::printf("OK %d\n", g_checks);
     return 0;
