@@ -776,7 +776,7 @@ cudaError_t reduce_by_key(void* temp, size_t temp_bytes, const K* d_keys_in, con
  * ever moves to a lower index, and a tile writes only after its look-back,
  * i.e. after every lower tile has loaded its items.
  *
- * One pass: tiles of 256 threads x 4 groups x 4 consecutive items (4096
+ * One pass: tiles of 512 threads x 4 groups x 4 consecutive items (8192
  * items), tile ids from an atomic counter; the per-group selected counts are
  * scanned across lanes, warps and (decoupled look-back, every wait bounded
  * by %globaltimer at 4 s, error 5 at byte 4 of temp) tiles; each selected
@@ -798,7 +798,7 @@ struct NonZero {
 
 namespace select_detail {
 
-constexpr int kBlock = 256;
+constexpr int kBlock = 512;  // 8192-item tiles: fewer look-back windows per item
 constexpr int kWarps = kBlock / 32;
 constexpr int kChunks = 4;
 constexpr int kGroup = 4;
