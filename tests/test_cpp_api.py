@@ -68,3 +68,18 @@ def test_comparator_program_runs(tmp_path):
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     assert run.returncode == 0, run.stdout + run.stderr
     assert run.stdout.startswith("OK "), run.stdout
+
+
+def test_predicate_encoding_runs_on_cpu(tmp_path, lcpp):
+    """Predicate<T> (the C ABI's predicate encoding) is host code: built and run here
+    (linked against the library for its status strings; no device call)."""
+    gxx = _gxx()
+    exe = tmp_path / "predicate_host_test"
+    src = ROOT / "tests" / "cpp" / "predicate_host_test.cpp"
+    r = subprocess.run([gxx, "-std=c++17", "-O1", "-Wall", "-Wextra", "-Werror", f"-I{ROOT / 'include'}",
+                        f"-I{CUDA / 'include'}", str(src), "-o", str(exe), f"-L{LIBDIR}", "-llcpp_b200",
+                        f"-Wl,-rpath,{LIBDIR}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert run.stdout.startswith("OK "), run.stdout
