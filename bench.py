@@ -30,7 +30,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -94,7 +93,7 @@ OPS = {
     "select": dict(metric="Gitems/s i32 DeviceSelect::If(even) @2^30", unit="Gitems/s", log2n=30, dtype="i32",
                    workload="DeviceSelect::If x % 2 == 0 over uniform i32, seed 1", bytes=6, kbytes=6,
                    kernel="compact_kernel"),
-    # DeviceSegmentedRadixSort (SURVEY next-row widening): 2^27 u32 keys in
+    # DeviceSegmentedRadixSort: 2^27 u32 keys in
     # segments of 1..2047 keys (sizes uniform, seed 1), contiguous.  All
     # segments are short, so the one-block-per-segment kernel does the whole
     # sort: it reads and writes every key once (8 B per item, the op's and
@@ -150,13 +149,13 @@ def measured_peak():
 
 
 def profiled_traffic(op: str):
-    """DRAM bytes per item of the dominant kernel from the committed ncu
-    summary (a line 'traffic_bytes_per_item[<op>]: X')."""
-    p = ROOT / "profiles" / "README.md"
+    """DRAM bytes per item of one launch of the dominant kernel, from the
+    committed ncu figures (profiles/traffic.json)."""
+    p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
         return None
-    m = re.search(rf"traffic_bytes_per_item\[{op}\]:\s*([0-9.]+)", p.read_text())
-    return float(m.group(1)) if m else None
+    v = json.loads(p.read_text()).get(op)
+    return float(v) if isinstance(v, (int, float)) else None
 
 
 class ClockSampler:
@@ -446,6 +445,36 @@ def cpu_threads_for(op: str) -> int:
     return O.cpu_threads() if (op in ("sort", "bits") or op.startswith(("pairs", "dist"))) else 1
 
 
+def reference_items(op: str, log2n: int) -> int:
+    """Items one step of the reference arm processes: the full workload of the
+    op's configuration when the host finishes it in about a second per step
+    (the sorts up to 2^28 keys, the linear scans and reductions up to 2^30
+    items), else a 2^26-item sample (the distributed 2^32-key sort,
+    the segmented and decomposed sorts)."""
+    if op in ("sort", "bits", "pairs", "pairs_f32", "pairs_u64", "merge"):
+        return 1 << min(log2n, 28)
+    if op in ("scan", "reduce", "reduce_max", "argmin", "select", "scan_by_key", "reduce_by_key"):
+        return 1 << min(log2n, 30)
+    return 1 << min(log2n, 26)
+
+
+def single_thread_sort_leg(n: int, seed: int, min_seconds: float = 3.0):
+    """The reference tests' own host check, a single-threaded comparison sort
+    (std::sort, tests/device_radix_sort_one_sweep.cpp:169), restated with
+    numpy's sort on one thread: keys per second over at least min_seconds."""
+    from oracle import oracle as O
+    x = O.generate(O.GEN_U32_UNIFORM, n, seed=seed)
+    np_sort = __import__("numpy").sort
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        np_sort(x)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return n * reps / el, reps
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -453,29 +482,36 @@ def run_reference(args):
     cfg = OPS[args.op]
     log2n = args.log2n or cfg["log2n"]
     threads = cpu_threads_for(args.op)
-    n_sample = 1 << (20 if args.op == "segsort" else 22)
-    fn = cpu_fn(args.op, n_sample, threads)
+    n_items = reference_items(args.op, log2n)
+    fn = cpu_fn(args.op, n_items, threads)
     for _ in range(args.warmup):
         fn()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         fn()
     el = time.perf_counter() - t0
-    v = n_sample * args.steps / el / 1e9
-    sample = (f"2^{n_sample.bit_length() - 1} items of the {cfg['workload']} stream per step; "
-              + ("multi-threaded LSD restatement of the onesweep semantics" if threads > 1
-                 else "sequential host reference of the reference's tests"))
+    v = n_items * args.steps / el / 1e9
+    full = n_items == (1 << log2n) and not cfg.get("distributed")
+    lg = n_items.bit_length() - 1
+    how = ("multi-threaded LSD restatement of the onesweep semantics" if threads > 1
+           else "sequential host reference of the reference's tests")
+    sample = (f"the full workload (2^{lg} items) per step; {how}" if full
+              else f"2^{lg} items of the {cfg['workload']} stream per step; {how}")
     line = {
         "impl": "reference", "metric": cfg["metric"], "value": v, "unit": cfg["unit"], "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
         "higher_is_better": True, "scaling": "strong" if cfg.get("distributed") else "weak", "vs_baseline": None,
         "dtype": cfg["dtype"], "data": DATA,
-        "config": {"workload": f"{cfg['workload']}, 2^{log2n} items " + ("in total" if cfg.get("distributed") else "per GPU")
-                   + "; each step runs a bounded "
-                               f"2^{n_sample.bit_length() - 1}-item sample of it on the host"},
+        "config": {"workload": f"{cfg['workload']}, n=2^{log2n} " + ("in total" if cfg.get("distributed") else "per GPU"),
+                   "items_per_step": n_items, "same_config": full},
         "cpu_baseline": {"value": v, "unit": cfg["unit"], "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": cfg["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if args.op in ("sort", "bits"):
+        ips, reps = single_thread_sort_leg(n_items, 0 if args.op == "sort" else 1)
+        line["cpu_baseline"]["single_thread"] = {
+            "value": ips / 1e9, "unit": cfg["unit"], "cores": 1, "kind": "port",
+            "sample": f"2^{lg} keys x {reps} runs of numpy.sort on one thread (the reference tests' std::sort check)"}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -650,6 +686,11 @@ def run_ours(args):
                "sample": f"2^24 items of the {cfg['workload']} stream x {reps} runs; "
                          + ("multi-threaded LSD restatement of the onesweep semantics" if threads > 1
                             else "sequential host reference of the reference's tests")}
+        if args.op in ("sort", "bits"):
+            ips1, reps1 = single_thread_sort_leg(1 << 24, 0 if args.op == "sort" else 1)
+            cpu["single_thread"] = {"value": ips1 / 1e9, "unit": cfg["unit"], "cores": 1, "kind": "port",
+                                    "sample": f"2^24 keys x {reps1} runs of numpy.sort on one thread "
+                                              "(the reference tests' std::sort check)"}
 
     line = {
         "metric": cfg["metric"], "value": value, "unit": cfg["unit"], "n_gpus": 1, "steps": args.steps,

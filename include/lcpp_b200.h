@@ -223,8 +223,11 @@ lcpp_status lcpp_scan_inclusive_sum_by_key(void* temp, size_t temp_bytes, const 
  * 215,089,152 items of an 8-byte type; larger counts return
  * LCPP_ERR_TEMP_TOO_SMALL before any device work.  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress, with
- * that device current) and caches it; make that first call before any stream
- * capture.  All calls on one device share the array: calls that may overlap
+ * that device current) and caches it with the context's unique ID; a call
+ * that finds another context current on the device (after cudaDeviceReset)
+ * looks it up again.  Make the first call on a device, and the first call
+ * after a reset, before any stream capture.  All calls on one device share
+ * the array: calls that may overlap
  * on the GPU (different streams, no ordering between them) race and give
  * wrong results.  Every GPU that loads the library holds the array until the
  * process exits.  Nothing in this call allocates memory. */

@@ -49,7 +49,15 @@ struct NaturalOrder {
     __device__ __forceinline__ bool skip(T x) const { return x != x; }
 };
 
-/* A user comparator: equivalence is "neither compares less". */
+/* A user comparator: equivalence is "neither compares less".  The parallel
+ * combine (b replaces a when strictly better, or equivalent with a smaller
+ * index) equals the reference's sequential fold from item 0
+ * (src/lcpp/device/device_reduce.h:571-600) for every strict weak order.
+ * Comparators that are not strict weak orders are outside that parity
+ * domain; `<` over floating-point input holding NaN is one: NaN is then
+ * "equivalent" to every value, so [5, NaN, 3] may give (NaN, 1) here where
+ * the sequential fold gives (3, 2).  The comparator-free ArgMin / ArgMax
+ * (NaturalOrder) skip NaN items instead. */
 template <typename Compare>
 struct CompareOrder {
     Compare compare;

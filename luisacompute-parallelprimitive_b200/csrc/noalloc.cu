@@ -13,6 +13,12 @@
 // loads the library holds it until the process exits, and every call on a
 // device shares that device's copy.  Its host-side name is only a stand-in,
 // so host code passes the device address obtained with cudaGetSymbolAddress.
+// That address belongs to the device's current context: it is cached per
+// device together with the context's unique ID and looked up again when the
+// ID changes (after cudaDeviceReset the library image is loaded again and
+// the array may sit elsewhere).
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -31,10 +37,40 @@ static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 namespace {
 
 std::mutex g_mu;
-void* g_addr[64] = {};
+struct Cached {
+    unsigned long long ctx_id;  // 0: nothing cached
+    void* addr;
+};
+Cached g_cache[64] = {};
+PFN_cuCtxGetCurrent g_get_current = nullptr;
+PFN_cuCtxGetId g_get_id = nullptr;
 
-// Device address of g_scratch on the current device, looked up once per
-// device (with that device current) and cached.
+// Unique ID of the calling thread's current context, 0 when there is none.
+// The two driver functions come through the runtime's entry-point query, so
+// the library needs no link-time dependency on the driver library.
+unsigned long long current_context_id()
+{
+    if (!g_get_current || !g_get_id) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_get_current = reinterpret_cast<PFN_cuCtxGetCurrent>(f);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_get_id = reinterpret_cast<PFN_cuCtxGetId>(f);
+        if (!g_get_current || !g_get_id) return 0;
+    }
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (g_get_current(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+    if (g_get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
+// Device address of g_scratch on the current device, with that device
+// current: looked up at the first call on the device and again whenever the
+// device's context has changed since, else taken from the cache.
 cudaError_t scratch_address(void** out)
 {
     int dev = 0;
@@ -42,13 +78,14 @@ cudaError_t scratch_address(void** out)
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_addr[dev]) {
+    const unsigned long long id = current_context_id();
+    if (id == 0 || g_cache[dev].ctx_id != id) {
         void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_scratch);
+        e = cudaGetSymbolAddress(&p, g_scratch);  // creates the primary context if none is current
         if (e != cudaSuccess) return e;
-        g_addr[dev] = p;
+        g_cache[dev] = Cached{current_context_id(), p};
     }
-    *out = g_addr[dev];
+    *out = g_cache[dev].addr;
     return cudaSuccess;
 }
 

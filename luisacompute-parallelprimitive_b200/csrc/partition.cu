@@ -7,6 +7,21 @@
 using namespace lcpp;
 using namespace lcpp::sel;
 
+namespace {
+
+// True when [out, out + n items) and [in, in + n items) share a byte: the
+// partitions write rejected items from the end of the output backwards, so
+// any overlap with the input could overwrite items a later tile has not
+// read yet (the reference checks the same, device_partition.h:270-285).
+bool ranges_overlap(const void* in, const void* out, uint64_t num_items, int item_bytes)
+{
+    const char *a0 = static_cast<const char*>(in), *b0 = static_cast<const char*>(out);
+    const size_t len = size_t(num_items) * size_t(item_bytes);
+    return num_items && a0 < b0 + len && b0 < a0 + len;
+}
+
+}  // namespace
+
 extern "C" {
 
 lcpp_status lcpp_partition_temp_bytes(uint64_t num_items, size_t* temp_bytes)
@@ -32,8 +47,8 @@ lcpp_status lcpp_partition_flagged(void* temp, size_t temp_bytes, const void* d_
     if (st != LCPP_OK) return st;
     const int fb = flag_bytes(flag_dtype);
     if (!fb) return LCPP_ERR_UNSUPPORTED_DTYPE;
-    if (num_items && (!d_flags || !d_out || d_out == d_in || misaligned(d_flags, fb) ||
-                      misaligned(d_out, dtype_bytes(dtype))))
+    if (num_items && (!d_flags || !d_out || ranges_overlap(d_in, d_out, num_items, dtype_bytes(dtype)) ||
+                      misaligned(d_flags, fb) || misaligned(d_out, dtype_bytes(dtype))))
         return LCPP_ERR_INVALID_ARG;
     return with_bits_type(dtype, [&](auto t) {
         using T = decltype(t);
@@ -57,7 +72,9 @@ lcpp_status lcpp_partition_if(void* temp, size_t temp_bytes, const void* d_in, v
     const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     lcpp_status st = check(temp, temp_bytes, d_in, dtype_bytes(dtype), d_num_selected_out, num_items, false);
     if (st != LCPP_OK) return st;
-    if (num_items && (!d_out || d_out == d_in || misaligned(d_out, dtype_bytes(dtype)))) return LCPP_ERR_INVALID_ARG;
+    if (num_items && (!d_out || ranges_overlap(d_in, d_out, num_items, dtype_bytes(dtype)) ||
+                      misaligned(d_out, dtype_bytes(dtype))))
+        return LCPP_ERR_INVALID_ARG;
     return with_value_type(dtype, [&](auto t) {
         using T = decltype(t);
         ClausePick<T> pick;
@@ -85,12 +102,9 @@ lcpp_status lcpp_partition_if_three_way(void* temp, size_t temp_bytes, const voi
                       misaligned(d_second_out, tb) || misaligned(d_unselected_out, tb)))
         return LCPP_ERR_INVALID_ARG;
     // the outputs must not overlap the input (device_partition.h:270-285)
-    auto overlaps = [&](const void* o) {
-        const char *a0 = static_cast<const char*>(d_in), *b0 = static_cast<const char*>(o);
-        const size_t len = size_t(num_items) * size_t(tb);
-        return num_items && a0 < b0 + len && b0 < a0 + len;
-    };
-    if (overlaps(d_first_out) || overlaps(d_second_out) || overlaps(d_unselected_out)) return LCPP_ERR_INVALID_ARG;
+    if (ranges_overlap(d_in, d_first_out, num_items, tb) || ranges_overlap(d_in, d_second_out, num_items, tb) ||
+        ranges_overlap(d_in, d_unselected_out, num_items, tb))
+        return LCPP_ERR_INVALID_ARG;
     return with_value_type(dtype, [&](auto t) {
         using T = decltype(t);
         ClausePick<T> first, second;

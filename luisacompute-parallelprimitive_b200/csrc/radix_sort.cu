@@ -35,7 +35,6 @@
 //    (the reference splits at 2^28 keys into portions, :1056, and its
 //    portion carry is never written, agent_radix_sort_onesweep.h:362);
 //  - every spin is bounded (kWaitLimitNs) and reports LCPP_ERR_LOOKBACK_TIMEOUT.
-#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -256,51 +255,37 @@ struct OnesweepArgs {
     uint32_t* error;
 };
 
-// Tile policy of one onesweep configuration.
-//   BLOCK x ITEMS keys per tile (warp-striped, ITEMS slots per lane);
-//   PEERS: how a lane finds the lanes holding its digit in one slot --
-//     0: 8 ballots; 1: a shared-memory mask word per digit; 2: a mask word
-//     per low-5-bit digit class (one per bank: conflict-free) + 3 ballots;
-//   WINDOW: predecessor tiles read per look-back round trip;
-//   GROUP: slots ranked together (their mask ORs, loads and ballots are
-//     independent, so one __syncwarp covers the group and the chains overlap);
-//   MIN_BLOCKS: resident blocks per SM requested from the register allocator
-//     (0: left to the compiler);
-//   PACK: tile ranks kept as 16-bit pairs (fewer live registers);
-//   SLEEP_NS: __nanosleep between polls of a status word that is not
-//     published yet (spinning warps take issue slots from the others).
-template <int BLOCK, int ITEMS, int PEERS, int WINDOW, int GROUP = 1, int MIN_BLOCKS = 0, bool PACK = false,
-          int SLEEP_NS = 32, bool PTX_VOTE = false>
+// Tile policy of one onesweep configuration: BLOCK x ITEMS keys per tile
+// (warp-striped, ITEMS slots per lane), WINDOW predecessor tiles read per
+// look-back round trip, MIN_BLOCKS resident blocks per SM asked of the
+// register allocator.
+template <int BLOCK, int ITEMS, int WINDOW, int MIN_BLOCKS>
 struct Policy {
     static constexpr int kBlock = BLOCK;
     static constexpr int kItems = ITEMS;
-    static constexpr int kPeers = PEERS;
     static constexpr int kWindow = WINDOW;
-    static constexpr int kGroup = GROUP;
     static constexpr int kMinBlocks = MIN_BLOCKS;
-    static constexpr bool kPack = PACK;
-    static constexpr int kSleepNs = SLEEP_NS;  // back-off between polls of an unpublished status word
-    static constexpr bool kPtxVote = PTX_VOTE;  // ranking ballots / warp barrier as PTX
     static constexpr int kTile = BLOCK * ITEMS;
     static constexpr int kWarps = BLOCK / kWarp;
-    // mask words per warp and mask set; mask sets alternate by group parity
-    static constexpr int kMaskWords = PEERS == 1 ? kDigits : (PEERS == 2 ? 32 : 0);
-    static constexpr int kMaskSets = 2 * GROUP;
+    static constexpr int kSleepNs = 32;  // back-off between polls of an unpublished status word
+    // Peer masks: one word per low-5-bit digit class and slot, two slots per
+    // set, two sets alternating by slot pair.
+    static constexpr int kMaskWords = 2 * 32;
 };
 
+// Shared memory of one onesweep block.  The staging tile (keys, and values
+// for pairs) has its own storage, so every key is written to its tile rank
+// as soon as it is ranked: no rank array stays live in registers, and the
+// digit threads start their look-back while other warps are still ranking.
 template <typename U, typename V, bool PAIRS, typename P, typename OffT>
 struct OnesweepSmem {
     static constexpr int kTile = P::kTile;
     static constexpr int kWarps = P::kWarps;
-    union {
-        U keys[kTile];                        // transformed keys in tile-rank order
-        uint32_t counters[kWarps * kDigits];  // per-warp digit counters, then rank bases
-    } u;
+    U keys[kTile];                        // transformed keys in tile-rank order
     V vals[PAIRS ? kTile : 1];
-    // per mask set: lanes holding each digit (PEERS 1) or each low-5-bit
-    // digit class (PEERS 2)
-    uint32_t peer_masks[P::kMaskWords ? P::kMaskSets * kWarps * P::kMaskWords : 1];
-    OffT gofs[kDigits];  // output index = gofs[digit] + tile position
+    uint32_t counters[kWarps * kDigits];  // per-warp digit counters, then rank bases
+    uint32_t peer_masks[2 * kWarps * P::kMaskWords];
+    OffT gofs[kDigits];         // output index = gofs[digit] + tile position
     uint32_t totals[kDigits];   // keys of each digit in the tile
     uint32_t dstarts[kDigits];  // first tile rank of each digit
     uint32_t warp_sums[8];
@@ -367,22 +352,6 @@ __device__ __forceinline__ OffT lookback_digit(const ST* status, uint32_t tile, 
     }
 }
 
-
-// Lanes of the warp holding the same 8-bit digit: one ballot per digit bit
-// narrows the set (warp-level multisplit, Ashkiani et al., PPoPP 2016).  On
-// sm_100 this is cheaper than __match_any_sync.
-__device__ __forceinline__ uint32_t digit_peers(uint32_t d)
-{
-    uint32_t peers = 0xffffffffu;
-#pragma unroll
-    for (int b = 0; b < kRadixBits; ++b) {
-        const bool bit = (d >> b) & 1u;
-        const uint32_t vote = __ballot_sync(0xffffffffu, bit);
-        peers &= bit ? vote : ~vote;
-    }
-    return peers;
-}
-
 // Digit extraction for the onesweep kernel.  BYTE: the pass covers a whole
 // byte of a 4-byte key (shift % 8 == 0, 8 bits), so one byte permute
 // extracts it.
@@ -400,11 +369,6 @@ __device__ __forceinline__ uint32_t pass_digit(U t, int shift, uint32_t mask, ui
     }
 }
 
-
-
-
-
-
 // Everything after the tile id is known.  FULL: the tile has kTile keys (all
 // but possibly the last tile), compiled without any per-key bounds logic.
 template <bool FULL, bool BYTE, typename P, typename U, typename V, bool PAIRS, int KIND, typename ST, typename OffT>
@@ -414,8 +378,6 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
     using SB = StatusBits<ST>;
     constexpr int BLOCK = P::kBlock;
     constexpr int ITEMS = P::kItems;
-    constexpr int PEERS = P::kPeers;
-    constexpr int G = P::kGroup;
     constexpr int kTile = P::kTile;
     constexpr int kWarps = P::kWarps;
     const int tid = threadIdx.x;
@@ -431,26 +393,7 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
     // the tile, slot i of lane l is position w*ITEMS*32 + i*32 + l.
     U keys[ITEMS];
     V vals[PAIRS ? ITEMS : 1];
-    // tile rank of each slot; 16-bit pairs when P::kPack (ranks < 65536)
-    uint32_t rank[P::kPack ? (ITEMS + 1) / 2 : ITEMS];
-    auto set_rank = [&](int i, uint32_t r) {
-        if constexpr (P::kPack) {
-            if (i & 1)
-                rank[i >> 1] |= r << 16;
-            else
-                rank[i >> 1] = r;
-        } else {
-            rank[i] = r;
-        }
-    };
-    auto get_rank = [&](int i) -> uint32_t {
-        if constexpr (P::kPack)
-            return (i & 1) ? (rank[i >> 1] >> 16) : (rank[i >> 1] & 0xffffu);
-        else
-            return rank[i];
-    };
-    const uint32_t counters_base =
-        static_cast<uint32_t>(__cvta_generic_to_shared(s.u.counters + warp * kDigits));
+    const uint32_t counters_base = static_cast<uint32_t>(__cvta_generic_to_shared(s.counters + warp * kDigits));
     {
         const int warp_base = warp * ITEMS * kWarp + lane;
         const U* src = a.keys_in + tile_base + warp_base;
@@ -478,7 +421,7 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
     uint32_t total = 0;
     if (tid < kDigits) {
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) total += s.u.counters[w * kDigits + tid];
+        for (int w = 0; w < kWarps; ++w) total += s.counters[w * kDigits + tid];
         st_relaxed(a.status + uint64_t(tile) * kDigits + tid,
                    ST(total) | (tile == 0 ? SB::kInclusive : SB::kPartial));
     }
@@ -487,14 +430,80 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
         uint32_t run = dstart;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) {
-            const uint32_t c = s.u.counters[w * kDigits + tid];
-            s.u.counters[w * kDigits + tid] = run;
+            const uint32_t c = s.counters[w * kDigits + tid];
+            s.counters[w * kDigits + tid] = run;
             run += c;
         }
         s.totals[tid] = total;
         s.dstarts[tid] = dstart;
     }
     __syncthreads();
+
+    // Stable ranking, each key written to the staging tile at its rank: keys
+    // of one slot are ranked in lane order among equal digits, slots in
+    // order; the digit's leader lane advances the warp's rank counter by the
+    // number of peers and the returned value is the first tile rank of the
+    // group.  The leader's atomic is predicated rather than branched around,
+    // so the atomics of both slots of a pair are issued back to back;
+    // shared-memory operations of one warp complete in issue order, which
+    // keeps consecutive slots consistent.
+    {
+        const uint32_t lt = lanemask_lt();
+        constexpr uint32_t kSetBytes = uint32_t(kWarps * P::kMaskWords) * 4u;
+        const uint32_t masks_base =
+            static_cast<uint32_t>(__cvta_generic_to_shared(s.peer_masks + warp * P::kMaskWords));
+#pragma unroll
+        for (int i0 = 0; i0 < ITEMS; i0 += 2) {
+            uint32_t d[2], peers[2], maddr[2], base[2];
+            // Each lane ORs its bit into the mask word of its digit's low 5
+            // bits (32 words, one per bank, so these accesses never
+            // conflict), and one ballot per remaining bit narrows the class
+            // to the digit.  Slot g of a pair uses half g of the pair's mask
+            // set; every lane clears its word once all lanes have read it
+            // (the shuffle below depends on every lane's read), and the next
+            // pair's warp barrier orders the clears before the pair after it
+            // reuses the set.
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                if (i0 + g < ITEMS) {
+                    const int i = i0 + g;
+                    d[g] = in_tile(i) ? digit(keys[i]) : dmask;
+                    maddr[g] = masks_base + uint32_t((i0 >> 1) & 1) * kSetBytes + (uint32_t(g) * 32u + (d[g] & 31u)) * 4u;
+                    shared_red_or(maddr[g], 1u << lane);
+                }
+            }
+            warp_barrier();
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                if (i0 + g < ITEMS) {
+                    peers[g] = shared_load(maddr[g]);
+#pragma unroll
+                    for (int b = 5; b < kRadixBits; ++b) {
+                        const bool bit = (d[g] >> b) & 1u;
+                        const uint32_t vote = warp_ballot(bit);
+                        peers[g] &= bit ? vote : ~vote;
+                    }
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                if (i0 + g < ITEMS) {
+                    const int leader = 31 - __clz(peers[g]);
+                    base[g] = shared_add_if(lane == leader, counters_base + d[g] * 4u, uint32_t(__popc(peers[g])));
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                if (i0 + g < ITEMS) {
+                    base[g] = warp_shfl(base[g], 31 - __clz(peers[g]));
+                    shared_store_if(true, maddr[g], 0u);
+                    const uint32_t r = base[g] + __popc(peers[g] & lt);
+                    s.keys[r] = keys[i0 + g];
+                    if constexpr (PAIRS) s.vals[r] = vals[i0 + g];
+                }
+            }
+        }
+    }
 
     // Publishes the inclusive count of digit d and its output base, and
     // checks that the digit's keys land inside the output (a broken
@@ -509,102 +518,13 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
         if (a.status_next) a.status_next[uint64_t(tile) * kDigits + d] = 0;
     };
 
-    // Stable ranking: keys of one slot are ranked in lane order among equal
-    // digits, slots in order; the digit's leader lane advances the warp's
-    // rank counter by the number of peers and the returned value is the
-    // first tile rank of the group.  The leader's atomic is predicated rather
-    // than branched around, so the atomics of all slots are issued back to
-    // back; shared-memory operations of one warp complete in issue order,
-    // which keeps consecutive slots consistent.
-    {
-        const uint32_t lt = lanemask_lt();
-        constexpr int kMaskWords = P::kMaskWords;
-        constexpr uint32_t kSetBytes = uint32_t(kWarps * kMaskWords) * 4u;
-        const uint32_t masks_base =
-            static_cast<uint32_t>(__cvta_generic_to_shared(s.peer_masks + warp * kMaskWords));
-#pragma unroll
-        for (int i0 = 0; i0 < ITEMS; i0 += G) {
-            uint32_t d[G], peers[G], maddr[G], base[G];
-            // Each lane ORs its bit into the mask word of its digit (PEERS 1)
-            // or of its digit's low 5 bits (PEERS 2: 32 words, one per bank,
-            // so these accesses never conflict, and one ballot per remaining
-            // bit narrows the class to the digit).  Slot g of a group uses
-            // mask set g of the group's parity; every lane clears its word
-            // once all lanes have read it (the shuffle below depends on every
-            // lane's read), and the next group's __syncwarp orders the clears
-            // before the group after it reuses the set.
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                if (i0 + g < ITEMS) {
-                    const int i = i0 + g;
-                    d[g] = in_tile(i) ? digit(keys[i]) : dmask;
-                    if constexpr (PEERS != 0) {
-                        const uint32_t w = PEERS == 1 ? d[g] : (d[g] & 31u);
-                        maddr[g] = masks_base + uint32_t(((i0 / G) & 1) * G + g) * kSetBytes + w * 4u;
-                        shared_red_or(maddr[g], 1u << lane);
-                    }
-                }
-            }
-            if constexpr (PEERS != 0) {
-                if constexpr (P::kPtxVote)
-                    warp_barrier();
-                else
-                    __syncwarp();
-            }
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                if (i0 + g < ITEMS) {
-                    if constexpr (PEERS == 0) {
-                        peers[g] = digit_peers(d[g]);
-                    } else {
-                        peers[g] = shared_load(maddr[g]);
-                        if constexpr (PEERS == 2) {
-#pragma unroll
-                            for (int b = 5; b < kRadixBits; ++b) {
-                                const bool bit = (d[g] >> b) & 1u;
-                                const uint32_t vote = P::kPtxVote ? warp_ballot(bit) : __ballot_sync(0xffffffffu, bit);
-                                peers[g] &= bit ? vote : ~vote;
-                            }
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                if (i0 + g < ITEMS) {
-                    const int leader = 31 - __clz(peers[g]);
-                    base[g] = shared_add_if(lane == leader, counters_base + d[g] * 4u, uint32_t(__popc(peers[g])));
-                }
-            }
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                if (i0 + g < ITEMS) {
-                    base[g] = P::kPtxVote ? warp_shfl(base[g], 31 - __clz(peers[g]))
-                                          : __shfl_sync(0xffffffffu, base[g], 31 - __clz(peers[g]));
-                    if constexpr (PEERS == 1) shared_store_if(lane == 31 - __clz(peers[g]), maddr[g], 0u);
-                    if constexpr (PEERS == 2) shared_store_if(true, maddr[g], 0u);
-                    set_rank(i0 + g, base[g] + __popc(peers[g] & lt));
-                }
-            }
-        }
-    }
-    __syncthreads();  // rank counters are dead; the key tile reuses their storage
-
     // Decoupled look-back, one digit per thread, P::kWindow predecessor tiles
-    // per round trip.
+    // per round trip.  A digit thread starts as soon as its own warp has
+    // ranked its keys, while other warps may still be ranking.
     if (tid < kDigits) {
         OffT prefix = 0;
         if (tile > 0) prefix = lookback_digit<ST, OffT, P::kWindow, P::kSleepNs>(a.status, tile, tid, a.error);
         finish_digit(tid, prefix);
-    }
-
-    {
-#pragma unroll
-        for (int i = 0; i < ITEMS; ++i) s.u.keys[get_rank(i)] = keys[i];
-        if constexpr (PAIRS) {
-#pragma unroll
-            for (int i = 0; i < ITEMS; ++i) s.vals[get_rank(i)] = vals[i];
-        }
     }
     __syncthreads();
     if (s.bad) {
@@ -618,7 +538,7 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
     {
         OffT out_pos[ITEMS];
 #pragma unroll
-        for (int i = 0; i < ITEMS; ++i) keys[i] = s.u.keys[i * BLOCK + tid];
+        for (int i = 0; i < ITEMS; ++i) keys[i] = s.keys[i * BLOCK + tid];
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) out_pos[i] = s.gofs[digit(keys[i])] + OffT(i * BLOCK + tid);
         if constexpr (PAIRS) {
@@ -645,7 +565,6 @@ onesweep_kernel(OnesweepArgs<U, V, ST, OffT> a)
     constexpr int kWarps = Smem::kWarps;
     static_assert(BLOCK >= kDigits, "one thread per digit");
     static_assert(kTile <= 65536, "tile ranks fit 16 bits");
-    static_assert(sizeof(U) * kTile >= sizeof(uint32_t) * kWarps * kDigits, "counter overlay");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>(smem_raw);
 
@@ -654,10 +573,8 @@ onesweep_kernel(OnesweepArgs<U, V, ST, OffT> a)
         s.tile_id = atomicAdd(a.tile_counter, 1u);
         s.bad = 0;
     }
-    for (int i = tid; i < kWarps * kDigits; i += BLOCK) s.u.counters[i] = 0;
-    if constexpr (P::kMaskWords != 0) {
-        for (int i = tid; i < P::kMaskSets * kWarps * P::kMaskWords; i += BLOCK) s.peer_masks[i] = 0;
-    }
+    for (int i = tid; i < kWarps * kDigits; i += BLOCK) s.counters[i] = 0;
+    for (int i = tid; i < 2 * kWarps * P::kMaskWords; i += BLOCK) s.peer_masks[i] = 0;
     __syncthreads();
     const uint32_t tile = s.tile_id;
     const uint64_t tile_base = uint64_t(tile) * kTile;
@@ -682,7 +599,7 @@ namespace {
 
 // Smallest tile (keys per onesweep block) of any configuration; sizes the
 // look-back rows in temp storage.
-constexpr uint64_t kMinTile = 4096;
+constexpr uint64_t kMinTile = 5120;
 constexpr int kHistBlock = 1024;
 
 struct Layout {
@@ -828,71 +745,54 @@ lcpp_status launch_passes(const Layout& L, unsigned char* temp, const SortCall& 
     return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;
 }
 
-// Onesweep tile variant for 4-byte unsigned ascending keys without values,
-// selectable with the environment variable LCPP_ONESWEEP_VARIANT (tuning
-// sweeps); read once per process.
-int onesweep_variant()
+// Tile policies (block threads, keys per thread, look-back window, blocks
+// per SM), one per key / value size class, measured on B200 (2^28 4-byte,
+// 2^27 8-byte keys): 4-byte keys 448 x 28, 70.3 Gkeys/s (512 x 24: 69.0);
+// 4-byte pairs 512 x 16, 46.5 (512 x 14: 44.1); 8-byte keys 384 x 16, 21.3
+// (256 x 20: 19.5); pairs with an 8-byte key or value 256 x 20, 16.6
+// (384 x 16: 16.3).  A build may define these macros to other values; only
+// the chosen policy of each class is compiled.
+#ifndef LCPP_ONESWEEP_4B_KEYS
+#define LCPP_ONESWEEP_4B_KEYS 448, 28, 8, 2
+#endif
+#ifndef LCPP_ONESWEEP_4B_PAIRS
+#define LCPP_ONESWEEP_4B_PAIRS 512, 16, 8, 2
+#endif
+#ifndef LCPP_ONESWEEP_8B_KEYS
+#define LCPP_ONESWEEP_8B_KEYS 384, 16, 8, 2
+#endif
+#ifndef LCPP_ONESWEEP_8B_PAIRS
+#define LCPP_ONESWEEP_8B_PAIRS 256, 20, 8, 2
+#endif
+
+template <typename U, typename V, bool PAIRS, typename P, int KIND>
+lcpp_status run_policy(const Layout& L, unsigned char* temp, const SortCall& c, uint64_t n,
+                       const KeyCodec<U>& codec, int begin_bit, int end_bit, int passes, cudaStream_t stream)
 {
-    static const int v = [] {
-        const char* e = std::getenv("LCPP_ONESWEEP_VARIANT");
-        return e ? std::atoi(e) : 0;
-    }();
-    return v;
+    // 64-bit status words and offsets from 2^30 keys on
+    if (L.wide)
+        return launch_passes<U, V, PAIRS, P, KIND, uint64_t, uint64_t>(L, temp, c, n, codec, begin_bit, end_bit,
+                                                                       passes, stream);
+    return launch_passes<U, V, PAIRS, P, KIND, uint32_t, uint32_t>(L, temp, c, n, codec, begin_bit, end_bit, passes,
+                                                                   stream);
 }
 
 template <typename U, typename V, bool PAIRS, int KIND>
 lcpp_status run_kind(const Layout& L, unsigned char* temp, const SortCall& c, uint64_t n,
                      const KeyCodec<U>& codec, int begin_bit, int end_bit, int passes, cudaStream_t stream)
 {
-#define LCPP_PASSES(...)                                                                                    \
-    (L.wide ? launch_passes<U, V, PAIRS, Policy<__VA_ARGS__>, KIND, uint64_t, uint64_t>(L, temp, c, n, codec,      \
-                                                                                      begin_bit, end_bit, passes, \
-                                                                                      stream)                     \
-            : launch_passes<U, V, PAIRS, Policy<__VA_ARGS__>, KIND, uint32_t, uint32_t>(L, temp, c, n, codec,      \
-                                                                                      begin_bit, end_bit, passes, \
-                                                                                      stream))
-    if constexpr (sizeof(U) == 4 && !PAIRS) {
-        if constexpr (KIND == kPlain) {
-            switch (onesweep_variant()) {
-            case 1: return LCPP_PASSES(384, 20, 0, 8);  // 8 ballots per digit
-            case 2: return LCPP_PASSES(256, 24, 1, 8);  // shared-memory peer masks
-            case 3: return LCPP_PASSES(256, 24, 2, 8);  // slots ranked one at a time, CUDA intrinsics
-            case 4: return LCPP_PASSES(256, 24, 2, 8, 4, 0, false, 32, true);      // slots ranked in fours
-            case 5: return LCPP_PASSES(256, 24, 2, 8, 2, 4, true, 32, true);       // 4 blocks per SM, 16-bit ranks
-            case 6: return LCPP_PASSES(256, 24, 2, 8, 2, 1, false, 32, true);      // 2 blocks per SM
-            case 7: return LCPP_PASSES(256, 24, 2, 8, 2, 0, false, 0, true);       // look-back without back-off
-            case 8: return LCPP_PASSES(256, 24, 2, 8, 2, 0, false, 400, true);     // 400 ns back-off
-            default: break;
-            }
-        }
-        // Measured best on B200 for 4-byte keys: 256 x 24 keys per tile,
-        // peers from low-5-bit shared masks plus 3 ballots, slots ranked in
-        // pairs, votes / shuffles / warp barrier as PTX, 3 blocks per SM
-        // (80 registers).  Variants 1-8 were within 1.5 % of it or slower;
-        // the look-back back-off made no difference.
-        return LCPP_PASSES(256, 24, 2, 8, 2, 0, false, 32, true);
-    } else if constexpr (sizeof(U) == 4 && sizeof(V) == 4) {
-        switch (onesweep_variant()) {
-        case 11: return LCPP_PASSES(384, 15, 0, 8);  // 8 ballots per digit
-        case 12: return LCPP_PASSES(512, 12, 2, 8);
-        case 13: return LCPP_PASSES(512, 16, 2, 8);
-        default: break;
-        }
-        // Measured best on B200 for 4-byte keys with 4-byte values (u32/u32
-        // 2^28: 42.0 Gkeys/s against 38.2 with 8 ballots at 384 x 15).
-        return LCPP_PASSES(512, 14, 2, 8);
-    } else {
-        switch (onesweep_variant()) {
-        case 21: return LCPP_PASSES(256, 16, 0, 8);  // 8 ballots per digit
-        case 22: return LCPP_PASSES(256, 20, 2, 8);
-        case 23: return LCPP_PASSES(384, 16, 2, 8);
-        default: break;
-        }
-        // Measured best on B200 with an 8-byte key or value (u64/i32 2^27:
-        // 16.2 Gkeys/s against 13.1 with 8 ballots at 256 x 16).
-        return LCPP_PASSES(256, 24, 2, 8);
-    }
-#undef LCPP_PASSES
+    if constexpr (sizeof(U) == 4 && !PAIRS)
+        return run_policy<U, V, PAIRS, Policy<LCPP_ONESWEEP_4B_KEYS>, KIND>(L, temp, c, n, codec, begin_bit, end_bit,
+                                                                            passes, stream);
+    else if constexpr (sizeof(U) == 4 && sizeof(V) == 4)
+        return run_policy<U, V, PAIRS, Policy<LCPP_ONESWEEP_4B_PAIRS>, KIND>(L, temp, c, n, codec, begin_bit,
+                                                                             end_bit, passes, stream);
+    else if constexpr (!PAIRS)
+        return run_policy<U, V, PAIRS, Policy<LCPP_ONESWEEP_8B_KEYS>, KIND>(L, temp, c, n, codec, begin_bit,
+                                                                            end_bit, passes, stream);
+    else
+        return run_policy<U, V, PAIRS, Policy<LCPP_ONESWEEP_8B_PAIRS>, KIND>(L, temp, c, n, codec, begin_bit,
+                                                                             end_bit, passes, stream);
 }
 
 template <typename U, typename V, bool PAIRS>

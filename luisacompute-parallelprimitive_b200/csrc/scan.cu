@@ -624,18 +624,6 @@ constexpr int kBlock = 256;
 constexpr int kChunks = 4;
 constexpr int kStages = 3;
 
-// Kernel for aligned data, selectable with the environment variable
-// LCPP_SCAN_VARIANT (A/B timing; read once per process): 0 the persistent
-// bulk-copy kernel, 1 one tile per block.
-int scan_variant()
-{
-    static const int v = [] {
-        const char* e = std::getenv("LCPP_SCAN_VARIANT");
-        return e ? std::atoi(e) : 0;
-    }();
-    return v;
-}
-
 uint64_t tile_items(int tb) { return uint64_t(kBlock) * uint64_t(16 / tb) * kChunks; }
 
 struct Layout {
@@ -665,7 +653,9 @@ template <typename T, typename Op, int MODE, bool PACKED>
 void launch_kernel(const T* in, T* out, uint64_t n, uint64_t tiles, T init, const TileState<T, PACKED>& ts,
                    Ctrl* ctrl, bool aligned, cudaStream_t stream)
 {
-    if (aligned && scan_variant() == 0) {
+    // 16-byte aligned input and output: the persistent bulk-copy kernel;
+    // otherwise one tile per block with register loads.
+    if (aligned) {
         auto kernel = scan_bulk_kernel<T, Op, MODE, kBlock, kChunks, PACKED, kStages>;
         constexpr size_t smem = size_t(kStages) * kBlock * 16 * kChunks;
         set_max_dynamic_smem(reinterpret_cast<const void*>(kernel), smem);
@@ -673,9 +663,6 @@ void launch_kernel(const T* in, T* out, uint64_t n, uint64_t tiles, T init, cons
             uint64_t(device_sm_count()) * resident_blocks(reinterpret_cast<const void*>(kernel), kBlock, smem);
         const unsigned grid = unsigned(tiles < resident ? tiles : resident);
         kernel<<<grid, kBlock, smem, stream>>>(in, out, n, tiles, init, ts, ctrl);
-    } else if (aligned) {
-        scan_kernel<T, Op, MODE, kBlock, kChunks, PACKED, true><<<unsigned(tiles), kBlock, 0, stream>>>(
-            in, out, n, init, ts, ctrl);
     } else {
         scan_kernel<T, Op, MODE, kBlock, kChunks, PACKED, false><<<unsigned(tiles), kBlock, 0, stream>>>(
             in, out, n, init, ts, ctrl);

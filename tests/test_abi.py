@@ -168,6 +168,11 @@ def test_misuse_new_families_without_device(lcpp):
     arr, k = clauses((0, 0, 5, 0))
     assert lib.lcpp_partition_if(a, big, b, b, n_sel, 10, lcpp.I32, arr, k, None) == lcpp.ERR_INVALID_ARG
     assert lib.lcpp_partition_flagged(a, big, b, c, b, n_sel, 10, lcpp.I32, lcpp.U8, None) == lcpp.ERR_INVALID_ARG
+    # a partly overlapping output (a few items past the input's start) is
+    # rejected too: the rejected items are written backwards from its end
+    assert lib.lcpp_partition_if(a, big, b, vp(0x200008), n_sel, 10, lcpp.I32, arr, k, None) == lcpp.ERR_INVALID_ARG
+    assert lib.lcpp_partition_flagged(a, big, b, c, vp(0x1FFFF8), n_sel, 10, lcpp.I32, lcpp.U8,
+                                      None) == lcpp.ERR_INVALID_ARG
     assert lib.lcpp_partition_if_three_way(a, big, b, vp(0x200004), vp(0x800000), vp(0x900000), n_sel, 10,
                                            lcpp.I32, arr, k, arr, k, None) == lcpp.ERR_INVALID_ARG
     two, three = ctypes.c_size_t(), ctypes.c_size_t()

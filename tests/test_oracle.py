@@ -218,6 +218,23 @@ def test_arg_extremum_vs_numpy(oracle, dtype):
     assert oracle.arg_extremum_compare(y, False, lambda a, b: a < b) == oracle.arg_extremum(y, False)
 
 
+def test_arg_extremum_compare_nan_is_sequential(oracle):
+    """The comparator ArgMin of the reference is a sequential fold from item 0
+    (device_reduce.h:571-600): with `<`, a NaN item never replaces the best
+    and, once best, is never replaced.  These are the answers for input with
+    NaN; the device comparator path is held to them only for strict weak
+    orders (NaN input with `<` is outside that domain)."""
+    less = lambda a, b: a < b  # noqa: E731
+    x = np.array([5.0, np.nan, 3.0], np.float32)
+    best, idx = oracle.arg_extremum_compare(x, True, less)
+    assert (float(best), idx) == (3.0, 2)
+    best, idx = oracle.arg_extremum_compare(x, False, less)
+    assert (float(best), idx) == (5.0, 0)
+    y = np.array([np.nan, 1.0, -2.0], np.float32)
+    best, idx = oracle.arg_extremum_compare(y, True, less)
+    assert np.isnan(best) and idx == 0
+
+
 def test_scan_by_key_golden(oracle, golden):
     """device_scan_test.cpp:324-446: ExclusiveSumByKey over ones, keys i/100;
     InclusiveSumByKey of int64 ones across three tiles; parity key equality."""
