@@ -18,8 +18,13 @@ Arms:
                     stream, clocks sampled during the timed region, and the
                     CPU baseline (oracle port, all host threads, bounded
                     sample) on rank 0.
-                    N > 1 (torchrun): the distributed sort, 2^28 keys per GPU
-                    (weak scaling), max over ranks.
+                    N > 1 (torchrun): the distributed sort
+                    (lcpp_dist_sort_keys), 2^28 keys per GPU (weak scaling),
+                    max over ranks; the line also carries a bit-exact parity
+                    check of three gathered distributed sorts (the run exits
+                    non-zero when it fails), per-phase times, and the 2^32-key
+                    strong-scaling sort with the 1-GPU sort of the same keys
+                    timed on rank 0 in the same job.
   --impl reference  the reference's own path on the host cores: its CPU
                     restatement (oracle port; the reference cannot be built
                     here), all host threads, a bounded sample of the same
@@ -263,11 +268,11 @@ class Workload:
             self.dec = L.Decomposer(8, [(0, L.U32), (4, L.I32)])
             self.temp = L.alloc_temp(L.DeviceRadixSort.GetDecomposedTempStorageBytes(n))
         elif op == "merge":
-            from lcpp_b200.distributed import GpuOps
-            self.gops = GpuOps()
+            from lcpp_b200 import distributed as D
+            self.merge_sorted = D.merge_sorted
             half = n // 2
             keys = fill(T.uint32, L.GEN_U32_UNIFORM, 1)
-            self.inputs = [self.gops.local_sort(keys[:half].clone()), self.gops.local_sort(keys[half:].clone())]
+            self.inputs = [D.local_sort(keys[:half].clone()), D.local_sort(keys[half:].clone())]
             self.outputs = [T.empty(n, dtype=T.uint32, device=dev)]
             self.temp = None
             del keys
@@ -315,7 +320,7 @@ class Workload:
         elif op.startswith("pairs"):
             self.rs.SortPairs(t, i[0], o[0], i[1], o[1], n)
         elif op == "merge":
-            self.gops.merge(i[0], i[1], o[0])
+            self.merge_sorted(i[0], i[1], o[0])
         elif op == "decomposed":
             self.rs.SortKeys(t, i[0], o[0], n, self.dec)
         elif op == "segsort":
@@ -551,14 +556,16 @@ def run_ours(args):
             init = dict(init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local),
                                 **init)
+        rc = 0
         try:
             if cfg.get("distributed"):  # fixed total, sharded evenly (strong scaling)
                 n_local = (1 << log2n) // world
                 res = D.bench_distributed_sort(n_local, args.steps, args.warmup, dist, ClockSampler,
                                                measured_peak(), seed=cfg["seed"], zipf=cfg["zipf"],
                                                metric=cfg["metric"], scaling="strong")
-            else:  # the default sort: 2^28 keys per GPU (weak scaling)
-                res = D.bench_distributed_sort(n, args.steps, args.warmup, dist, ClockSampler, measured_peak())
+            else:  # the default sort: 2^28 keys per GPU (weak scaling), plus 2^32 keys in total
+                res = D.bench_distributed_sort(n, args.steps, args.warmup, dist, ClockSampler, measured_peak(),
+                                               strong_2p32=world > 1)
             if rank == 0 and world == 1 and not args.no_cpu_baseline:
                 threads = cpu_threads_for("sort")
                 ips, reps = cpu_sample("sort", 1 << 24, threads, 10.0)
@@ -568,12 +575,14 @@ def run_ours(args):
             if rank == 0:
                 os.write(json_out, (json.dumps(res) + "\n").encode())
             dist.barrier()
+            if not res.get("parity_bit_exact", True):
+                rc = 1
         finally:
             dist.destroy_process_group()
             sys.stdout.flush()
             os.dup2(json_out, 1)
             os.close(json_out)
-        return 0
+        return rc
 
     w = Workload(args.op, n)
     stream = torch.cuda.current_stream()

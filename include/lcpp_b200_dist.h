@@ -1,11 +1,21 @@
 /*
- * lcpp_b200_dist.h -- device building blocks of the distributed sort.
+ * lcpp_b200_dist.h -- sort, scan and reduce across GPUs, one process per GPU.
  *
  * No counterpart in the reference (LCPP is single-GPU; it has no NCCL, MPI
- * or peer-copy code).  The distributed sort itself is orchestrated on the
- * host (luisacompute-parallelprimitive_b200/lcpp_b200/distributed.py) with
- * torch.distributed over NCCL for the exchange; these calls are the device
- * work it needs besides the local sorts.
+ * or peer-copy code).  Each distributed call shards one Device-level call of
+ * the reference over the ranks of a communicator and gives the result that
+ * call gives on the concatenation of the ranks' inputs in rank order:
+ *   lcpp_dist_sort_keys       DeviceRadixSort::SortKeys (device_radix_sort.h:399-425)
+ *   lcpp_dist_inclusive_sum   DeviceScan::InclusiveSum (device_scan.h:337-346)
+ *   lcpp_dist_exclusive_sum   DeviceScan::ExclusiveSum (device_scan.h:321-336)
+ *   lcpp_dist_reduce          DeviceReduce::Reduce (device_reduce.h:229-252)
+ * The communicator wraps an NCCL communicator (libnccl.so.2 is loaded at
+ * run time, only by these calls).  Every rank of the communicator makes the
+ * same calls in the same order, each on its own GPU (the current device when
+ * the communicator was created), with its own temp storage.  The lower part
+ * of this header holds the device building blocks the calls use (sorted
+ * search, merge path, CUDA IPC buffers), exported for callers that compose
+ * their own exchange.
  */
 #ifndef LCPP_B200_DIST_H
 #define LCPP_B200_DIST_H
@@ -17,6 +27,98 @@
 #ifdef __cplusplus
 extern "C" {
 #endif
+
+/* ------------------------------------------------------------------------
+ * Communicator
+ * ---------------------------------------------------------------------- */
+typedef struct lcpp_comm_s* lcpp_comm;
+
+#define LCPP_COMM_ID_BYTES 128
+
+/* A new communicator ID (an NCCL unique ID): one rank creates it and hands
+ * the LCPP_COMM_ID_BYTES bytes to every rank by the caller's own means. */
+lcpp_status lcpp_comm_unique_id(void* id);
+
+/* Collective: every rank calls it with the same ID and nranks, its own rank,
+ * and its GPU current.  Returns LCPP_ERR_COMM when NCCL cannot be loaded or
+ * fails. */
+lcpp_status lcpp_comm_init(const void* id, int nranks, int rank, lcpp_comm* comm);
+
+/* Wraps a caller-owned ncclComm_t (not destroyed by lcpp_comm_destroy). */
+lcpp_status lcpp_comm_from_nccl(void* nccl_comm, lcpp_comm* comm);
+
+/* Releases the communicator and every peer mapping it opened.  Call it after
+ * the last distributed call of every rank has completed. */
+lcpp_status lcpp_comm_destroy(lcpp_comm comm);
+
+lcpp_status lcpp_comm_rank(lcpp_comm comm, int* rank, int* nranks);
+
+/* ------------------------------------------------------------------------
+ * Distributed sort (keys only)
+ *
+ * Rank r passes its n_r keys and receives the keys at global sorted
+ * positions [n_0 + ... + n_{r-1}, n_0 + ... + n_r) of the ascending stable
+ * sort of all ranks' keys (concatenated in rank order): as many keys as it
+ * passed, so keys_out has the size of keys_in and may be the same buffer.
+ * Keys compare as DeviceRadixSort compares them (all bits; -0.0 and +0.0
+ * equal, kept in input order).  Every step runs on the device; the call
+ * waits on the host once, for the G x (G + 1) split matrix.
+ *
+ * exchange: LCPP_EXCHANGE_PEER -- ranks of one host read each other's
+ *   sorted runs over NVLink (CUDA IPC mappings of the peers' temp storage,
+ *   opened at the first call and again whenever a peer's temp allocation
+ *   changes; temp must come from cudaMalloc, as PyTorch's caching allocator
+ *   does); LCPP_EXCHANGE_NCCL -- NCCL send / receive of the runs;
+ *   LCPP_EXCHANGE_AUTO -- peer when every rank is on one host and exported
+ *   its buffer, else NCCL.
+ * times (optional): per-phase device times of this call (the call then
+ *   waits for its own completion). */
+typedef enum lcpp_exchange {
+    LCPP_EXCHANGE_AUTO = 0,
+    LCPP_EXCHANGE_PEER = 1,
+    LCPP_EXCHANGE_NCCL = 2
+} lcpp_exchange;
+
+typedef struct lcpp_dist_sort_times {
+    float local_sort_ms;     /* histogram + onesweep passes of the local keys */
+    float splitters_ms;      /* splitter rounds, tie split, split matrix */
+    float host_wait_ms;      /* host blocked reading the split matrix */
+    float exchange_merge_ms; /* first merge level over peer memory (or NCCL exchange + first level) */
+    float local_merge_ms;    /* remaining merge levels */
+    float total_ms;          /* device time of the whole call */
+    float host_ms;           /* host time of the whole call */
+    int peer_exchange;       /* 1: runs read over peer memory, 0: NCCL send / receive */
+} lcpp_dist_sort_times;
+
+lcpp_status lcpp_dist_sort_keys_temp_bytes(lcpp_comm comm, lcpp_dtype key_dtype, uint64_t n_local,
+                                           size_t* temp_bytes);
+lcpp_status lcpp_dist_sort_keys(lcpp_comm comm, void* temp, size_t temp_bytes, const void* keys_in,
+                                void* keys_out, uint64_t n_local, lcpp_dtype key_dtype, int exchange,
+                                lcpp_dist_sort_times* times, lcpp_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Distributed scan and reduce
+ *
+ * Inclusive / exclusive sum over all ranks' items in rank order: rank r's
+ * out[i] = (items of ranks < r) + in[0] + ... + in[i] (exclusive: up to
+ * in[i - 1]); integer sums wrap.  Reduce: *d_out on every rank = init (op)
+ * items of rank 0 (op) ... (op) items of rank G - 1, the per-rank results
+ * combined in rank order (floating-point results identical on every rank
+ * and from run to run).  No host wait.
+ * ---------------------------------------------------------------------- */
+lcpp_status lcpp_dist_scan_temp_bytes(lcpp_comm comm, lcpp_dtype dtype, uint64_t n_local, size_t* temp_bytes);
+lcpp_status lcpp_dist_inclusive_sum(lcpp_comm comm, void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                                    uint64_t n_local, lcpp_dtype dtype, lcpp_stream_t stream);
+lcpp_status lcpp_dist_exclusive_sum(lcpp_comm comm, void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                                    uint64_t n_local, lcpp_dtype dtype, lcpp_stream_t stream);
+lcpp_status lcpp_dist_reduce_temp_bytes(lcpp_comm comm, lcpp_dtype dtype, uint64_t n_local, size_t* temp_bytes);
+lcpp_status lcpp_dist_reduce(lcpp_comm comm, void* temp, size_t temp_bytes, const void* d_in, void* d_out,
+                             uint64_t n_local, lcpp_op op, const void* init, lcpp_dtype dtype,
+                             lcpp_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Device building blocks
+ * ---------------------------------------------------------------------- */
 
 /* For each query q[i] (an order-preserving key image: the key after the
  * sort's ascending bijection, as unsigned 32-bit for 4-byte keys or 64-bit

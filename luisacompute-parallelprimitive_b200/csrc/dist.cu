@@ -3,24 +3,10 @@
 #include <cstring>
 
 #include "../../include/lcpp_b200_dist.h"
-#include "common.cuh"
+#include "dist.cuh"
 
 namespace lcpp {
 namespace dist {
-
-// Order-preserving image of a key (the ascending radix bijection) with the
-// +-0.0 fold, i.e. the value whose order the radix sort realises.
-template <typename U>
-__device__ __forceinline__ U key_image(U k, const KeyCodec<U>& c)
-{
-    constexpr int kBits = sizeof(U) * 8;
-    constexpr U kHigh = U(1) << (kBits - 1);
-    using S = typename std::conditional<sizeof(U) == 4, int32_t, int64_t>::type;
-    const U sign = U(S(k) >> (kBits - 1));
-    U t = k ^ U(c.xor_pos ^ (sign & (c.xor_pos ^ c.xor_neg)));
-    if (c.fold_zero && t == U(kHigh - 1)) t = kHigh;
-    return t;
-}
 
 template <typename U>
 __global__ void search_sorted_kernel(const U* __restrict__ sorted, uint64_t n, const U* __restrict__ queries,
@@ -28,17 +14,7 @@ __global__ void search_sorted_kernel(const U* __restrict__ sorted, uint64_t n, c
 {
     const uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= nq) return;
-    const U q = queries[i];
-    uint64_t lo = 0, hi = n;  // first index whose image is >= q (> q when upper)
-    while (lo < hi) {
-        const uint64_t mid = lo + (hi - lo) / 2;
-        const U v = key_image(sorted[mid], codec);
-        if (upper ? (v <= q) : (v < q))
-            lo = mid + 1;
-        else
-            hi = mid;
-    }
-    out[i] = lo;
+    out[i] = count_below(sorted, n, queries[i], upper != 0, codec);
 }
 
 }  // namespace dist

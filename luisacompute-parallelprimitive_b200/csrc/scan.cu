@@ -321,8 +321,9 @@ __device__ __forceinline__ void store_items(T* out, uint64_t n, uint64_t tbase, 
 // MODE: 0 exclusive (with init), 1 inclusive, 2 inclusive with init.
 template <typename T, typename Op, int MODE, int BLOCK, int CHUNKS, bool PACKED, bool VECTOR>
 __global__ void __launch_bounds__(BLOCK)
-scan_kernel(const T* in, T* out, uint64_t n, T init, TileState<T, PACKED> ts, Ctrl* ctrl)
+scan_kernel(const T* in, T* out, uint64_t n, T init, const T* init_dev, TileState<T, PACKED> ts, Ctrl* ctrl)
 {
+    if (init_dev) init = *init_dev;  // initial value held in device memory
     using Shape = TileShape<T, BLOCK, CHUNKS>;
     constexpr int VEC = Shape::kVec;
     constexpr int WARPS = Shape::kWarps;
@@ -446,8 +447,10 @@ struct StageSmem {
 //   refill tile k's stage with the next tile id (STAGES - 1 tiles ahead).
 template <typename T, typename Op, int MODE, int BLOCK, int CHUNKS, bool PACKED, int STAGES>
 __global__ void __launch_bounds__(BLOCK)
-scan_bulk_kernel(const T* in, T* out, uint64_t n, uint64_t tiles, T init, TileState<T, PACKED> ts, Ctrl* ctrl)
+scan_bulk_kernel(const T* in, T* out, uint64_t n, uint64_t tiles, T init, const T* init_dev, TileState<T, PACKED> ts,
+                 Ctrl* ctrl)
 {
+    if (init_dev) init = *init_dev;  // initial value held in device memory
     using Shape = TileShape<T, BLOCK, CHUNKS>;
     constexpr int VEC = Shape::kVec;
     constexpr int WARPS = Shape::kWarps;
@@ -650,8 +653,8 @@ Layout make_layout(int tb, uint64_t n)
 }
 
 template <typename T, typename Op, int MODE, bool PACKED>
-void launch_kernel(const T* in, T* out, uint64_t n, uint64_t tiles, T init, const TileState<T, PACKED>& ts,
-                   Ctrl* ctrl, bool aligned, cudaStream_t stream)
+void launch_kernel(const T* in, T* out, uint64_t n, uint64_t tiles, T init, const T* init_dev,
+                   const TileState<T, PACKED>& ts, Ctrl* ctrl, bool aligned, cudaStream_t stream)
 {
     // 16-byte aligned input and output: the persistent bulk-copy kernel;
     // otherwise one tile per block with register loads.
@@ -662,16 +665,16 @@ void launch_kernel(const T* in, T* out, uint64_t n, uint64_t tiles, T init, cons
         const uint64_t resident =
             uint64_t(device_sm_count()) * resident_blocks(reinterpret_cast<const void*>(kernel), kBlock, smem);
         const unsigned grid = unsigned(tiles < resident ? tiles : resident);
-        kernel<<<grid, kBlock, smem, stream>>>(in, out, n, tiles, init, ts, ctrl);
+        kernel<<<grid, kBlock, smem, stream>>>(in, out, n, tiles, init, init_dev, ts, ctrl);
     } else {
         scan_kernel<T, Op, MODE, kBlock, kChunks, PACKED, false><<<unsigned(tiles), kBlock, 0, stream>>>(
-            in, out, n, init, ts, ctrl);
+            in, out, n, init, init_dev, ts, ctrl);
     }
 }
 
 template <typename T, typename Op, int MODE>
 lcpp_status launch(unsigned char* temp, const Layout& L, const T* in, T* out, uint64_t n, T init,
-                   cudaStream_t stream)
+                   const T* init_dev, cudaStream_t stream)
 {
     constexpr bool PACKED = sizeof(T) == 4;
     const size_t zero = (PACKED ? L.flags + size_t(L.tiles) * 8 : L.flags + size_t(L.tiles) * 4) - L.ctrl;
@@ -687,37 +690,38 @@ lcpp_status launch(unsigned char* temp, const Layout& L, const T* in, T* out, ui
     }
     const bool aligned = ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
     diag::KernelTimer timer(2 /* LCPP_KERNEL_SCAN */, n, stream);
-    launch_kernel<T, Op, MODE>(in, out, n, L.tiles, init, ts, ctrl, aligned, stream);
+    launch_kernel<T, Op, MODE>(in, out, n, L.tiles, init, init_dev, ts, ctrl, aligned, stream);
     return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;
 }
 
 template <typename T, int MODE>
 lcpp_status by_op(unsigned char* temp, const Layout& L, const void* in, void* out, uint64_t n,
-                  lcpp_op op, const void* init, cudaStream_t stream)
+                  lcpp_op op, const void* init, const void* init_dev, cudaStream_t stream)
 {
     T init_v{};
     if (init) memcpy(&init_v, init, sizeof(T));
     const T* i = static_cast<const T*>(in);
     T* o = static_cast<T*>(out);
+    const T* id = static_cast<const T*>(init_dev);
     switch (op) {
-    case LCPP_OP_SUM: return launch<T, SumOp, MODE>(temp, L, i, o, n, init_v, stream);
-    case LCPP_OP_MIN: return launch<T, MinOp, MODE>(temp, L, i, o, n, init_v, stream);
-    case LCPP_OP_MAX: return launch<T, MaxOp, MODE>(temp, L, i, o, n, init_v, stream);
+    case LCPP_OP_SUM: return launch<T, SumOp, MODE>(temp, L, i, o, n, init_v, id, stream);
+    case LCPP_OP_MIN: return launch<T, MinOp, MODE>(temp, L, i, o, n, init_v, id, stream);
+    case LCPP_OP_MAX: return launch<T, MaxOp, MODE>(temp, L, i, o, n, init_v, id, stream);
     default: return LCPP_ERR_UNSUPPORTED_DTYPE;
     }
 }
 
 template <int MODE>
 lcpp_status by_type(unsigned char* temp, const Layout& L, const void* in, void* out, uint64_t n,
-                    lcpp_op op, const void* init, lcpp_dtype dt, cudaStream_t stream)
+                    lcpp_op op, const void* init, const void* init_dev, lcpp_dtype dt, cudaStream_t stream)
 {
     switch (dt) {
-    case LCPP_I32: return by_op<int32_t, MODE>(temp, L, in, out, n, op, init, stream);
-    case LCPP_U32: return by_op<uint32_t, MODE>(temp, L, in, out, n, op, init, stream);
-    case LCPP_F32: return by_op<float, MODE>(temp, L, in, out, n, op, init, stream);
-    case LCPP_I64: return by_op<int64_t, MODE>(temp, L, in, out, n, op, init, stream);
-    case LCPP_U64: return by_op<uint64_t, MODE>(temp, L, in, out, n, op, init, stream);
-    case LCPP_F64: return by_op<double, MODE>(temp, L, in, out, n, op, init, stream);
+    case LCPP_I32: return by_op<int32_t, MODE>(temp, L, in, out, n, op, init, init_dev, stream);
+    case LCPP_U32: return by_op<uint32_t, MODE>(temp, L, in, out, n, op, init, init_dev, stream);
+    case LCPP_F32: return by_op<float, MODE>(temp, L, in, out, n, op, init, init_dev, stream);
+    case LCPP_I64: return by_op<int64_t, MODE>(temp, L, in, out, n, op, init, init_dev, stream);
+    case LCPP_U64: return by_op<uint64_t, MODE>(temp, L, in, out, n, op, init, init_dev, stream);
+    case LCPP_F64: return by_op<double, MODE>(temp, L, in, out, n, op, init, init_dev, stream);
     default: return LCPP_ERR_UNSUPPORTED_DTYPE;
     }
 }
@@ -733,11 +737,18 @@ size_t temp_bytes(lcpp_dtype dt, uint64_t n)
 lcpp_status run(void* temp, size_t temp_bytes_given, const void* in, void* out, uint64_t n,
                 lcpp_op op, const void* init, lcpp_dtype dt, int mode, cudaStream_t stream)
 {
+    return run_with_init(temp, temp_bytes_given, in, out, n, op, init, nullptr, dt, mode, stream);
+}
+
+lcpp_status run_with_init(void* temp, size_t temp_bytes_given, const void* in, void* out, uint64_t n, lcpp_op op,
+                          const void* init, const void* init_dev, lcpp_dtype dt, int mode, cudaStream_t stream)
+{
     const int tb = dtype_bytes(dt);
     if (tb == 0) return LCPP_ERR_UNSUPPORTED_DTYPE;
     if (op != LCPP_OP_SUM && op != LCPP_OP_MIN && op != LCPP_OP_MAX) return LCPP_ERR_UNSUPPORTED_DTYPE;
-    if (mode != 1 && !init) return LCPP_ERR_INVALID_ARG;
+    if (mode != 1 && !init && !init_dev) return LCPP_ERR_INVALID_ARG;
     if (n == 0) return LCPP_OK;
+    if (init_dev && reinterpret_cast<uintptr_t>(init_dev) % tb) return LCPP_ERR_INVALID_ARG;
     if (!in || !out) return LCPP_ERR_INVALID_ARG;
     if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) % tb) return LCPP_ERR_INVALID_ARG;
     if (!temp || (reinterpret_cast<uintptr_t>(temp) & (kTempAlign - 1))) return LCPP_ERR_INVALID_ARG;
@@ -746,9 +757,9 @@ lcpp_status run(void* temp, size_t temp_bytes_given, const void* in, void* out, 
     if (L.tiles > 0x7fffffffull) return LCPP_ERR_INVALID_ARG;
     unsigned char* t = static_cast<unsigned char*>(temp);
     switch (mode) {
-    case 0: return by_type<0>(t, L, in, out, n, op, init, dt, stream);
-    case 1: return by_type<1>(t, L, in, out, n, op, init, dt, stream);
-    default: return by_type<2>(t, L, in, out, n, op, init, dt, stream);
+    case 0: return by_type<0>(t, L, in, out, n, op, init, init_dev, dt, stream);
+    case 1: return by_type<1>(t, L, in, out, n, op, init, init_dev, dt, stream);
+    default: return by_type<2>(t, L, in, out, n, op, init, init_dev, dt, stream);
     }
 }
 

@@ -46,6 +46,14 @@ class KernelTime(ctypes.Structure):
     _fields_ = [("kind", ctypes.c_int), ("ms", ctypes.c_float), ("items", ctypes.c_uint64)]
 
 
+class DistSortTimes(ctypes.Structure):
+    """lcpp_dist_sort_times (include/lcpp_b200_dist.h)."""
+    _fields_ = [("local_sort_ms", ctypes.c_float), ("splitters_ms", ctypes.c_float),
+                ("host_wait_ms", ctypes.c_float), ("exchange_merge_ms", ctypes.c_float),
+                ("local_merge_ms", ctypes.c_float), ("total_ms", ctypes.c_float), ("host_ms", ctypes.c_float),
+                ("peer_exchange", ctypes.c_int)]
+
+
 class LcppError(RuntimeError):
     def __init__(self, status: int, what: str):
         self.status = status
@@ -140,6 +148,18 @@ def lib() -> ctypes.CDLL:
         "lcpp_dist_ipc_open": ([vp, ctypes.POINTER(ctypes.c_void_p)], i),
         "lcpp_dist_ipc_close": ([vp], i),
         "lcpp_dist_ipc_free": ([vp], i),
+        "lcpp_comm_unique_id": ([vp], i),
+        "lcpp_comm_init": ([vp, i, i, ctypes.POINTER(ctypes.c_void_p)], i),
+        "lcpp_comm_from_nccl": ([vp, ctypes.POINTER(ctypes.c_void_p)], i),
+        "lcpp_comm_destroy": ([vp], i),
+        "lcpp_comm_rank": ([vp, ip, ip], i),
+        "lcpp_dist_sort_keys_temp_bytes": ([vp, i, u64, szp], i),
+        "lcpp_dist_sort_keys": ([vp, vp, sz, vp, vp, u64, i, i, ctypes.POINTER(DistSortTimes), vp], i),
+        "lcpp_dist_scan_temp_bytes": ([vp, i, u64, szp], i),
+        "lcpp_dist_inclusive_sum": ([vp, vp, sz, vp, vp, u64, i, vp], i),
+        "lcpp_dist_exclusive_sum": ([vp, vp, sz, vp, vp, u64, i, vp], i),
+        "lcpp_dist_reduce_temp_bytes": ([vp, i, u64, szp], i),
+        "lcpp_dist_reduce": ([vp, vp, sz, vp, vp, u64, i, vp, i, vp], i),
         "lcpp_diag_timing_enable": ([i], i),
         "lcpp_diag_wait_timeout_probe": ([vp, sz, u64, vp], i),
         "lcpp_diag_timing_read": ([ctypes.POINTER(KernelTime), i, ip], i),

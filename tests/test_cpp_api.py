@@ -83,3 +83,35 @@ def test_predicate_encoding_runs_on_cpu(tmp_path, lcpp):
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0, run.stdout + run.stderr
     assert run.stdout.startswith("OK "), run.stdout
+
+
+DIST_SRC = ROOT / "tests" / "cpp" / "dist_api_test.cpp"
+
+
+def _dist_cmd(gxx, out: Path):
+    return [gxx, "-std=c++17", "-O2", "-Wall", "-Wextra", "-Werror", f"-I{ROOT / 'include'}",
+            f"-I{CUDA / 'include'}", str(DIST_SRC), "-o", str(out), f"-L{LIBDIR}", "-llcpp_b200",
+            f"-L{CUDA / 'lib64'}", "-lcudart", f"-Wl,-rpath,{LIBDIR}", f"-Wl,-rpath,{CUDA / 'lib64'}"]
+
+
+def test_dist_program_compiles():
+    """The multi-process C++ caller of the distributed C ABI builds (-Wall -Werror)."""
+    gxx = _gxx()
+    r = subprocess.run([gxx, "-std=c++17", "-fsyntax-only", "-Wall", "-Wextra", "-Werror", f"-I{ROOT / 'include'}",
+                        f"-I{CUDA / 'include'}", str(DIST_SRC)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
+@pytest.mark.gpu
+def test_dist_program_runs(tmp_path):
+    """A C++ program sorts, scans and reduces across one process per GPU
+    (up to 8) through the distributed C ABI, with no Python involved."""
+    import torch
+    gxx = _gxx()
+    exe = tmp_path / "dist_api_test"
+    r = subprocess.run(_dist_cmd(gxx, exe), capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    ranks = max(1, min(8, torch.cuda.device_count()))
+    run = subprocess.run([str(exe), str(ranks)], capture_output=True, text=True, timeout=600)
+    assert run.returncode == 0, run.stdout + run.stderr
+    assert run.stdout.startswith(f"OK {ranks}"), run.stdout

@@ -1,7 +1,10 @@
-"""Host logic of the distributed sort on CPU: gloo process groups of 2 and 3
-ranks run lcpp_b200.distributed's splitter selection and exchange with
-numpy stand-ins for the two device operations (local sort, sorted search).
-The GPU path is covered by tests/test_distributed_gpu.py."""
+"""The distributed sort, scan and reduce algorithms on the CPU: gloo process
+groups of 2 and 3 ranks run the host model of lcpp_dist_sort_keys /
+lcpp_dist_inclusive_sum / lcpp_dist_exclusive_sum / lcpp_dist_reduce
+(tests/dist_model.py: the library's steps and collectives, numpy for the
+device work), against a stable host sort of all ranks' keys and numpy
+prefix sums / folds.  The device path is covered by
+tests/test_distributed_gpu.py."""
 from __future__ import annotations
 
 import os
@@ -13,40 +16,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from lcpp_b200.distributed import distributed_sort_keys, key_images_np
-
-
-class NumpyOps:
-    """Test-only host versions of the device operations."""
-
-    device = torch.device("cpu")
-
-    def local_sort(self, keys):
-        a = keys.numpy()
-        return torch.from_numpy(a[np.argsort(key_images_np(a), kind="stable")].copy())
-
-    def search(self, sorted_keys, queries, upper):
-        img = key_images_np(sorted_keys.numpy())
-        q = queries.astype(np.uint64)
-        return torch.from_numpy(np.searchsorted(img, q, side="right" if upper else "left").astype(np.int64))
-
-    def search_bits(self, sorted_keys, queries, upper):
-        q = queries.numpy().view(np.uint32 if queries.element_size() == 4 else np.uint64)
-        return self.search(sorted_keys, q, upper)
-
-    def merge(self, a, b, out):
-        ab = np.concatenate([a.numpy(), b.numpy()])
-        out.copy_(torch.from_numpy(ab[np.argsort(key_images_np(ab), kind="stable")].copy()))
-
-    def merge_level(self, pairs):
-        for a, b, out in pairs:
-            if b is None:
-                out.copy_(a)
-            else:
-                self.merge(a, b, out)
-
-    def empty_like(self, t):
-        return torch.empty_like(t)
+import dist_model
 
 
 def _free_port():
@@ -78,6 +48,8 @@ def _shards(case, world):
         keys = rng.standard_normal(total).astype(np.float32)
         keys[::11] = 0.0
         keys[5::13] = -0.0
+    elif case == "top":  # keys at the very top of the range (last sub-bucket edges)
+        keys = (np.uint32(0xFFFFFFFF) - rng.integers(0, 3, total, dtype=np.uint64).astype(np.uint32))
     out, pos = [], 0
     for s in sizes:
         out.append(keys[pos:pos + s].copy())
@@ -85,45 +57,97 @@ def _shards(case, world):
     return out
 
 
-def _worker(rank, world, port, case, q):
+def _scan_shards(dtype, world):
+    rng = np.random.default_rng(5)
+    sizes = [2000 + 101 * r for r in range(world)]
+    sizes[-1] = 0 if world > 2 else sizes[-1]  # an empty rank
+    if np.dtype(dtype).kind == "f":
+        x = rng.random(sum(sizes)).astype(dtype)
+    else:
+        x = rng.integers(-1000, 1001, sum(sizes)).astype(dtype)
+        x[::97] = np.iinfo(dtype).max  # sums wrap
+    out, pos = [], 0
+    for s in sizes:
+        out.append(x[pos:pos + s].copy())
+        pos += s
+    return out
+
+
+def _worker(rank, world, port, kind, case, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        shard = torch.from_numpy(_shards(case, world)[rank])
-        res = distributed_sort_keys(shard, dist, NumpyOps())
-        q.put((rank, res.numpy().copy()))
+        if kind == "sort":
+            res = dist_model.sort_keys(_shards(case, world)[rank], dist)
+        else:
+            x = _scan_shards(np.dtype(case), world)[rank]
+            res = (dist_model.scan(x, dist, False), dist_model.scan(x, dist, True),
+                   dist_model.reduce(x, dist, "sum", 0), dist_model.reduce(x, dist, "min", 7),
+                   dist_model.reduce(x, dist, "max", 0 if x.dtype.kind == "u" else -3))
+        q.put((rank, res))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-@pytest.mark.parametrize("case", ["uniform", "heavy", "equal", "u64", "i32", "f32", "empty_rank"])
-def test_distributed_sort_gloo(world, case):
+def _run(world, kind, case):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, kind, case, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=120) for _ in range(world))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
+    return got
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("case", ["uniform", "heavy", "equal", "u64", "i32", "f32", "empty_rank", "top"])
+def test_distributed_sort_gloo(world, case):
+    got = _run(world, "sort", case)
     shards = _shards(case, world)
     allk = np.concatenate(shards)
-    expect = allk[np.argsort(key_images_np(allk), kind="stable")]
-    N = allk.size
+    expect = allk[np.argsort(dist_model.images(allk), kind="stable")]
+    pos = 0
+    ubits = np.uint32 if allk.itemsize == 4 else np.uint64
+    for r in range(world):
+        n = shards[r].size
+        assert got[r].size == n  # every rank gets as many keys as it passed
+        # the stable global sort, bit for bit (+-0.0 in input order)
+        np.testing.assert_array_equal(got[r].view(ubits), expect[pos:pos + n].view(ubits))
+        pos += n
+    assert pos == allk.size
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("dtype", ["int32", "uint64", "float32"])
+def test_distributed_scan_reduce_gloo(world, dtype):
+    got = _run(world, "scan", dtype)
+    shards = _scan_shards(np.dtype(dtype), world)
+    allx = np.concatenate(shards)
+    if allx.dtype.kind == "f":
+        inc = np.cumsum(allx.astype(np.float64))
+        tol = 1e-6 * np.log2(max(allx.size, 2))
+    else:
+        inc = np.cumsum(allx.astype(np.uint64), dtype=np.uint64).astype(allx.dtype)  # wraps
+    exc = np.concatenate([np.zeros(1, inc.dtype), inc[:-1]])
     pos = 0
     for r in range(world):
-        lo, hi = r * N // world, (r + 1) * N // world
-        assert got[r].size == hi - lo  # exact balance, duplicates included
-        # same multiset of bit patterns in the same key order; equal keys are
-        # interchangeable for a keys-only sort except for +-0.0, compared by image
-        # the merge of the received runs keeps equal keys in (source rank,
-        # local position) order, so the result is the stable global sort bit
-        # for bit (+-0.0 included)
-        ubits = np.uint32 if got[r].itemsize == 4 else np.uint64
-        np.testing.assert_array_equal(got[r].view(ubits), expect[lo:hi].view(ubits))
-        pos = hi
-    assert pos == N
+        n = shards[r].size
+        a, e, s, mn, mx = got[r]
+        if allx.dtype.kind == "f":
+            np.testing.assert_allclose(a.astype(np.float64), inc[pos:pos + n], rtol=tol, atol=tol)
+            np.testing.assert_allclose(e.astype(np.float64), exc[pos:pos + n], rtol=tol, atol=tol)
+            assert abs(float(s) - allx.astype(np.float64).sum()) <= tol * max(1.0, abs(float(s)))
+        else:
+            np.testing.assert_array_equal(a, inc[pos:pos + n])
+            np.testing.assert_array_equal(e, exc[pos:pos + n])
+            assert s == inc[-1]
+        assert mn == min(allx.min(), allx.dtype.type(7))
+        assert mx == max(allx.max(), allx.dtype.type(0 if allx.dtype.kind == "u" else -3))
+        pos += n
+    # every rank gets the same reductions
+    assert len({(float(got[r][2]), float(got[r][3]), float(got[r][4])) for r in range(world)}) == 1

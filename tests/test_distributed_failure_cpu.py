@@ -16,7 +16,7 @@ torch = pytest.importorskip("torch")
 import torch.distributed as dist  # noqa: E402
 import torch.multiprocessing as mp  # noqa: E402
 
-from test_distributed_cpu import NumpyOps  # noqa: E402
+import dist_model  # noqa: E402
 
 
 def _free_port():
@@ -29,7 +29,6 @@ def _worker(rank, port, mode, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=2, timeout=timedelta(seconds=4))
-    from lcpp_b200.distributed import distributed_sort_keys
     if rank == 1:
         if mode == "dies":
             os._exit(3)  # gone before any collective of the sort
@@ -37,7 +36,7 @@ def _worker(rank, port, mode, q):
         os._exit(0)
     t0 = time.perf_counter()
     try:
-        distributed_sort_keys(torch.from_numpy(np.arange(1000, dtype=np.uint32)), dist, NumpyOps())
+        dist_model.sort_keys(np.arange(1000, dtype=np.uint32), dist)
         q.put(("finished", time.perf_counter() - t0))
     except Exception as e:  # noqa: BLE001 - any error is the expected outcome
         q.put(("error", time.perf_counter() - t0, type(e).__name__))
