@@ -25,6 +25,10 @@ Arms:
                     non-zero when it fails), per-phase times, and the 2^32-key
                     strong-scaling sort with the 1-GPU sort of the same keys
                     timed on rank 0 in the same job.
+  --impl cub        NVIDIA CUB from the CUDA toolkit on the same GPU and the
+                    same inputs (the comparison the reference's own benchmark
+                    makes, tests/cub_bench_kernels.cu:20-75): ops sort, pairs,
+                    scan, reduce; one GPU.
   --impl reference  the reference's own path on the host cores: its CPU
                     restatement (oracle port; the reference cannot be built
                     here), all host threads, a bounded sample of the same
@@ -136,7 +140,7 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "cub"], default="ours")
     ap.add_argument("--op", choices=sorted(OPS), default="sort")
     ap.add_argument("--log2n", type=int, default=None, help="items per GPU = 2^log2n (default: the config's)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -521,6 +525,70 @@ def run_reference(args):
     return 0
 
 
+CUB_OPS = {"sort": 0, "pairs": 1, "scan": 2, "reduce": 3}
+
+
+def run_cub(args):
+    """The same workload through cub::DeviceRadixSort / DeviceScan /
+    DeviceReduce (luisacompute-parallelprimitive_b200/cub_arm), device-resident
+    inputs, CUDA events around the timed steps."""
+    import ctypes
+
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cfg = OPS[args.op]
+    if args.op not in CUB_OPS:
+        print(json.dumps({"impl": "cub", "unavailable": f"no CUB arm for --op {args.op}"}), flush=True)
+        return 0
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    log2n = args.log2n or cfg["log2n"]
+    n = 1 << log2n
+    so = ROOT / "luisacompute-parallelprimitive_b200" / "lcpp_b200" / "libcub_arm.so"
+    lib = ctypes.CDLL(str(so))
+    vp = ctypes.c_void_p
+    lib.cub_arm_run.argtypes = [ctypes.c_int, vp, ctypes.POINTER(ctypes.c_size_t), vp, vp, vp, vp, ctypes.c_uint64,
+                                vp]
+    lib.cub_arm_run.restype = ctypes.c_int
+    ver = lib.cub_arm_version()
+    w = Workload(args.op, n)  # same generators and seeds as our arm
+    i, o = w.inputs, w.outputs
+    ptr = lambda lst, k: vp(lst[k].data_ptr()) if len(lst) > k else vp(0)  # noqa: E731
+    op = CUB_OPS[args.op]
+    stream = torch.cuda.current_stream()
+    nbytes = ctypes.c_size_t(0)
+    assert lib.cub_arm_run(op, None, ctypes.byref(nbytes), ptr(i, 0), ptr(o, 0), ptr(i, 1), ptr(o, 1), n,
+                           vp(stream.cuda_stream)) == 0
+    temp = torch.empty(max(nbytes.value, 1), dtype=torch.uint8, device="cuda")
+
+    def step():
+        assert lib.cub_arm_run(op, vp(temp.data_ptr()), ctypes.byref(nbytes), ptr(i, 0), ptr(o, 0), ptr(i, 1),
+                               ptr(o, 1), n, vp(stream.cuda_stream)) == 0
+
+    for _ in range(args.warmup):
+        step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    value = n / (ms * 1e-3) / 1e9
+    print(json.dumps({
+        "impl": "cub", "metric": cfg["metric"], "value": value, "unit": cfg["unit"], "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": cfg["dtype"], "data": DATA,
+        "config": {"workload": f"{cfg['workload']}, n=2^{log2n}", "library": f"CUB {ver // 100000}.{ver // 100 % 1000}.{ver % 100} "
+                                                                           "(CUDA toolkit headers)",
+                   "l2": "inputs larger than L2; no flush"},
+        "op_roofline": {"bytes_per_item": cfg["bytes"], "achieved": cfg["bytes"] * n / (ms * 1e-3) / 1e9}}),
+        flush=True)
+    return 0
+
+
 def run_ours(args):
     import torch
 
@@ -720,6 +788,8 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.impl == "cub":
+        return run_cub(args)
     return run_ours(args)
 
 

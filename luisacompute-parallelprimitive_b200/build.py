@@ -20,6 +20,10 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "lcpp_b200" / "liblcpp_b200.so"
+# NVIDIA CUB behind a small C ABI: the comparison arm of bench.py --impl cub
+# only, kept out of liblcpp_b200
+CUB_SRC = PKG / "cub_arm" / "cub_arm.cu"
+CUB_LIB = PKG / "lcpp_b200" / "libcub_arm.so"
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 NVCC_FLAGS = [
@@ -68,6 +72,11 @@ def build(verbose_ptxas: bool = False, jobs: int | None = None) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    if CUB_SRC.exists() and (not CUB_LIB.exists() or CUB_SRC.stat().st_mtime > CUB_LIB.stat().st_mtime):
+        cmd = [NVCC, *NVCC_FLAGS, "-shared", str(CUB_SRC), "-o", str(CUB_LIB)]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed for {CUB_SRC.name}:\n{r.stdout}\n{r.stderr}")
     return LIB
 
 

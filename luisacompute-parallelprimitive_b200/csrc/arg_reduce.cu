@@ -35,6 +35,7 @@ template <bool IS_MIN>
 lcpp_status run(void* temp, size_t temp_bytes, const void* in, void* out_v, uint32_t* out_i, uint64_t n,
                 lcpp_dtype dt, cudaStream_t stream)
 {
+    diag::Range nvtx_range("lcpp DeviceReduce::ArgMin/ArgMax");
     const int tb = dtype_bytes(dt);
     if (!tb) return LCPP_ERR_UNSUPPORTED_DTYPE;
     if (!out_v || !out_i) return LCPP_ERR_INVALID_ARG;

@@ -11,6 +11,8 @@
 #include <cstring>
 #include <type_traits>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "../../include/lcpp_b200.h"
 
 namespace lcpp {
@@ -214,6 +216,16 @@ void set_max_dynamic_smem(const void* kernel, size_t bytes);
 int resident_blocks(const void* kernel, int block, size_t dynamic_smem);
 
 namespace diag {
+// Names the host-side extent of one library call in profiler timelines
+// (NVTX; header-only, close to free when no profiler is attached).
+class Range {
+public:
+    explicit Range(const char* name) { nvtxRangePushA(name); }
+    ~Range() { nvtxRangePop(); }
+    Range(const Range&) = delete;
+    Range& operator=(const Range&) = delete;
+};
+
 // Brackets one kernel launch with CUDA events when timing is enabled
 // (lcpp_diag_timing_enable); otherwise a no-op.
 class KernelTimer {

@@ -187,6 +187,7 @@ lcpp_status decomposed_sort(void* temp, size_t temp_bytes_given, const void* key
                             int begin_bit, int end_bit, int descending, lcpp_dtype vdt, bool pairs, bool double_buffer,
                             cudaStream_t stream)
 {
+    diag::Range nvtx_range("lcpp DeviceRadixSort (decomposed keys)");
     using namespace dec;
     Members m{};
     uint32_t total_bits = 0;

@@ -493,6 +493,7 @@ lcpp_status finish_comm(ncclComm_t c, bool owned, lcpp_comm* out)
 lcpp_status dist_scan(lcpp_comm comm, void* temp, size_t temp_bytes, const void* d_in, void* d_out,
                       uint64_t n_local, lcpp_dtype dtype, bool exclusive, lcpp_stream_t stream)
 {
+    diag::Range nvtx_range("lcpp dist scan");
     if (!comm) return LCPP_ERR_INVALID_ARG;
     const int tb = dtype_bytes(dtype);
     if (!tb) return LCPP_ERR_UNSUPPORTED_DTYPE;
@@ -595,6 +596,7 @@ lcpp_status lcpp_dist_sort_keys(lcpp_comm comm, void* temp, size_t temp_bytes, c
                                 uint64_t n_local, lcpp_dtype key_dtype, int exchange, lcpp_dist_sort_times* times,
                                 lcpp_stream_t stream)
 {
+    diag::Range nvtx_range("lcpp dist sort_keys");
     using clock = std::chrono::steady_clock;
     if (!comm) return LCPP_ERR_INVALID_ARG;
     const int kb = dtype_bytes(key_dtype);
@@ -824,6 +826,7 @@ lcpp_status lcpp_dist_reduce_temp_bytes(lcpp_comm comm, lcpp_dtype dtype, uint64
 lcpp_status lcpp_dist_reduce(lcpp_comm comm, void* temp, size_t temp_bytes, const void* d_in, void* d_out,
                              uint64_t n_local, lcpp_op op, const void* init, lcpp_dtype dtype, lcpp_stream_t stream)
 {
+    diag::Range nvtx_range("lcpp dist reduce");
     if (!comm || !init || !d_out) return LCPP_ERR_INVALID_ARG;
     const int tb = dtype_bytes(dtype);
     if (!tb) return LCPP_ERR_UNSUPPORTED_DTYPE;

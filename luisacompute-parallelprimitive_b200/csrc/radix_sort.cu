@@ -823,6 +823,7 @@ lcpp_status sort(void* temp, size_t temp_bytes_given, const void* keys_in, void*
                  int* selector, uint64_t n, int begin_bit, int end_bit, int descending,
                  lcpp_dtype kdt, lcpp_dtype vdt, bool pairs, bool double_buffer, cudaStream_t stream)
 {
+    diag::Range nvtx_range("lcpp DeviceRadixSort");
     if (!key_dtype_ok(kdt)) return LCPP_ERR_UNSUPPORTED_DTYPE;
     if (pairs && !key_dtype_ok(vdt)) return LCPP_ERR_UNSUPPORTED_DTYPE;
     const int kb = dtype_bytes(kdt);

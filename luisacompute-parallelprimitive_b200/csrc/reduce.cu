@@ -217,6 +217,7 @@ size_t temp_bytes(lcpp_dtype dt, uint64_t n)
 lcpp_status run(void* temp, size_t temp_bytes_given, const void* in, void* out, uint64_t n,
                 lcpp_op op, const void* init, lcpp_dtype dt, cudaStream_t stream)
 {
+    diag::Range nvtx_range("lcpp DeviceReduce");
     const int tb = dtype_bytes(dt);
     if (tb == 0) return LCPP_ERR_UNSUPPORTED_DTYPE;
     if (op != LCPP_OP_SUM && op != LCPP_OP_MIN && op != LCPP_OP_MAX) return LCPP_ERR_UNSUPPORTED_DTYPE;

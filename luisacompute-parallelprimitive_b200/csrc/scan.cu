@@ -743,6 +743,7 @@ lcpp_status run(void* temp, size_t temp_bytes_given, const void* in, void* out, 
 lcpp_status run_with_init(void* temp, size_t temp_bytes_given, const void* in, void* out, uint64_t n, lcpp_op op,
                           const void* init, const void* init_dev, lcpp_dtype dt, int mode, cudaStream_t stream)
 {
+    diag::Range nvtx_range("lcpp DeviceScan");
     const int tb = dtype_bytes(dt);
     if (tb == 0) return LCPP_ERR_UNSUPPORTED_DTYPE;
     if (op != LCPP_OP_SUM && op != LCPP_OP_MIN && op != LCPP_OP_MAX) return LCPP_ERR_UNSUPPORTED_DTYPE;

@@ -405,6 +405,7 @@ lcpp_status segmented_sort(void* temp, size_t temp_bytes_given, const void* keys
                            const uint32_t* end_offsets, int begin_bit, int end_bit, int descending, lcpp_dtype kdt,
                            lcpp_dtype vdt, bool pairs, bool double_buffer, cudaStream_t stream)
 {
+    diag::Range nvtx_range("lcpp DeviceSegmentedRadixSort");
     using namespace seg;
     const int kb = dtype_bytes(kdt);
     const int vb = pairs ? dtype_bytes(vdt) : 0;
