@@ -703,6 +703,10 @@ def run_ours(args):
     # library: the upload of step s+1 and the download of step s-1 overlap the
     # op of step s (double-buffered device buffers; the per-step time is the
     # whole run, fill and drain included, divided by the steps).
+    # pinned host buffers are first touched on the GPU's NUMA node
+    from lcpp_b200.distributed import bind_to_gpu_numa_node
+    all_cpus = os.sched_getaffinity(0)
+    numa = bind_to_gpu_numa_node(local)
     host_in = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t) for t in w.inputs]
     host_out = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in w.outputs] for _ in range(2)]
     d_in = [[torch.empty_like(t) for t in w.inputs] for _ in range(2)]
@@ -747,7 +751,9 @@ def run_ours(args):
            "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in w.inputs),
            "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in w.outputs),
            "steps": k_e2e, "ms_per_step": e2e_ms,
-           "pipeline": "3 streams: H2D of step s+1 and D2H of step s-1 overlap the op of step s"}
+           "pipeline": "3 streams: H2D of step s+1 and D2H of step s-1 overlap the op of step s",
+           "numa_node": numa}
+    os.sched_setaffinity(0, all_cpus)  # the CPU baseline below uses every host core
     host_out = host_out[(k_e2e - 1) % 2]
     if args.op in ("sort", "bits", "merge"):  # sanity: what came back is ordered
         ho = host_out[0].numpy()

@@ -964,38 +964,23 @@ struct Args {
     uint32_t* ranks;  // kOutRanks: the exclusive count of selected items before each item
 };
 
-/* SEL: kSelFlag (pick(flag)), kSelIf (pick(item)), kSelUnique (key change by
- * `equal`); OUT: kOutSelect, kOutPartition, kOutThreeWay (pick = first,
- * pick2 = second). */
-template <typename T, typename F, typename V, int SEL, int OUT, typename Pick, typename Pick2, typename Equal>
-__global__ void __launch_bounds__(kBlock)
-compact_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st, Pick pick, Pick2 pick2, Equal equal)
+/* Selection bits of one warp's items x (bit j * kGroup + e): pick(flag)
+ * (kSelFlag), pick(item) (kSelIf; three-way: sel2 = !pick && pick2), or a
+ * key change against the previous item by `equal` (kSelUnique: neighbours
+ * from registers, shuffles, or one load for the warp's first item). */
+template <typename T, typename F, int SEL, bool THREE, typename Pick, typename Pick2, typename Equal>
+__device__ __forceinline__ void select_bits(const T (&x)[kChunks][kGroup], const F (&f)[kChunks][kGroup], const T* in,
+                                            uint64_t n, uint64_t warp_base, int lane, Pick pick, Pick2 pick2,
+                                            Equal equal, uint32_t& sel1, uint32_t& sel2)
 {
-    constexpr bool THREE = OUT == kOutThreeWay;
-    constexpr bool HAS_V = !std::is_same<V, NoValue>::value;
-    __shared__ uint32_t s_tile;
-    __shared__ uint64_t s_total[kWarps];
-    __shared__ uint64_t s_excl[kWarps];
-    __shared__ uint64_t s_prefix;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (threadIdx.x == 0) s_tile = atomicAdd(&ctrl->tile_counter, 1u);
-    __syncthreads();
-    const uint64_t tile = s_tile;
-    const uint64_t n = a.n;
-    const uint64_t warp_base = tile * kTileItems + uint64_t(warp) * (32 * kChunks * kGroup);
-
-    T x[kChunks][kGroup];
-    uint32_t sel1 = 0, sel2 = 0;  // bit j * kGroup + e
+    sel1 = sel2 = 0;
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
         const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
-        load4(a.in, n, g, a.vector, x[j]);
         if constexpr (SEL == kSelFlag) {
-            F f[kGroup];
-            load4(a.flags, n, g, a.vector, f);
 #pragma unroll
             for (int e = 0; e < kGroup; ++e)
-                if (g + e < n && pick(f[e])) sel1 |= 1u << (j * kGroup + e);
+                if (g + e < n && pick(f[j][e])) sel1 |= 1u << (j * kGroup + e);
         } else if constexpr (SEL == kSelIf) {
 #pragma unroll
             for (int e = 0; e < kGroup; ++e) {
@@ -1025,14 +1010,19 @@ compact_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st, Pick
                 else if (j > 0)
                     h = !equal(prev_chunk, x[j][0]);
                 else
-                    h = i == 0 || !equal(a.in[i - 1], x[j][0]);
+                    h = i == 0 || !equal(in[i - 1], x[j][0]);
                 if (h) sel1 |= 1u << (j * kGroup + e);
             }
         }
     }
+}
 
-    /* packed counts: group columns scanned across lanes, carried across columns */
-    uint64_t pre[kChunks];
+/* Per chunk: this lane's exclusive packed count within the warp (group
+ * columns scanned across lanes, carried across columns); returns the warp's
+ * packed total. */
+template <bool THREE>
+__device__ __forceinline__ uint64_t chunk_prefixes(uint32_t sel1, uint32_t sel2, int lane, uint64_t (&pre)[kChunks])
+{
     uint64_t carry = 0;
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
@@ -1047,40 +1037,20 @@ compact_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st, Pick
         pre[j] = carry + incl - c;
         carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    if (lane == 0) s_total[warp] = carry;
-    __syncthreads();
-    if (warp == 0) {
-        const uint64_t t = lane < kWarps ? s_total[lane] : 0;
-        uint64_t incl = t;
-#pragma unroll
-        for (int d = 1; d < kWarps; d <<= 1) {
-            const uint64_t y = __shfl_up_sync(0xffffffffu, incl, d);
-            if (lane >= d) incl += y;
-        }
-        if (lane < kWarps) s_excl[lane] = incl - t;
-        const uint64_t aggregate = __shfl_sync(0xffffffffu, incl, kWarps - 1);
-        uint64_t prefix = 0;
-        if (tile == 0) {
-            if (lane == 0) st.publish(0, kInclusive, aggregate);
-        } else {
-            if (lane == 0) st.publish(tile, kPartial, aggregate);
-            prefix = look_back<THREE>(tile, st, ctrl);
-            if (lane == 0) st.publish(tile, kInclusive, prefix + aggregate);
-        }
-        if (lane == 0) {
-            s_prefix = prefix;
-            if (tile == gridDim.x - 1 && a.num_selected) {
-                a.num_selected[0] = uint32_t(prefix + aggregate);
-                if constexpr (THREE) a.num_selected[1] = uint32_t((prefix + aggregate) >> 32);
-            }
-        }
-    }
-    __syncthreads();
+    return carry;
+}
 
-    uint64_t unsel_end = 0;  // three-way: size of the unselected region
-    if constexpr (THREE) unsel_end = n - ctrl->totals[0] - ctrl->totals[1];
+/* Stores one warp's items once their output positions are known:
+ * warp_prefix = selected items before the warp (packed), pre = per chunk. */
+template <typename T, typename F, typename V, int OUT>
+__device__ __forceinline__ void scatter_items(const Args<T, F, V>& a, const T (&x)[kChunks][kGroup], uint32_t sel1,
+                                              uint32_t sel2, const uint64_t (&pre)[kChunks], uint64_t warp_prefix,
+                                              uint64_t warp_base, int lane, uint64_t unsel_end)
+{
+    constexpr bool THREE = OUT == kOutThreeWay;
+    constexpr bool HAS_V = !std::is_same<V, NoValue>::value;
+    const uint64_t n = a.n;
     V v[kGroup];
-    const uint64_t warp_prefix = s_prefix + s_excl[warp];
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
         const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
@@ -1125,6 +1095,308 @@ compact_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st, Pick
     }
 }
 
+/* SEL: kSelFlag (pick(flag)), kSelIf (pick(item)), kSelUnique (key change by
+ * `equal`); OUT: kOutSelect, kOutPartition, kOutThreeWay (pick = first,
+ * pick2 = second).  One 8192-item tile per block, register loads (any
+ * alignment). */
+template <typename T, typename F, typename V, int SEL, int OUT, typename Pick, typename Pick2, typename Equal>
+__global__ void __launch_bounds__(kBlock)
+compact_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st, Pick pick, Pick2 pick2, Equal equal)
+{
+    constexpr bool THREE = OUT == kOutThreeWay;
+    __shared__ uint32_t s_tile;
+    __shared__ uint64_t s_total[kWarps];
+    __shared__ uint64_t s_excl[kWarps];
+    __shared__ uint64_t s_prefix;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) s_tile = atomicAdd(&ctrl->tile_counter, 1u);
+    __syncthreads();
+    const uint64_t tile = s_tile;
+    const uint64_t n = a.n;
+    const uint64_t warp_base = tile * kTileItems + uint64_t(warp) * (32 * kChunks * kGroup);
+
+    T x[kChunks][kGroup];
+    F f[kChunks][kGroup];
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+        const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
+        load4(a.in, n, g, a.vector, x[j]);
+        if constexpr (SEL == kSelFlag) load4(a.flags, n, g, a.vector, f[j]);
+    }
+    uint32_t sel1, sel2;
+    select_bits<T, F, SEL, THREE>(x, f, a.in, n, warp_base, lane, pick, pick2, equal, sel1, sel2);
+    uint64_t pre[kChunks];
+    const uint64_t carry = chunk_prefixes<THREE>(sel1, sel2, lane, pre);
+    if (lane == 0) s_total[warp] = carry;
+    __syncthreads();
+    if (warp == 0) {
+        const uint64_t t = lane < kWarps ? s_total[lane] : 0;
+        uint64_t incl = t;
+#pragma unroll
+        for (int d = 1; d < kWarps; d <<= 1) {
+            const uint64_t y = __shfl_up_sync(0xffffffffu, incl, d);
+            if (lane >= d) incl += y;
+        }
+        if (lane < kWarps) s_excl[lane] = incl - t;
+        const uint64_t aggregate = __shfl_sync(0xffffffffu, incl, kWarps - 1);
+        uint64_t prefix = 0;
+        if (tile == 0) {
+            if (lane == 0) st.publish(0, kInclusive, aggregate);
+        } else {
+            if (lane == 0) st.publish(tile, kPartial, aggregate);
+            prefix = look_back<THREE>(tile, st, ctrl);
+            if (lane == 0) st.publish(tile, kInclusive, prefix + aggregate);
+        }
+        if (lane == 0) {
+            s_prefix = prefix;
+            if (tile == gridDim.x - 1 && a.num_selected) {
+                a.num_selected[0] = uint32_t(prefix + aggregate);
+                if constexpr (THREE) a.num_selected[1] = uint32_t((prefix + aggregate) >> 32);
+            }
+        }
+    }
+    __syncthreads();
+    const uint64_t unsel_end = THREE ? n - ctrl->totals[0] - ctrl->totals[1] : 0;
+    scatter_items<T, F, V, OUT>(a, x, sel1, sel2, pre, s_prefix + s_excl[warp], warp_base, lane, unsel_end);
+}
+
+/* ---- Persistent variant for 16-byte aligned data ---------------------------
+ * Like the plain scan's persistent kernel: each block keeps kBulkStages tiles
+ * of items (and flags) in flight in shared memory, filled by bulk
+ * asynchronous copies (cp.async.bulk, completion on an mbarrier, no
+ * multicast) up to two tiles ahead.  Per iteration:
+ *   A(k+1): selection counts of tile k+1 as soon as its data is in, and its
+ *           partial count published -- before the look-back of tile k, so no
+ *           later tile's look-back waits on a tile merely queued behind this
+ *           block's current one;
+ *   look-back of tile k (warp 0), its inclusive count published;
+ *   B(k):   tile k's items from shared memory, scattered to their positions;
+ *   the stage of tile k refilled with the block's next tile.
+ * Tile ids come from the atomic counter in increasing order per block, so
+ * the smallest unfinished tile is always one a block is working on.  The
+ * last (partial) tile is loaded with guarded plain loads. */
+constexpr int kBulkBlock = 256;
+constexpr int kBulkWarps = kBulkBlock / 32;
+constexpr uint64_t kBulkTile = uint64_t(kBulkBlock) * kChunks * kGroup;  // 4096 items
+constexpr int kBulkStages = 3;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool bulk_try_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+/* Bounded wait for phase `parity` of `bar`; false on timeout or when another
+ * thread of the call recorded an error. */
+__device__ __forceinline__ bool bulk_wait(uint64_t* bar, uint32_t parity, Ctrl* ctrl)
+{
+    uint64_t t0 = 0;
+    uint32_t spins = 0;
+    while (!bulk_try_wait(bar, parity)) {
+        if (++spins == 16) {
+            spins = 0;
+            if (*static_cast<volatile unsigned int*>(&ctrl->error)) return false;
+            const uint64_t now = global_ns();
+            if (t0 == 0)
+                t0 = now;
+            else if (now - t0 > kWaitLimitNs)
+                return false;
+        }
+    }
+    return true;
+}
+
+template <typename T, typename F, int SEL>
+constexpr size_t bulk_smem_bytes()
+{
+    return size_t(kBulkStages) * kBulkTile * (sizeof(T) + (SEL == kSelFlag ? sizeof(F) : 0));
+}
+
+template <typename T, typename F, typename V, int SEL, int OUT, typename Pick, typename Pick2, typename Equal>
+__global__ void __launch_bounds__(kBulkBlock)
+compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st, uint64_t tiles, Pick pick,
+                    Pick2 pick2, Equal equal)
+{
+    constexpr bool THREE = OUT == kOutThreeWay;
+    constexpr bool FLAGS = SEL == kSelFlag;
+    constexpr uint32_t kItemBytes = uint32_t(kBulkTile * sizeof(T));
+    constexpr uint32_t kFlagBytes = FLAGS ? uint32_t(kBulkTile * sizeof(F)) : 0u;
+    extern __shared__ __align__(128) unsigned char bulk_smem[];
+    T* sx = reinterpret_cast<T*>(bulk_smem);                                            // [stage][tile]
+    F* sf = reinterpret_cast<F*>(bulk_smem + size_t(kBulkStages) * kItemBytes);         // [stage][tile]
+    __shared__ __align__(8) uint64_t s_bar[kBulkStages];
+    __shared__ uint64_t s_tile[kBulkStages];
+    __shared__ uint32_t s_pending;  // bit s: a copy into stage s is in flight
+    __shared__ uint32_t s_phase;    // bit s: parity of the next completion of stage s
+    __shared__ uint32_t s_sel[kBulkStages][2][kBulkBlock];
+    __shared__ uint64_t s_total[kBulkStages][kBulkWarps];
+    __shared__ uint64_t s_excl[kBulkStages][kBulkWarps];
+    __shared__ uint64_t s_agg[kBulkStages];
+    __shared__ uint64_t s_prefix[kBulkStages];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint64_t n = a.n;
+    const int toff = warp * (32 * kChunks * kGroup);  // the warp's first item in the tile
+
+    // next tile id for stage s, and its copy when the tile is full (thread 0)
+    auto acquire = [&](int s) {
+        if (*static_cast<volatile unsigned int*>(&ctrl->error)) {
+            s_tile[s] = tiles;
+            return;
+        }
+        const uint64_t t = atomicAdd(&ctrl->tile_counter, 1u);
+        s_tile[s] = t;
+        if (t < tiles && (t + 1) * kBulkTile <= n) {
+            s_pending |= 1u << s;
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&s_bar[s])),
+                         "r"(kItemBytes + kFlagBytes)
+                         : "memory");
+            bulk_copy(sx + size_t(s) * kBulkTile, a.in + t * kBulkTile, kItemBytes, &s_bar[s]);
+            if constexpr (FLAGS)
+                bulk_copy(sf + size_t(s) * kBulkTile, a.flags + t * kBulkTile, kFlagBytes, &s_bar[s]);
+        }
+    };
+    auto retire = [&](int s) {  // thread 0, after the barrier that follows the wait
+        if (((s_pending >> s) & 1u) && !*static_cast<volatile unsigned int*>(&ctrl->error)) {
+            s_phase ^= 1u << s;
+            s_pending &= ~(1u << s);
+        }
+    };
+    // this thread's items of the tile in stage s
+    auto load = [&](int s, uint64_t tile, bool wait, T (&x)[kChunks][kGroup], F (&f)[kChunks][kGroup]) {
+        const uint64_t warp_base = tile * kBulkTile + uint64_t(toff);
+        if ((tile + 1) * kBulkTile <= n) {
+            if (wait && !bulk_wait(&s_bar[s], (s_phase >> s) & 1u, ctrl)) atomicCAS(&ctrl->error, 0u, kErrTimeout);
+#pragma unroll
+            for (int j = 0; j < kChunks; ++j) {
+                const int at = toff + (j * 32 + lane) * kGroup;
+                memcpy(x[j], sx + size_t(s) * kBulkTile + at, sizeof(x[j]));
+                if constexpr (FLAGS) memcpy(f[j], sf + size_t(s) * kBulkTile + at, sizeof(f[j]));
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < kChunks; ++j) {
+                const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
+                load4(a.in, n, g, false, x[j]);
+                if constexpr (FLAGS) load4(a.flags, n, g, false, f[j]);
+            }
+        }
+    };
+    // A: selection bits (kept for B) and the warp's count (all threads)
+    auto phase_a = [&](int s, uint64_t tile) {
+        T x[kChunks][kGroup];
+        F f[kChunks][kGroup];
+        load(s, tile, true, x, f);
+        uint32_t sel1, sel2;
+        select_bits<T, F, SEL, THREE>(x, f, a.in, n, tile * kBulkTile + uint64_t(toff), lane, pick, pick2, equal,
+                                      sel1, sel2);
+        s_sel[s][0][tid] = sel1;
+        s_sel[s][1][tid] = sel2;
+        uint64_t c = uint64_t(__popc(sel1));
+        if constexpr (THREE) c |= uint64_t(__popc(sel2)) << 32;
+        c = warp_sum(c);
+        if (lane == 0) s_total[s][warp] = c;
+    };
+    // A, warp 0 after a barrier: the tile's aggregate and its partial status
+    auto publish = [&](int s, uint64_t tile) {
+        const uint64_t t = lane < kBulkWarps ? s_total[s][lane] : 0;
+        uint64_t incl = t;
+#pragma unroll
+        for (int d = 1; d < kBulkWarps; d <<= 1) {
+            const uint64_t y = __shfl_up_sync(0xffffffffu, incl, d);
+            if (lane >= d) incl += y;
+        }
+        if (lane < kBulkWarps) s_excl[s][lane] = incl - t;
+        const uint64_t aggregate = __shfl_sync(0xffffffffu, incl, kBulkWarps - 1);
+        if (lane == 0) {
+            s_agg[s] = aggregate;
+            st.publish(tile, tile == 0 ? kInclusive : kPartial, aggregate);
+        }
+    };
+
+    if (tid == 0) {
+        s_pending = 0;
+        s_phase = 0;
+        for (int s = 0; s < kBulkStages; ++s)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&s_bar[s])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int s = 0; s < kBulkStages; ++s) acquire(s);
+    }
+    __syncthreads();
+    if (s_tile[0] < tiles) phase_a(0, s_tile[0]);
+    __syncthreads();
+    if (tid == 0) retire(0);
+    if (warp == 0 && s_tile[0] < tiles) publish(0, s_tile[0]);
+
+    const uint64_t unsel_end = THREE ? n - ctrl->totals[0] - ctrl->totals[1] : 0;
+    for (uint32_t k = 0;; ++k) {
+        const int s = int(k % kBulkStages);
+        const int ns = int((k + 1) % kBulkStages);
+        const uint64_t tile = s_tile[s];
+        if (tile >= tiles) break;
+        const uint64_t next = s_tile[ns];
+        if (next < tiles) phase_a(ns, next);
+        __syncthreads();  // (1) counts of tile k+1 visible
+        if (warp == 0) {
+            if (lane == 0) retire(ns);
+            if (next < tiles) publish(ns, next);
+            uint64_t prefix = 0;
+            if (tile > 0) {
+                prefix = look_back<THREE>(tile, st, ctrl);
+                if (lane == 0) st.publish(tile, kInclusive, prefix + s_agg[s]);
+            }
+            if (lane == 0) {
+                s_prefix[s] = prefix;
+                if (tile == tiles - 1 && a.num_selected) {
+                    a.num_selected[0] = uint32_t(prefix + s_agg[s]);
+                    if constexpr (THREE) a.num_selected[1] = uint32_t((prefix + s_agg[s]) >> 32);
+                }
+            }
+        }
+        __syncthreads();  // (2) prefix of tile k visible
+        {
+            T x[kChunks][kGroup];
+            F f[kChunks][kGroup];
+            load(s, tile, false, x, f);
+            const uint32_t sel1 = s_sel[s][0][tid], sel2 = s_sel[s][1][tid];
+            uint64_t pre[kChunks];
+            chunk_prefixes<THREE>(sel1, sel2, lane, pre);
+            scatter_items<T, F, V, OUT>(a, x, sel1, sel2, pre, s_prefix[s] + s_excl[s][warp],
+                                        tile * kBulkTile + uint64_t(toff), lane, unsel_end);
+        }
+        __syncthreads();  // (3) stage s is free
+        if (tid == 0) {
+            // the stage's generic-proxy reads are ordered before the copy that refills it
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            acquire(s);
+        }
+    }
+    // copies not retired (only after an error): wait for them, bounded,
+    // before the block's shared memory goes away
+    if (tid == 0 && s_pending) {
+        for (int s = 0; s < kBulkStages; ++s)
+            if ((s_pending >> s) & 1u)
+                if (!bulk_wait(&s_bar[s], (s_phase >> s) & 1u, ctrl)) atomicCAS(&ctrl->error, 0u, kErrTimeout);
+    }
+}
+
 struct Layout {
     size_t ctrl, word, second_p, second_i, total;
     uint64_t tiles;
@@ -1133,7 +1405,8 @@ struct Layout {
 inline Layout layout(uint64_t n, bool three)
 {
     Layout L{};
-    L.tiles = n ? (n + kTileItems - 1) / kTileItems : 0;
+    // status rows for the smaller tile of the two kernels
+    L.tiles = n ? (n + kBulkTile - 1) / kBulkTile : 0;
     auto up = [](size_t x) { return (x + kAlign - 1) / kAlign * kAlign; };
     L.ctrl = 0;
     L.word = kAlign;
@@ -1164,11 +1437,11 @@ cudaError_t launch(void* temp, size_t temp_bytes, Args<T, F, V> a, Pick pick, Pi
     cudaError_t e = cudaMemsetAsync(t, 0, L.word + size_t(L.tiles) * 8, stream);
     if (e != cudaSuccess) return e;
     Ctrl* ctrl = reinterpret_cast<Ctrl*>(t);
+    int dev = 0, sms = 0;
+    e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
     if constexpr (THREE) {
-        int dev = 0, sms = 0;
-        e = cudaGetDevice(&dev);
-        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (e != cudaSuccess) return e;
         const uint64_t want = (a.n + kBlock - 1) / kBlock;
         const unsigned grid = unsigned(std::min<uint64_t>(want, uint64_t(sms > 0 ? sms : 1) * 8));
         count_kernel<<<grid, kBlock, 0, stream>>>(a.in, a.n, ctrl, pick, pick2);
@@ -1179,7 +1452,22 @@ cudaError_t launch(void* temp, size_t temp_bytes, Args<T, F, V> a, Pick pick, Pi
                aligned16(a.vout) && aligned16(a.out2) && aligned16(a.out3) && aligned16(a.ranks);
     Status<THREE> st{reinterpret_cast<uint64_t*>(t + L.word), reinterpret_cast<uint32_t*>(t + L.second_p),
                      reinterpret_cast<uint32_t*>(t + L.second_i)};
-    compact_kernel<T, F, V, SEL, OUT><<<unsigned(L.tiles), kBlock, 0, stream>>>(a, ctrl, st, pick, pick2, equal);
+    if (a.vector) {
+        // 16-byte aligned: the persistent bulk-copy kernel, as many blocks as are resident
+        auto kernel = compact_bulk_kernel<T, F, V, SEL, OUT, Pick, Pick2, Equal>;
+        constexpr size_t smem = bulk_smem_bytes<T, F, SEL>();
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        int per_sm = 0;
+        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kBulkBlock, smem);
+        if (e != cudaSuccess) return e;
+        const uint64_t tiles = (a.n + kBulkTile - 1) / kBulkTile;
+        const uint64_t resident = uint64_t(sms > 0 ? sms : 1) * uint64_t(per_sm > 0 ? per_sm : 1);
+        kernel<<<unsigned(std::min(tiles, resident)), kBulkBlock, smem, stream>>>(a, ctrl, st, tiles, pick, pick2,
+                                                                                 equal);
+    } else {
+        const uint64_t tiles = (a.n + kTileItems - 1) / kTileItems;
+        compact_kernel<T, F, V, SEL, OUT><<<unsigned(tiles), kBlock, 0, stream>>>(a, ctrl, st, pick, pick2, equal);
+    }
     return cudaGetLastError();
 }
 

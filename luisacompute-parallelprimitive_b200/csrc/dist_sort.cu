@@ -370,7 +370,10 @@ SortLayout sort_layout(int kb, uint64_t n, int G)
     L.tie_recv = take(16 * size_t(G) * G);
     L.pos = take(8 * size_t(G) * (G + 1));
     L.barrier = take(8);
-    L.splits_bytes = 8 * size_t(ceil_div(n, kMergeTileKeys) + 4 * uint64_t(G) + 8);
+    // split points of one merge level: lcpp_dist_merge_batch_temp_bytes gives
+    // align_up(8 (blocks + merges), 256) with blocks <= ceil(n / tile) + merges
+    // and merges <= G
+    L.splits_bytes = align_up(8 * size_t(ceil_div(n, kMergeTileKeys) + 2 * uint64_t(G)), kTempAlign);
     L.splits = take(L.splits_bytes);
     L.total = off;
     return L;

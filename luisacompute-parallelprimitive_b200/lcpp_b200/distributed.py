@@ -358,6 +358,7 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
         testgen_fill
     G, r = dist.get_world_size(), dist.get_rank()
     dev = torch.device("cuda", torch.cuda.current_device())
+    all_cpus = os.sched_getaffinity(0)
     numa = bind_to_gpu_numa_node(dev.index)
     comm = Comm(dist)
     try:
@@ -446,6 +447,7 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
             strong = strong_scaling_2p32(comm, dist)
     finally:
         comm.close(dist)
+        os.sched_setaffinity(0, all_cpus)
 
     onesweep = [x[1] for x in recs if x[0] == KERNEL_SORT_ONESWEEP]
     avg_pass = sum(onesweep) / max(1, len(onesweep))

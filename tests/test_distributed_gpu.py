@@ -157,6 +157,28 @@ def _worker(rank, world, port, base, q):
         dist.destroy_process_group()
 
 
+def _collect(q, procs, world, limit_s):
+    """Results of all workers; fails as soon as one exits without its
+    result (instead of waiting out the whole limit)."""
+    import queue
+    import time
+    got, t0 = {}, time.monotonic()
+    while len(got) < world:
+        try:
+            t = q.get(timeout=5)
+            got[t[0]] = t[1:]
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            if dead or time.monotonic() - t0 > limit_s:
+                for p in procs:
+                    p.kill()
+                pytest.fail(f"workers failed (exit codes {dead}) or timed out")
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return got
+
+
 @pytest.mark.parametrize("world", [2, 3, 4, 8])
 def test_multi_rank(world):
     """One process per GPU: the distributed sort in both exchange modes and
@@ -172,10 +194,7 @@ def test_multi_rank(world):
     procs = [ctx.Process(target=_worker, args=(r, world, port, base, q)) for r in range(world)]
     for p in procs:
         p.start()
-    got = {t[0]: t[1:] for t in (q.get(timeout=600) for _ in range(world))}
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
+    got = _collect(q, procs, world, 600)
     assert all(got[r][3] == 1 for r in range(world))  # one host: peer exchange
     for name, *_ in _cases(0, base):
         allk = np.concatenate([got[r][0][name][0] for r in range(world)])
