@@ -4,6 +4,8 @@
 #pragma once
 
 #include <cstring>
+#include <limits>
+#include <type_traits>
 
 #include "../../include/lcpp_b200.h"
 #include "../../include/lcpp_b200_device.cuh"
@@ -14,6 +16,12 @@ namespace sel {
 
 namespace sd = lcpp_b200::device::select_detail;
 using lcpp_b200::device::NoValue;
+
+// Internal clause kind: x % d == r for a divisor d whose magnitude is a
+// power of two, evaluated with a mask instead of a division (a holds
+// |d| - 1); C's remainder keeps the sign of x, so a negative signed x with
+// low bits set has remainder (x & (|d| - 1)) - |d|.
+constexpr int kClauseModPow2 = 100;
 
 // AND of up to LCPP_MAX_CLAUSES clauses on a value of type T (the C ABI's
 // stand-in for the reference's predicate lambdas).
@@ -40,6 +48,17 @@ struct ClausePick {
             case LCPP_CLAUSE_MOD_EQ:
                 if constexpr (std::is_integral<T>::value) r = x % a[c] == b[c];
                 else r = false;
+                break;
+            case kClauseModPow2:
+                if constexpr (std::is_integral<T>::value) {
+                    using W = typename std::make_unsigned<T>::type;
+                    W rem = W(x) & W(a[c]);
+                    if constexpr (std::is_signed<T>::value)
+                        if (x < T(0) && rem != W(0)) rem -= W(a[c]) + W(1);
+                    r = T(rem) == b[c];
+                } else {
+                    r = false;
+                }
                 break;
             default:
                 if constexpr (std::is_integral<T>::value) r = (x & a[c]) != 0;
@@ -84,8 +103,22 @@ lcpp_status make_pick(const lcpp_clause* clauses, int count, ClausePick<T>& p)
         p.a[c] = from_bits<T>(clauses[c].a);
         p.b[c] = from_bits<T>(clauses[c].b);
         if (k == LCPP_CLAUSE_MOD_EQ || k == LCPP_CLAUSE_BITS_ANY) {
-            if constexpr (!std::is_integral<T>::value) return LCPP_ERR_INVALID_ARG;
-            else if (k == LCPP_CLAUSE_MOD_EQ && p.a[c] == T(0)) return LCPP_ERR_INVALID_ARG;
+            if constexpr (!std::is_integral<T>::value) {
+                return LCPP_ERR_INVALID_ARG;
+            } else {
+                if (k == LCPP_CLAUSE_MOD_EQ && p.a[c] == T(0)) return LCPP_ERR_INVALID_ARG;
+                if (k == LCPP_CLAUSE_MOD_EQ) {
+                    // |d| a power of two (the most negative value excluded): mask
+                    using W = typename std::make_unsigned<T>::type;
+                    const T d = p.a[c];
+                    const bool most_negative = std::is_signed<T>::value && d == std::numeric_limits<T>::min();
+                    const W mag = (std::is_signed<T>::value && d < T(0)) ? W(W(0) - W(d)) : W(d);
+                    if (!most_negative && (mag & (mag - 1)) == 0) {
+                        p.kind[c] = kClauseModPow2;
+                        p.a[c] = T(mag - 1);
+                    }
+                }
+            }
         }
     }
     return LCPP_OK;

@@ -8,7 +8,9 @@ tests/test_distributed_gpu.py."""
 from __future__ import annotations
 
 import os
+import queue
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -97,7 +99,17 @@ def _run(world, kind, case):
     procs = [ctx.Process(target=_worker, args=(r, world, port, kind, case, q)) for r in range(world)]
     for p in procs:
         p.start()
-    got = dict(q.get(timeout=120) for _ in range(world))
+    got, t0 = {}, time.monotonic()
+    while len(got) < world:  # fail as soon as a worker exits without its result
+        try:
+            r, res = q.get(timeout=2)
+            got[r] = res
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            if dead or time.monotonic() - t0 > 120:
+                for p in procs:
+                    p.kill()
+                pytest.fail(f"workers failed (exit codes {dead}) or timed out")
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

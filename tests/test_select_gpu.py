@@ -229,6 +229,32 @@ def test_select_and_partition_vs_oracle(lcpp, oracle, dtype):
             np.testing.assert_array_equal(host(o)[:w.size], w)
 
 
+@pytest.mark.parametrize("dtype", [np.int32, np.uint32, np.int64, np.uint64])
+def test_mod_eq_divisors_vs_oracle(lcpp, oracle, dtype):
+    """x % d == r with the C remainder for power-of-two |d| (a masked form
+    inside the kernel), other divisors and the most negative divisor, over
+    items spanning the type's full range including its extremes."""
+    info = np.iinfo(dtype)
+    n = 70_001
+    rng = np.random.default_rng(7)
+    x = rng.integers(info.min, info.max, size=n, dtype=dtype, endpoint=True)
+    x[:8] = [info.min, info.max, 0, 1, info.min + 1, info.max - 1, 2, 3]
+    if info.min < 0:
+        x[8::5] = rng.integers(-40, 40, size=x[8::5].size)
+        cases = [(1, 0), (2, 0), (2, 1), (2, -1), (-2, -1), (8, -3), (-16, 5), (1 << 20, -(1 << 19)),
+                 (int(info.max) // 2 + 1, 0), (3, -2), (-5, 4), (int(info.min), 0), (int(info.min), -1)]
+    else:
+        x[8::5] = rng.integers(0, 80, size=x[8::5].size)
+        cases = [(1, 0), (2, 0), (2, 1), (8, 3), (1 << 20, 77), (int(info.max) // 2 + 1, 5), (3, 2), (12, 4)]
+    for d, r in cases:
+        clauses = [(6, 0, d, r)]
+        got, _ = _run_select(lcpp, "if", x, clauses=clauses)
+        np.testing.assert_array_equal(got, oracle.select(x, oracle.clause_mask(x, clauses)), err_msg=f"{d} {r}")
+        clauses = [(6, 1, d, r)]
+        got, _ = _run_select(lcpp, "if", x, clauses=clauses)
+        np.testing.assert_array_equal(got, oracle.select(x, oracle.clause_mask(x, clauses)), err_msg=f"not {d} {r}")
+
+
 def test_unique_by_key_vs_oracle(lcpp, oracle):
     rng = np.random.default_rng(4)
     for n in (4097, 1_000_003):
