@@ -280,8 +280,12 @@ def _timed_steps(fn, steps, dist, stream):
 
 
 def _phase_times(comm, keys, out, dist):
-    """Per-phase times of one call, max over ranks per phase."""
+    """Per-phase times of one call, max over ranks per phase.  The ranks
+    start together: a rank that arrives late would otherwise show up as the
+    others' wait in their first collective (the splitter rounds)."""
     import torch
+    dist.barrier()
+    torch.cuda.synchronize()
     _, t = distributed_sort_keys(keys, comm, out=out, times=True)
     names = ["local_sort_ms", "splitters_ms", "host_wait_ms", "exchange_merge_ms", "local_merge_ms", "total_ms",
              "host_ms"]
