@@ -824,11 +824,15 @@ struct Ctrl {
     unsigned int totals[2];  // three-way: both selected counts (counting pass)
 };
 
-__device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t* p)
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p)
 {
     uint64_t v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(uint64_t* p, uint64_t v)
+{
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ void st_release_u64(uint64_t* p, uint64_t v)
 {
@@ -877,15 +881,26 @@ struct Status {
     uint64_t* word;       // (first count << 32) | status
     uint32_t* second_p;   // three-way: second count of the partial
     uint32_t* second_i;   // three-way: second count of the inclusive prefix
+    // The word carries the first count, so a relaxed store publishes it; the
+    // three-way form's second count is stored first and released by the word.
     __device__ __forceinline__ void publish(uint64_t t, uint32_t status, uint64_t packed) const
     {
-        if constexpr (THREE)
+        const uint64_t w = (uint64_t(uint32_t(packed)) << 32) | status;
+        if constexpr (THREE) {
             *static_cast<volatile uint32_t*>((status == kPartial ? second_p : second_i) + t) = uint32_t(packed >> 32);
-        st_release_u64(word + t, (uint64_t(uint32_t(packed)) << 32) | status);
+            st_release_u64(word + t, w);
+        } else {
+            st_relaxed_u64(word + t, w);
+        }
     }
 };
 
-/* Exclusive packed count of `tile` (> 0), run by one whole warp. */
+/* Exclusive packed count of `tile` (> 0), run by one whole warp: lane l
+ * inspects tile base - l, so one round trip covers 32 predecessors; the walk
+ * ends at the nearest inclusive tile.  Status words are read relaxed: the
+ * first count travels in the word itself, and the three-way form's second
+ * count is read after an acquire fence.  Every wait is bounded; on timeout
+ * the error is recorded and the walk stops. */
 template <bool THREE>
 __device__ __forceinline__ uint64_t look_back(uint64_t tile, const Status<THREE>& st, Ctrl* ctrl)
 {
@@ -895,13 +910,13 @@ __device__ __forceinline__ uint64_t look_back(uint64_t tile, const Status<THREE>
     while (true) {
         const int64_t j = base - lane;
         uint64_t val = 0;
-        uint32_t status = kInclusive;
+        uint32_t status = kInclusive;  // lanes before tile 0 end the walk
         if (j >= 0) {
             uint64_t m;
             uint32_t spins = 0;
             uint64_t t0 = 0;
             bool gave_up = false;
-            while (((m = ld_acquire_u64(st.word + j)) & 3u) == kInvalid) {
+            while (((m = ld_relaxed_u64(st.word + j)) & 3u) == kInvalid) {
                 if (++spins == 64) {
                     spins = 0;
                     const uint64_t now = global_ns();
@@ -909,7 +924,7 @@ __device__ __forceinline__ uint64_t look_back(uint64_t tile, const Status<THREE>
                         t0 = now;
                     } else if (now - t0 > kWaitLimitNs || *static_cast<volatile unsigned int*>(&ctrl->error)) {
                         atomicCAS(&ctrl->error, 0u, kErrTimeout);
-                        gave_up = true;
+                        gave_up = true;  // stop here, contributing nothing
                         break;
                     }
                 }
@@ -917,10 +932,12 @@ __device__ __forceinline__ uint64_t look_back(uint64_t tile, const Status<THREE>
             if (!gave_up) {
                 status = uint32_t(m & 3u);
                 val = m >> 32;
-                if constexpr (THREE)
+                if constexpr (THREE) {
+                    asm volatile("fence.acq_rel.gpu;" ::: "memory");
                     val |= uint64_t(*static_cast<const volatile uint32_t*>(
                                (status == kPartial ? st.second_p : st.second_i) + j))
                            << 32;
+                }
             }
         }
         const uint32_t mask = __ballot_sync(0xffffffffu, status == kInclusive);
@@ -964,6 +981,38 @@ struct Args {
     uint32_t* ranks;  // kOutRanks: the exclusive count of selected items before each item
 };
 
+/* Selection mask of one thread's items (bit j * G + e set when pick holds;
+ * bits at and above C * G are unspecified).  A predicate type may provide
+ * its own select_mask overload, found by argument-dependent lookup, that
+ * evaluates it over all the items at once. */
+template <typename Pick, typename X, int C, int G>
+__device__ __forceinline__ uint32_t select_mask(const Pick& pick, const X (&x)[C][G])
+{
+    uint32_t m = 0;
+#pragma unroll
+    for (int j = 0; j < C; ++j)
+#pragma unroll
+        for (int e = 0; e < G; ++e)
+            if (pick(x[j][e])) m |= 1u << (j * G + e);
+    return m;
+}
+
+/* Bits of a thread's items that lie below n (bit j * kGroup + e). */
+__device__ __forceinline__ uint32_t valid_mask(uint64_t warp_base, int lane, uint64_t n)
+{
+    constexpr uint32_t kAll = (kChunks * kGroup == 32) ? ~0u : ((1u << (kChunks * kGroup)) - 1u);
+    if (warp_base + uint64_t(32 * kChunks * kGroup) <= n) return kAll;
+    uint32_t m = 0;
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+        const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
+#pragma unroll
+        for (int e = 0; e < kGroup; ++e)
+            if (g + e < n) m |= 1u << (j * kGroup + e);
+    }
+    return m;
+}
+
 /* Selection bits of one warp's items x (bit j * kGroup + e): pick(flag)
  * (kSelFlag), pick(item) (kSelIf; three-way: sel2 = !pick && pick2), or a
  * key change against the previous item by `equal` (kSelUnique: neighbours
@@ -974,23 +1023,12 @@ __device__ __forceinline__ void select_bits(const T (&x)[kChunks][kGroup], const
                                             Equal equal, uint32_t& sel1, uint32_t& sel2)
 {
     sel1 = sel2 = 0;
-#pragma unroll
-    for (int j = 0; j < kChunks; ++j) {
-        const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
-        if constexpr (SEL == kSelFlag) {
-#pragma unroll
-            for (int e = 0; e < kGroup; ++e)
-                if (g + e < n && pick(f[j][e])) sel1 |= 1u << (j * kGroup + e);
-        } else if constexpr (SEL == kSelIf) {
-#pragma unroll
-            for (int e = 0; e < kGroup; ++e) {
-                if (g + e >= n) continue;
-                const bool s1 = pick(x[j][e]);
-                if (s1) sel1 |= 1u << (j * kGroup + e);
-                if constexpr (THREE)
-                    if (!s1 && pick2(x[j][e])) sel2 |= 1u << (j * kGroup + e);
-            }
-        }
+    if constexpr (SEL == kSelFlag) {
+        sel1 = select_mask(pick, f) & valid_mask(warp_base, lane, n);
+    } else if constexpr (SEL == kSelIf) {
+        const uint32_t valid = valid_mask(warp_base, lane, n);
+        sel1 = select_mask(pick, x) & valid;
+        if constexpr (THREE) sel2 = select_mask(pick2, x) & valid & ~sel1;
     }
     if constexpr (SEL == kSelUnique) {
 #pragma unroll
@@ -1071,25 +1109,25 @@ __device__ __forceinline__ void scatter_items(const Args<T, F, V>& a, const T (&
                 for (int e = 0; e < kGroup; ++e)
                     if (g + e < n) a.ranks[g + e] = r[e];
             }
-            continue;
-        }
+        } else {
 #pragma unroll
-        for (int e = 0; e < kGroup; ++e) {
-            const uint64_t i = g + e;
-            if (i >= n) continue;
-            const int b = j * kGroup + e;
-            if ((sel1 >> b) & 1u) {
-                a.out[pos1] = x[j][e];
-                if constexpr (HAS_V) a.vout[pos1] = v[e];
-                ++pos1;
-            } else if constexpr (THREE) {
-                if ((sel2 >> b) & 1u) {
-                    a.out2[pos2++] = x[j][e];
-                } else {
-                    a.out3[unsel_end - 1 - (i - pos1 - pos2)] = x[j][e];
+            for (int e = 0; e < kGroup; ++e) {
+                const uint64_t i = g + e;
+                if (i >= n) continue;
+                const int b = j * kGroup + e;
+                if ((sel1 >> b) & 1u) {
+                    a.out[pos1] = x[j][e];
+                    if constexpr (HAS_V) a.vout[pos1] = v[e];
+                    ++pos1;
+                } else if constexpr (THREE) {
+                    if ((sel2 >> b) & 1u) {
+                        a.out2[pos2++] = x[j][e];
+                    } else {
+                        a.out3[unsel_end - 1 - (i - pos1 - pos2)] = x[j][e];
+                    }
+                } else if constexpr (OUT == kOutPartition) {
+                    a.out[n - 1 - (i - pos1)] = x[j][e];
                 }
-            } else if constexpr (OUT == kOutPartition) {
-                a.out[n - 1 - (i - pos1)] = x[j][e];
             }
         }
     }
@@ -1164,20 +1202,41 @@ compact_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st, Pick
  * Like the plain scan's persistent kernel: each block keeps kBulkStages tiles
  * of items (and flags) in flight in shared memory, filled by bulk
  * asynchronous copies (cp.async.bulk, completion on an mbarrier, no
- * multicast) up to two tiles ahead.  Per iteration:
- *   A(k+1): selection counts of tile k+1 as soon as its data is in, and its
- *           partial count published -- before the look-back of tile k, so no
- *           later tile's look-back waits on a tile merely queued behind this
- *           block's current one;
- *   look-back of tile k (warp 0), its inclusive count published;
- *   B(k):   tile k's items from shared memory, scattered to their positions;
- *   the stage of tile k refilled with the block's next tile.
+ * multicast) up to two tiles ahead.  8 or 16 data warps (BulkShape) and
+ * one look-back warp; per iteration, concurrently:
+ *   data warps -- A(k+1): selection bits and counts of tile k+1 as soon as
+ *           its data is in, and its partial count published; staged outputs
+ *           (select / partition / three-way without values): tile k+1
+ *           compacted in place in its shared-memory stage (its items are in
+ *           registers since A) -- selected items first, then the second
+ *           category, then the rest in reverse;
+ *   look-back warp -- the look-back of tile k, its inclusive count
+ *           published;
+ * then, with tile k's prefix known: tile k written out with contiguous
+ * stores (staged), or its items re-read from shared memory and scattered to
+ * their positions (values, ranks); and tile k's stage refilled with the
+ * block's next tile.
  * Tile ids come from the atomic counter in increasing order per block, so
  * the smallest unfinished tile is always one a block is working on.  The
  * last (partial) tile is loaded with guarded plain loads. */
-constexpr int kBulkBlock = 256;
-constexpr int kBulkWarps = kBulkBlock / 32;
-constexpr uint64_t kBulkTile = uint64_t(kBulkBlock) * kChunks * kGroup;  // 4096 items
+template <int BLOCK>
+struct BulkShape {
+    static constexpr int kBlock = BLOCK;  // data threads; one more warp runs the look-backs
+    static constexpr int kWarps = BLOCK / 32;
+    static constexpr int kThreads = BLOCK + 32;
+    static constexpr uint64_t kTile = uint64_t(BLOCK) * kChunks * kGroup;
+};
+/* 512 data threads (8192-item tiles) when an item and its flag take at most
+ * 4 bytes, else 256 (4096-item tiles): bigger tiles mean fewer look-backs,
+ * and fewer tiles in flight for each look-back to walk past. */
+template <typename T, typename F, int SEL>
+constexpr int bulk_block()
+{
+    return sizeof(T) + (SEL == kSelFlag ? sizeof(F) : 0) <= 4 ? 512 : 256;
+}
+template <typename T, typename F, int SEL>
+using BulkOf = BulkShape<bulk_block<T, F, SEL>()>;
+constexpr uint64_t kBulkTileMin = uint64_t(256) * kChunks * kGroup;  // status rows are sized for it
 constexpr int kBulkStages = 3;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
@@ -1227,18 +1286,22 @@ __device__ __forceinline__ bool bulk_wait(uint64_t* bar, uint32_t parity, Ctrl* 
 template <typename T, typename F, int SEL>
 constexpr size_t bulk_smem_bytes()
 {
-    return size_t(kBulkStages) * kBulkTile * (sizeof(T) + (SEL == kSelFlag ? sizeof(F) : 0));
+    return size_t(kBulkStages) * BulkOf<T, F, SEL>::kTile * (sizeof(T) + (SEL == kSelFlag ? sizeof(F) : 0));
 }
 
 template <typename T, typename F, typename V, int SEL, int OUT, typename Pick, typename Pick2, typename Equal>
-__global__ void __launch_bounds__(kBulkBlock)
+__global__ void __launch_bounds__(BulkOf<T, F, SEL>::kThreads)
 compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st, uint64_t tiles, Pick pick,
                     Pick2 pick2, Equal equal)
 {
+    using S = BulkOf<T, F, SEL>;
     constexpr bool THREE = OUT == kOutThreeWay;
     constexpr bool FLAGS = SEL == kSelFlag;
-    constexpr uint32_t kItemBytes = uint32_t(kBulkTile * sizeof(T));
-    constexpr uint32_t kFlagBytes = FLAGS ? uint32_t(kBulkTile * sizeof(F)) : 0u;
+    constexpr bool STAGED = std::is_same<V, NoValue>::value && OUT != kOutRanks;
+    constexpr int kSelRows = STAGED ? 1 : kBulkStages;
+    constexpr int kSelCols = STAGED ? 1 : S::kBlock;
+    constexpr uint32_t kItemBytes = uint32_t(S::kTile * sizeof(T));
+    constexpr uint32_t kFlagBytes = FLAGS ? uint32_t(S::kTile * sizeof(F)) : 0u;
     extern __shared__ __align__(128) unsigned char bulk_smem[];
     T* sx = reinterpret_cast<T*>(bulk_smem);                                            // [stage][tile]
     F* sf = reinterpret_cast<F*>(bulk_smem + size_t(kBulkStages) * kItemBytes);         // [stage][tile]
@@ -1246,14 +1309,16 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
     __shared__ uint64_t s_tile[kBulkStages];
     __shared__ uint32_t s_pending;  // bit s: a copy into stage s is in flight
     __shared__ uint32_t s_phase;    // bit s: parity of the next completion of stage s
-    __shared__ uint32_t s_sel[kBulkStages][2][kBulkBlock];
-    __shared__ uint64_t s_total[kBulkStages][kBulkWarps];
-    __shared__ uint64_t s_excl[kBulkStages][kBulkWarps];
+    __shared__ uint32_t s_sel[kSelRows][2][kSelCols];  // unstaged outputs: selection bits from A to B
+    __shared__ uint64_t s_total[kBulkStages][S::kWarps];
+    __shared__ uint64_t s_excl[kBulkStages][S::kWarps];
     __shared__ uint64_t s_agg[kBulkStages];
     __shared__ uint64_t s_prefix[kBulkStages];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint64_t n = a.n;
     const int toff = warp * (32 * kChunks * kGroup);  // the warp's first item in the tile
+    // barrier of the data warps alone (the look-back warp runs on meanwhile)
+    auto data_sync = [] { asm volatile("bar.sync 1, %0;" ::"n"(S::kBlock) : "memory"); };
 
     // next tile id for stage s, and its copy when the tile is full (thread 0)
     auto acquire = [&](int s) {
@@ -1263,14 +1328,14 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
         }
         const uint64_t t = atomicAdd(&ctrl->tile_counter, 1u);
         s_tile[s] = t;
-        if (t < tiles && (t + 1) * kBulkTile <= n) {
+        if (t < tiles && (t + 1) * S::kTile <= n) {
             s_pending |= 1u << s;
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&s_bar[s])),
                          "r"(kItemBytes + kFlagBytes)
                          : "memory");
-            bulk_copy(sx + size_t(s) * kBulkTile, a.in + t * kBulkTile, kItemBytes, &s_bar[s]);
+            bulk_copy(sx + size_t(s) * S::kTile, a.in + t * S::kTile, kItemBytes, &s_bar[s]);
             if constexpr (FLAGS)
-                bulk_copy(sf + size_t(s) * kBulkTile, a.flags + t * kBulkTile, kFlagBytes, &s_bar[s]);
+                bulk_copy(sf + size_t(s) * S::kTile, a.flags + t * S::kTile, kFlagBytes, &s_bar[s]);
         }
     };
     auto retire = [&](int s) {  // thread 0, after the barrier that follows the wait
@@ -1281,14 +1346,14 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
     };
     // this thread's items of the tile in stage s
     auto load = [&](int s, uint64_t tile, bool wait, T (&x)[kChunks][kGroup], F (&f)[kChunks][kGroup]) {
-        const uint64_t warp_base = tile * kBulkTile + uint64_t(toff);
-        if ((tile + 1) * kBulkTile <= n) {
+        const uint64_t warp_base = tile * S::kTile + uint64_t(toff);
+        if ((tile + 1) * S::kTile <= n) {
             if (wait && !bulk_wait(&s_bar[s], (s_phase >> s) & 1u, ctrl)) atomicCAS(&ctrl->error, 0u, kErrTimeout);
 #pragma unroll
             for (int j = 0; j < kChunks; ++j) {
                 const int at = toff + (j * 32 + lane) * kGroup;
-                memcpy(x[j], sx + size_t(s) * kBulkTile + at, sizeof(x[j]));
-                if constexpr (FLAGS) memcpy(f[j], sf + size_t(s) * kBulkTile + at, sizeof(f[j]));
+                memcpy(x[j], sx + size_t(s) * S::kTile + at, sizeof(x[j]));
+                if constexpr (FLAGS) memcpy(f[j], sf + size_t(s) * S::kTile + at, sizeof(f[j]));
             }
         } else {
 #pragma unroll
@@ -1299,16 +1364,17 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
             }
         }
     };
-    // A: selection bits (kept for B) and the warp's count (all threads)
-    auto phase_a = [&](int s, uint64_t tile) {
-        T x[kChunks][kGroup];
+    // A: selection bits and the warp's count (all threads); the items stay
+    // in x for the staged outputs
+    auto phase_a = [&](int s, uint64_t tile, T (&x)[kChunks][kGroup], uint32_t& sel1, uint32_t& sel2) {
         F f[kChunks][kGroup];
         load(s, tile, true, x, f);
-        uint32_t sel1, sel2;
-        select_bits<T, F, SEL, THREE>(x, f, a.in, n, tile * kBulkTile + uint64_t(toff), lane, pick, pick2, equal,
+        select_bits<T, F, SEL, THREE>(x, f, a.in, n, tile * S::kTile + uint64_t(toff), lane, pick, pick2, equal,
                                       sel1, sel2);
-        s_sel[s][0][tid] = sel1;
-        s_sel[s][1][tid] = sel2;
+        if constexpr (!STAGED) {
+            s_sel[s][0][tid] = sel1;
+            s_sel[s][1][tid] = sel2;
+        }
         uint64_t c = uint64_t(__popc(sel1));
         if constexpr (THREE) c |= uint64_t(__popc(sel2)) << 32;
         c = warp_sum(c);
@@ -1316,21 +1382,108 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
     };
     // A, warp 0 after a barrier: the tile's aggregate and its partial status
     auto publish = [&](int s, uint64_t tile) {
-        const uint64_t t = lane < kBulkWarps ? s_total[s][lane] : 0;
+        const uint64_t t = lane < S::kWarps ? s_total[s][lane] : 0;
         uint64_t incl = t;
 #pragma unroll
-        for (int d = 1; d < kBulkWarps; d <<= 1) {
+        for (int d = 1; d < S::kWarps; d <<= 1) {
             const uint64_t y = __shfl_up_sync(0xffffffffu, incl, d);
             if (lane >= d) incl += y;
         }
-        if (lane < kBulkWarps) s_excl[s][lane] = incl - t;
-        const uint64_t aggregate = __shfl_sync(0xffffffffu, incl, kBulkWarps - 1);
+        if (lane < S::kWarps) s_excl[s][lane] = incl - t;
+        const uint64_t aggregate = __shfl_sync(0xffffffffu, incl, S::kWarps - 1);
         if (lane == 0) {
             s_agg[s] = aggregate;
             st.publish(tile, tile == 0 ? kInclusive : kPartial, aggregate);
         }
     };
+    // staged outputs, all threads after the barrier that follows publish(s):
+    // the tile's items compacted in place in stage s -- selected at [0, c1),
+    // second category at [c1, c1 + c2), the rest at [c1 + c2, items) in
+    // reverse order -- from the registers phase A left them in
+    auto stage = [&](int s, uint64_t tile, const T (&x)[kChunks][kGroup], uint32_t sel1, uint32_t sel2) {
+        const uint32_t items = uint32_t(n - tile * S::kTile < S::kTile ? n - tile * S::kTile : S::kTile);
+        // per-lane counts of each chunk packed in bytes (a chunk holds 128 items of the warp)
+        uint32_t c1 = 0, c2 = 0;
+#pragma unroll
+        for (int j = 0; j < kChunks; ++j) {
+            c1 |= uint32_t(__popc((sel1 >> (j * kGroup)) & 0xFu)) << (8 * j);
+            if constexpr (THREE) c2 |= uint32_t(__popc((sel2 >> (j * kGroup)) & 0xFu)) << (8 * j);
+        }
+        uint32_t i1 = c1, i2 = c2;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t y1 = __shfl_up_sync(0xffffffffu, i1, d);
+            uint32_t y2 = 0;
+            if constexpr (THREE) y2 = __shfl_up_sync(0xffffffffu, i2, d);
+            if (lane >= d) {
+                i1 += y1;
+                if constexpr (THREE) i2 += y2;
+            }
+        }
+        const uint32_t t1 = __shfl_sync(0xffffffffu, i1, 31);
+        uint32_t t2 = 0;
+        if constexpr (THREE) t2 = __shfl_sync(0xffffffffu, i2, 31);
+        const uint32_t e1 = i1 - c1, e2 = i2 - c2;
+        const uint64_t we = s_excl[s][warp];
+        const uint32_t agg1 = uint32_t(s_agg[s]);
+        uint32_t b1 = uint32_t(we), b2 = agg1 + uint32_t(we >> 32);  // chunk bases
+        T* out = sx + size_t(s) * S::kTile;
+#pragma unroll
+        for (int j = 0; j < kChunks; ++j) {
+            uint32_t p1 = b1 + ((e1 >> (8 * j)) & 0xFFu), p2 = b2 + ((e2 >> (8 * j)) & 0xFFu);
+            b1 += (t1 >> (8 * j)) & 0xFFu;
+            if constexpr (THREE) b2 += (t2 >> (8 * j)) & 0xFFu;
+            const uint32_t t0 = uint32_t(toff + (j * 32 + lane) * kGroup);
+#pragma unroll
+            for (int e = 0; e < kGroup; ++e) {
+                const int b = j * kGroup + e;
+                if ((sel1 >> b) & 1u) {
+                    out[p1++] = x[j][e];
+                } else if (THREE && ((sel2 >> b) & 1u)) {
+                    out[p2++] = x[j][e];
+                } else if constexpr (OUT != kOutSelect) {
+                    // rank among the tile's unselected items: t minus the selected ones before it
+                    const uint32_t t = t0 + uint32_t(e);
+                    const uint32_t q = t - p1 - (THREE ? p2 - agg1 : 0u);
+                    if (t < items) out[items - 1 - q] = x[j][e];
+                }
+            }
+        }
+    };
+    // staged outputs, after the look-back of the tile in stage s: its
+    // compacted items written with contiguous stores
+    auto write_out = [&](int s, uint64_t tile, uint64_t unsel_end) {
+        const uint64_t start = tile * S::kTile;
+        const uint32_t items = uint32_t(n - start < S::kTile ? n - start : S::kTile);
+        const uint64_t agg = s_agg[s], prefix = s_prefix[s];
+        const uint32_t c1 = uint32_t(agg);
+        const T* in = sx + size_t(s) * S::kTile;
+        if constexpr (OUT == kOutSelect) {
+            T* o1 = a.out + uint32_t(prefix);
+            for (uint32_t m = uint32_t(tid); m < c1; m += S::kBlock) o1[m] = in[m];
+        } else if constexpr (OUT == kOutPartition) {
+            // unselected rank q (in order) goes to n - 1 - (start - prefix + q), staged at items - 1 - q
+            T* o1 = a.out + prefix;
+            T* o0 = a.out + (n - start - items + prefix);
+            for (uint32_t m = uint32_t(tid); m < items; m += S::kBlock) (m < c1 ? o1 : o0)[m] = in[m];
+        } else {
+            const uint32_t c2 = uint32_t(agg >> 32);
+            const uint64_t p1 = uint32_t(prefix), p2 = prefix >> 32;
+            const uint64_t u = start - p1 - p2;  // unselected items before the tile
+            for (uint32_t m = uint32_t(tid); m < items; m += S::kBlock) {
+                if (m < c1)
+                    a.out[p1 + m] = in[m];
+                else if (m < c1 + c2)
+                    a.out2[p2 + (m - c1)] = in[m];
+                else
+                    a.out3[unsel_end - u - items + m] = in[m];
+            }
+        }
+    };
 
+    T x[kChunks][kGroup];
+    uint32_t sel1 = 0, sel2 = 0;
+    const bool data = warp < S::kWarps;
     if (tid == 0) {
         s_pending = 0;
         s_phase = 0;
@@ -1340,10 +1493,19 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
         for (int s = 0; s < kBulkStages; ++s) acquire(s);
     }
     __syncthreads();
-    if (s_tile[0] < tiles) phase_a(0, s_tile[0]);
+    if (data && s_tile[0] < tiles) {
+        phase_a(0, s_tile[0], x, sel1, sel2);
+        data_sync();
+        if (warp == 0) {
+            if (lane == 0) retire(0);
+            publish(0, s_tile[0]);
+        }
+        if constexpr (STAGED) {
+            data_sync();
+            stage(0, s_tile[0], x, sel1, sel2);
+        }
+    }
     __syncthreads();
-    if (tid == 0) retire(0);
-    if (warp == 0 && s_tile[0] < tiles) publish(0, s_tile[0]);
 
     const uint64_t unsel_end = THREE ? n - ctrl->totals[0] - ctrl->totals[1] : 0;
     for (uint32_t k = 0;; ++k) {
@@ -1352,11 +1514,20 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
         const uint64_t tile = s_tile[s];
         if (tile >= tiles) break;
         const uint64_t next = s_tile[ns];
-        if (next < tiles) phase_a(ns, next);
-        __syncthreads();  // (1) counts of tile k+1 visible
-        if (warp == 0) {
-            if (lane == 0) retire(ns);
-            if (next < tiles) publish(ns, next);
+        if (data) {
+            if (next < tiles) {
+                phase_a(ns, next, x, sel1, sel2);
+                data_sync();  // counts of tile k+1 visible
+                if (warp == 0) {
+                    if (lane == 0) retire(ns);
+                    publish(ns, next);
+                }
+                if constexpr (STAGED) {
+                    data_sync();  // offsets of tile k+1 visible
+                    stage(ns, next, x, sel1, sel2);
+                }
+            }
+        } else {
             uint64_t prefix = 0;
             if (tile > 0) {
                 prefix = look_back<THREE>(tile, st, ctrl);
@@ -1370,20 +1541,24 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
                 }
             }
         }
-        __syncthreads();  // (2) prefix of tile k visible
-        {
-            T x[kChunks][kGroup];
-            F f[kChunks][kGroup];
-            load(s, tile, false, x, f);
-            const uint32_t sel1 = s_sel[s][0][tid], sel2 = s_sel[s][1][tid];
-            uint64_t pre[kChunks];
-            chunk_prefixes<THREE>(sel1, sel2, lane, pre);
-            scatter_items<T, F, V, OUT>(a, x, sel1, sel2, pre, s_prefix[s] + s_excl[s][warp],
-                                        tile * kBulkTile + uint64_t(toff), lane, unsel_end);
+        __syncthreads();  // prefix of tile k visible
+        if (data) {
+            if constexpr (STAGED) {
+                write_out(s, tile, unsel_end);
+            } else {
+                T xs[kChunks][kGroup];
+                F f[kChunks][kGroup];
+                load(s, tile, false, xs, f);
+                const uint32_t b1 = s_sel[s][0][tid], b2 = s_sel[s][1][tid];
+                uint64_t pre[kChunks];
+                chunk_prefixes<THREE>(b1, b2, lane, pre);
+                scatter_items<T, F, V, OUT>(a, xs, b1, b2, pre, s_prefix[s] + s_excl[s][warp],
+                                            tile * S::kTile + uint64_t(toff), lane, unsel_end);
+            }
         }
-        __syncthreads();  // (3) stage s is free
+        __syncthreads();  // stage s is free
         if (tid == 0) {
-            // the stage's generic-proxy reads are ordered before the copy that refills it
+            // the stage's generic-proxy accesses are ordered before the copy that refills it
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             acquire(s);
         }
@@ -1406,7 +1581,7 @@ inline Layout layout(uint64_t n, bool three)
 {
     Layout L{};
     // status rows for the smaller tile of the two kernels
-    L.tiles = n ? (n + kBulkTile - 1) / kBulkTile : 0;
+    L.tiles = n ? (n + kBulkTileMin - 1) / kBulkTileMin : 0;
     auto up = [](size_t x) { return (x + kAlign - 1) / kAlign * kAlign; };
     L.ctrl = 0;
     L.word = kAlign;
@@ -1454,15 +1629,16 @@ cudaError_t launch(void* temp, size_t temp_bytes, Args<T, F, V> a, Pick pick, Pi
                      reinterpret_cast<uint32_t*>(t + L.second_i)};
     if (a.vector) {
         // 16-byte aligned: the persistent bulk-copy kernel, as many blocks as are resident
+        using Shape = BulkOf<T, F, SEL>;
         auto kernel = compact_bulk_kernel<T, F, V, SEL, OUT, Pick, Pick2, Equal>;
         constexpr size_t smem = bulk_smem_bytes<T, F, SEL>();
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         int per_sm = 0;
-        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kBulkBlock, smem);
+        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, Shape::kThreads, smem);
         if (e != cudaSuccess) return e;
-        const uint64_t tiles = (a.n + kBulkTile - 1) / kBulkTile;
+        const uint64_t tiles = (a.n + Shape::kTile - 1) / Shape::kTile;
         const uint64_t resident = uint64_t(sms > 0 ? sms : 1) * uint64_t(per_sm > 0 ? per_sm : 1);
-        kernel<<<unsigned(std::min(tiles, resident)), kBulkBlock, smem, stream>>>(a, ctrl, st, tiles, pick, pick2,
+        kernel<<<unsigned(std::min(tiles, resident)), Shape::kThreads, smem, stream>>>(a, ctrl, st, tiles, pick, pick2,
                                                                                  equal);
     } else {
         const uint64_t tiles = (a.n + kTileItems - 1) / kTileItems;

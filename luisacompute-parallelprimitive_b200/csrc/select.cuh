@@ -23,6 +23,17 @@ using lcpp_b200::device::NoValue;
 // low bits set has remainder (x & (|d| - 1)) - |d|.
 constexpr int kClauseModPow2 = 100;
 
+// x % (mask + 1) == r with C's remainder (sign of x), mask + 1 a power of two.
+template <typename T>
+__device__ __forceinline__ bool mod_pow2_eq(T x, T mask, T r)
+{
+    using W = typename std::make_unsigned<T>::type;
+    W rem = W(x) & W(mask);
+    if constexpr (std::is_signed<T>::value)
+        if (x < T(0) && rem != W(0)) rem -= W(mask) + W(1);
+    return T(rem) == r;
+}
+
 // AND of up to LCPP_MAX_CLAUSES clauses on a value of type T (the C ABI's
 // stand-in for the reference's predicate lambdas).
 template <typename T>
@@ -50,15 +61,8 @@ struct ClausePick {
                 else r = false;
                 break;
             case kClauseModPow2:
-                if constexpr (std::is_integral<T>::value) {
-                    using W = typename std::make_unsigned<T>::type;
-                    W rem = W(x) & W(a[c]);
-                    if constexpr (std::is_signed<T>::value)
-                        if (x < T(0) && rem != W(0)) rem -= W(a[c]) + W(1);
-                    r = T(rem) == b[c];
-                } else {
-                    r = false;
-                }
+                if constexpr (std::is_integral<T>::value) r = mod_pow2_eq(x, a[c], b[c]);
+                else r = false;
                 break;
             default:
                 if constexpr (std::is_integral<T>::value) r = (x & a[c]) != 0;
@@ -71,6 +75,49 @@ struct ClausePick {
         return true;
     }
 };
+
+// The compaction kernels' form: every item of a thread at once (bit
+// j * G + e), one dispatch per clause instead of one per item; found by
+// argument-dependent lookup.
+template <typename T, int C, int G>
+__device__ __forceinline__ uint32_t select_mask(const ClausePick<T>& p, const T (&x)[C][G])
+{
+    auto each = [&](auto test) {
+        uint32_t r = 0;
+#pragma unroll
+        for (int j = 0; j < C; ++j)
+#pragma unroll
+            for (int e = 0; e < G; ++e) r |= uint32_t(test(x[j][e])) << (j * G + e);
+        return r;
+    };
+    uint32_t m = ~0u;
+#pragma unroll
+    for (int c = 0; c < LCPP_MAX_CLAUSES; ++c) {
+        if (c >= p.count) break;
+        const T a = p.a[c], b = p.b[c];
+        uint32_t r = 0;
+        switch (p.kind[c]) {
+        case LCPP_CLAUSE_LT: r = each([&](T v) { return v < a; }); break;
+        case LCPP_CLAUSE_LE: r = each([&](T v) { return v <= a; }); break;
+        case LCPP_CLAUSE_GT: r = each([&](T v) { return v > a; }); break;
+        case LCPP_CLAUSE_GE: r = each([&](T v) { return v >= a; }); break;
+        case LCPP_CLAUSE_EQ: r = each([&](T v) { return v == a; }); break;
+        case LCPP_CLAUSE_NE: r = each([&](T v) { return v != a; }); break;
+        case LCPP_CLAUSE_MOD_EQ:
+            if constexpr (std::is_integral<T>::value) r = each([&](T v) { return v % a == b; });
+            break;
+        case kClauseModPow2:
+            if constexpr (std::is_integral<T>::value) r = each([&](T v) { return mod_pow2_eq(v, a, b); });
+            break;
+        default:
+            if constexpr (std::is_integral<T>::value) r = each([&](T v) { return (v & a) != 0; });
+            break;
+        }
+        if (p.negate[c]) r = ~r;
+        m &= r;
+    }
+    return m;
+}
 
 template <typename T>
 T from_bits(uint64_t bits)
