@@ -360,6 +360,82 @@ cudaError_t ArgMax(void* temp, size_t temp_bytes, const T* d_in, T* d_out, uint3
  * (LCPP_ERR_LOOKBACK_TIMEOUT) at byte 4 of temp storage.
  * ------------------------------------------------------------------------- */
 
+/* Bulk asynchronous copies global -> shared (cp.async.bulk, completion on an
+ * mbarrier, no multicast) for the persistent kernels below. */
+namespace bulk_detail {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
+
+/* dst, src and bytes multiples of 16 */
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool try_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ uint64_t now_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+/* Bounded wait for phase `parity` of `bar`: false after limit_ns, or as soon
+ * as another thread of the call has recorded an error in *error. */
+__device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, const unsigned int* error, uint64_t limit_ns)
+{
+    uint64_t t0 = 0;
+    uint32_t spins = 0;
+    while (!try_wait(bar, parity)) {
+        if (++spins == 16) {
+            spins = 0;
+            if (*static_cast<const volatile unsigned int*>(error)) return false;
+            const uint64_t now = now_ns();
+            if (t0 == 0)
+                t0 = now;
+            else if (now - t0 > limit_ns)
+                return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void init_barrier(uint64_t* bar)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)) : "memory");
+}
+
+/* thread 0 before the block's first copy, after init_barrier */
+__device__ __forceinline__ void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+/* one arrival that expects `bytes` of copies on bar */
+__device__ __forceinline__ void expect_bytes(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+/* orders this thread's (and, after a barrier, the block's) generic-proxy
+ * accesses to shared memory before a later bulk copy into it */
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+}  // namespace bulk_detail
+
 /* key equality (the reference's default `lhs == rhs`) */
 struct EqualTo {
     template <typename K>
@@ -440,17 +516,62 @@ __device__ __forceinline__ uint64_t global_ns()
     return t;
 }
 
-/* Tile status: meta[t] = (head count << 32) | status, released after the
- * value it announces (partial[t] or inclusive[t]) is stored. */
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p)
+{
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(uint64_t* p, uint64_t v)
+{
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+/* Tile status.  Packed (4-byte values, head counts below 2^30): meta[t] =
+ * (value << 32) | (head count << 2) | status, one word published and read
+ * with relaxed accesses.  Otherwise meta[t] = (head count << 32) | status,
+ * released after the value it announces (partial[t] or inclusive[t]) is
+ * stored, and read with acquire. */
 template <typename V>
 struct TileStatus {
     uint64_t* meta;
     V* partial;
     V* inclusive;
+    bool packed;
     __device__ __forceinline__ void publish(uint64_t t, uint32_t status, const Acc<V>& a) const
     {
+        if constexpr (sizeof(V) == 4) {
+            if (packed) {
+                uint32_t bits;
+                memcpy(&bits, &a.v, 4);
+                st_relaxed_u64(meta + t, (uint64_t(bits) << 32) | (uint64_t(a.c) << 2) | status);
+                return;
+            }
+        }
         *static_cast<volatile V*>(status == kPartial ? partial + t : inclusive + t) = a.v;
         st_release_u64(meta + t, (uint64_t(a.c) << 32) | status);
+    }
+    /* tile t's status word (0 = not published yet) */
+    __device__ __forceinline__ uint64_t word(uint64_t t) const
+    {
+        return packed ? ld_relaxed_u64(meta + t) : ld_acquire_u64(meta + t);
+    }
+    /* the pair a published word announces */
+    __device__ __forceinline__ Acc<V> pair(uint64_t t, uint64_t m) const
+    {
+        Acc<V> r;
+        r.has = 1;
+        if constexpr (sizeof(V) == 4) {
+            if (packed) {
+                r.c = uint32_t(m >> 2) & 0x3fffffffu;
+                const uint32_t bits = uint32_t(m >> 32);
+                memcpy(&r.v, &bits, 4);
+                return r;
+            }
+        }
+        r.c = uint32_t(m >> 32);
+        r.v = *static_cast<const volatile V*>((m & 3u) == kPartial ? partial + t : inclusive + t);
+        return r;
     }
 };
 
@@ -472,7 +593,7 @@ __device__ __forceinline__ Acc<V> look_back(uint64_t tile, const TileStatus<V>& 
             uint32_t spins = 0;
             uint64_t t0 = 0;
             bool gave_up = false;
-            while (((m = ld_acquire_u64(ts.meta + j)) & 3u) == kInvalid) {
+            while (((m = ts.word(uint64_t(j))) & 3u) == kInvalid) {
                 if (++spins == 64) {
                     spins = 0;
                     const uint64_t now = global_ns();
@@ -487,9 +608,7 @@ __device__ __forceinline__ Acc<V> look_back(uint64_t tile, const TileStatus<V>& 
             }
             if (!gave_up) {
                 status = uint32_t(m & 3u);
-                val.c = uint32_t(m >> 32);
-                val.has = 1;
-                val.v = *static_cast<const volatile V*>(status == kPartial ? ts.partial + j : ts.inclusive + j);
+                val = ts.pair(uint64_t(j), m);
             }
         }
         const bool stop = status == kInclusive || (!COUNT && val.has && val.c != 0);
@@ -541,34 +660,13 @@ __device__ __forceinline__ void store_group(T* p, uint64_t n, uint64_t g, bool v
     }
 }
 
-/* One tile per block.  mode: kModeExclusive / kModeInclusive /
- * kModeInclusiveInit write out[]; kModeReduce writes unique_out[],
- * out[] (= the aggregates) and *num_runs. */
-template <typename K, typename V, bool COUNT, typename Equal, typename Op>
-__global__ void __launch_bounds__(kBlock, (sizeof(K) + sizeof(V) <= 8) ? 3 : 2)
-by_key_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* num_runs, uint64_t n, int mode,
-              V init, bool vector, Ctrl* ctrl, TileStatus<V> ts, Equal equal, Op op)
+/* Head flags of a thread's items (bit j * kGroup + e); padding past n is a
+ * head of its own.  `before` is the key preceding the warp's first item
+ * (ignored for item 0). */
+template <typename K, typename Equal>
+__device__ __forceinline__ uint32_t head_bits(const K (&k)[kChunks][kGroup], K before, uint64_t n,
+                                              uint64_t warp_base, int lane, const Equal& equal)
 {
-    __shared__ uint32_t s_tile;
-    __shared__ Acc<V> s_total[kWarps];
-    __shared__ Acc<V> s_excl[kWarps];
-    __shared__ Acc<V> s_prefix;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (threadIdx.x == 0) s_tile = atomicAdd(&ctrl->tile_counter, 1u);
-    __syncthreads();
-    const uint64_t tile = s_tile;
-    const uint64_t warp_base = tile * kTileItems + uint64_t(warp) * (32 * kChunks * kGroup);
-
-    K k[kChunks][kGroup];
-    V v[kChunks][kGroup];
-#pragma unroll
-    for (int j = 0; j < kChunks; ++j) {
-        const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
-        load_group(keys, n, g, vector, k[j]);
-        load_group(values, n, g, vector, v[j]);
-    }
-
-    /* head flags: bit j * kGroup + e; padding past n is a head of its own */
     uint32_t heads = 0;
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
@@ -588,13 +686,20 @@ by_key_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* n
             else if (j > 0)
                 h = !equal(prev_chunk, k[j][0]);
             else
-                h = i == 0 || !equal(keys[i - 1], k[j][0]);
+                h = i == 0 || !equal(before, k[j][0]);
             heads |= uint32_t(h) << (j * kGroup + e);
         }
     }
+    return heads;
+}
 
-    /* per-lane group folds, then warp scans chunk by chunk */
-    Acc<V> pre[kChunks];
+/* Per-lane group folds, then warp scans chunk by chunk: pre[j] = the
+ * exclusive prefix of chunk j's group within the warp; returns the warp's
+ * total (every lane). */
+template <bool COUNT, typename V, typename Op>
+__device__ __forceinline__ Acc<V> group_scans(const V (&v)[kChunks][kGroup], uint32_t heads, int lane,
+                                              Acc<V> (&pre)[kChunks], const Op& op)
+{
     Acc<V> carry{0, 0, V{}};
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
@@ -618,33 +723,36 @@ by_key_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* n
         pre[j] = seg<COUNT>(carry, ex, op);
         carry = seg<COUNT>(carry, shfl_acc(x, 31), op);
     }
-    if (lane == 0) s_total[warp] = carry;
-    __syncthreads();
+    return carry;
+}
 
-    if (warp == 0) {
-        Acc<V> x = lane < kWarps ? s_total[lane] : Acc<V>{0, 0, V{}};
+/* Warp 0: the tile's warp totals folded in order; excl[w] = the prefix of
+ * warp w within the tile; returns the tile's aggregate (every lane). */
+template <bool COUNT, int WARPS, typename V, typename Op>
+__device__ __forceinline__ Acc<V> block_fold(const Acc<V>* total, Acc<V>* excl, int lane, const Op& op)
+{
+    Acc<V> x = lane < WARPS ? total[lane] : Acc<V>{0, 0, V{}};
 #pragma unroll
-        for (int d = 1; d < kWarps; d <<= 1) {
-            const Acc<V> y = shfl_up_acc(x, d);
-            if (lane >= d) x = seg<COUNT>(y, x, op);
-        }
-        Acc<V> ex = shfl_up_acc(x, 1);
-        if (lane == 0) ex = Acc<V>{0, 0, V{}};
-        if (lane < kWarps) s_excl[lane] = ex;
-        const Acc<V> aggregate = shfl_acc(x, kWarps - 1);
-        Acc<V> prefix{0, 0, V{}};
-        if (tile == 0) {
-            if (lane == 0) ts.publish(0, kInclusive, aggregate);
-        } else {
-            if (lane == 0) ts.publish(tile, kPartial, aggregate);
-            prefix = look_back<COUNT>(tile, ts, ctrl, op);
-            if (lane == 0) ts.publish(tile, kInclusive, seg<COUNT>(prefix, aggregate, op));
-        }
-        if (lane == 0) s_prefix = prefix;
+    for (int d = 1; d < WARPS; d <<= 1) {
+        const Acc<V> y = shfl_up_acc(x, d);
+        if (lane >= d) x = seg<COUNT>(y, x, op);
     }
-    __syncthreads();
+    Acc<V> ex = shfl_up_acc(x, 1);
+    if (lane == 0) ex = Acc<V>{0, 0, V{}};
+    if (lane < WARPS) excl[lane] = ex;
+    return shfl_acc(x, WARPS - 1);
+}
 
-    const Acc<V> warp_prefix = seg<COUNT>(s_prefix, s_excl[warp], op);
+/* Outputs of a thread's items once the exclusive prefix of its warp is
+ * known.  mode: kModeExclusive / kModeInclusive / kModeInclusiveInit write
+ * out[]; kModeReduce (COUNT only; k holds the keys) writes unique_out[],
+ * out[] (= the aggregates) and *num_runs. */
+template <bool COUNT, int KC, typename K, typename V, typename Op>
+__device__ __forceinline__ void emit(const K (&k)[KC][kGroup], const V (&v)[kChunks][kGroup], uint32_t heads,
+                                     const Acc<V> (&pre)[kChunks], const Acc<V>& warp_prefix, uint64_t warp_base,
+                                     int lane, uint64_t n, int mode, V init, V* out, K* unique_out,
+                                     uint32_t* num_runs, bool vector, const Op& op)
+{
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
         const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
@@ -669,20 +777,267 @@ by_key_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* n
                 o[e] = P.v;
             } else if (mode == kModeInclusiveInit) {
                 o[e] = op(init, P.v);
-            } else if (i < n) {
-                if (h) {
-                    const uint32_t r = P.c - 1;
-                    unique_out[r] = k[j][e];
-                    if (r > 0) out[r - 1] = E.v;
-                }
-                if (i == n - 1) {
-                    out[P.c - 1] = P.v;
-                    *num_runs = P.c;
+            } else if constexpr (COUNT) {
+                if (i < n) {
+                    if (h) {
+                        const uint32_t r = P.c - 1;
+                        unique_out[r] = k[j][e];
+                        if (r > 0) out[r - 1] = E.v;
+                    }
+                    if (i == n - 1) {
+                        out[P.c - 1] = P.v;
+                        *num_runs = P.c;
+                    }
                 }
             }
             E = P;
         }
         if (mode != kModeReduce) store_group(out, n, g, vector, o);
+    }
+}
+
+/* One tile per block (any alignment). */
+template <typename K, typename V, bool COUNT, typename Equal, typename Op>
+__global__ void __launch_bounds__(kBlock, (sizeof(K) + sizeof(V) <= 8) ? 3 : 2)
+by_key_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* num_runs, uint64_t n, int mode,
+              V init, bool vector, Ctrl* ctrl, TileStatus<V> ts, Equal equal, Op op)
+{
+    __shared__ uint32_t s_tile;
+    __shared__ Acc<V> s_total[kWarps];
+    __shared__ Acc<V> s_excl[kWarps];
+    __shared__ Acc<V> s_prefix;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) s_tile = atomicAdd(&ctrl->tile_counter, 1u);
+    __syncthreads();
+    const uint64_t tile = s_tile;
+    const uint64_t warp_base = tile * kTileItems + uint64_t(warp) * (32 * kChunks * kGroup);
+
+    K k[kChunks][kGroup];
+    V v[kChunks][kGroup];
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+        const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
+        load_group(keys, n, g, vector, k[j]);
+        load_group(values, n, g, vector, v[j]);
+    }
+    const K before = lane == 0 && warp_base > 0 && warp_base < n ? keys[warp_base - 1] : K{};
+    const uint32_t heads = head_bits(k, before, n, warp_base, lane, equal);
+    Acc<V> pre[kChunks];
+    const Acc<V> carry = group_scans<COUNT>(v, heads, lane, pre, op);
+    if (lane == 0) s_total[warp] = carry;
+    __syncthreads();
+
+    if (warp == 0) {
+        const Acc<V> aggregate = block_fold<COUNT, kWarps>(s_total, s_excl, lane, op);
+        Acc<V> prefix{0, 0, V{}};
+        if (tile == 0) {
+            if (lane == 0) ts.publish(0, kInclusive, aggregate);
+        } else {
+            if (lane == 0) ts.publish(tile, kPartial, aggregate);
+            prefix = look_back<COUNT>(tile, ts, ctrl, op);
+            if (lane == 0) ts.publish(tile, kInclusive, seg<COUNT>(prefix, aggregate, op));
+        }
+        if (lane == 0) s_prefix = prefix;
+    }
+    __syncthreads();
+    emit<COUNT>(k, v, heads, pre, seg<COUNT>(s_prefix, s_excl[warp], op), warp_base, lane, n, mode, init, out,
+                unique_out, num_runs, vector, op);
+}
+
+/* ---- Persistent variant for 16-byte aligned keys and values ---------------
+ * Like the compaction's: tiles are taken from the atomic counter and their
+ * keys and values bulk-copied into a three-stage shared-memory ring.  Eight
+ * data warps and one look-back warp; per iteration, concurrently:
+ *   data warps -- A(k+1): heads and warp scans of tile k+1 from its stage
+ *           (heads and per-chunk prefixes stay in registers), its partial
+ *           published;
+ *   look-back warp -- the look-back of tile k, its inclusive published;
+ * then, with tile k's prefix known, the data warps re-read tile k's values
+ * (and keys) from its stage, write its outputs, and the stage is refilled
+ * with the block's next tile.  The two register sets alternate. */
+constexpr int kBulkThreads = kBlock + 32;
+constexpr int kBulkStages = 3;
+constexpr int kIdSlots = 4;  // tile ids of tiles k .. k+3 (k+3: acquired at the end of iteration k)
+
+template <typename K, typename V>
+constexpr size_t bulk_smem_bytes()
+{
+    return size_t(kBulkStages) * kTileItems * (sizeof(K) + sizeof(V));
+}
+
+/* What A(k) leaves in registers for the output phase of tile k. */
+template <typename V>
+struct TileRegs {
+    uint64_t tile;
+    uint32_t heads;
+    Acc<V> pre[kChunks];
+};
+
+template <typename K, typename V, bool COUNT, typename Equal, typename Op>
+__global__ void __launch_bounds__(kBulkThreads, (sizeof(K) + sizeof(V) <= 8) ? 2 : 1)
+by_key_bulk_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* num_runs, uint64_t n, int mode,
+                   V init, bool vector, uint64_t tiles, Ctrl* ctrl, TileStatus<V> ts, Equal equal, Op op)
+{
+    constexpr uint32_t kKeyBytes = uint32_t(kTileItems * sizeof(K));
+    constexpr uint32_t kValueBytes = uint32_t(kTileItems * sizeof(V));
+    extern __shared__ __align__(128) unsigned char bulk_smem[];
+    K* sk = reinterpret_cast<K*>(bulk_smem);                                     // [stage][tile]
+    V* sv = reinterpret_cast<V*>(bulk_smem + size_t(kBulkStages) * kKeyBytes);  // [stage][tile]
+    __shared__ __align__(8) uint64_t s_bar[kBulkStages];
+    __shared__ uint64_t s_id[kIdSlots];  // tile id of the block's i-th tile at i % kIdSlots
+    __shared__ uint32_t s_pending;       // bit s: a copy into stage s is in flight
+    __shared__ uint32_t s_phase;         // bit s: parity of the next completion of stage s
+    __shared__ Acc<V> s_total[kBulkStages][kWarps];
+    __shared__ Acc<V> s_excl[kBulkStages][kWarps];
+    __shared__ Acc<V> s_agg[kBulkStages];
+    __shared__ Acc<V> s_prefix[kBulkStages];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool data = warp < kWarps;
+    const int toff = warp * (32 * kChunks * kGroup);  // the warp's first item in the tile
+    auto data_sync = [] { asm volatile("bar.sync 1, %0;" ::"n"(kBlock) : "memory"); };
+
+    // the block's i-th tile: its id, and its copy into stage i % 3 when full (thread 0)
+    auto acquire = [&](uint32_t i) {
+        const int s = int(i % kBulkStages);
+        if (*static_cast<volatile unsigned int*>(&ctrl->error)) {
+            s_id[i % kIdSlots] = tiles;
+            return;
+        }
+        const uint64_t t = atomicAdd(&ctrl->tile_counter, 1u);
+        s_id[i % kIdSlots] = t;
+        if (t < tiles && (t + 1) * kTileItems <= n) {
+            s_pending |= 1u << s;
+            bulk_detail::expect_bytes(&s_bar[s], kKeyBytes + kValueBytes);
+            bulk_detail::bulk_copy(sk + size_t(s) * kTileItems, keys + t * kTileItems, kKeyBytes, &s_bar[s]);
+            bulk_detail::bulk_copy(sv + size_t(s) * kTileItems, values + t * kTileItems, kValueBytes, &s_bar[s]);
+        }
+    };
+    // this thread's keys and values of the block's i-th tile
+    auto load = [&](uint32_t i, uint64_t tile, bool wait, K (&k)[kChunks][kGroup], V (&v)[kChunks][kGroup],
+                    bool want_keys) {
+        const int s = int(i % kBulkStages);
+        const uint64_t warp_base = tile * kTileItems + uint64_t(toff);
+        if ((tile + 1) * kTileItems <= n) {
+            if (wait && !bulk_detail::wait(&s_bar[s], (s_phase >> s) & 1u, &ctrl->error, kWaitLimitNs))
+                atomicCAS(&ctrl->error, 0u, kErrTimeout);
+#pragma unroll
+            for (int j = 0; j < kChunks; ++j) {
+                const int at = toff + (j * 32 + lane) * kGroup;
+                if (want_keys) memcpy(k[j], sk + size_t(s) * kTileItems + at, sizeof(k[j]));
+                memcpy(v[j], sv + size_t(s) * kTileItems + at, sizeof(v[j]));
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < kChunks; ++j) {
+                const uint64_t g = warp_base + uint64_t(j * 32 + lane) * kGroup;
+                if (want_keys) load_group(keys, n, g, false, k[j]);
+                load_group(values, n, g, false, v[j]);
+            }
+        }
+    };
+    // A(i): heads and warp scans of the block's i-th tile into r, its warp totals into s_total
+    auto phase_a = [&](uint32_t i, TileRegs<V>& r) {
+        const int s = int(i % kBulkStages);
+        const uint64_t tile = s_id[i % kIdSlots];
+        const uint64_t warp_base = tile * kTileItems + uint64_t(toff);
+        K k[kChunks][kGroup];
+        V v[kChunks][kGroup];
+        load(i, tile, true, k, v, true);
+        K before{};
+        if (lane == 0 && warp_base > 0 && warp_base < n) {
+            const bool staged = (tile + 1) * kTileItems <= n && toff > 0;
+            before = staged ? sk[size_t(s) * kTileItems + toff - 1] : keys[warp_base - 1];
+        }
+        r.tile = tile;
+        r.heads = head_bits(k, before, n, warp_base, lane, equal);
+        const Acc<V> carry = group_scans<COUNT>(v, r.heads, lane, r.pre, op);
+        if (lane == 0) s_total[s][warp] = carry;
+    };
+    // after A(i) and a barrier of the data warps: warp 0 folds the warp
+    // totals and publishes the tile's partial, thread 0 retires its copy
+    auto after_a = [&](uint32_t i) {
+        const int s = int(i % kBulkStages);
+        if (warp != 0) return;
+        const uint64_t tile = s_id[i % kIdSlots];
+        const Acc<V> aggregate = block_fold<COUNT, kWarps>(s_total[s], s_excl[s], lane, op);
+        if (lane == 0) {
+            s_agg[s] = aggregate;
+            ts.publish(tile, tile == 0 ? kInclusive : kPartial, aggregate);
+            if (((s_pending >> s) & 1u) && !*static_cast<volatile unsigned int*>(&ctrl->error)) {
+                s_phase ^= 1u << s;
+                s_pending &= ~(1u << s);
+            }
+        }
+    };
+    // the look-back warp: tile i's exclusive prefix, its inclusive published
+    auto look = [&](uint32_t i) {
+        const int s = int(i % kBulkStages);
+        const uint64_t tile = s_id[i % kIdSlots];
+        Acc<V> prefix{0, 0, V{}};
+        if (tile > 0) {
+            prefix = look_back<COUNT>(tile, ts, ctrl, op);
+            if (lane == 0) ts.publish(tile, kInclusive, seg<COUNT>(prefix, s_agg[s], op));
+        }
+        if (lane == 0) s_prefix[s] = prefix;
+    };
+    // one iteration: A(i + 1) into nxt and the look-back of tile i, then
+    // tile i's outputs from cur and its stage, and the stage refilled
+    auto step = [&](uint32_t i, const TileRegs<V>& cur, TileRegs<V>& nxt) -> bool {
+        if (s_id[i % kIdSlots] >= tiles) return false;
+        const bool has_next = s_id[(i + 1) % kIdSlots] < tiles;
+        if (data) {
+            if (has_next) {
+                phase_a(i + 1, nxt);
+                data_sync();
+                after_a(i + 1);
+            }
+        } else {
+            look(i);
+        }
+        __syncthreads();  // tile i's prefix, tile i+1's warp offsets
+        if (data) {
+            const int s = int(i % kBulkStages);
+            K k[kChunks][kGroup];
+            V v[kChunks][kGroup];
+            load(i, cur.tile, false, k, v, COUNT);
+            emit<COUNT>(k, v, cur.heads, cur.pre, seg<COUNT>(s_prefix[s], s_excl[s][warp], op),
+                        cur.tile * kTileItems + uint64_t(toff), lane, n, mode, init, out, unique_out, num_runs,
+                        vector, op);
+        }
+        __syncthreads();  // stage i % 3 is free
+        if (tid == 0) {
+            bulk_detail::fence_proxy_async();
+            acquire(i + kBulkStages);
+        }
+        return true;
+    };
+
+    if (tid == 0) {
+        s_pending = 0;
+        s_phase = 0;
+        for (int s = 0; s < kBulkStages; ++s) bulk_detail::init_barrier(&s_bar[s]);
+        bulk_detail::fence_barrier_init();
+        for (uint32_t i = 0; i < uint32_t(kBulkStages); ++i) acquire(i);
+    }
+    __syncthreads();
+    TileRegs<V> ra, rb;
+    if (data && s_id[0] < tiles) {
+        phase_a(0, ra);
+        data_sync();
+        after_a(0);
+    }
+    __syncthreads();
+    for (uint32_t i = 0;; i += 2) {
+        if (!step(i, ra, rb)) break;
+        if (!step(i + 1, rb, ra)) break;
+    }
+    // copies not retired (only after an error): wait for them, bounded,
+    // before the block's shared memory goes away
+    if (tid == 0 && s_pending) {
+        for (int s = 0; s < kBulkStages; ++s)
+            if ((s_pending >> s) & 1u)
+                if (!bulk_detail::wait(&s_bar[s], (s_phase >> s) & 1u, &ctrl->error, kWaitLimitNs))
+                    atomicCAS(&ctrl->error, 0u, kErrTimeout);
     }
 }
 
@@ -717,11 +1072,29 @@ cudaError_t launch(void* temp, size_t temp_bytes, const K* keys, const V* values
     unsigned char* t = static_cast<unsigned char*>(temp);
     cudaError_t e = cudaMemsetAsync(t, 0, L.meta + size_t(L.tiles) * 8, stream);
     if (e != cudaSuccess) return e;
+    // head counts stay below 2^30 for the scans (0 or 1) and below n for ReduceByKey
+    const bool packed = sizeof(V) == 4 && (!COUNT || n < (uint64_t(1) << 30));
     TileStatus<V> ts{reinterpret_cast<uint64_t*>(t + L.meta), reinterpret_cast<V*>(t + L.partial),
-                     reinterpret_cast<V*>(t + L.inclusive)};
+                     reinterpret_cast<V*>(t + L.inclusive), packed};
+    Ctrl* ctrl = reinterpret_cast<Ctrl*>(t);
     const bool vector = aligned16(keys) && aligned16(values) && (mode == kModeReduce || aligned16(out));
-    by_key_kernel<K, V, COUNT><<<unsigned(L.tiles), kBlock, 0, stream>>>(
-        keys, values, out, unique_out, num_runs, n, mode, init, vector, reinterpret_cast<Ctrl*>(t), ts, equal, op);
+    if (aligned16(keys) && aligned16(values)) {
+        // the persistent bulk-copy kernel, as many blocks as are resident
+        auto kernel = by_key_bulk_kernel<K, V, COUNT, Equal, Op>;
+        constexpr size_t smem = bulk_smem_bytes<K, V>();
+        int dev = 0, sms = 0, per_sm = 0;
+        e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kBulkThreads, smem);
+        if (e != cudaSuccess) return e;
+        const uint64_t resident = uint64_t(sms > 0 ? sms : 1) * uint64_t(per_sm > 0 ? per_sm : 1);
+        kernel<<<unsigned(std::min(L.tiles, resident)), kBulkThreads, smem, stream>>>(
+            keys, values, out, unique_out, num_runs, n, mode, init, vector, L.tiles, ctrl, ts, equal, op);
+    } else {
+        by_key_kernel<K, V, COUNT><<<unsigned(L.tiles), kBlock, 0, stream>>>(
+            keys, values, out, unique_out, num_runs, n, mode, init, vector, ctrl, ts, equal, op);
+    }
     return cudaGetLastError();
 }
 
@@ -1239,48 +1612,14 @@ using BulkOf = BulkShape<bulk_block<T, F, SEL>()>;
 constexpr uint64_t kBulkTileMin = uint64_t(256) * kChunks * kGroup;  // status rows are sized for it
 constexpr int kBulkStages = 3;
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
-
-__device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
-{
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ bool bulk_try_wait(uint64_t* bar, uint32_t parity)
-{
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return done != 0;
-}
+using bulk_detail::bulk_copy;
+using bulk_detail::smem_u32;
 
 /* Bounded wait for phase `parity` of `bar`; false on timeout or when another
  * thread of the call recorded an error. */
 __device__ __forceinline__ bool bulk_wait(uint64_t* bar, uint32_t parity, Ctrl* ctrl)
 {
-    uint64_t t0 = 0;
-    uint32_t spins = 0;
-    while (!bulk_try_wait(bar, parity)) {
-        if (++spins == 16) {
-            spins = 0;
-            if (*static_cast<volatile unsigned int*>(&ctrl->error)) return false;
-            const uint64_t now = global_ns();
-            if (t0 == 0)
-                t0 = now;
-            else if (now - t0 > kWaitLimitNs)
-                return false;
-        }
-    }
-    return true;
+    return bulk_detail::wait(bar, parity, &ctrl->error, kWaitLimitNs);
 }
 
 template <typename T, typename F, int SEL>
@@ -1330,9 +1669,7 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
         s_tile[s] = t;
         if (t < tiles && (t + 1) * S::kTile <= n) {
             s_pending |= 1u << s;
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&s_bar[s])),
-                         "r"(kItemBytes + kFlagBytes)
-                         : "memory");
+            bulk_detail::expect_bytes(&s_bar[s], kItemBytes + kFlagBytes);
             bulk_copy(sx + size_t(s) * S::kTile, a.in + t * S::kTile, kItemBytes, &s_bar[s]);
             if constexpr (FLAGS)
                 bulk_copy(sf + size_t(s) * S::kTile, a.flags + t * S::kTile, kFlagBytes, &s_bar[s]);
@@ -1487,9 +1824,8 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
     if (tid == 0) {
         s_pending = 0;
         s_phase = 0;
-        for (int s = 0; s < kBulkStages; ++s)
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&s_bar[s])) : "memory");
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int s = 0; s < kBulkStages; ++s) bulk_detail::init_barrier(&s_bar[s]);
+        bulk_detail::fence_barrier_init();
         for (int s = 0; s < kBulkStages; ++s) acquire(s);
     }
     __syncthreads();
@@ -1559,7 +1895,7 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
         __syncthreads();  // stage s is free
         if (tid == 0) {
             // the stage's generic-proxy accesses are ordered before the copy that refills it
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            bulk_detail::fence_proxy_async();
             acquire(s);
         }
     }

@@ -279,14 +279,17 @@ def _timed_steps(fn, steps, dist, stream):
     return ms.item()
 
 
-def _phase_times(comm, keys, out, dist):
+def _phase_times(comm, keys, out, dist, exchange="auto"):
     """Per-phase times of one call, max over ranks per phase.  The ranks
     start together: a rank that arrives late would otherwise show up as the
     others' wait in their first collective (the splitter rounds)."""
     import torch
     dist.barrier()
     torch.cuda.synchronize()
-    _, t = distributed_sort_keys(keys, comm, out=out, times=True)
+    distributed_sort_keys(keys, comm, out=out, exchange=exchange)  # warm for this exchange
+    dist.barrier()
+    torch.cuda.synchronize()
+    _, t = distributed_sort_keys(keys, comm, out=out, exchange=exchange, times=True)
     names = ["local_sort_ms", "splitters_ms", "host_wait_ms", "exchange_merge_ms", "local_merge_ms", "total_ms",
              "host_ms"]
     v = torch.tensor([t[k] for k in names], dtype=torch.float64, device="cuda")
@@ -386,6 +389,8 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
             diag_timing_enable(False)
         value = G * n_local / (ms * 1e-3) / 1e9
         phases = _phase_times(comm, keys, out, dist)
+        # the same call with the runs exchanged by NCCL send / recv instead of peer loads
+        phases_nccl = _phase_times(comm, keys, out, dist, exchange="nccl")
 
         # e2e: pinned host keys -> device, distributed sort, this rank's part
         # -> host, pipelined over three streams (upload of step s+1 and
@@ -481,6 +486,7 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
                    "l2": "inputs larger than L2; no flush"},
         "parity_bit_exact": all(parity.values()), "parity_cases": parity,
         "phases_ms": phases,
+        "phases_ms_nccl_exchange": phases_nccl,
         "roofline": {"bound": "hbm", "kernel": "onesweep_kernel (one 8-bit pass)", "achieved": achieved,
                      "peak": peak_gbs, "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak_gbs,
                      "algorithmic_bytes_per_launch": 8 * n_local, "avg_launch_ms": avg_pass, "traffic": None},
