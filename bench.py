@@ -123,7 +123,7 @@ OPS = {
     # every key once (8 B per output key).
     "merge": dict(metric="Gkeys/s uint32 merge of two sorted runs @2^28", unit="Gkeys/s", log2n=28, dtype="u32",
                   workload="merge path of two sorted u32 runs of 2^27 keys, uniform, seed 1", bytes=8, kbytes=8,
-                  kernel="merge_block_kernel"),
+                  kernel="merge_bulk_kernel"),
     # Distributed SortKeys of 2^32 keys in total (seed 7), sharded evenly:
     # strong scaling over N GPUs (N = 1 is the 1-GPU-equivalent run).
     "dist": dict(metric="Gkeys/s uint32 distributed SortKeys @2^32", unit="Gkeys/s", log2n=32, dtype="u32",

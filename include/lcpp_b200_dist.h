@@ -128,17 +128,23 @@ lcpp_status lcpp_dist_reduce(lcpp_comm comm, void* temp, size_t temp_bytes, cons
 lcpp_status lcpp_dist_search_sorted(const void* sorted, uint64_t n, const void* queries, uint64_t num_queries,
                                     int upper, uint64_t* out, lcpp_dtype key_dtype, lcpp_stream_t stream);
 
-/* Temp bytes of lcpp_dist_merge_sorted for `total` = na + nb keys (the split
- * points of the output blocks). */
+/* Temp bytes of lcpp_dist_merge_sorted for `total` = na + nb keys: a
+ * 256-byte control area (byte 4: the device error word, as
+ * lcpp_device_status reads it) and the split points of the output blocks. */
 lcpp_status lcpp_dist_merge_temp_bytes(uint64_t total, size_t* temp_bytes);
 
 /* Merge two runs sorted ascending by DeviceRadixSort (keys of key_dtype,
  * compared by the same order-preserving image): out[0, na + nb) receives the
  * merged keys; among equal images the keys of `a` come first.  `out` must not
- * overlap `a` or `b`; temp (256-byte aligned) holds the output blocks' split
- * points.  Merge path (Green, McColl & Bader, 2012): one small kernel finds
- * each output block's split point by binary search, a second merges each
- * block in shared memory. */
+ * overlap `a` or `b`; temp (256-byte aligned) holds the control area and the
+ * output blocks' split points.  The runs must lie in device allocations (the
+ * merge bulk-copies them from the 16-byte boundary at or below each range's
+ * start).  Merge path (Green, McColl & Bader, 2012): one small kernel finds
+ * each output block's split point by binary search, a second -- persistent,
+ * the next block's inputs bulk-copied into shared memory while it merges the
+ * current one -- merges each block in shared memory.  Every wait of the
+ * second is bounded; on expiry LCPP_ERR_LOOKBACK_TIMEOUT is recorded in the
+ * error word. */
 lcpp_status lcpp_dist_merge_sorted(void* temp, size_t temp_bytes, const void* a, uint64_t na, const void* b,
                                    uint64_t nb, void* out, lcpp_dtype key_dtype, lcpp_stream_t stream);
 

@@ -2,6 +2,7 @@
 // (include/lcpp_b200_dist.h).
 #include <cstring>
 
+#include "../../include/lcpp_b200_device.cuh"
 #include "../../include/lcpp_b200_dist.h"
 #include "dist.cuh"
 
@@ -121,88 +122,191 @@ __device__ __forceinline__ U merge_image(U k, const KeyCodec<U>& c)
         return key_image(k, c);
 }
 
-// One output tile per block: gather a[i0, i1) ++ b[j0, j1) into shared
-// memory, each thread finds where its kMergeItems outputs start (co-rank by
-// binary search in shared memory, 32-bit indices) and merges them serially
-// with one shared-memory load per output, then the tile is stored coalesced.
+/* ---- Persistent merge with bulk-copied inputs ------------------------------
+ * Blocks take output tiles blockIdx.x, blockIdx.x + gridDim.x, ...; while a
+ * block merges one tile, the inputs of its next tile -- a[i0, i1) and
+ * b[j0, j1), contiguous ranges of the two runs, which may live in another
+ * GPU's memory -- are bulk-copied (cp.async.bulk, no multicast) into the
+ * other of two shared-memory stages.  A bulk copy needs 16-byte aligned
+ * addresses and sizes: each range is copied from the 16-byte boundary at or
+ * below its start (inside the same allocation) up to the last boundary at
+ * or below its end, and the few keys past that boundary are loaded by plain
+ * loads.  Per tile: each thread finds where its kMergeItems outputs start
+ * (co-rank by binary search in shared memory, 32-bit indices), merges them
+ * serially with one shared-memory load per output, and the tile is stored
+ * coalesced through the same stage. */
+constexpr int kMergeStages = 2;
+constexpr size_t kMergeCtrlBytes = 256;  // error word at byte 4 of the merge temp, split points after
+
+template <typename U>
+struct MergeStage {
+    static constexpr int kVec = 16 / int(sizeof(U));
+    // a part (from up to kVec - 1 keys before a[i0]), padding to 16 bytes, b part (likewise)
+    static constexpr int kKeys = int(kMergeTile) + 3 * kVec;
+};
+
+template <typename U>
+constexpr size_t merge_smem_bytes()
+{
+    return size_t(kMergeStages) * MergeStage<U>::kKeys * sizeof(U);
+}
+
+/* Where a tile's inputs sit in its stage. */
+template <typename U>
+struct MergeTileInfo {
+    const U* a;      // a + lo_a: stage index 0
+    const U* b;      // b + lo_b: stage index b_at
+    U* out;          // out + o0
+    int a_first;     // stage index of a[i0]
+    int a_plain;     // stage indices [a_plain, a_end) come by plain loads
+    int a_end;       // stage index past a[i1 - 1]
+    int b_at;        // b part's first stage index (16-byte aligned)
+    int b_first;     // stage index of b[j0] relative to b_at
+    int b_plain;
+    int b_end;
+};
+
 template <typename U, bool PLAIN>
 __global__ void __launch_bounds__(kMergeBlock)
-merge_block_kernel(const MergeBatch<U> mb, const uint64_t* __restrict__ all_splits, KeyCodec<U> codec)
+merge_bulk_kernel(const MergeBatch<U> mb, const uint64_t* __restrict__ all_splits, KeyCodec<U> codec,
+                  uint64_t blocks, uint32_t* error)
 {
-    __shared__ U s[kMergeTile];
+    namespace bd = lcpp_b200::device::bulk_detail;
+    constexpr int E = MergeStage<U>::kVec;
+    constexpr int kStage = MergeStage<U>::kKeys;
+    extern __shared__ __align__(128) unsigned char merge_smem[];
+    U* const stages = reinterpret_cast<U*>(merge_smem);
+    __shared__ __align__(8) uint64_t s_bar[kMergeStages];
+    __shared__ MergeTileInfo<U> s_info[kMergeStages];
     const int tid = threadIdx.x;
-    const int m = batch_slot(mb.block_start, mb.count, blockIdx.x);
-    const uint64_t blk = blockIdx.x - mb.block_start[m];
-    const U* __restrict__ a = mb.a[m];
-    const U* __restrict__ b = mb.b[m];
-    U* __restrict__ out = mb.out[m];
-    const uint64_t* splits = all_splits + mb.split_start[m];
-    const uint64_t total = mb.na[m] + mb.nb[m];
-    const uint64_t o0 = blk * kMergeTile;
-    const uint64_t o1 = min(o0 + kMergeTile, total);
-    const uint64_t i0 = splits[blk], i1 = splits[blk + 1];
-    const uint64_t j0 = o0 - i0, j1 = o1 - i1;
-    const int la = int(i1 - i0), lb = int(j1 - j0), len = int(o1 - o0);
-    // Gather: all of a thread's loads are issued before any is stored, so
-    // their latencies (HBM, or NVLink when a run lives in another GPU's
-    // memory) overlap.
-    {
-        const U* pa = a + i0;
-        const U* pb = b + j0 - la;  // pb[idx] = b[j0 + idx - la] for idx >= la
+
+    // thread 0: the inputs of output tile `blk` into stage st
+    auto issue = [&](uint64_t blk, int st) {
+        const int m = batch_slot(mb.block_start, mb.count, blk);
+        const uint64_t local = blk - mb.block_start[m];
+        const uint64_t* splits = all_splits + mb.split_start[m];
+        const uint64_t total = mb.na[m] + mb.nb[m];
+        const uint64_t o0 = local * kMergeTile;
+        const uint64_t o1 = min(o0 + kMergeTile, total);
+        const uint64_t i0 = splits[local], i1 = splits[local + 1];
+        const uint64_t j0 = o0 - i0, j1 = o1 - i1;
+        // the key index (signed: it may lie up to E - 1 keys before the run)
+        // at the 16-byte boundary at or below p + i
+        auto lower16 = [](const U* p, uint64_t i) -> int64_t {
+            return int64_t(i) - int64_t((reinterpret_cast<uintptr_t>(p + i) & 15u) / sizeof(U));
+        };
+        const U* pa = mb.a[m];
+        const U* pb = mb.b[m];
+        const int64_t si0 = int64_t(i0), si1 = int64_t(i1), sj0 = int64_t(j0), sj1 = int64_t(j1);
+        MergeTileInfo<U> t;
+        const int64_t lo_a = si1 > si0 ? lower16(pa, i0) : si0;
+        const int64_t hi_a = si1 > si0 ? max(lo_a, lower16(pa, i1)) : si0;
+        const int64_t lo_b = sj1 > sj0 ? lower16(pb, j0) : sj0;
+        const int64_t hi_b = sj1 > sj0 ? max(lo_b, lower16(pb, j1)) : sj0;
+        t.a = pa + lo_a;
+        t.a_first = int(si0 - lo_a);
+        t.a_plain = int(max(hi_a, si0) - lo_a);
+        t.a_end = int(si1 - lo_a);
+        t.b_at = (t.a_end + E - 1) / E * E;
+        t.b = pb + lo_b;
+        t.b_first = int(sj0 - lo_b);
+        t.b_plain = int(max(hi_b, sj0) - lo_b);
+        t.b_end = int(sj1 - lo_b);
+        t.out = mb.out[m] + o0;
+        s_info[st] = t;
+        const uint32_t bytes_a = uint32_t((hi_a - lo_a) * sizeof(U));
+        const uint32_t bytes_b = uint32_t((hi_b - lo_b) * sizeof(U));
+        U* dst = stages + size_t(st) * kStage;
+        bd::expect_bytes(&s_bar[st], bytes_a + bytes_b);
+        if (bytes_a) bd::bulk_copy(dst, t.a, bytes_a, &s_bar[st]);
+        if (bytes_b) bd::bulk_copy(dst + t.b_at, t.b, bytes_b, &s_bar[st]);
+    };
+
+    uint64_t blk = blockIdx.x;
+    if (tid == 0) {
+        for (int st = 0; st < kMergeStages; ++st) bd::init_barrier(&s_bar[st]);
+        bd::fence_barrier_init();
+        if (blk < blocks) issue(blk, 0);
+    }
+    __syncthreads();
+    uint32_t phase = 0;  // bit st: parity of the next completion of stage st
+    bool pending_next = false;
+    for (int st = 0; blk < blocks; blk += gridDim.x, st ^= 1) {
+        const uint64_t next = blk + gridDim.x;
+        pending_next = next < blocks;
+        if (tid == 0 && pending_next) {
+            bd::fence_proxy_async();  // the other stage's reads and plain stores (previous tile) come first
+            issue(next, st ^ 1);
+        }
+        if (!bd::wait(&s_bar[st], (phase >> st) & 1u, error, kWaitLimitNs)) atomicCAS(error, 0u, kDevErrTimeout);
+        phase ^= 1u << st;
+        U* const sm = stages + size_t(st) * kStage;
+        const MergeTileInfo<U> t = s_info[st];
+        // keys past the last 16-byte boundary of each range
+        if (tid < E - 1) {
+            const int i = t.a_plain + tid;
+            if (i < t.a_end) sm[i] = t.a[i];
+        } else if (tid >= 32 && tid < 32 + E - 1) {
+            const int i = t.b_plain + tid - 32;
+            if (i < t.b_end) sm[t.b_at + i] = t.b[i];
+        }
+        __syncthreads();
+        if (*static_cast<volatile uint32_t*>(error)) break;
+        const U* sa = sm + t.a_first;
+        const U* sb = sm + t.b_at + t.b_first;
+        const int la = t.a_end - t.a_first, lb = t.b_end - t.b_first, len = la + lb;
         U v[kMergeItems];
+        const int ot = tid * kMergeItems;
+        if (ot < len) {
+            // co-rank: number of a-keys among this thread's first ot outputs
+            int lo = ot > lb ? ot - lb : 0;
+            int hi = ot < la ? ot : la;
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (merge_image<PLAIN>(sa[mid], codec) <= merge_image<PLAIN>(sb[ot - mid - 1], codec))
+                    lo = mid + 1;
+                else
+                    hi = mid;
+            }
+            // serial merge; reads past a run's end are clamped to its last key (or its first slot)
+            const int a_last = la > 0 ? la - 1 : 0, b_last = lb > 0 ? lb - 1 : 0;
+            int ia = lo, ib = ot - lo;
+            U ka = sa[ia < la ? ia : a_last];
+            U kb = sb[ib < lb ? ib : b_last];
+#pragma unroll
+            for (int k = 0; k < kMergeItems; ++k) {
+                const bool take_a =
+                    ib >= lb || (ia < la && merge_image<PLAIN>(ka, codec) <= merge_image<PLAIN>(kb, codec));
+                v[k] = take_a ? ka : kb;
+                if (take_a) {
+                    ++ia;
+                    ka = sa[ia < la ? ia : a_last];
+                } else {
+                    ++ib;
+                    kb = sb[ib < lb ? ib : b_last];
+                }
+            }
+        }
+        __syncthreads();  // every thread is done reading the stage
+        if (ot < len) {
+#pragma unroll
+            for (int k = 0; k < kMergeItems; ++k)
+                if (ot + k < len) sm[ot + k] = v[k];
+        }
+        __syncthreads();
 #pragma unroll
         for (int k = 0; k < kMergeItems; ++k) {
             const int idx = tid + k * kMergeBlock;
-            if (idx < len) v[k] = (idx < la ? pa : pb)[idx];
+            if (idx < len) t.out[idx] = sm[idx];
         }
-#pragma unroll
-        for (int k = 0; k < kMergeItems; ++k) {
-            const int idx = tid + k * kMergeBlock;
-            if (idx < len) s[idx] = v[k];
-        }
+        __syncthreads();  // the stage is free for the tile after next
+        pending_next = false;
     }
-    __syncthreads();
-    U v[kMergeItems];
-    const int ot = tid * kMergeItems;
-    if (ot < len) {
-        // co-rank: number of a-keys among this thread's first ot outputs
-        int lo = ot > lb ? ot - lb : 0;
-        int hi = ot < la ? ot : la;
-        while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if (merge_image<PLAIN>(s[mid], codec) <= merge_image<PLAIN>(s[la + ot - mid - 1], codec))
-                lo = mid + 1;
-            else
-                hi = mid;
-        }
-        // serial merge; ia / ib index s[] (the b part starts at la)
-        int ia = lo, ib = la + ot - lo;
-        const int a_end = la, b_end = la + lb;
-        U ka = s[ia < b_end ? ia : b_end - 1];
-        U kb = s[ib < b_end ? ib : b_end - 1];
-#pragma unroll
-        for (int k = 0; k < kMergeItems; ++k) {
-            const bool take_a =
-                ib >= b_end || (ia < a_end && merge_image<PLAIN>(ka, codec) <= merge_image<PLAIN>(kb, codec));
-            v[k] = take_a ? ka : kb;
-            int next = take_a ? ++ia : ++ib;
-            next = next < b_end ? next : b_end - 1;
-            const U x = s[next];
-            ka = take_a ? x : ka;
-            kb = take_a ? kb : x;
-        }
-    }
-    __syncthreads();
-    if (ot < len) {
-#pragma unroll
-        for (int k = 0; k < kMergeItems; ++k)
-            if (ot + k < len) s[ot + k] = v[k];
-    }
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < kMergeItems; ++k) {
-        const int idx = tid + k * kMergeBlock;
-        if (idx < len) out[o0 + idx] = s[idx];
+    // a copy issued for a tile this block will not merge (only after an
+    // error): wait for it, bounded, before the block's shared memory goes away
+    if (tid == 0 && pending_next) {
+        const int st = int(((blk - blockIdx.x) / gridDim.x + 1) & 1);
+        if (!bd::wait(&s_bar[st], (phase >> st) & 1u, error, kWaitLimitNs)) atomicCAS(error, 0u, kDevErrTimeout);
     }
 }
 
@@ -239,7 +343,7 @@ extern "C" lcpp_status lcpp_dist_merge_batch_temp_bytes(int count, const uint64_
         return LCPP_ERR_INVALID_ARG;
     uint64_t bs[LCPP_MERGE_BATCH_MAX + 1], ss[LCPP_MERGE_BATCH_MAX + 1];
     if (!dist::batch_layout(count, na, nb, bs, ss)) return LCPP_ERR_INVALID_ARG;
-    *temp_bytes = count ? align_up(size_t(ss[count]) * 8, kTempAlign) : 0;
+    *temp_bytes = count ? dist::kMergeCtrlBytes + align_up(size_t(ss[count]) * 8, kTempAlign) : 0;
     return LCPP_OK;
 }
 
@@ -265,8 +369,14 @@ extern "C" lcpp_status lcpp_dist_merge_sorted_batch(void* temp, size_t temp_byte
     if (st != LCPP_OK) return st;
     if (!temp || (reinterpret_cast<uintptr_t>(temp) & (kTempAlign - 1))) return LCPP_ERR_INVALID_ARG;
     if (temp_bytes < need) return LCPP_ERR_TEMP_TOO_SMALL;
-    uint64_t* splits = static_cast<uint64_t*>(temp);
+    // byte 4: the error word of the merge's bounded waits; split points after the control area
+    uint32_t* error = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(temp) + 4);
+    uint64_t* splits = reinterpret_cast<uint64_t*>(static_cast<unsigned char*>(temp) + kMergeCtrlBytes);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (cudaMemsetAsync(temp, 0, kMergeCtrlBytes, s) != cudaSuccess) return LCPP_ERR_CUDA;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return LCPP_ERR_CUDA;
     const bool plain = key_dtype == LCPP_U32 || key_dtype == LCPP_U64;
     auto go = [&](auto tag) {
         using U = decltype(tag);
@@ -283,13 +393,23 @@ extern "C" lcpp_status lcpp_dist_merge_sorted_batch(void* temp, size_t temp_byte
         const auto c = make_codec<U>(key_dtype, false);
         const unsigned sgrid = unsigned(ceil_div(mb.split_start[count], 256));
         merge_split_kernel<U><<<sgrid, 256, 0, s>>>(mb, splits, c);
-        const unsigned grid = unsigned(mb.block_start[count]);
-        if (grid == 0) return;
-        diag::KernelTimer timer(5 /* LCPP_KERNEL_MERGE */, mb.split_start[count] - count, s);
+        const uint64_t blocks = mb.block_start[count];
+        if (blocks == 0) return;
+        // persistent: as many blocks as are resident
+        auto launch = [&](auto kernel) {
+            constexpr size_t smem = merge_smem_bytes<U>();
+            int per_sm = 0;
+            if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess ||
+                cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kMergeBlock, smem) != cudaSuccess)
+                return;  // reported by cudaGetLastError below
+            const uint64_t resident = uint64_t(sms > 0 ? sms : 1) * uint64_t(per_sm > 0 ? per_sm : 1);
+            diag::KernelTimer timer(5 /* LCPP_KERNEL_MERGE */, mb.split_start[count] - count, s);
+            kernel<<<unsigned(std::min(blocks, resident)), kMergeBlock, smem, s>>>(mb, splits, c, blocks, error);
+        };
         if (plain)
-            merge_block_kernel<U, true><<<grid, kMergeBlock, 0, s>>>(mb, splits, c);
+            launch(merge_bulk_kernel<U, true>);
         else
-            merge_block_kernel<U, false><<<grid, kMergeBlock, 0, s>>>(mb, splits, c);
+            launch(merge_bulk_kernel<U, false>);
     };
     if (kb == 4)
         go(uint32_t{});

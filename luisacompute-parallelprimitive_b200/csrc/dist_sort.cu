@@ -143,6 +143,7 @@ constexpr int kSubBits = 16;
 constexpr uint32_t kSubEdges = (1u << kSubBits) + 1;  // sub-bucket edges per boundary and round
 constexpr int kMaxRanks = 64;
 constexpr uint64_t kMergeTileKeys = 3840;  // output keys per merge block (dist.cu)
+constexpr size_t kMergeCtrlBytes = 256;    // the merge temp's control area (dist.cu)
 
 }  // namespace
 }  // namespace dist
@@ -371,9 +372,9 @@ SortLayout sort_layout(int kb, uint64_t n, int G)
     L.pos = take(8 * size_t(G) * (G + 1));
     L.barrier = take(8);
     // split points of one merge level: lcpp_dist_merge_batch_temp_bytes gives
-    // align_up(8 (blocks + merges), 256) with blocks <= ceil(n / tile) + merges
-    // and merges <= G
-    L.splits_bytes = align_up(8 * size_t(ceil_div(n, kMergeTileKeys) + 2 * uint64_t(G)), kTempAlign);
+    // 256 + align_up(8 (blocks + merges), 256) with blocks <= ceil(n / tile) +
+    // merges and merges <= G
+    L.splits_bytes = kMergeCtrlBytes + align_up(8 * size_t(ceil_div(n, kMergeTileKeys) + 2 * uint64_t(G)), kTempAlign);
     L.splits = take(L.splits_bytes);
     L.total = off;
     return L;

@@ -303,7 +303,7 @@ def strong_scaling_2p32(comm: Comm, dist, steps: int = 3, warmup: int = 2):
     """2^32 u32 keys in total (seed 7), uniform and Zipf(1.1) hashed, sharded
     evenly over the ranks: ms per distributed sort (max over ranks), and --
     on rank 0, alone, in the same job -- the single-GPU sort of the same
-    2^32 uniform keys (the 1-GPU-equivalent run)."""
+    2^32 keys of each distribution (the 1-GPU-equivalent runs)."""
     import torch
 
     from . import GEN_U32_UNIFORM, GEN_U32_ZIPF, testgen_fill
@@ -324,30 +324,32 @@ def strong_scaling_2p32(comm: Comm, dist, steps: int = 3, warmup: int = 2):
         del keys, out
         comm._temps.clear()
         torch.cuda.empty_cache()
-    one = torch.tensor([0.0], dtype=torch.float64, device="cuda")
+    # the 1-GPU-equivalent runs: rank 0 alone sorts all 2^32 keys of each distribution
+    one = torch.zeros(2, dtype=torch.float64, device="cuda")
     if r == 0:
         keys = torch.empty(total, dtype=torch.uint32, device=comm.device)
-        testgen_fill(keys, GEN_U32_UNIFORM, seed=7)
         out = torch.empty_like(keys)
         temp = alloc_temp(DeviceRadixSort.GetSortKeysTempStorageBytes(dtype_code(keys), total), comm.device)
         rs = DeviceRadixSort()
-        for _ in range(warmup):
-            rs.SortKeys(temp, keys, out, total)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(steps):
-            rs.SortKeys(temp, keys, out, total)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        one[0] = e0.elapsed_time(e1) / steps
+        for q, gen in enumerate((GEN_U32_UNIFORM, GEN_U32_ZIPF)):
+            testgen_fill(keys, gen, seed=7)
+            for _ in range(warmup):
+                rs.SortKeys(temp, keys, out, total)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(steps):
+                rs.SortKeys(temp, keys, out, total)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            one[q] = e0.elapsed_time(e1) / steps
         del keys, out, temp
         torch.cuda.empty_cache()
     dist.all_reduce(one)
-    t1 = one.item()
-    res["one_gpu_ms"] = t1
-    res["one_gpu_gkeys_per_s"] = total / (t1 * 1e-3) / 1e9
-    for name in ("uniform", "zipf"):
+    for q, name in enumerate(("uniform", "zipf")):
+        t1 = one[q].item()
+        res[name]["one_gpu_ms"] = t1
+        res[name]["one_gpu_gkeys_per_s"] = total / (t1 * 1e-3) / 1e9
         res[name]["speedup_vs_one_gpu"] = t1 / res[name]["ms"]
     return res
 
