@@ -855,14 +855,27 @@ by_key_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* n
  * then, with tile k's prefix known, the data warps re-read tile k's values
  * (and keys) from its stage, write its outputs, and the stage is refilled
  * with the block's next tile.  The two register sets alternate. */
-constexpr int kBulkThreads = kBlock + 32;
+template <int BLOCK>
+struct KeyShape {
+    static constexpr int kBlock = BLOCK;  // data threads; one more warp runs the look-backs
+    static constexpr int kWarps = BLOCK / 32;
+    static constexpr int kThreads = BLOCK + 32;
+    static constexpr uint64_t kTile = uint64_t(BLOCK) * kChunks * kGroup;
+};
+/* ReduceByKey's look-back walks to an inclusive tile past every tile in
+ * flight (about one round trip per 32 of them), so its throughput grows
+ * with the tile: 8192 items (16 data warps) when a key and a value take at
+ * most 8 bytes (192 KB of stages); the scans stop at the first predecessor
+ * holding a head and keep 4096-item tiles (two blocks per SM). */
+template <bool COUNT, typename K, typename V>
+using KeyBulkOf = KeyShape<(COUNT && sizeof(K) + sizeof(V) <= 8) ? 512 : 256>;
 constexpr int kBulkStages = 3;
 constexpr int kIdSlots = 4;  // tile ids of tiles k .. k+3 (k+3: acquired at the end of iteration k)
 
-template <typename K, typename V>
+template <typename K, typename V, bool COUNT>
 constexpr size_t bulk_smem_bytes()
 {
-    return size_t(kBulkStages) * kTileItems * (sizeof(K) + sizeof(V));
+    return size_t(kBulkStages) * KeyBulkOf<COUNT, K, V>::kTile * (sizeof(K) + sizeof(V));
 }
 
 /* What A(k) leaves in registers for the output phase of tile k. */
@@ -874,12 +887,13 @@ struct TileRegs {
 };
 
 template <typename K, typename V, bool COUNT, typename Equal, typename Op>
-__global__ void __launch_bounds__(kBulkThreads, (sizeof(K) + sizeof(V) <= 8) ? 2 : 1)
+__global__ void __launch_bounds__(KeyBulkOf<COUNT, K, V>::kThreads, (!COUNT && sizeof(K) + sizeof(V) <= 8) ? 2 : 1)
 by_key_bulk_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32_t* num_runs, uint64_t n, int mode,
                    V init, bool vector, uint64_t tiles, Ctrl* ctrl, TileStatus<V> ts, Equal equal, Op op)
 {
-    constexpr uint32_t kKeyBytes = uint32_t(kTileItems * sizeof(K));
-    constexpr uint32_t kValueBytes = uint32_t(kTileItems * sizeof(V));
+    using S = KeyBulkOf<COUNT, K, V>;
+    constexpr uint32_t kKeyBytes = uint32_t(S::kTile * sizeof(K));
+    constexpr uint32_t kValueBytes = uint32_t(S::kTile * sizeof(V));
     extern __shared__ __align__(128) unsigned char bulk_smem[];
     K* sk = reinterpret_cast<K*>(bulk_smem);                                     // [stage][tile]
     V* sv = reinterpret_cast<V*>(bulk_smem + size_t(kBulkStages) * kKeyBytes);  // [stage][tile]
@@ -887,14 +901,14 @@ by_key_bulk_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32
     __shared__ uint64_t s_id[kIdSlots];  // tile id of the block's i-th tile at i % kIdSlots
     __shared__ uint32_t s_pending;       // bit s: a copy into stage s is in flight
     __shared__ uint32_t s_phase;         // bit s: parity of the next completion of stage s
-    __shared__ Acc<V> s_total[kBulkStages][kWarps];
-    __shared__ Acc<V> s_excl[kBulkStages][kWarps];
+    __shared__ Acc<V> s_total[kBulkStages][S::kWarps];
+    __shared__ Acc<V> s_excl[kBulkStages][S::kWarps];
     __shared__ Acc<V> s_agg[kBulkStages];
     __shared__ Acc<V> s_prefix[kBulkStages];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const bool data = warp < kWarps;
+    const bool data = warp < S::kWarps;
     const int toff = warp * (32 * kChunks * kGroup);  // the warp's first item in the tile
-    auto data_sync = [] { asm volatile("bar.sync 1, %0;" ::"n"(kBlock) : "memory"); };
+    auto data_sync = [] { asm volatile("bar.sync 1, %0;" ::"n"(S::kBlock) : "memory"); };
 
     // the block's i-th tile: its id, and its copy into stage i % 3 when full (thread 0)
     auto acquire = [&](uint32_t i) {
@@ -905,26 +919,26 @@ by_key_bulk_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32
         }
         const uint64_t t = atomicAdd(&ctrl->tile_counter, 1u);
         s_id[i % kIdSlots] = t;
-        if (t < tiles && (t + 1) * kTileItems <= n) {
+        if (t < tiles && (t + 1) * S::kTile <= n) {
             s_pending |= 1u << s;
             bulk_detail::expect_bytes(&s_bar[s], kKeyBytes + kValueBytes);
-            bulk_detail::bulk_copy(sk + size_t(s) * kTileItems, keys + t * kTileItems, kKeyBytes, &s_bar[s]);
-            bulk_detail::bulk_copy(sv + size_t(s) * kTileItems, values + t * kTileItems, kValueBytes, &s_bar[s]);
+            bulk_detail::bulk_copy(sk + size_t(s) * S::kTile, keys + t * S::kTile, kKeyBytes, &s_bar[s]);
+            bulk_detail::bulk_copy(sv + size_t(s) * S::kTile, values + t * S::kTile, kValueBytes, &s_bar[s]);
         }
     };
     // this thread's keys and values of the block's i-th tile
     auto load = [&](uint32_t i, uint64_t tile, bool wait, K (&k)[kChunks][kGroup], V (&v)[kChunks][kGroup],
                     bool want_keys) {
         const int s = int(i % kBulkStages);
-        const uint64_t warp_base = tile * kTileItems + uint64_t(toff);
-        if ((tile + 1) * kTileItems <= n) {
+        const uint64_t warp_base = tile * S::kTile + uint64_t(toff);
+        if ((tile + 1) * S::kTile <= n) {
             if (wait && !bulk_detail::wait(&s_bar[s], (s_phase >> s) & 1u, &ctrl->error, kWaitLimitNs))
                 atomicCAS(&ctrl->error, 0u, kErrTimeout);
 #pragma unroll
             for (int j = 0; j < kChunks; ++j) {
                 const int at = toff + (j * 32 + lane) * kGroup;
-                if (want_keys) memcpy(k[j], sk + size_t(s) * kTileItems + at, sizeof(k[j]));
-                memcpy(v[j], sv + size_t(s) * kTileItems + at, sizeof(v[j]));
+                if (want_keys) memcpy(k[j], sk + size_t(s) * S::kTile + at, sizeof(k[j]));
+                memcpy(v[j], sv + size_t(s) * S::kTile + at, sizeof(v[j]));
             }
         } else {
 #pragma unroll
@@ -939,14 +953,14 @@ by_key_bulk_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32
     auto phase_a = [&](uint32_t i, TileRegs<V>& r) {
         const int s = int(i % kBulkStages);
         const uint64_t tile = s_id[i % kIdSlots];
-        const uint64_t warp_base = tile * kTileItems + uint64_t(toff);
+        const uint64_t warp_base = tile * S::kTile + uint64_t(toff);
         K k[kChunks][kGroup];
         V v[kChunks][kGroup];
         load(i, tile, true, k, v, true);
         K before{};
         if (lane == 0 && warp_base > 0 && warp_base < n) {
-            const bool staged = (tile + 1) * kTileItems <= n && toff > 0;
-            before = staged ? sk[size_t(s) * kTileItems + toff - 1] : keys[warp_base - 1];
+            const bool staged = (tile + 1) * S::kTile <= n && toff > 0;
+            before = staged ? sk[size_t(s) * S::kTile + toff - 1] : keys[warp_base - 1];
         }
         r.tile = tile;
         r.heads = head_bits(k, before, n, warp_base, lane, equal);
@@ -959,7 +973,7 @@ by_key_bulk_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32
         const int s = int(i % kBulkStages);
         if (warp != 0) return;
         const uint64_t tile = s_id[i % kIdSlots];
-        const Acc<V> aggregate = block_fold<COUNT, kWarps>(s_total[s], s_excl[s], lane, op);
+        const Acc<V> aggregate = block_fold<COUNT, S::kWarps>(s_total[s], s_excl[s], lane, op);
         if (lane == 0) {
             s_agg[s] = aggregate;
             ts.publish(tile, tile == 0 ? kInclusive : kPartial, aggregate);
@@ -1001,7 +1015,7 @@ by_key_bulk_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32
             V v[kChunks][kGroup];
             load(i, cur.tile, false, k, v, COUNT);
             emit<COUNT>(k, v, cur.heads, cur.pre, seg<COUNT>(s_prefix[s], s_excl[s][warp], op),
-                        cur.tile * kTileItems + uint64_t(toff), lane, n, mode, init, out, unique_out, num_runs,
+                        cur.tile * S::kTile + uint64_t(toff), lane, n, mode, init, out, unique_out, num_runs,
                         vector, op);
         }
         __syncthreads();  // stage i % 3 is free
@@ -1080,17 +1094,19 @@ cudaError_t launch(void* temp, size_t temp_bytes, const K* keys, const V* values
     const bool vector = aligned16(keys) && aligned16(values) && (mode == kModeReduce || aligned16(out));
     if (aligned16(keys) && aligned16(values)) {
         // the persistent bulk-copy kernel, as many blocks as are resident
+        using S = KeyBulkOf<COUNT, K, V>;
         auto kernel = by_key_bulk_kernel<K, V, COUNT, Equal, Op>;
-        constexpr size_t smem = bulk_smem_bytes<K, V>();
+        constexpr size_t smem = bulk_smem_bytes<K, V, COUNT>();
         int dev = 0, sms = 0, per_sm = 0;
         e = cudaGetDevice(&dev);
         if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kBulkThreads, smem);
+        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, S::kThreads, smem);
         if (e != cudaSuccess) return e;
+        const uint64_t tiles = (n + S::kTile - 1) / S::kTile;  // <= L.tiles status rows
         const uint64_t resident = uint64_t(sms > 0 ? sms : 1) * uint64_t(per_sm > 0 ? per_sm : 1);
-        kernel<<<unsigned(std::min(L.tiles, resident)), kBulkThreads, smem, stream>>>(
-            keys, values, out, unique_out, num_runs, n, mode, init, vector, L.tiles, ctrl, ts, equal, op);
+        kernel<<<unsigned(std::min(tiles, resident)), S::kThreads, smem, stream>>>(
+            keys, values, out, unique_out, num_runs, n, mode, init, vector, tiles, ctrl, ts, equal, op);
     } else {
         by_key_kernel<K, V, COUNT><<<unsigned(L.tiles), kBlock, 0, stream>>>(
             keys, values, out, unique_out, num_runs, n, mode, init, vector, ctrl, ts, equal, op);
