@@ -994,36 +994,41 @@ by_key_bulk_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32
         }
         if (lane == 0) s_prefix[s] = prefix;
     };
-    // one iteration: A(i + 1) into nxt and the look-back of tile i, then
-    // tile i's outputs from cur and its stage, and the stage refilled
+    // Hand-offs between the data warps and the look-back warp (named
+    // barriers over the whole block: one side arrives, the other waits).
+    // Barrier 3, "aggregate ready": tile i+1's aggregate is published and
+    // tile i's prefix has been consumed; barrier 2, "prefix ready".  Each
+    // side arrives once per tile and only after the other side's previous
+    // arrival was consumed, so no barrier ever sees two arrivals of a side.
+    auto agg_ready_signal = [] { asm volatile("bar.arrive 3, %0;" ::"n"(S::kThreads) : "memory"); };
+    auto agg_ready_wait = [] { asm volatile("bar.sync 3, %0;" ::"n"(S::kThreads) : "memory"); };
+    auto prefix_ready_signal = [] { asm volatile("bar.arrive 2, %0;" ::"n"(S::kThreads) : "memory"); };
+    auto prefix_ready_wait = [] { asm volatile("bar.sync 2, %0;" ::"n"(S::kThreads) : "memory"); };
+    // data warps, one iteration: A(i + 1) into nxt, then, once tile i's
+    // prefix is known, tile i's outputs from cur and its stage, and the
+    // stage refilled; false after the block's last tile
     auto step = [&](uint32_t i, const TileRegs<V>& cur, TileRegs<V>& nxt) -> bool {
-        if (s_id[i % kIdSlots] >= tiles) return false;
         const bool has_next = s_id[(i + 1) % kIdSlots] < tiles;
-        if (data) {
-            if (has_next) {
-                phase_a(i + 1, nxt);
-                data_sync();
-                after_a(i + 1);
-            }
-        } else {
-            look(i);
+        if (has_next) {
+            phase_a(i + 1, nxt);
+            data_sync();
+            after_a(i + 1);
         }
-        __syncthreads();  // tile i's prefix, tile i+1's warp offsets
-        if (data) {
-            const int s = int(i % kBulkStages);
-            K k[kChunks][kGroup];
-            V v[kChunks][kGroup];
-            load(i, cur.tile, false, k, v, COUNT);
-            emit<COUNT>(k, v, cur.heads, cur.pre, seg<COUNT>(s_prefix[s], s_excl[s][warp], op),
-                        cur.tile * S::kTile + uint64_t(toff), lane, n, mode, init, out, unique_out, num_runs,
-                        vector, op);
-        }
-        __syncthreads();  // stage i % 3 is free
+        prefix_ready_wait();  // tile i's prefix
+        if (has_next) agg_ready_signal();
+        const int s = int(i % kBulkStages);
+        K k[kChunks][kGroup];
+        V v[kChunks][kGroup];
+        load(i, cur.tile, false, k, v, COUNT);
+        emit<COUNT>(k, v, cur.heads, cur.pre, seg<COUNT>(s_prefix[s], s_excl[s][warp], op),
+                    cur.tile * S::kTile + uint64_t(toff), lane, n, mode, init, out, unique_out, num_runs, vector,
+                    op);
+        data_sync();  // stage i % 3 is free
         if (tid == 0) {
             bulk_detail::fence_proxy_async();
             acquire(i + kBulkStages);
         }
-        return true;
+        return has_next;
     };
 
     if (tid == 0) {
@@ -1034,17 +1039,28 @@ by_key_bulk_kernel(const K* keys, const V* values, V* out, K* unique_out, uint32
         for (uint32_t i = 0; i < uint32_t(kBulkStages); ++i) acquire(i);
     }
     __syncthreads();
-    TileRegs<V> ra, rb;
-    if (data && s_id[0] < tiles) {
-        phase_a(0, ra);
-        data_sync();
-        after_a(0);
+    if (s_id[0] < tiles) {
+        if (data) {
+            TileRegs<V> ra, rb;
+            phase_a(0, ra);
+            data_sync();
+            after_a(0);
+            agg_ready_signal();
+            for (uint32_t i = 0;; i += 2) {
+                if (!step(i, ra, rb)) break;
+                if (!step(i + 1, rb, ra)) break;
+            }
+        } else {
+            // the look-back warp: one tile after the other, as their aggregates appear
+            for (uint32_t i = 0;; ++i) {
+                agg_ready_wait();
+                look(i);
+                prefix_ready_signal();
+                if (s_id[(i + 1) % kIdSlots] >= tiles) break;
+            }
+        }
     }
     __syncthreads();
-    for (uint32_t i = 0;; i += 2) {
-        if (!step(i, ra, rb)) break;
-        if (!step(i + 1, rb, ra)) break;
-    }
     // copies not retired (only after an error): wait for them, bounded,
     // before the block's shared memory goes away
     if (tid == 0 && s_pending) {
@@ -1837,6 +1853,16 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
     T x[kChunks][kGroup];
     uint32_t sel1 = 0, sel2 = 0;
     const bool data = warp < S::kWarps;
+    // Hand-offs between the data warps and the look-back warp (named
+    // barriers over the whole block: one side arrives, the other waits).
+    // Barrier 3, "aggregate ready": tile k+1's aggregate is published and
+    // tile k's prefix has been consumed; barrier 2, "prefix ready".  Each
+    // side arrives once per tile and only after the other side's previous
+    // arrival was consumed, so no barrier ever sees two arrivals of a side.
+    auto agg_ready_signal = [] { asm volatile("bar.arrive 3, %0;" ::"n"(S::kThreads) : "memory"); };
+    auto agg_ready_wait = [] { asm volatile("bar.sync 3, %0;" ::"n"(S::kThreads) : "memory"); };
+    auto prefix_ready_signal = [] { asm volatile("bar.arrive 2, %0;" ::"n"(S::kThreads) : "memory"); };
+    auto prefix_ready_wait = [] { asm volatile("bar.sync 2, %0;" ::"n"(S::kThreads) : "memory"); };
     if (tid == 0) {
         s_pending = 0;
         s_phase = 0;
@@ -1845,76 +1871,85 @@ compact_bulk_kernel(Args<T, F, V> a, Ctrl* ctrl, Status<OUT == kOutThreeWay> st,
         for (int s = 0; s < kBulkStages; ++s) acquire(s);
     }
     __syncthreads();
-    if (data && s_tile[0] < tiles) {
-        phase_a(0, s_tile[0], x, sel1, sel2);
-        data_sync();
-        if (warp == 0) {
-            if (lane == 0) retire(0);
-            publish(0, s_tile[0]);
-        }
-        if constexpr (STAGED) {
+
+    const uint64_t unsel_end = THREE ? n - ctrl->totals[0] - ctrl->totals[1] : 0;
+    if (s_tile[0] < tiles) {
+        if (data) {
+            phase_a(0, s_tile[0], x, sel1, sel2);
             data_sync();
-            stage(0, s_tile[0], x, sel1, sel2);
+            if (warp == 0) {
+                if (lane == 0) retire(0);
+                publish(0, s_tile[0]);
+            }
+            if constexpr (STAGED) {
+                data_sync();
+                stage(0, s_tile[0], x, sel1, sel2);
+            }
+            agg_ready_signal();
+            for (uint32_t k = 0;; ++k) {
+                const int s = int(k % kBulkStages);
+                const int ns = int((k + 1) % kBulkStages);
+                const uint64_t tile = s_tile[s];
+                const uint64_t next = s_tile[ns];
+                const bool has_next = next < tiles;
+                if (has_next) {
+                    phase_a(ns, next, x, sel1, sel2);
+                    data_sync();  // counts of tile k+1 visible
+                    if (warp == 0) {
+                        if (lane == 0) retire(ns);
+                        publish(ns, next);
+                    }
+                    if constexpr (STAGED) {
+                        data_sync();  // offsets of tile k+1 visible
+                        stage(ns, next, x, sel1, sel2);
+                    }
+                }
+                prefix_ready_wait();  // tile k's prefix
+                if (has_next) agg_ready_signal();
+                if constexpr (STAGED) {
+                    write_out(s, tile, unsel_end);
+                } else {
+                    T xs[kChunks][kGroup];
+                    F f[kChunks][kGroup];
+                    load(s, tile, false, xs, f);
+                    const uint32_t b1 = s_sel[s][0][tid], b2 = s_sel[s][1][tid];
+                    uint64_t pre[kChunks];
+                    chunk_prefixes<THREE>(b1, b2, lane, pre);
+                    scatter_items<T, F, V, OUT>(a, xs, b1, b2, pre, s_prefix[s] + s_excl[s][warp],
+                                                tile * S::kTile + uint64_t(toff), lane, unsel_end);
+                }
+                data_sync();  // stage s is free
+                if (tid == 0) {
+                    // the stage's generic-proxy accesses are ordered before the copy that refills it
+                    bulk_detail::fence_proxy_async();
+                    acquire(s);
+                }
+                if (!has_next) break;
+            }
+        } else {
+            // the look-back warp: one tile after the other, as their aggregates appear
+            for (uint32_t k = 0;; ++k) {
+                const int s = int(k % kBulkStages);
+                agg_ready_wait();
+                const uint64_t tile = s_tile[s];
+                uint64_t prefix = 0;
+                if (tile > 0) {
+                    prefix = look_back<THREE>(tile, st, ctrl);
+                    if (lane == 0) st.publish(tile, kInclusive, prefix + s_agg[s]);
+                }
+                if (lane == 0) {
+                    s_prefix[s] = prefix;
+                    if (tile == tiles - 1 && a.num_selected) {
+                        a.num_selected[0] = uint32_t(prefix + s_agg[s]);
+                        if constexpr (THREE) a.num_selected[1] = uint32_t((prefix + s_agg[s]) >> 32);
+                    }
+                }
+                prefix_ready_signal();
+                if (s_tile[(k + 1) % kBulkStages] >= tiles) break;
+            }
         }
     }
     __syncthreads();
-
-    const uint64_t unsel_end = THREE ? n - ctrl->totals[0] - ctrl->totals[1] : 0;
-    for (uint32_t k = 0;; ++k) {
-        const int s = int(k % kBulkStages);
-        const int ns = int((k + 1) % kBulkStages);
-        const uint64_t tile = s_tile[s];
-        if (tile >= tiles) break;
-        const uint64_t next = s_tile[ns];
-        if (data) {
-            if (next < tiles) {
-                phase_a(ns, next, x, sel1, sel2);
-                data_sync();  // counts of tile k+1 visible
-                if (warp == 0) {
-                    if (lane == 0) retire(ns);
-                    publish(ns, next);
-                }
-                if constexpr (STAGED) {
-                    data_sync();  // offsets of tile k+1 visible
-                    stage(ns, next, x, sel1, sel2);
-                }
-            }
-        } else {
-            uint64_t prefix = 0;
-            if (tile > 0) {
-                prefix = look_back<THREE>(tile, st, ctrl);
-                if (lane == 0) st.publish(tile, kInclusive, prefix + s_agg[s]);
-            }
-            if (lane == 0) {
-                s_prefix[s] = prefix;
-                if (tile == tiles - 1 && a.num_selected) {
-                    a.num_selected[0] = uint32_t(prefix + s_agg[s]);
-                    if constexpr (THREE) a.num_selected[1] = uint32_t((prefix + s_agg[s]) >> 32);
-                }
-            }
-        }
-        __syncthreads();  // prefix of tile k visible
-        if (data) {
-            if constexpr (STAGED) {
-                write_out(s, tile, unsel_end);
-            } else {
-                T xs[kChunks][kGroup];
-                F f[kChunks][kGroup];
-                load(s, tile, false, xs, f);
-                const uint32_t b1 = s_sel[s][0][tid], b2 = s_sel[s][1][tid];
-                uint64_t pre[kChunks];
-                chunk_prefixes<THREE>(b1, b2, lane, pre);
-                scatter_items<T, F, V, OUT>(a, xs, b1, b2, pre, s_prefix[s] + s_excl[s][warp],
-                                            tile * S::kTile + uint64_t(toff), lane, unsel_end);
-            }
-        }
-        __syncthreads();  // stage s is free
-        if (tid == 0) {
-            // the stage's generic-proxy accesses are ordered before the copy that refills it
-            bulk_detail::fence_proxy_async();
-            acquire(s);
-        }
-    }
     // copies not retired (only after an error): wait for them, bounded,
     // before the block's shared memory goes away
     if (tid == 0 && s_pending) {

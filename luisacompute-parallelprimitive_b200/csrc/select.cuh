@@ -163,6 +163,12 @@ lcpp_status make_pick(const lcpp_clause* clauses, int count, ClausePick<T>& p)
                     if (!most_negative && (mag & (mag - 1)) == 0) {
                         p.kind[c] = kClauseModPow2;
                         p.a[c] = T(mag - 1);
+                        if (p.b[c] == T(0)) {
+                            // remainder 0 for either sign exactly when the low bits are
+                            // clear: !((x & (|d| - 1)) != 0)
+                            p.kind[c] = LCPP_CLAUSE_BITS_ANY;
+                            p.negate[c] = !p.negate[c];
+                        }
                     }
                 }
             }
