@@ -527,9 +527,15 @@ __device__ __forceinline__ void st_relaxed_u64(uint64_t* p, uint64_t v)
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-/* Tile status.  Packed (4-byte values, head counts below 2^30): meta[t] =
+/* Consecutive tiles' status words sit one 128-byte line apart: the few
+ * dozen most recent words are read by every block's look-back at once, and
+ * packed into two or three lines those reads queue at one L2 slice. */
+constexpr uint64_t kMetaStride = 16;
+
+/* Tile status (tile t's word at meta[t * kMetaStride]).  Packed (4-byte
+ * values, head counts below 2^30): meta =
  * (value << 32) | (head count << 2) | status, one word published and read
- * with relaxed accesses.  Otherwise meta[t] = (head count << 32) | status,
+ * with relaxed accesses.  Otherwise meta = (head count << 32) | status,
  * released after the value it announces (partial[t] or inclusive[t]) is
  * stored, and read with acquire. */
 template <typename V>
@@ -544,17 +550,17 @@ struct TileStatus {
             if (packed) {
                 uint32_t bits;
                 memcpy(&bits, &a.v, 4);
-                st_relaxed_u64(meta + t, (uint64_t(bits) << 32) | (uint64_t(a.c) << 2) | status);
+                st_relaxed_u64(meta + t * kMetaStride, (uint64_t(bits) << 32) | (uint64_t(a.c) << 2) | status);
                 return;
             }
         }
         *static_cast<volatile V*>(status == kPartial ? partial + t : inclusive + t) = a.v;
-        st_release_u64(meta + t, (uint64_t(a.c) << 32) | status);
+        st_release_u64(meta + t * kMetaStride, (uint64_t(a.c) << 32) | status);
     }
     /* tile t's status word (0 = not published yet) */
     __device__ __forceinline__ uint64_t word(uint64_t t) const
     {
-        return packed ? ld_relaxed_u64(meta + t) : ld_acquire_u64(meta + t);
+        return packed ? ld_relaxed_u64(meta + t * kMetaStride) : ld_acquire_u64(meta + t * kMetaStride);
     }
     /* the pair a published word announces */
     __device__ __forceinline__ Acc<V> pair(uint64_t t, uint64_t m) const
@@ -1083,7 +1089,7 @@ inline Layout layout(uint64_t n, size_t value_bytes)
     auto up = [](size_t x) { return (x + kAlign - 1) / kAlign * kAlign; };
     L.ctrl = 0;
     L.meta = kAlign;
-    L.partial = up(L.meta + size_t(L.tiles) * 8);
+    L.partial = up(L.meta + size_t(L.tiles) * 8 * kMetaStride);
     L.inclusive = up(L.partial + size_t(L.tiles) * value_bytes);
     L.total = up(L.inclusive + size_t(L.tiles) * value_bytes);
     return L;
@@ -1100,7 +1106,7 @@ cudaError_t launch(void* temp, size_t temp_bytes, const K* keys, const V* values
         return cudaErrorInvalidValue;
     if (L.tiles > 0xffffffffull) return cudaErrorInvalidValue;
     unsigned char* t = static_cast<unsigned char*>(temp);
-    cudaError_t e = cudaMemsetAsync(t, 0, L.meta + size_t(L.tiles) * 8, stream);
+    cudaError_t e = cudaMemsetAsync(t, 0, L.meta + size_t(L.tiles) * 8 * kMetaStride, stream);
     if (e != cudaSuccess) return e;
     // head counts stay below 2^30 for the scans (0 or 1) and below n for ReduceByKey
     const bool packed = sizeof(V) == 4 && (!COUNT || n < (uint64_t(1) << 30));
@@ -1281,9 +1287,14 @@ __device__ __forceinline__ uint64_t warp_sum(uint64_t v)
     return v;
 }
 
+/* Consecutive tiles' status words sit one 128-byte line apart: the few
+ * dozen most recent words are read by every block's look-back at once, and
+ * packed into two or three lines those reads queue at one L2 slice. */
+constexpr uint64_t kStatusStride = 16;
+
 template <bool THREE>
 struct Status {
-    uint64_t* word;       // (first count << 32) | status
+    uint64_t* word;       // (first count << 32) | status, tile t at word[t * kStatusStride]
     uint32_t* second_p;   // three-way: second count of the partial
     uint32_t* second_i;   // three-way: second count of the inclusive prefix
     // The word carries the first count, so a relaxed store publishes it; the
@@ -1293,9 +1304,9 @@ struct Status {
         const uint64_t w = (uint64_t(uint32_t(packed)) << 32) | status;
         if constexpr (THREE) {
             *static_cast<volatile uint32_t*>((status == kPartial ? second_p : second_i) + t) = uint32_t(packed >> 32);
-            st_release_u64(word + t, w);
+            st_release_u64(word + t * kStatusStride, w);
         } else {
-            st_relaxed_u64(word + t, w);
+            st_relaxed_u64(word + t * kStatusStride, w);
         }
     }
 };
@@ -1321,7 +1332,7 @@ __device__ __forceinline__ uint64_t look_back(uint64_t tile, const Status<THREE>
             uint32_t spins = 0;
             uint64_t t0 = 0;
             bool gave_up = false;
-            while (((m = ld_relaxed_u64(st.word + j)) & 3u) == kInvalid) {
+            while (((m = ld_relaxed_u64(st.word + uint64_t(j) * kStatusStride)) & 3u) == kInvalid) {
                 if (++spins == 64) {
                     spins = 0;
                     const uint64_t now = global_ns();
@@ -1972,7 +1983,7 @@ inline Layout layout(uint64_t n, bool three)
     auto up = [](size_t x) { return (x + kAlign - 1) / kAlign * kAlign; };
     L.ctrl = 0;
     L.word = kAlign;
-    L.second_p = up(L.word + size_t(L.tiles) * 8);
+    L.second_p = up(L.word + size_t(L.tiles) * 8 * kStatusStride);
     L.second_i = up(L.second_p + (three ? size_t(L.tiles) * 4 : 0));
     L.total = up(L.second_i + (three ? size_t(L.tiles) * 4 : 0));
     return L;
@@ -1996,7 +2007,7 @@ cudaError_t launch(void* temp, size_t temp_bytes, Args<T, F, V> a, Pick pick, Pi
     const Layout L = layout(a.n, THREE);
     if (!temp || reinterpret_cast<uintptr_t>(temp) % kAlign || temp_bytes < L.total) return cudaErrorInvalidValue;
     unsigned char* t = static_cast<unsigned char*>(temp);
-    cudaError_t e = cudaMemsetAsync(t, 0, L.word + size_t(L.tiles) * 8, stream);
+    cudaError_t e = cudaMemsetAsync(t, 0, L.word + size_t(L.tiles) * 8 * kStatusStride, stream);
     if (e != cudaSuccess) return e;
     Ctrl* ctrl = reinterpret_cast<Ctrl*>(t);
     int dev = 0, sms = 0;

@@ -124,17 +124,19 @@ __device__ __forceinline__ U merge_image(U k, const KeyCodec<U>& c)
 
 /* ---- Persistent merge with bulk-copied inputs ------------------------------
  * Blocks take output tiles blockIdx.x, blockIdx.x + gridDim.x, ...; while a
- * block merges one tile, the inputs of its next tile -- a[i0, i1) and
- * b[j0, j1), contiguous ranges of the two runs, which may live in another
- * GPU's memory -- are bulk-copied (cp.async.bulk, no multicast) into the
- * other of two shared-memory stages.  A bulk copy needs 16-byte aligned
- * addresses and sizes: each range is copied from the 16-byte boundary at or
- * below its start (inside the same allocation) up to the last boundary at
- * or below its end, and the few keys past that boundary are loaded by plain
- * loads.  Per tile: each thread finds where its kMergeItems outputs start
- * (co-rank by binary search in shared memory, 32-bit indices), merges them
- * serially with one shared-memory load per output, and the tile is stored
- * coalesced through the same stage. */
+ * block merges one tile, the inputs of its next kMergeStages - 1 tiles --
+ * a[i0, i1) and b[j0, j1), contiguous ranges of the two runs, which may
+ * live in another GPU's memory -- are bulk-copied (cp.async.bulk, no
+ * multicast) into the other shared-memory stages.  A bulk copy needs
+ * 16-byte aligned addresses and sizes: each range is copied from the
+ * 16-byte boundary at or below its start (inside the same allocation) up
+ * to the last boundary at or below its end, and the few keys past that
+ * boundary are loaded by plain loads.  Per tile: each thread finds where
+ * its kMergeItems outputs start (co-rank by binary search in shared memory,
+ * 32-bit indices), merges them serially with one shared-memory load per
+ * output, and the tile is stored coalesced through the same stage. */
+// stages per block: one tile merging, the next one's inputs in flight (three
+// stages measured slower locally and no faster over NVLink)
 constexpr int kMergeStages = 2;
 constexpr size_t kMergeCtrlBytes = 256;  // error word at byte 4 of the merge temp, split points after
 
@@ -223,23 +225,33 @@ merge_bulk_kernel(const MergeBatch<U> mb, const uint64_t* __restrict__ all_split
     };
 
     uint64_t blk = blockIdx.x;
+    uint32_t pending = 0;  // thread 0: bit st = a copy into stage st is in flight
     if (tid == 0) {
         for (int st = 0; st < kMergeStages; ++st) bd::init_barrier(&s_bar[st]);
         bd::fence_barrier_init();
-        if (blk < blocks) issue(blk, 0);
+        for (int q = 0; q + 1 < kMergeStages; ++q) {
+            const uint64_t b = blk + uint64_t(q) * gridDim.x;
+            if (b < blocks) {
+                issue(b, q);
+                pending |= 1u << q;
+            }
+        }
     }
     __syncthreads();
     uint32_t phase = 0;  // bit st: parity of the next completion of stage st
-    bool pending_next = false;
-    for (int st = 0; blk < blocks; blk += gridDim.x, st ^= 1) {
-        const uint64_t next = blk + gridDim.x;
-        pending_next = next < blocks;
-        if (tid == 0 && pending_next) {
-            bd::fence_proxy_async();  // the other stage's reads and plain stores (previous tile) come first
-            issue(next, st ^ 1);
+    for (uint32_t k = 0; blk < blocks; ++k, blk += gridDim.x) {
+        const int st = int(k % kMergeStages);
+        const uint64_t ahead = blk + uint64_t(kMergeStages - 1) * gridDim.x;
+        if (tid == 0 && ahead < blocks) {
+            // the stage of the previous tile: its reads and plain stores come first
+            const int fs = int((k + kMergeStages - 1) % kMergeStages);
+            bd::fence_proxy_async();
+            issue(ahead, fs);
+            pending |= 1u << fs;
         }
         if (!bd::wait(&s_bar[st], (phase >> st) & 1u, error, kWaitLimitNs)) atomicCAS(error, 0u, kDevErrTimeout);
         phase ^= 1u << st;
+        pending &= ~(1u << st);
         U* const sm = stages + size_t(st) * kStage;
         const MergeTileInfo<U> t = s_info[st];
         // keys past the last 16-byte boundary of each range
@@ -299,14 +311,15 @@ merge_bulk_kernel(const MergeBatch<U> mb, const uint64_t* __restrict__ all_split
             const int idx = tid + k * kMergeBlock;
             if (idx < len) t.out[idx] = sm[idx];
         }
-        __syncthreads();  // the stage is free for the tile after next
-        pending_next = false;
+        __syncthreads();  // the stage is free for a later tile
     }
-    // a copy issued for a tile this block will not merge (only after an
-    // error): wait for it, bounded, before the block's shared memory goes away
-    if (tid == 0 && pending_next) {
-        const int st = int(((blk - blockIdx.x) / gridDim.x + 1) & 1);
-        if (!bd::wait(&s_bar[st], (phase >> st) & 1u, error, kWaitLimitNs)) atomicCAS(error, 0u, kDevErrTimeout);
+    // copies issued for tiles this block will not merge (only after an
+    // error): wait for them, bounded, before the block's shared memory goes away
+    if (tid == 0 && pending) {
+        for (int st = 0; st < kMergeStages; ++st)
+            if ((pending >> st) & 1u)
+                if (!bd::wait(&s_bar[st], (phase >> st) & 1u, error, kWaitLimitNs))
+                    atomicCAS(error, 0u, kDevErrTimeout);
     }
 }
 
