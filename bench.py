@@ -62,7 +62,7 @@ DATA = "synthetic (splitmix64 counter streams; see include/lcpp_b200_testgen.h)"
 OPS = {
     "sort": dict(metric="Gkeys/s uint32 SortKeys @2^28", unit="Gkeys/s", log2n=28, dtype="u32",
                  workload="SortKeys u32 uniform full range, bits [0,32), seed 0", bytes=36, kbytes=8,
-                 kernel="onesweep_kernel (one 8-bit pass)"),
+                 kernel="onesweep_bulk_kernel (one 8-bit pass)"),
     "pairs": dict(metric="Gkeys/s uint32->uint32 SortPairs @2^28", unit="Gkeys/s", log2n=28, dtype="u32",
                   workload="SortPairs u32 uniform keys, u32 values = index, seed 1", bytes=68, kbytes=16,
                   kernel="onesweep_kernel (one 8-bit pass)"),
@@ -74,7 +74,7 @@ OPS = {
                       kernel="onesweep_kernel (one 8-bit pass)"),
     "bits": dict(metric="Gkeys/s uint32 SortKeys bits [8,24) @2^27", unit="Gkeys/s", log2n=27, dtype="u32",
                  workload="SortKeys u32 uniform, begin_bit 8, end_bit 24, seed 1", bytes=20, kbytes=8,
-                 kernel="onesweep_kernel (one 8-bit pass)"),
+                 kernel="onesweep_bulk_kernel (one 8-bit pass)"),
     "scan": dict(metric="Gitems/s int32 InclusiveSum @2^30", unit="Gitems/s", log2n=30, dtype="i32",
                  workload="InclusiveSum i32 uniform in [-1000,1000], seed 1", bytes=8, kbytes=8,
                  kernel="scan_bulk_kernel"),
@@ -128,10 +128,10 @@ OPS = {
     # strong scaling over N GPUs (N = 1 is the 1-GPU-equivalent run).
     "dist": dict(metric="Gkeys/s uint32 distributed SortKeys @2^32", unit="Gkeys/s", log2n=32, dtype="u32",
                  workload="distributed SortKeys u32 uniform, seed 7", bytes=36, kbytes=8,
-                 kernel="onesweep_kernel (one 8-bit pass)", distributed=True, seed=7, zipf=False),
+                 kernel="onesweep_bulk_kernel (one 8-bit pass)", distributed=True, seed=7, zipf=False),
     "dist_zipf": dict(metric="Gkeys/s uint32 distributed SortKeys Zipf(1.1) @2^32", unit="Gkeys/s", log2n=32,
                       dtype="u32", workload="distributed SortKeys u32 Zipf(1.1) hashed, seed 7", bytes=36, kbytes=8,
-                      kernel="onesweep_kernel (one 8-bit pass)", distributed=True, seed=7, zipf=True),
+                      kernel="onesweep_bulk_kernel (one 8-bit pass)", distributed=True, seed=7, zipf=True),
 }
 
 

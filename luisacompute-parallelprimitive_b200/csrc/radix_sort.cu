@@ -15,7 +15,10 @@
 //      look-back, stage the tile in shared memory in digit order and write it
 //      out so that each digit's run is stored contiguously (the reference's
 //      AgentRadixSortOneSweep, agent_radix_sort_onesweep.h:224-511, with
-//      BlockRadixRankMatchEarlyCounts, block_radix_rank.h:207-486).
+//      BlockRadixRankMatchEarlyCounts, block_radix_rank.h:207-486).  Keys-only
+//      sorts of 4-byte keys whose buffers are 16-byte aligned run the same
+//      tile work in onesweep_bulk_kernel: persistent blocks that bulk-copy
+//      their next tile into shared memory while the current one is ranked.
 //
 // B200 budget: at the measured ~6.5 TB/s an 8-bit pass over 4-byte keys has
 // about 11 SM cycles per 32 keys, and the integer ALU pipe issues about two
@@ -283,7 +286,7 @@ struct OnesweepSmem {
     static constexpr int kWarps = P::kWarps;
     U keys[kTile];                        // transformed keys in tile-rank order
     V vals[PAIRS ? kTile : 1];
-    uint32_t counters[kWarps * kDigits];  // per-warp digit counters, then rank bases
+    alignas(16) uint32_t counters[kWarps * kDigits];  // per-warp digit counters, then rank bases
     uint32_t peer_masks[2 * kWarps * P::kMaskWords];
     OffT gofs[kDigits];         // output index = gofs[digit] + tile position
     uint32_t totals[kDigits];   // keys of each digit in the tile
@@ -369,11 +372,24 @@ __device__ __forceinline__ uint32_t pass_digit(U t, int shift, uint32_t mask, ui
     }
 }
 
+struct NoHook {
+    __device__ __forceinline__ void operator()() const {}
+};
+
 // Everything after the tile id is known.  FULL: the tile has kTile keys (all
 // but possibly the last tile), compiled without any per-key bounds logic.
-template <bool FULL, bool BYTE, typename P, typename U, typename V, bool PAIRS, int KIND, typename ST, typename OffT>
-__device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>& a,
-                                             OnesweepSmem<U, V, PAIRS, P, OffT>& s, uint32_t tile, int valid)
+// staged: the tile's keys already sit in shared memory (bulk-copied, same
+// order as in global memory), or null to load them from global memory.
+// after_counts runs on every thread right after the block barrier that
+// follows the early counts, the first point at which every thread has its
+// keys in registers.  PERSIST: the block goes on to another tile, so the
+// rank counters are cleared before returning.  Returns false when the tile
+// broke an invariant (the error word is set and nothing was stored).
+template <bool FULL, bool BYTE, bool PERSIST, typename P, typename U, typename V, bool PAIRS, int KIND, typename ST,
+          typename OffT, typename Hook = NoHook>
+__device__ __forceinline__ bool process_tile(const OnesweepArgs<U, V, ST, OffT>& a,
+                                             OnesweepSmem<U, V, PAIRS, P, OffT>& s, uint32_t tile, int valid,
+                                             const U* staged = nullptr, Hook after_counts = Hook())
 {
     using SB = StatusBits<ST>;
     constexpr int BLOCK = P::kBlock;
@@ -396,9 +412,14 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
     const uint32_t counters_base = static_cast<uint32_t>(__cvta_generic_to_shared(s.counters + warp * kDigits));
     {
         const int warp_base = warp * ITEMS * kWarp + lane;
-        const U* src = a.keys_in + tile_base + warp_base;
+        if (staged) {
 #pragma unroll
-        for (int i = 0; i < ITEMS; ++i) keys[i] = in_tile(i) ? src[i * kWarp] : U(0);
+            for (int i = 0; i < ITEMS; ++i) keys[i] = staged[warp_base + i * kWarp];
+        } else {
+            const U* src = a.keys_in + tile_base + warp_base;
+#pragma unroll
+            for (int i = 0; i < ITEMS; ++i) keys[i] = in_tile(i) ? src[i * kWarp] : U(0);
+        }
         if constexpr (PAIRS) {
             const V* vsrc = a.vals_in + tile_base + warp_base;
 #pragma unroll
@@ -414,6 +435,7 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
             shared_red_add(counters_base + (in_tile(i) ? digit(keys[i]) : dmask) * 4u, 1u);
     }
     __syncthreads();
+    after_counts();
 
     // Per digit: tile total (published at once), block-wide digit start,
     // then counters[w][d] := digit start + count of d in warps < w, the
@@ -529,7 +551,14 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
     __syncthreads();
     if (s.bad) {
         if (tid == 0) report_error(a.error, kDevErrInternal);
-        return;
+        return false;
+    }
+    if constexpr (PERSIST) {
+        // The rank counters are dead from here on (the stores use gofs):
+        // clear them for the next tile's early counts.
+        static_assert((kWarps * kDigits) % 4 == 0, "16-byte clears");
+        uint4* c4 = reinterpret_cast<uint4*>(s.counters);
+        for (int i = tid; i < kWarps * kDigits / 4; i += BLOCK) c4[i] = make_uint4(0u, 0u, 0u, 0u);
     }
 
     // Digit-ordered tile -> global: consecutive threads write consecutive
@@ -553,6 +582,7 @@ __device__ __forceinline__ void process_tile(const OnesweepArgs<U, V, ST, OffT>&
             }
         }
     }
+    return true;
 }
 
 template <typename U, typename V, bool PAIRS, typename P, int KIND, bool BYTE, typename ST, typename OffT>
@@ -579,9 +609,153 @@ onesweep_kernel(OnesweepArgs<U, V, ST, OffT> a)
     const uint32_t tile = s.tile_id;
     const uint64_t tile_base = uint64_t(tile) * kTile;
     if (tile_base + kTile <= a.n)
-        process_tile<true, BYTE, P, U, V, PAIRS, KIND, ST, OffT>(a, s, tile, kTile);
+        process_tile<true, BYTE, false, P, U, V, PAIRS, KIND, ST, OffT>(a, s, tile, kTile);
     else
-        process_tile<false, BYTE, P, U, V, PAIRS, KIND, ST, OffT>(a, s, tile, int(a.n - tile_base));
+        process_tile<false, BYTE, false, P, U, V, PAIRS, KIND, ST, OffT>(a, s, tile, int(a.n - tile_base));
+}
+
+// ---------------------------------------------------------------------------
+// Persistent onesweep pass for keys-only sorts whose key buffers are 16-byte
+// aligned.  One block per resident slot; each block takes tile ids from the
+// pass's atomic counter in increasing order.  As soon as every thread holds
+// its keys of tile k in registers (the barrier after the early counts), one
+// thread takes the block's next tile id and starts a bulk asynchronous copy
+// (cp.async.bulk global -> shared, completion on an mbarrier, no multicast)
+// of that tile into the block's input buffer, so the HBM read of tile k+1
+// runs during the ranking, look-back and stores of tile k.  The last tile,
+// when partial, is read with guarded plain loads.
+//
+// Forward progress: a block's next tile is taken while its current tile is in
+// flight, so every tile id below the smallest unpublished one belongs to a
+// block that has published it or is about to (the current tile of a running
+// block publishes its partial counts before any wait), as with one tile per
+// block.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void os_mbar_init(uint64_t* bar)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(uint32_t(__cvta_generic_to_shared(bar))) : "memory");
+}
+
+// one arrival expecting `bytes`, then the copy that delivers them
+__device__ __forceinline__ void os_bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
+{
+    const uint32_t b = uint32_t(__cvta_generic_to_shared(bar));
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(bytes) : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            uint32_t(__cvta_generic_to_shared(dst))),
+        "l"(src), "r"(bytes), "r"(b)
+        : "memory");
+}
+
+// Bounded wait for phase `parity` of `bar`: false after kWaitLimitNs.
+__device__ __forceinline__ bool os_mbar_wait(uint64_t* bar, uint32_t parity)
+{
+    const uint32_t b = uint32_t(__cvta_generic_to_shared(bar));
+    uint64_t t0 = 0;
+    uint32_t spins = 0;
+    while (true) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(b), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if (++spins == 16) {
+            spins = 0;
+            const uint64_t now = global_timer_ns();
+            if (t0 == 0)
+                t0 = now;
+            else if (now - t0 > kWaitLimitNs)
+                return false;
+        }
+    }
+}
+
+template <typename U, typename V, typename P, typename OffT>
+struct OnesweepBulkSmem {
+    alignas(16) U in[P::kTile];  // the next tile, bulk-copied in global order
+    OnesweepSmem<U, V, false, P, OffT> s;
+    uint64_t bar;
+    uint32_t next_tile;
+};
+
+template <typename U, typename V, typename P, int KIND, bool BYTE, typename ST, typename OffT>
+__global__ void __launch_bounds__(P::kBlock, P::kMinBlocks)
+onesweep_bulk_kernel(OnesweepArgs<U, V, ST, OffT> a, uint32_t tiles)
+{
+    using Smem = OnesweepBulkSmem<U, V, P, OffT>;
+    constexpr int BLOCK = P::kBlock;
+    constexpr int kTile = P::kTile;
+    constexpr int kWarps = P::kWarps;
+    constexpr uint32_t kTileBytes = uint32_t(kTile * sizeof(U));
+    static_assert(BLOCK >= kDigits, "one thread per digit");
+    static_assert(kTile <= 65536, "tile ranks fit 16 bits");
+    static_assert(kTileBytes % 16 == 0, "bulk copies move multiples of 16 bytes");
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    Smem& m = *reinterpret_cast<Smem*>(smem_raw);
+
+    const int tid = threadIdx.x;
+    const uint64_t full_tiles = a.n / kTile;
+    // thread 0: take the next tile id and, for a full tile, start its copy
+    auto acquire = [&]() {
+        const uint32_t t = atomicAdd(a.tile_counter, 1u);
+        m.next_tile = t;
+        if (t < full_tiles) os_bulk_load(m.in, a.keys_in + uint64_t(t) * kTile, kTileBytes, &m.bar);
+    };
+    if (tid == 0) {
+        m.s.bad = 0;
+        os_mbar_init(&m.bar);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        acquire();
+    }
+    for (int i = tid; i < kWarps * kDigits; i += BLOCK) m.s.counters[i] = 0;
+    for (int i = tid; i < 2 * kWarps * P::kMaskWords; i += BLOCK) m.s.peer_masks[i] = 0;
+    __syncthreads();
+
+    uint32_t phase = 0;
+    bool in_flight = false;  // a copy this block started has not been waited for
+    while (true) {
+        const uint32_t tile = m.next_tile;
+        if (tile >= tiles) break;
+        // The hook runs after every thread has read the input buffer: the
+        // buffer's generic-proxy reads are ordered before the copy that
+        // refills it.
+        auto refill = [&]() {
+            if (tid == 0) {
+                m.s.bad = 0;
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                acquire();
+            }
+        };
+        bool ok;
+        if (tile < full_tiles) {
+            // every thread observes the copy's completion; the block leaves
+            // together if any of them gave up
+            if (__syncthreads_or(!os_mbar_wait(&m.bar, phase))) {
+                if (tid == 0) report_error(a.error, kDevErrTimeout);
+                in_flight = true;
+                break;
+            }
+            phase ^= 1u;
+            ok = process_tile<true, BYTE, true, P, U, V, false, KIND, ST, OffT>(a, m.s, tile, kTile, m.in, refill);
+        } else {
+            ok = process_tile<false, BYTE, true, P, U, V, false, KIND, ST, OffT>(
+                a, m.s, tile, int(a.n - uint64_t(tile) * kTile), nullptr, refill);
+        }
+        // the copy started by refill, if any, is for m.next_tile
+        if (!ok) {
+            in_flight = m.next_tile < full_tiles;
+            break;
+        }
+        __syncthreads();  // staging tile, counters and next_tile are free / visible
+    }
+    // Only after an error: wait (bounded) for this block's copy in flight
+    // before its shared memory is released.
+    if (tid == 0 && in_flight && !os_mbar_wait(&m.bar, phase)) report_error(a.error, kDevErrTimeout);
 }
 
 // Wait-timeout probe: one thread waits, with the look-back's bounded wait
@@ -694,16 +868,27 @@ lcpp_status launch_histogram(const Layout& L, unsigned char* temp, const U* keys
     return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;
 }
 
-template <typename U, typename V, bool PAIRS, typename P, int KIND, typename ST, typename OffT, bool BYTE>
+template <typename U, typename V, bool PAIRS, typename P, int KIND, typename ST, typename OffT, bool BYTE, bool BULK>
 void launch_pass(const OnesweepArgs<U, V, ST, OffT>& a, uint64_t tiles, cudaStream_t stream)
 {
-    using Smem = OnesweepSmem<U, V, PAIRS, P, OffT>;
-    auto kernel = onesweep_kernel<U, V, PAIRS, P, KIND, BYTE, ST, OffT>;
-    set_smem_once(kernel, sizeof(Smem));
-    kernel<<<unsigned(tiles), P::kBlock, sizeof(Smem), stream>>>(a);
+    if constexpr (BULK) {
+        static_assert(!PAIRS, "the persistent pass sorts keys only");
+        using Smem = OnesweepBulkSmem<U, V, P, OffT>;
+        auto kernel = onesweep_bulk_kernel<U, V, P, KIND, BYTE, ST, OffT>;
+        set_smem_once(kernel, sizeof(Smem));
+        const uint64_t slots =
+            uint64_t(device_sm_count()) *
+            uint64_t(std::max(1, resident_blocks(reinterpret_cast<const void*>(kernel), P::kBlock, sizeof(Smem))));
+        kernel<<<unsigned(std::min<uint64_t>(tiles, slots)), P::kBlock, sizeof(Smem), stream>>>(a, uint32_t(tiles));
+    } else {
+        using Smem = OnesweepSmem<U, V, PAIRS, P, OffT>;
+        auto kernel = onesweep_kernel<U, V, PAIRS, P, KIND, BYTE, ST, OffT>;
+        set_smem_once(kernel, sizeof(Smem));
+        kernel<<<unsigned(tiles), P::kBlock, sizeof(Smem), stream>>>(a);
+    }
 }
 
-template <typename U, typename V, bool PAIRS, typename P, int KIND, typename ST, typename OffT>
+template <typename U, typename V, bool PAIRS, typename P, int KIND, typename ST, typename OffT, bool BULK>
 lcpp_status launch_passes(const Layout& L, unsigned char* temp, const SortCall& c, uint64_t n,
                           const KeyCodec<U>& codec, int begin_bit, int end_bit, int passes,
                           cudaStream_t stream)
@@ -737,9 +922,9 @@ lcpp_status launch_passes(const Layout& L, unsigned char* temp, const SortCall& 
         a.error = &ctrl->error;
         diag::KernelTimer timer(1 /* LCPP_KERNEL_SORT_ONESWEEP */, n, stream);
         if (sizeof(U) == 4 && a.shift % 8 == 0 && a.digit_mask == 0xffu)
-            launch_pass<U, V, PAIRS, P, KIND, ST, OffT, true>(a, tiles, stream);
+            launch_pass<U, V, PAIRS, P, KIND, ST, OffT, true, BULK>(a, tiles, stream);
         else
-            launch_pass<U, V, PAIRS, P, KIND, ST, OffT, false>(a, tiles, stream);
+            launch_pass<U, V, PAIRS, P, KIND, ST, OffT, false, BULK>(a, tiles, stream);
         timer.stop();
     }
     return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;
@@ -750,10 +935,16 @@ lcpp_status launch_passes(const Layout& L, unsigned char* temp, const SortCall& 
 // 2^27 8-byte keys): 4-byte keys 448 x 28, 70.3 Gkeys/s (512 x 24: 69.0);
 // 4-byte pairs 512 x 16, 46.5 (512 x 14: 44.1); 8-byte keys 384 x 16, 21.3
 // (256 x 20: 19.5); pairs with an 8-byte key or value 256 x 20, 16.6
-// (384 x 16: 16.3).  A build may define these macros to other values; only
-// the chosen policy of each class is compiled.
+// (384 x 16: 16.3).  The persistent bulk-copy pass for 4-byte keys holds two
+// tiles per block (input and staging), so its tile is 448 x 24 to keep two
+// blocks per SM: 0.9095 ms per pass at 2^28 (512 x 20: 0.949; 384 x 28:
+// 0.918).  A build may define these macros to other values; only the chosen
+// policy of each class is compiled.
 #ifndef LCPP_ONESWEEP_4B_KEYS
 #define LCPP_ONESWEEP_4B_KEYS 448, 28, 8, 2
+#endif
+#ifndef LCPP_ONESWEEP_4B_KEYS_BULK
+#define LCPP_ONESWEEP_4B_KEYS_BULK 448, 24, 8, 2
 #endif
 #ifndef LCPP_ONESWEEP_4B_PAIRS
 #define LCPP_ONESWEEP_4B_PAIRS 512, 16, 8, 2
@@ -765,26 +956,40 @@ lcpp_status launch_passes(const Layout& L, unsigned char* temp, const SortCall& 
 #define LCPP_ONESWEEP_8B_PAIRS 256, 20, 8, 2
 #endif
 
-template <typename U, typename V, bool PAIRS, typename P, int KIND>
+template <typename U, typename V, bool PAIRS, typename P, int KIND, bool BULK = false>
 lcpp_status run_policy(const Layout& L, unsigned char* temp, const SortCall& c, uint64_t n,
                        const KeyCodec<U>& codec, int begin_bit, int end_bit, int passes, cudaStream_t stream)
 {
     // 64-bit status words and offsets from 2^30 keys on
     if (L.wide)
-        return launch_passes<U, V, PAIRS, P, KIND, uint64_t, uint64_t>(L, temp, c, n, codec, begin_bit, end_bit,
-                                                                       passes, stream);
-    return launch_passes<U, V, PAIRS, P, KIND, uint32_t, uint32_t>(L, temp, c, n, codec, begin_bit, end_bit, passes,
-                                                                   stream);
+        return launch_passes<U, V, PAIRS, P, KIND, uint64_t, uint64_t, BULK>(L, temp, c, n, codec, begin_bit,
+                                                                             end_bit, passes, stream);
+    return launch_passes<U, V, PAIRS, P, KIND, uint32_t, uint32_t, BULK>(L, temp, c, n, codec, begin_bit, end_bit,
+                                                                         passes, stream);
+}
+
+// Every pass of the call reads its keys from a 16-byte aligned buffer, so
+// the persistent pass can bulk-copy whole tiles.  One tile shape for all of
+// a call's passes: each pass clears the look-back rows of the next one for
+// its own tile count.
+bool sources_aligned(const SortCall& c, int passes)
+{
+    for (int p = 0; p < passes; ++p)
+        if (reinterpret_cast<uintptr_t>(c.keys_src[p]) % 16 != 0) return false;
+    return true;
 }
 
 template <typename U, typename V, bool PAIRS, int KIND>
 lcpp_status run_kind(const Layout& L, unsigned char* temp, const SortCall& c, uint64_t n,
                      const KeyCodec<U>& codec, int begin_bit, int end_bit, int passes, cudaStream_t stream)
 {
-    if constexpr (sizeof(U) == 4 && !PAIRS)
+    if constexpr (sizeof(U) == 4 && !PAIRS) {
+        if (sources_aligned(c, passes))
+            return run_policy<U, V, PAIRS, Policy<LCPP_ONESWEEP_4B_KEYS_BULK>, KIND, true>(
+                L, temp, c, n, codec, begin_bit, end_bit, passes, stream);
         return run_policy<U, V, PAIRS, Policy<LCPP_ONESWEEP_4B_KEYS>, KIND>(L, temp, c, n, codec, begin_bit, end_bit,
                                                                             passes, stream);
-    else if constexpr (sizeof(U) == 4 && sizeof(V) == 4)
+    } else if constexpr (sizeof(U) == 4 && sizeof(V) == 4)
         return run_policy<U, V, PAIRS, Policy<LCPP_ONESWEEP_4B_PAIRS>, KIND>(L, temp, c, n, codec, begin_bit,
                                                                              end_bit, passes, stream);
     else if constexpr (!PAIRS)

@@ -108,10 +108,12 @@ def test_empty_input(lcpp):
 
 # ------------------------------------------------- oracle, dtypes x edge sizes
 # around the tiles of every key / value class (4-byte keys 448 x 28 = 12544,
-# 4-byte pairs 512 x 16 = 8192, 8-byte keys 384 x 16 = 6144, pairs with an
-# 8-byte key or value 256 x 20 = 5120) and multiples of them
-EDGE_SIZES = [1, 2, 31, 33, 255, 5119, 5120, 5121, 6143, 6144, 6145, 8191, 8192, 8193, 12543, 12544, 12545,
-              25089, 65537, 1_000_003]
+# or 448 x 24 = 10752 in the persistent bulk-copy pass, 4-byte pairs 512 x 16
+# = 8192, 8-byte keys 384 x 16 = 6144, pairs with an 8-byte key or value
+# 256 x 20 = 5120) and multiples of them; 3,500,017 keys give every
+# persistent block of a pass several tiles and a partial last tile
+EDGE_SIZES = [1, 2, 31, 33, 255, 5119, 5120, 5121, 6143, 6144, 6145, 8191, 8192, 8193, 10751, 10752, 10753,
+              12543, 12544, 12545, 21505, 25089, 65537, 1_000_003, 3_500_017]
 
 
 def _random_keys(dtype, n, seed):
@@ -137,6 +139,32 @@ def test_keys_vs_oracle(oracle, dtype, n):
         got = gpu_sort(keys, descending=desc)
         exp = oracle.radix_sort(keys, descending=desc, threads=4)
         np.testing.assert_array_equal(got.view(np.uint8), exp.view(np.uint8), err_msg=f"desc={desc}")
+
+
+@pytest.mark.parametrize("dtype", [np.uint32, np.int32, np.float32])
+@pytest.mark.parametrize("n", [10753, 3_500_017])
+@pytest.mark.parametrize("begin,end", [(0, 32), (4, 27)])
+def test_keys_bulk_and_register_paths_agree(oracle, dtype, n, begin, end):
+    """Keys-only 4-byte sorts take the persistent bulk-copy pass when every
+    pass reads a 16-byte aligned buffer and the register-load pass
+    otherwise; buffers 4 bytes past a 16-byte boundary force the latter.
+    Both must equal the oracle bit for bit."""
+    import lcpp_b200 as L
+    from gpu_helpers import NP_TO_CODE
+
+    keys = _random_keys(dtype, n, n + begin)
+    kd = NP_TO_CODE[np.dtype(dtype)]
+    exp = oracle.radix_sort(keys, begin_bit=begin, end_bit=end, threads=4)
+    rs = L.DeviceRadixSort()
+    for off in (0, 1):
+        src = torch.empty(n + 4, dtype=torch.from_numpy(keys[:0]).dtype, device="cuda")
+        dst = torch.empty_like(src)
+        src[off:off + n].copy_(torch.from_numpy(keys).to("cuda"))
+        temp = L.alloc_temp(rs.GetSortKeysTempStorageBytes(kd, n))
+        rs.SortKeys(temp, src[off:off + n], dst[off:off + n], n, begin, end)
+        assert L.device_status(temp) == L.OK
+        got = dst[off:off + n].cpu().numpy()
+        np.testing.assert_array_equal(got.view(np.uint8), exp.view(np.uint8), err_msg=f"buffer offset {off}")
 
 
 @pytest.mark.parametrize("kdtype,vdtype", [(np.uint32, np.uint32), (np.float32, np.uint32),
