@@ -156,6 +156,11 @@ struct lcpp_comm_s {
     std::vector<std::array<unsigned char, 64>> handle;  // per rank: handle of the mapping in `base`
     std::vector<void*> base;                            // per rank: mapped allocation, or null
     cudaEvent_t ev[5] = {};
+    // LCPP_EXCHANGE_COPY: one stream per source rank for the pulls, the fork
+    // event and one join event per source rank (created at first use)
+    std::vector<cudaStream_t> pull_stream;
+    std::vector<cudaEvent_t> pull_done;
+    cudaEvent_t pull_fork = nullptr;
 };
 
 namespace lcpp {
@@ -573,6 +578,11 @@ lcpp_status lcpp_comm_destroy(lcpp_comm comm)
         if (b && cudaIpcCloseMemHandle(b) != cudaSuccess) st = LCPP_ERR_CUDA;
     for (auto& e : comm->ev)
         if (e) cudaEventDestroy(e);
+    for (auto& e : comm->pull_done)
+        if (e) cudaEventDestroy(e);
+    for (auto& q : comm->pull_stream)
+        if (q) cudaStreamDestroy(q);
+    if (comm->pull_fork) cudaEventDestroy(comm->pull_fork);
     if (comm->owned && nccl().comm_destroy(comm->nccl) != ncclSuccess) st = LCPP_ERR_COMM;
     delete comm;
     return st;
@@ -605,7 +615,7 @@ lcpp_status lcpp_dist_sort_keys(lcpp_comm comm, void* temp, size_t temp_bytes, c
     if (!comm) return LCPP_ERR_INVALID_ARG;
     const int kb = dtype_bytes(key_dtype);
     if (!kb) return LCPP_ERR_UNSUPPORTED_DTYPE;
-    if (exchange < LCPP_EXCHANGE_AUTO || exchange > LCPP_EXCHANGE_NCCL) return LCPP_ERR_INVALID_ARG;
+    if (exchange < LCPP_EXCHANGE_AUTO || exchange > LCPP_EXCHANGE_COPY) return LCPP_ERR_INVALID_ARG;
     if (n_local && (!keys_in || !keys_out)) return LCPP_ERR_INVALID_ARG;
     if ((reinterpret_cast<uintptr_t>(keys_in) | reinterpret_cast<uintptr_t>(keys_out)) % kb) return LCPP_ERR_INVALID_ARG;
     if (!ok_temp(temp)) return LCPP_ERR_INVALID_ARG;
@@ -706,36 +716,44 @@ lcpp_status lcpp_dist_sort_keys(lcpp_comm comm, void* temp, size_t temp_bytes, c
     const auto w1 = clock::now();
     if (err) return lcpp_status(err);
     auto seg = [&](int src, int dst) { return pos[size_t(src) * (G + 1) + dst]; };
-    bool peer = exchange != LCPP_EXCHANGE_NCCL;
-    for (int q = 0; q < G; ++q) peer = peer && desc[q].ipc_ok && desc[q].host == desc[0].host;
-    if (exchange == LCPP_EXCHANGE_PEER && !peer) return LCPP_ERR_COMM;
+    bool mapped = exchange != LCPP_EXCHANGE_NCCL;
+    for (int q = 0; q < G; ++q) mapped = mapped && desc[q].ipc_ok && desc[q].host == desc[0].host;
+    if ((exchange == LCPP_EXCHANGE_PEER || exchange == LCPP_EXCHANGE_COPY) && !mapped) return LCPP_ERR_COMM;
+    const bool pull = mapped && exchange == LCPP_EXCHANGE_COPY;
+    const bool peer = mapped && !pull;
 
     // 5. exchange and the first merge level
     std::vector<Run> runs(G), next;
     void* bufs[2];
     int levels = 0;
     while ((1 << levels) < G) ++levels;
+    // rank q's exchange buffer as seen from this rank (its IPC mapping)
+    auto exchange_buffer = [&](int q, const unsigned char** xq) -> lcpp_status {
+        if (q == r) {
+            *xq = static_cast<const unsigned char*>(x);
+            return LCPP_OK;
+        }
+        if (!comm->base[q] || memcmp(comm->handle[q].data(), desc[q].ipc, 64) != 0) {
+            if (comm->base[q]) cudaIpcCloseMemHandle(comm->base[q]);
+            comm->base[q] = nullptr;
+            cudaIpcMemHandle_t hq;
+            memcpy(&hq, desc[q].ipc, sizeof(hq));
+            void* bq = nullptr;
+            if (cudaIpcOpenMemHandle(&bq, hq, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                return LCPP_ERR_COMM;
+            }
+            comm->base[q] = bq;
+            memcpy(comm->handle[q].data(), desc[q].ipc, 64);
+        }
+        *xq = static_cast<const unsigned char*>(comm->base[q]) + desc[q].offset;
+        return LCPP_OK;
+    };
     if (peer) {
         for (int q = 0; q < G; ++q) {
-            const unsigned char* xq;
-            if (q == r) {
-                xq = static_cast<const unsigned char*>(x);
-            } else {
-                if (!comm->base[q] || memcmp(comm->handle[q].data(), desc[q].ipc, 64) != 0) {
-                    if (comm->base[q]) cudaIpcCloseMemHandle(comm->base[q]);
-                    comm->base[q] = nullptr;
-                    cudaIpcMemHandle_t hq;
-                    memcpy(&hq, desc[q].ipc, sizeof(hq));
-                    void* bq = nullptr;
-                    if (cudaIpcOpenMemHandle(&bq, hq, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
-                        cudaGetLastError();
-                        return LCPP_ERR_COMM;
-                    }
-                    comm->base[q] = bq;
-                    memcpy(comm->handle[q].data(), desc[q].ipc, 64);
-                }
-                xq = static_cast<const unsigned char*>(comm->base[q]) + desc[q].offset;
-            }
+            const unsigned char* xq = nullptr;
+            const lcpp_status st = exchange_buffer(q, &xq);
+            if (st != LCPP_OK) return st;
             runs[q] = Run{xq + seg(q, r) * kb, seg(q, r + 1) - seg(q, r)};
         }
         // levels alternate between the run buffer and the output, ending in the output
@@ -747,6 +765,45 @@ lcpp_status lcpp_dist_sort_keys(lcpp_comm comm, void* temp, size_t temp_bytes, c
         // no rank overwrites its exchange buffer (its next call's local sort)
         // before every rank has read its runs from it
         LCPP_NCCL_TRY(N.all_reduce(t + L.barrier, t + L.barrier, 1, ncclInt32, ncclSum, comm->nccl, s));
+    } else if (pull) {
+        // Copy engines pull every run (this rank's own included) into the run
+        // buffer, one stream per source rank so the pulls from different
+        // peers run at the same time; then all merge levels are local.
+        if (comm->pull_stream.empty()) {
+            comm->pull_stream.assign(G, nullptr);
+            comm->pull_done.assign(G, nullptr);
+            LCPP_CUDA_TRY(cudaEventCreateWithFlags(&comm->pull_fork, cudaEventDisableTiming));
+            for (int q = 0; q < G; ++q) {
+                LCPP_CUDA_TRY(cudaStreamCreateWithFlags(&comm->pull_stream[q], cudaStreamNonBlocking));
+                LCPP_CUDA_TRY(cudaEventCreateWithFlags(&comm->pull_done[q], cudaEventDisableTiming));
+            }
+        }
+        unsigned char* rb = t + L.rbuf;
+        uint64_t at = 0;
+        LCPP_CUDA_TRY(cudaEventRecord(comm->pull_fork, s));
+        for (int q = 0; q < G; ++q) {
+            const uint64_t cnt_in = seg(q, r + 1) - seg(q, r);
+            const unsigned char* xq = nullptr;
+            const lcpp_status st = exchange_buffer(q, &xq);
+            if (st != LCPP_OK) return st;
+            const cudaStream_t ps = comm->pull_stream[q];
+            LCPP_CUDA_TRY(cudaStreamWaitEvent(ps, comm->pull_fork, 0));
+            if (cnt_in)
+                LCPP_CUDA_TRY(cudaMemcpyAsync(rb + at * kb, xq + seg(q, r) * kb, cnt_in * kb,
+                                              cudaMemcpyDeviceToDevice, ps));
+            LCPP_CUDA_TRY(cudaEventRecord(comm->pull_done[q], ps));
+            LCPP_CUDA_TRY(cudaStreamWaitEvent(s, comm->pull_done[q], 0));
+            runs[q] = Run{rb + at * kb, cnt_in};
+            at += cnt_in;
+        }
+        // every rank has pulled its runs before any exchange buffer is
+        // overwritten (the merge levels below use this rank's as scratch)
+        LCPP_NCCL_TRY(N.all_reduce(t + L.barrier, t + L.barrier, 1, ncclInt32, ncclSum, comm->nccl, s));
+        bufs[0] = (levels & 1) ? keys_out : x;
+        bufs[1] = (levels & 1) ? x : keys_out;
+        const lcpp_status st = merge_level(runs, bufs[0], kb, key_dtype, t + L.splits, L.splits_bytes, next, s);
+        if (st != LCPP_OK) return st;
+        runs.swap(next);
     } else {
         unsigned char* rb = t + L.rbuf;
         uint64_t at = 0;
@@ -796,7 +853,7 @@ lcpp_status lcpp_dist_sort_keys(lcpp_comm comm, void* temp, size_t temp_bytes, c
         cudaEventElapsedTime(&z.total_ms, comm->ev[0], comm->ev[4]);
         z.host_wait_ms = std::chrono::duration<float, std::milli>(w1 - w0).count();
         z.host_ms = std::chrono::duration<float, std::milli>(clock::now() - t0).count();
-        z.peer_exchange = peer ? 1 : 0;
+        z.peer_exchange = peer ? 1 : pull ? 2 : 0;
         *times = z;
     }
     return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;

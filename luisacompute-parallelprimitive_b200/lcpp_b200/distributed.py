@@ -22,7 +22,7 @@ import os
 
 from . import DeviceRadixSort, DistSortTimes, OP_MIN, OP_SUM, _host_scalar, alloc_temp, check, dtype_code, lib
 
-EXCHANGE = {"auto": 0, "peer": 1, "nccl": 2}
+EXCHANGE = {"auto": 0, "peer": 1, "nccl": 2, "copy": 3}
 
 
 def _stream_ptr():
@@ -295,7 +295,8 @@ def _phase_times(comm, keys, out, dist, exchange="auto"):
     v = torch.tensor([t[k] for k in names], dtype=torch.float64, device="cuda")
     dist.all_reduce(v, op=dist.ReduceOp.MAX)
     d = dict(zip(names, v.tolist()))
-    d["exchange"] = "peer memory (CUDA IPC, plain loads over NVLink)" if t["peer_exchange"] else "NCCL send/recv"
+    d["exchange"] = {1: "peer memory (CUDA IPC, plain loads over NVLink)",
+                     2: "copy-engine pulls over CUDA IPC, local merges"}.get(t["peer_exchange"], "NCCL send/recv")
     return d
 
 
@@ -393,6 +394,9 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
         phases = _phase_times(comm, keys, out, dist)
         # the same call with the runs exchanged by NCCL send / recv instead of peer loads
         phases_nccl = _phase_times(comm, keys, out, dist, exchange="nccl")
+        # and with the runs pulled by copy engines, then merged locally
+        phases_copy = (_phase_times(comm, keys, out, dist, exchange="copy")
+                       if G > 1 and phases["exchange"].startswith("peer") else None)
 
         # e2e: pinned host keys -> device, distributed sort, this rank's part
         # -> host, pipelined over three streams (upload of step s+1 and
@@ -489,7 +493,8 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
         "parity_bit_exact": all(parity.values()), "parity_cases": parity,
         "phases_ms": phases,
         "phases_ms_nccl_exchange": phases_nccl,
-        "roofline": {"bound": "hbm", "kernel": "onesweep_kernel (one 8-bit pass)", "achieved": achieved,
+        "phases_ms_copy_exchange": phases_copy,
+        "roofline": {"bound": "hbm", "kernel": "onesweep_bulk_kernel (one 8-bit pass)", "achieved": achieved,
                      "peak": peak_gbs, "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak_gbs,
                      "algorithmic_bytes_per_launch": 8 * n_local, "avg_launch_ms": avg_pass, "traffic": None},
         "op_roofline": {"hbm_bytes_per_gpu": hbm_bytes, "nvlink_bytes_per_gpu": nvlink_bytes,

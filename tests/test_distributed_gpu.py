@@ -131,9 +131,13 @@ def _worker(rank, world, port, base, q):
             L.testgen_fill(keys, getattr(L, gen), seed=7, offset=rank * base)
             peer = distributed_sort_keys(keys, comm, exchange="auto")
             nccl = distributed_sort_keys(keys, comm, exchange="nccl")
+            pulled = distributed_sort_keys(keys, comm, exchange="copy")
             inplace = keys.clone()
             distributed_sort_keys(inplace, comm, out=inplace)
-            res[name] = (keys.cpu().numpy(), peer.cpu().numpy(), nccl.cpu().numpy(), inplace.cpu().numpy())
+            pulled_inplace = keys.clone()
+            distributed_sort_keys(pulled_inplace, comm, out=pulled_inplace, exchange="copy")
+            res[name] = (keys.cpu().numpy(), peer.cpu().numpy(), nccl.cpu().numpy(), inplace.cpu().numpy(),
+                         pulled.cpu().numpy(), pulled_inplace.cpu().numpy())
         # consecutive calls with a new temp allocation each time (the peers'
         # mappings are opened again)
         steps = []
@@ -181,8 +185,8 @@ def _collect(q, procs, world, limit_s):
 
 @pytest.mark.parametrize("world", [2, 3, 4, 8])
 def test_multi_rank(world):
-    """One process per GPU: the distributed sort in both exchange modes and
-    in place, 4 key types with rank-dependent sizes, consecutive calls on new
+    """One process per GPU: the distributed sort in its three exchange modes
+    (peer loads, NCCL send / receive, copy-engine pulls) and in place, 4 key types with rank-dependent sizes, consecutive calls on new
     temp allocations, scan and reduce -- all bit-exact against host
     references."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
@@ -202,9 +206,9 @@ def test_multi_rank(world):
         ubits = np.uint32 if allk.itemsize == 4 else np.uint64
         pos = 0
         for r in range(world):
-            keys, peer, nccl, inplace = got[r][0][name]
+            keys, peer, nccl, inplace, pulled, pulled_inplace = got[r][0][name]
             want = expect[pos:pos + keys.size].view(ubits)
-            for arr in (peer, nccl, inplace):
+            for arr in (peer, nccl, inplace, pulled, pulled_inplace):
                 np.testing.assert_array_equal(arr.view(ubits), want, err_msg=f"{name} rank {r}")
             pos += keys.size
     for s in range(3):
