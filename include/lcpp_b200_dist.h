@@ -69,9 +69,10 @@ lcpp_status lcpp_comm_rank(lcpp_comm comm, int* rank, int* nranks);
  *   opened at the first call and again whenever a peer's temp allocation
  *   changes; temp must come from cudaMalloc, as PyTorch's caching allocator
  *   does); LCPP_EXCHANGE_NCCL -- NCCL send / receive of the runs;
- *   LCPP_EXCHANGE_COPY -- ranks of one host pull each other's runs with
- *   copy-engine copies (cudaMemcpyAsync over the same IPC mappings, one
- *   stream per source rank) into a local run buffer, then merge locally;
+ *   LCPP_EXCHANGE_COPY -- ranks of one host push their runs into the
+ *   receivers' run buffers with copy-engine copies (cudaMemcpyAsync over the
+ *   same IPC mappings, one stream per receiver), then every merge level is
+ *   local;
  *   LCPP_EXCHANGE_AUTO -- peer when every rank is on one host and exported
  *   its buffer, else NCCL.
  * times (optional): per-phase device times of this call (the call then
@@ -91,7 +92,7 @@ typedef struct lcpp_dist_sort_times {
     float local_merge_ms;    /* remaining merge levels */
     float total_ms;          /* device time of the whole call */
     float host_ms;           /* host time of the whole call */
-    int peer_exchange;       /* 1: runs read over peer memory, 2: pulled by copy engines, 0: NCCL send / receive */
+    int peer_exchange;       /* 1: runs read over peer memory, 2: pushed by copy engines, 0: NCCL send / receive */
 } lcpp_dist_sort_times;
 
 lcpp_status lcpp_dist_sort_keys_temp_bytes(lcpp_comm comm, lcpp_dtype key_dtype, uint64_t n_local,

@@ -156,11 +156,11 @@ struct lcpp_comm_s {
     std::vector<std::array<unsigned char, 64>> handle;  // per rank: handle of the mapping in `base`
     std::vector<void*> base;                            // per rank: mapped allocation, or null
     cudaEvent_t ev[5] = {};
-    // LCPP_EXCHANGE_COPY: one stream per source rank for the pulls, the fork
-    // event and one join event per source rank (created at first use)
-    std::vector<cudaStream_t> pull_stream;
-    std::vector<cudaEvent_t> pull_done;
-    cudaEvent_t pull_fork = nullptr;
+    // LCPP_EXCHANGE_COPY: one stream per receiving rank for the pushes, the
+    // fork event and one join event per receiver (created at first use)
+    std::vector<cudaStream_t> push_stream;
+    std::vector<cudaEvent_t> push_done;
+    cudaEvent_t push_fork = nullptr;
 };
 
 namespace lcpp {
@@ -578,11 +578,11 @@ lcpp_status lcpp_comm_destroy(lcpp_comm comm)
         if (b && cudaIpcCloseMemHandle(b) != cudaSuccess) st = LCPP_ERR_CUDA;
     for (auto& e : comm->ev)
         if (e) cudaEventDestroy(e);
-    for (auto& e : comm->pull_done)
+    for (auto& e : comm->push_done)
         if (e) cudaEventDestroy(e);
-    for (auto& q : comm->pull_stream)
+    for (auto& q : comm->push_stream)
         if (q) cudaStreamDestroy(q);
-    if (comm->pull_fork) cudaEventDestroy(comm->pull_fork);
+    if (comm->push_fork) cudaEventDestroy(comm->push_fork);
     if (comm->owned && nccl().comm_destroy(comm->nccl) != ncclSuccess) st = LCPP_ERR_COMM;
     delete comm;
     return st;
@@ -719,8 +719,8 @@ lcpp_status lcpp_dist_sort_keys(lcpp_comm comm, void* temp, size_t temp_bytes, c
     bool mapped = exchange != LCPP_EXCHANGE_NCCL;
     for (int q = 0; q < G; ++q) mapped = mapped && desc[q].ipc_ok && desc[q].host == desc[0].host;
     if ((exchange == LCPP_EXCHANGE_PEER || exchange == LCPP_EXCHANGE_COPY) && !mapped) return LCPP_ERR_COMM;
-    const bool pull = mapped && exchange == LCPP_EXCHANGE_COPY;
-    const bool peer = mapped && !pull;
+    const bool push = mapped && exchange == LCPP_EXCHANGE_COPY;
+    const bool peer = mapped && !push;
 
     // 5. exchange and the first merge level
     std::vector<Run> runs(G), next;
@@ -765,39 +765,51 @@ lcpp_status lcpp_dist_sort_keys(lcpp_comm comm, void* temp, size_t temp_bytes, c
         // no rank overwrites its exchange buffer (its next call's local sort)
         // before every rank has read its runs from it
         LCPP_NCCL_TRY(N.all_reduce(t + L.barrier, t + L.barrier, 1, ncclInt32, ncclSum, comm->nccl, s));
-    } else if (pull) {
-        // Copy engines pull every run (this rank's own included) into the run
-        // buffer, one stream per source rank so the pulls from different
-        // peers run at the same time; then all merge levels are local.
-        if (comm->pull_stream.empty()) {
-            comm->pull_stream.assign(G, nullptr);
-            comm->pull_done.assign(G, nullptr);
-            LCPP_CUDA_TRY(cudaEventCreateWithFlags(&comm->pull_fork, cudaEventDisableTiming));
+    } else if (push) {
+        // Copy engines push this rank's run for every receiver q into q's run
+        // buffer (through the IPC mapping of q's temp storage, at the place
+        // q expects it: runs in source-rank order), one stream per receiver
+        // so the copies to different peers run at the same time; then every
+        // merge level is local.  A receiver does not touch its run buffer
+        // before the exchange, and the splitter collectives above order this
+        // call's pushes after the receiver's previous call.
+        if (comm->push_stream.empty()) {
+            comm->push_stream.assign(G, nullptr);
+            comm->push_done.assign(G, nullptr);
+            LCPP_CUDA_TRY(cudaEventCreateWithFlags(&comm->push_fork, cudaEventDisableTiming));
             for (int q = 0; q < G; ++q) {
-                LCPP_CUDA_TRY(cudaStreamCreateWithFlags(&comm->pull_stream[q], cudaStreamNonBlocking));
-                LCPP_CUDA_TRY(cudaEventCreateWithFlags(&comm->pull_done[q], cudaEventDisableTiming));
+                LCPP_CUDA_TRY(cudaStreamCreateWithFlags(&comm->push_stream[q], cudaStreamNonBlocking));
+                LCPP_CUDA_TRY(cudaEventCreateWithFlags(&comm->push_done[q], cudaEventDisableTiming));
             }
         }
-        unsigned char* rb = t + L.rbuf;
-        uint64_t at = 0;
-        LCPP_CUDA_TRY(cudaEventRecord(comm->pull_fork, s));
-        for (int q = 0; q < G; ++q) {
-            const uint64_t cnt_in = seg(q, r + 1) - seg(q, r);
+        LCPP_CUDA_TRY(cudaEventRecord(comm->push_fork, s));
+        for (int i = 0; i < G; ++i) {
+            const int q = (r + i) % G;  // receivers in a different order on every rank
             const unsigned char* xq = nullptr;
             const lcpp_status st = exchange_buffer(q, &xq);
             if (st != LCPP_OK) return st;
-            const cudaStream_t ps = comm->pull_stream[q];
-            LCPP_CUDA_TRY(cudaStreamWaitEvent(ps, comm->pull_fork, 0));
-            if (cnt_in)
-                LCPP_CUDA_TRY(cudaMemcpyAsync(rb + at * kb, xq + seg(q, r) * kb, cnt_in * kb,
-                                              cudaMemcpyDeviceToDevice, ps));
-            LCPP_CUDA_TRY(cudaEventRecord(comm->pull_done[q], ps));
-            LCPP_CUDA_TRY(cudaStreamWaitEvent(s, comm->pull_done[q], 0));
+            const SortLayout Lq = sort_layout(kb, desc[q].n, G);
+            unsigned char* rq = const_cast<unsigned char*>(xq) - Lq.xbuf + Lq.rbuf;
+            uint64_t at = 0;  // keys of lower source ranks ahead of this rank's run in q's buffer
+            for (int p2 = 0; p2 < r; ++p2) at += seg(p2, q + 1) - seg(p2, q);
+            const uint64_t cnt = seg(r, q + 1) - seg(r, q);
+            const cudaStream_t ps = comm->push_stream[q];
+            LCPP_CUDA_TRY(cudaStreamWaitEvent(ps, comm->push_fork, 0));
+            if (cnt)
+                LCPP_CUDA_TRY(cudaMemcpyAsync(rq + at * kb, static_cast<const unsigned char*>(x) + seg(r, q) * kb,
+                                              cnt * kb, cudaMemcpyDeviceToDevice, ps));
+            LCPP_CUDA_TRY(cudaEventRecord(comm->push_done[q], ps));
+            LCPP_CUDA_TRY(cudaStreamWaitEvent(s, comm->push_done[q], 0));
+        }
+        unsigned char* rb = t + L.rbuf;
+        uint64_t at = 0;
+        for (int q = 0; q < G; ++q) {
+            const uint64_t cnt_in = seg(q, r + 1) - seg(q, r);
             runs[q] = Run{rb + at * kb, cnt_in};
             at += cnt_in;
         }
-        // every rank has pulled its runs before any exchange buffer is
-        // overwritten (the merge levels below use this rank's as scratch)
+        // every rank's pushes have landed before any rank merges its run
+        // buffer or overwrites its exchange buffer (merge scratch below)
         LCPP_NCCL_TRY(N.all_reduce(t + L.barrier, t + L.barrier, 1, ncclInt32, ncclSum, comm->nccl, s));
         bufs[0] = (levels & 1) ? keys_out : x;
         bufs[1] = (levels & 1) ? x : keys_out;
@@ -853,7 +865,7 @@ lcpp_status lcpp_dist_sort_keys(lcpp_comm comm, void* temp, size_t temp_bytes, c
         cudaEventElapsedTime(&z.total_ms, comm->ev[0], comm->ev[4]);
         z.host_wait_ms = std::chrono::duration<float, std::milli>(w1 - w0).count();
         z.host_ms = std::chrono::duration<float, std::milli>(clock::now() - t0).count();
-        z.peer_exchange = peer ? 1 : pull ? 2 : 0;
+        z.peer_exchange = peer ? 1 : push ? 2 : 0;
         *times = z;
     }
     return cudaGetLastError() == cudaSuccess ? LCPP_OK : LCPP_ERR_CUDA;

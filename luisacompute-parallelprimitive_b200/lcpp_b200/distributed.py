@@ -296,7 +296,7 @@ def _phase_times(comm, keys, out, dist, exchange="auto"):
     dist.all_reduce(v, op=dist.ReduceOp.MAX)
     d = dict(zip(names, v.tolist()))
     d["exchange"] = {1: "peer memory (CUDA IPC, plain loads over NVLink)",
-                     2: "copy-engine pulls over CUDA IPC, local merges"}.get(t["peer_exchange"], "NCCL send/recv")
+                     2: "copy-engine pushes over CUDA IPC, local merges"}.get(t["peer_exchange"], "NCCL send/recv")
     return d
 
 
@@ -394,7 +394,7 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
         phases = _phase_times(comm, keys, out, dist)
         # the same call with the runs exchanged by NCCL send / recv instead of peer loads
         phases_nccl = _phase_times(comm, keys, out, dist, exchange="nccl")
-        # and with the runs pulled by copy engines, then merged locally
+        # and with the runs pushed by copy engines, then merged locally
         phases_copy = (_phase_times(comm, keys, out, dist, exchange="copy")
                        if G > 1 and phases["exchange"].startswith("peer") else None)
 

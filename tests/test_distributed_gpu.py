@@ -131,13 +131,13 @@ def _worker(rank, world, port, base, q):
             L.testgen_fill(keys, getattr(L, gen), seed=7, offset=rank * base)
             peer = distributed_sort_keys(keys, comm, exchange="auto")
             nccl = distributed_sort_keys(keys, comm, exchange="nccl")
-            pulled = distributed_sort_keys(keys, comm, exchange="copy")
+            pushed = distributed_sort_keys(keys, comm, exchange="copy")
             inplace = keys.clone()
             distributed_sort_keys(inplace, comm, out=inplace)
-            pulled_inplace = keys.clone()
-            distributed_sort_keys(pulled_inplace, comm, out=pulled_inplace, exchange="copy")
+            pushed_inplace = keys.clone()
+            distributed_sort_keys(pushed_inplace, comm, out=pushed_inplace, exchange="copy")
             res[name] = (keys.cpu().numpy(), peer.cpu().numpy(), nccl.cpu().numpy(), inplace.cpu().numpy(),
-                         pulled.cpu().numpy(), pulled_inplace.cpu().numpy())
+                         pushed.cpu().numpy(), pushed_inplace.cpu().numpy())
         # consecutive calls with a new temp allocation each time (the peers'
         # mappings are opened again)
         steps = []
@@ -186,7 +186,7 @@ def _collect(q, procs, world, limit_s):
 @pytest.mark.parametrize("world", [2, 3, 4, 8])
 def test_multi_rank(world):
     """One process per GPU: the distributed sort in its three exchange modes
-    (peer loads, NCCL send / receive, copy-engine pulls) and in place, 4 key types with rank-dependent sizes, consecutive calls on new
+    (peer loads, NCCL send / receive, copy-engine pushes) and in place, 4 key types with rank-dependent sizes, consecutive calls on new
     temp allocations, scan and reduce -- all bit-exact against host
     references."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
@@ -206,9 +206,9 @@ def test_multi_rank(world):
         ubits = np.uint32 if allk.itemsize == 4 else np.uint64
         pos = 0
         for r in range(world):
-            keys, peer, nccl, inplace, pulled, pulled_inplace = got[r][0][name]
+            keys, peer, nccl, inplace, pushed, pushed_inplace = got[r][0][name]
             want = expect[pos:pos + keys.size].view(ubits)
-            for arr in (peer, nccl, inplace, pulled, pulled_inplace):
+            for arr in (peer, nccl, inplace, pushed, pushed_inplace):
                 np.testing.assert_array_equal(arr.view(ubits), want, err_msg=f"{name} rank {r}")
             pos += keys.size
     for s in range(3):
