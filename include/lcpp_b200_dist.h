@@ -73,8 +73,9 @@ lcpp_status lcpp_comm_rank(lcpp_comm comm, int* rank, int* nranks);
  *   receivers' run buffers with copy-engine copies (cudaMemcpyAsync over the
  *   same IPC mappings, one stream per receiver), then every merge level is
  *   local;
- *   LCPP_EXCHANGE_AUTO -- peer when every rank is on one host and exported
- *   its buffer, else NCCL.
+ *   LCPP_EXCHANGE_AUTO -- when every rank is on one host and exported its
+ *   buffer: copy-engine pushes (COPY) from 4 ranks on, peer loads (PEER)
+ *   with 2 or 3 ranks; otherwise NCCL.
  * times (optional): per-phase device times of this call (the call then
  *   waits for its own completion). */
 typedef enum lcpp_exchange {

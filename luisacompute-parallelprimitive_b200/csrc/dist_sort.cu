@@ -142,6 +142,7 @@ static_assert(sizeof(Desc) == 128, "descriptor size");
 constexpr int kSubBits = 16;
 constexpr uint32_t kSubEdges = (1u << kSubBits) + 1;  // sub-bucket edges per boundary and round
 constexpr int kMaxRanks = 64;
+constexpr int kPushMinRanks = 4;  // AUTO exchange: copy-engine pushes from this many ranks on
 constexpr uint64_t kMergeTileKeys = 3840;  // output keys per merge block (dist.cu)
 constexpr size_t kMergeCtrlBytes = 256;    // the merge temp's control area (dist.cu)
 
@@ -719,7 +720,11 @@ lcpp_status lcpp_dist_sort_keys(lcpp_comm comm, void* temp, size_t temp_bytes, c
     bool mapped = exchange != LCPP_EXCHANGE_NCCL;
     for (int q = 0; q < G; ++q) mapped = mapped && desc[q].ipc_ok && desc[q].host == desc[0].host;
     if ((exchange == LCPP_EXCHANGE_PEER || exchange == LCPP_EXCHANGE_COPY) && !mapped) return LCPP_ERR_COMM;
-    const bool push = mapped && exchange == LCPP_EXCHANGE_COPY;
+    // AUTO on one host: copy-engine pushes from kPushMinRanks ranks on (at 4
+    // ranks on B200, exchange and first merge 1.70 ms against 2.31 ms with
+    // peer loads for 2^28 keys per rank), peer loads below that
+    const bool push = mapped && (exchange == LCPP_EXCHANGE_COPY ||
+                                 (exchange == LCPP_EXCHANGE_AUTO && G >= kPushMinRanks));
     const bool peer = mapped && !push;
 
     // 5. exchange and the first merge level

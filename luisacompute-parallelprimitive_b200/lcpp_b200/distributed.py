@@ -392,11 +392,13 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
             diag_timing_enable(False)
         value = G * n_local / (ms * 1e-3) / 1e9
         phases = _phase_times(comm, keys, out, dist)
-        # the same call with the runs exchanged by NCCL send / recv instead of peer loads
-        phases_nccl = _phase_times(comm, keys, out, dist, exchange="nccl")
-        # and with the runs pushed by copy engines, then merged locally
-        phases_copy = (_phase_times(comm, keys, out, dist, exchange="copy")
-                       if G > 1 and phases["exchange"].startswith("peer") else None)
+        # the same call under each explicit exchange (every rank takes the
+        # same branch: the condition is the auto choice, identical on all)
+        on_one_host = G > 1 and not phases["exchange"].startswith("NCCL")
+        by_exchange = {"nccl_send_recv": _phase_times(comm, keys, out, dist, exchange="nccl")}
+        if on_one_host:
+            by_exchange["peer_loads"] = _phase_times(comm, keys, out, dist, exchange="peer")
+            by_exchange["copy_engine_pushes"] = _phase_times(comm, keys, out, dist, exchange="copy")
 
         # e2e: pinned host keys -> device, distributed sort, this rank's part
         # -> host, pipelined over three streams (upload of step s+1 and
@@ -487,13 +489,13 @@ def bench_distributed_sort(n_local, steps, warmup, dist, clock_sampler_cls, peak
                    "parallelism": f"sort-partitioned over {G} GPUs ({phases['exchange']})" if G > 1 else "single GPU",
                    "algorithm": "lcpp_dist_sort_keys: local onesweep -> exact splitters refined 16 bits per round on "
                                 "the device (NCCL all-reduce per round, all-gather of boundary ties) -> one host read "
-                                "of the split matrix -> first merge level reading the runs straight from the owners' "
-                                "memory over NVLink -> local merge levels",
+                                "of the split matrix -> exchange: from 4 GPUs copy-engine pushes of every run into "
+                                "the receivers' run buffers over NVLink, then local merge levels; with 2-3 GPUs a "
+                                "first merge level reading the runs straight from the owners' memory",
                    "l2": "inputs larger than L2; no flush"},
         "parity_bit_exact": all(parity.values()), "parity_cases": parity,
         "phases_ms": phases,
-        "phases_ms_nccl_exchange": phases_nccl,
-        "phases_ms_copy_exchange": phases_copy,
+        "phases_ms_by_exchange": by_exchange,
         "roofline": {"bound": "hbm", "kernel": "onesweep_bulk_kernel (one 8-bit pass)", "achieved": achieved,
                      "peak": peak_gbs, "peak_source": peak_src, "unit": "GB/s", "frac": achieved / peak_gbs,
                      "algorithmic_bytes_per_launch": 8 * n_local, "avg_launch_ms": avg_pass, "traffic": None},

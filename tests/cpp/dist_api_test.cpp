@@ -122,7 +122,10 @@ void sort_and_check(lcpp_comm comm, int rank, int ranks, const std::vector<T>& k
     const std::vector<T> got = to_host(d, keys.size());
     CHECK(std::memcmp(got.data(), want.data(), want.size() * sizeof(T)) == 0);
     CHECK(lcpp_device_status(temp, nullptr) == LCPP_OK);
-    if (ranks > 1 && exchange != LCPP_EXCHANGE_NCCL) CHECK(times.peer_exchange == 1);
+    // one host: peer loads (2-3 ranks under AUTO, or PEER) or copy-engine
+    // pushes (4+ ranks under AUTO)
+    if (ranks > 1 && exchange == LCPP_EXCHANGE_PEER) CHECK(times.peer_exchange == 1);
+    if (ranks > 1 && exchange == LCPP_EXCHANGE_AUTO) CHECK(times.peer_exchange == (ranks >= 4 ? 2 : 1));
     cudaFree(d);
     cudaFree(temp);
     (void)rank;
